@@ -1,0 +1,436 @@
+"""Benchmark of the XingLing-0.68B token loop on B200.
+
+Workload (per GPU): the XingLing-0.68B shape in fp32 with seeded N(0, 0.02)
+weights (gains 1.0), a 32-id prompt (uniform ids, seed 0), then 128 greedy
+decode tokens (top_p 0, repetition penalty 1.0).  One step = that prefill +
+128 decode tokens.  The headline `value` is decode tokens/s from CUDA events
+on the engine's stream around each decode step (inputs resident in HBM;
+weights 2.75 GB per token, far above the 126 MB L2, so no flush is needed);
+`e2e` is the same metric through the public API (llm_cpp_engine
+next_token(int)), wall clock, including the per-token host->device copy of
+the step inputs from pinned memory and the device->host read of the result.
+Also reported: prefill of a 512-id prompt (seed 1), the LM-head kernel's
+roofline, the reference's own CPU path on the host cores, and at N > 1 the
+tensor-parallel decode latency (prompt 64, seed 4, greedy 256).
+
+  python bench.py [--gpus N --steps K --warmup W]          # this engine
+  python bench.py --impl reference [...]                   # reference CPU path
+N > 1 runs one engine per GPU (replicas, weak scaling) under torchrun.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "xingling-cpp_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+for _p in (PKG, ORACLE):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import xl_synth as S  # noqa: E402
+
+PROMPT, DECODE, PREFILL_N = 32, 128, 512
+REF_DECODE_SAMPLE = 32
+WEIGHT_DIR = os.environ.get("XL_BENCH_WEIGHTS", os.path.join(tempfile.gettempdir(), "xl_weights", "full"))
+METRIC = "decode tokens/s, XingLing-0.68B fp32, batch 1"
+
+
+def env_int(name: str, default: int) -> int:
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def peaks() -> tuple[dict, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def decode_bytes_per_token(shape: S.ModelShape, ctx: float) -> float:
+    """Algorithmic HBM bytes of one decode token: every Linear weight, bias and
+    gain, the tied LM head (whole embedding table), one embedding row, the
+    final gain, and K and V of `ctx` cached positions in every layer."""
+    H, F, V, L = shape.hidden, shape.ffn, shape.vocab, shape.layers
+    per_layer = 4 * (4 * H * H + 4 * H + 3 * F * H + 2 * F + H + 2 * H)
+    return L * per_layer + 4 * V * H + 4 * H + 4 * H + 2 * L * 4 * H * ctx
+
+
+def prefill_flops(shape: S.ModelShape, n: int) -> float:
+    H, F, L, V = shape.hidden, shape.ffn, shape.layers, shape.vocab
+    linear = 2.0 * n * (4 * H * H + 3 * F * H) * L
+    attn = 4.0 * 64 * shape.heads * L * n * (n + 1) / 2
+    return linear + attn + 2.0 * H * V
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.path = tempfile.mktemp(prefix="xl_clocks_", suffix=".csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sms, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 10 or (self.uuid and parts[1] != self.uuid):
+                    continue
+                try:
+                    sm, mx = float(parts[2]), float(parts[3])
+                except ValueError:
+                    continue
+                sms.append(sm)
+                smax = mx
+                for name, val in zip(names, parts[6:10]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ---------------------------------------------------------------------------
+def cpu_worker(args) -> None:
+    """CPU baseline in its own process (CUDA_VISIBLE_DEVICES=""): the reference's
+    CPU path (oracle/_ref) when built, else the oracle port; prefill of the
+    32-id prompt, then greedy decode for up to `budget` seconds."""
+    import numpy as np
+
+    import oracle
+
+    shape = S.FULL
+    kind = "reference" if oracle.ref_available() else "port"
+    model = oracle.Ref(shape) if kind == "reference" else oracle.Port(shape)
+    model.load(args.weights)
+    ids = S.prompt_ids(0, PROMPT, shape.vocab)
+
+    def pick(logits):
+        if kind == "reference":  # the reference's sample_cpu, greedy settings
+            return oracle.ref_sample(logits, 0.7, 0.0, 1.0, [], 0)[0]
+        return int(np.argmax(logits))
+
+    t0 = time.perf_counter()
+    tok = pick(model.prefill(ids))
+    t_prefill = time.perf_counter() - t0
+    n, t_dec = 0, 0.0
+    while n < DECODE and t_dec < args.budget:
+        t0 = time.perf_counter()
+        tok = pick(model.decode(tok))
+        t_dec += time.perf_counter() - t0
+        n += 1
+    print(json.dumps({"value": n / t_dec, "unit": "tokens/s", "cores": int(os.environ.get("OMP_NUM_THREADS", "1")),
+                      "kind": kind, "prefill_ms": 1e3 * t_prefill,
+                      "sample": f"prefill {PROMPT} ids + {n} greedy decode tokens of the {DECODE}-token workload"}))
+    sys.stdout.flush()
+    os._exit(0)  # the reference's Embedding destructor exits the process on GPU-less hosts
+
+
+def run_cpu_baseline(budget: float) -> dict | None:
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS=str(host_cores()))
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT"):
+        env.pop(k, None)
+    try:
+        r = subprocess.run([sys.executable, os.path.abspath(__file__), "--cpu-worker", "--budget", str(budget),
+                            "--weights", WEIGHT_DIR], env=env, capture_output=True, text=True, timeout=600)
+        for line in r.stdout.splitlines()[::-1]:
+            if line.startswith("{"):
+                return json.loads(line)
+        sys.stderr.write(r.stdout[-2000:] + r.stderr[-2000:])
+    except subprocess.TimeoutExpired:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+def reference_arm(args) -> None:
+    """The reference's own CPU implementation (oracle/_ref, else the oracle port),
+    all host threads, same metric: each step = prefill of the 32-id prompt and a
+    bounded sample of REF_DECODE_SAMPLE greedy decode tokens."""
+    if env_int("RANK", 0) != 0:
+        return
+    os.environ["CUDA_VISIBLE_DEVICES"] = ""
+    os.environ.setdefault("OMP_NUM_THREADS", str(host_cores()))
+    import numpy as np
+
+    import oracle
+
+    shape = S.FULL
+    S.write_weight_tree(WEIGHT_DIR, shape)
+    kind = "reference" if oracle.ref_available() else "port"
+    model = oracle.Ref(shape) if kind == "reference" else oracle.Port(shape)
+    model.load(WEIGHT_DIR)
+    ids = S.prompt_ids(0, PROMPT, shape.vocab)
+
+    def pick(logits):
+        if kind == "reference":
+            return oracle.ref_sample(logits, 0.7, 0.0, 1.0, [], 0)[0]
+        return int(np.argmax(logits))
+
+    def step():
+        tok = pick(model.prefill(ids))
+        t = 0.0
+        for _ in range(REF_DECODE_SAMPLE):
+            t0 = time.perf_counter()
+            tok = pick(model.decode(tok))
+            t += time.perf_counter() - t0
+        return t
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    dec = sum(step() for _ in range(args.steps))
+    wall = time.perf_counter() - t0
+    value = args.steps * REF_DECODE_SAMPLE / dec
+    cores = int(os.environ["OMP_NUM_THREADS"])
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wall / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"decode: prompt {PROMPT} ids (seed 0) + greedy tokens, XingLing-0.68B fp32",
+                   "model": "XingLing-0.68B", "prompt": PROMPT, "decode_tokens_per_step": REF_DECODE_SAMPLE,
+                   "device": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind,
+                         "sample": f"per step: prefill {PROMPT} + {REF_DECODE_SAMPLE} of the {DECODE} decode tokens"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    sys.stdout.flush()
+    os._exit(0)
+
+
+# ---------------------------------------------------------------------------
+def xl_arm(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import llm_cpp_engine
+
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    shape = S.FULL
+    if local == 0:
+        S.write_weight_tree(WEIGHT_DIR, shape)
+    barrier()
+    eng = llm_cpp_engine.InferenceEngine(f"cuda:{local}")
+    eng.load(WEIGHT_DIR)
+    ids = S.prompt_ids(0, PROMPT, shape.vocab)
+
+    def step():
+        w0 = time.perf_counter()
+        tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
+        pre_dev = eng.last_device_ms()
+        w1 = time.perf_counter()
+        dec_dev = 0.0
+        for _ in range(DECODE):
+            tok = eng.next_token(tok, top_p=0.0, repetition_penalty=1.0)
+            dec_dev += eng.last_device_ms()
+        w2 = time.perf_counter()
+        return pre_dev, dec_dev, w1 - w0, w2 - w1
+
+    for _ in range(args.warmup):
+        step()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        pass
+    with Clocks(uuid) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res = [step() for _ in range(args.steps)]
+        torch.cuda.synchronize()
+        barrier()
+        wall = time.perf_counter() - t0
+    clocks = clk.summary()
+
+    dec_dev_s = max_over_ranks(sum(r[1] for r in res) / 1e3)
+    step_dev_s = max_over_ranks(sum(r[0] + r[1] for r in res) / 1e3)
+    dec_wall_s = max_over_ranks(sum(r[3] for r in res))
+    wall = max_over_ranks(wall)
+    tokens = world * args.steps * DECODE
+    value = tokens / dec_dev_s
+    e2e = tokens / dec_wall_s
+
+    pk, pk_kind = peaks()
+    hbm = float(pk["hbm_gbs"])
+    # whole decode step vs the HBM roofline (context grows 32 -> 160 over a step)
+    ctx_mean = PROMPT + (DECODE - 1) / 2.0
+    step_bytes = decode_bytes_per_token(shape, ctx_mean)
+    step_gbs = step_bytes * (args.steps * DECODE) / (sum(r[1] for r in res) / 1e3) / 1e9
+
+    # the dominant kernel: fused final norm + tied LM head (streams the 932 MB table)
+    lm_ms = eng.profile_lm_head(20)
+    lm_bytes = 4.0 * shape.vocab * shape.hidden + shape.vocab + 4.0 * shape.vocab + 8.0 * shape.hidden
+    lm_gbs = lm_bytes / (lm_ms / 1e3) / 1e9
+
+    # prefill of the 512-id prompt (seed 1)
+    pids = S.prompt_ids(1, PREFILL_N, shape.vocab)
+    for _ in range(2):
+        eng.next_token(pids, top_p=0.0, repetition_penalty=1.0)
+    pre_dev, pre_wall = [], []
+    for _ in range(max(3, args.steps)):
+        w0 = time.perf_counter()
+        eng.next_token(pids, top_p=0.0, repetition_penalty=1.0)
+        pre_wall.append(time.perf_counter() - w0)
+        pre_dev.append(eng.last_device_ms())
+    pre_ms = statistics.median(pre_dev)
+    flops = prefill_flops(shape, PREFILL_N)
+    tf32_peak = float(pk.get("bf16_tflops", 1590.0)) / 2.0
+
+    tp_info = None
+    if world > 1:
+        tp_info = tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks)
+
+    if rank != 0:
+        return
+    cpu = run_cpu_baseline(args.cpu_budget) if world == 1 else None
+    h2d = 4 * PROMPT + 36 + DECODE * 32
+    d2h = (DECODE + 1) * 80
+    per_step_launches = (1 + 8 * shape.layers + 2) + DECODE * (5 * shape.layers + 2)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * step_dev_s / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,0.02) fp32 weights (gains 1.0), uniform random prompt ids",
+        "config": {"workload": f"decode: prompt {PROMPT} ids (seed 0) + {DECODE} greedy tokens, batch 1, per GPU",
+                   "model": "XingLing-0.68B", "prompt": PROMPT, "decode_tokens": DECODE,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (2.75 GB of weights per token vs 126 MB L2)",
+                   "value_timing": "CUDA events on the engine stream around each decode step; max over ranks"},
+        "roofline": {"bound": "hbm", "kernel": "norm_gemv_kernel<kGemvLogits> (final norm + tied LM head)",
+                     "achieved": lm_gbs, "peak": hbm, "unit": "GB/s", "frac": lm_gbs / hbm, "traffic": None,
+                     "peak_kind": pk_kind, "bytes_per_launch": lm_bytes, "avg_launch_ms": lm_ms},
+        "step_roofline": {"bound": "hbm", "achieved": step_gbs, "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm,
+                          "bytes_per_token": step_bytes, "mean_ctx": ctx_mean,
+                          "ms_per_token": 1e3 * (sum(r[1] for r in res) / 1e3) / (args.steps * DECODE)},
+        "prefill": {"prompt": PREFILL_N, "device_ms": pre_ms, "ttft_ms": 1e3 * statistics.median(pre_wall),
+                    "tokens_per_s": PREFILL_N / (pre_ms / 1e3), "tflops": flops / (pre_ms / 1e3) / 1e12,
+                    "tf32_peak_tflops": tf32_peak, "tf32_peak_kind": "half of the measured dense bf16 peak",
+                    "frac_of_tf32": flops / (pre_ms / 1e3) / 1e12 / tf32_peak,
+                    "hbm_floor_ms": 1e3 * decode_bytes_per_token(shape, 0) / (hbm * 1e9)},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "llm_cpp_engine.InferenceEngine.next_token"},
+        "gpu_launches": per_step_launches * args.steps,
+        "clocks": clocks,
+    }
+    if tp_info is not None:
+        line["tp"] = tp_info
+    print(json.dumps(line))
+    sys.stdout.flush()
+
+
+def tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks) -> dict:
+    """Tensor-parallel decode across all ranks: prompt 64 (seed 4), greedy 256."""
+    id_holder = [llm_cpp_engine.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(id_holder, src=0)
+    eng = llm_cpp_engine.InferenceEngine(f"cuda:{local}", tp=world, rank=rank, nccl_id=id_holder[0])
+    eng.load(WEIGHT_DIR)
+    ids = S.prompt_ids(4, 64, S.FULL.vocab)
+    n_dec = 256
+
+    def run():
+        tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
+        dev = 0.0
+        toks = [tok]
+        for _ in range(n_dec):
+            tok = eng.next_token(tok, top_p=0.0, repetition_penalty=1.0)
+            dev += eng.last_device_ms()
+            toks.append(tok)
+        return dev, toks
+
+    run()
+    dist.barrier()
+    dev, toks = run()
+    dev = max_over_ranks(dev)
+    del eng
+    return {"tp": world, "prompt": 64, "decode_tokens": n_dec, "ms_per_token": dev / n_dec,
+            "tokens_per_s": n_dec / (dev / 1e3), "first_tokens": toks[:8]}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["xl", "reference"], default="xl")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--budget", type=float, default=15.0, help=argparse.SUPPRESS)
+    ap.add_argument("--weights", default=WEIGHT_DIR, help=argparse.SUPPRESS)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.cpu_worker:
+        cpu_worker(args)
+    elif args.impl == "reference":
+        reference_arm(args)
+    else:
+        xl_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,208 @@
+/*
+ * xl_engine.h — C ABI of the B200-native XingLing token-loop engine
+ * (libxl_engine.so).
+ *
+ * The engine replaces the reference's InferenceEngine / Transformer stack
+ * (fancyovo/XingLing-cpp, include/inference.h:16-38, include/ops.h:174-201)
+ * behind plain C entry points: opaque handles, plain pointers and sizes, and
+ * an int status on every call (XL_OK = 0).  The reference exits the process
+ * on almost every error (include/utils.h:7-36); here each failure is a status
+ * code plus a message from xl_last_error().  The pybind11 module
+ * `llm_cpp_engine` (the reference's Python surface, src/bindings.cpp:7-39)
+ * is a thin layer over these calls.
+ *
+ * The op-level entry points (xl_op_*) run one kernel on device pointers the
+ * caller owns, on the caller's CUDA stream; they exist so that each kernel
+ * can be checked on its own against the oracle, as the reference's own C++
+ * tests check each op (tests/test_*.cu).
+ */
+#ifndef XL_ENGINE_H
+#define XL_ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XL_API __attribute__((visibility("default")))
+
+/* Status codes. */
+enum {
+    XL_OK = 0,
+    XL_ERR_ARG = 1,      /* bad argument (sizes, device string, empty prompt) */
+    XL_ERR_TOKEN = 2,    /* token id outside [0, vocab): reference exits, src/embedding.cu:77-81,113-116 */
+    XL_ERR_CTX = 3,      /* context full: reference exits, src/inference.cu:117-120, src/attn.cu:506-515 */
+    XL_ERR_IO = 4,       /* weight file missing or short: reference throws, src/tensor.cu:113-126 */
+    XL_ERR_CUDA = 5,     /* CUDA runtime error */
+    XL_ERR_NCCL = 6,     /* NCCL error (tensor-parallel engines) */
+    XL_ERR_STATE = 7,    /* call out of order (e.g. decode before load / prefill) */
+    XL_ERR_DEVICE = 8    /* a kernel reported an error through its status word */
+};
+
+/* Model shape.  xl_config_default fills the XingLing-0.68B constants of the
+ * reference's engine constructor (src/inference.cu:19-28): 16 layers, hidden
+ * 1536, 24 heads of 64, FFN 4096, vocab 151669, context 768, RoPE base 1e4.
+ * Smaller shapes (hidden a multiple of 64, ffn a multiple of 8) serve tests. */
+typedef struct xl_config {
+    int layers;
+    int hidden;
+    int heads;
+    int ffn;
+    int vocab;
+    int max_ctx;
+    float rope_base;
+} xl_config;
+
+typedef struct xl_engine xl_engine;
+
+/* Message of the last failed call on this thread ("" if none). */
+XL_API const char* xl_last_error(void);
+
+XL_API void xl_config_default(xl_config* cfg);
+
+/* InferenceEngine::InferenceEngine (src/inference.cu:18-40): builds the
+ * engine on CUDA device `device` (the reference's device string "cuda" is
+ * device 0).  Allocates every weight, the head-major KV cache and the work
+ * buffers once.  tp_size / tp_rank / nccl_id select tensor-parallel decode:
+ * tp_size 1 ignores the other two; otherwise nccl_id points to the
+ * XL_NCCL_ID_BYTES bytes from xl_nccl_unique_id() on rank 0, shared by all
+ * ranks, and every rank must create its engine concurrently. */
+#define XL_NCCL_ID_BYTES 128
+XL_API int xl_engine_create(const xl_config* cfg, int device, int tp_size, int tp_rank, const void* nccl_id,
+                            xl_engine** out);
+XL_API int xl_nccl_unique_id(void* out, int nbytes);
+
+/* Releases all device and host memory of the engine. */
+XL_API void xl_engine_destroy(xl_engine* e);
+
+/* InferenceEngine::load (src/inference.cu:44-46) -> Transformer::load
+ * (src/transformer.cu:139-146): reads the raw little-endian fp32 weight tree
+ * (embedding/weight.bin, norm/weight.bin, blocks/{i}/attn/{Q,K,V,W}/{weight,
+ * bias}.bin, blocks/{i}/ffn/{W1,V,W2}/{weight,bias}.bin,
+ * blocks/{i}/norm{1,2}/weight.bin) into device memory, this rank's shard only. */
+XL_API int xl_engine_load(xl_engine* e, const char* dir);
+
+/* InferenceEngine::next_token(vector) (src/inference.cu:116-136): prefill of
+ * `n` prompt ids (1 <= n <= max_ctx), resets the KV cache and the repetition
+ * set, samples the next id into *token_out and records it in the set. */
+XL_API int xl_engine_prefill(xl_engine* e, const int* ids, int n, float temperature, float top_p,
+                             float repetition_penalty, int* token_out);
+
+/* InferenceEngine::next_token(int) (src/inference.cu:138-151): one decode
+ * step at position ctx_len (XL_ERR_CTX when the cache is full). */
+XL_API int xl_engine_decode(xl_engine* e, int token, float temperature, float top_p, float repetition_penalty,
+                            int* token_out);
+
+/* Sampling-uniform control (no reference counterpart: the reference seeds a
+ * std::mt19937 from std::random_device, src/inference.cu:37-38).  Each
+ * next-token call consumes one uniform in [0, 1): first the queued values
+ * given to xl_engine_set_uniforms (replacing any queue), then the engine's
+ * Philox4x32-10 stream, key = seed, counter = draw index, u = (x0 >> 8) / 2^24. */
+XL_API int xl_engine_set_uniforms(xl_engine* e, const float* u, int n);
+XL_API int xl_engine_seed(xl_engine* e, uint64_t seed);
+/* The uniforms draws [start, start + n) of the Philox stream with key seed
+ * (host only, no GPU needed). */
+XL_API int xl_philox_uniforms(uint64_t seed, uint64_t start, int n, float* out);
+
+/* Tensor-parallel shard plan of rank `rank` of `tp` (host only): out[0] heads
+ * on this rank, out[1] its attention width (heads * 64), out[2] its FFN
+ * columns, out[3] first vocab id of its LM-head shard, out[4] shard size.
+ * Heads and FFN columns split evenly; the vocab splits into tp contiguous
+ * shards of ceil(vocab / tp) ids, the last one shorter.  No reference
+ * counterpart (the reference runs on one device). */
+XL_API int xl_tp_plan(const xl_config* cfg, int tp, int rank, int* out);
+
+/* Copies this rank's logits of the last step (after the repetition penalty,
+ * before temperature) to host memory: n must equal xl_engine_vocab_shard(). */
+XL_API int xl_engine_last_logits(xl_engine* e, float* out, int n);
+XL_API int xl_engine_vocab_shard(const xl_engine* e, int* begin, int* count);
+
+/* KVcache::n of the reference (src/attn.cu:11-16): cached positions. */
+XL_API int xl_engine_ctx_len(const xl_engine* e);
+
+/* Copies cache rows [0, npos) of one layer, as the reference's position-major
+ * [npos][heads][64] layout, for this rank's heads. */
+XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, float* v_out);
+
+/* Device time of the last prefill / decode call in milliseconds (CUDA events
+ * around the device work, excluding host copies). */
+XL_API int xl_engine_last_device_ms(const xl_engine* e, float* ms);
+
+/* Launches the engine's fused final-norm + LM-head kernel (the largest single
+ * kernel of a decode step: it streams the whole tied embedding table) `iters`
+ * times back to back on the engine's stream and returns the mean duration
+ * from CUDA events.  Leaves the logits of the last step unchanged in value. */
+XL_API int xl_engine_profile_lm_head(xl_engine* e, int iters, float* avg_ms);
+
+/* ---- op-level entry points (device pointers, caller's stream) ---------- */
+
+/* RMSNorm::forward (src/rmsnorm.cu:112-147) fused with
+ * Linear::forward_vec (src/linear.cu:309-357), plus epilogues:
+ * mode 0: y = W.norm(x) + b;  mode 1: SwiGLU over interleaved (W1, V) rows,
+ * y[j] = silu(a_j + b_2j) * (c_j + b_2j+1) (src/ffn.cu:126-139);
+ * mode 2: y += W.x + b (residual, src/transformer.cu:54-59).
+ * gamma may be NULL (no norm).  W is [m][k] row-major, k % 4 == 0. */
+XL_API int xl_op_norm_gemv(int mode, const float* x, const float* gamma, const float* w, const float* b, float* y,
+                           int m, int k, void* stream);
+
+/* The RoPE angle table of src/rope.cu:47-68 on the host:
+ * out[(pos * 32 + j) * 2 + {0, 1}] = {cos, sin}(base^(-2j/64) * pos) for
+ * pos < max_ctx, j < 32, each angle formed in fp32 as the reference does.
+ * Ops taking `rope` expect this table copied to device memory. */
+XL_API int xl_rope_table(float base, int max_ctx, float* out);
+
+/* RoPE::forward_vec (src/rope.cu:130-165) + KV append +
+ * MultiHeadAttention::forward (src/attn.cu:490-547) for one token at
+ * position pos (device int).  qkv = [q | k | v] of `heads` heads (pre-RoPE);
+ * kc / vc are head-major [heads][max_ctx][64].  workspace: at least
+ * xl_op_attn_decode_workspace_bytes(heads, max_ctx) bytes, zero-filled
+ * before first use (the kernel leaves it zeroed). */
+XL_API size_t xl_op_attn_decode_workspace_bytes(int heads, int max_ctx);
+XL_API int xl_op_attn_decode(const float* qkv, const float* rope, float* kc, float* vc, float* out, const int* pos,
+                             int heads, int max_ctx, void* workspace, void* stream);
+
+/* Embedding::inverse (src/embedding.cu:173-205) fused with the final RMSNorm
+ * (gamma may be NULL) and the repetition penalty of sample_cpu
+ * (src/inference.cu:71-74): logits[v] = E[v].x, penalised where
+ * rep_flags[v] != 0; *argmax_out receives the id of the largest logit
+ * (lowest id on ties).  workspace: xl_op_lm_head_workspace_bytes() bytes,
+ * zero-filled before first use. */
+XL_API size_t xl_op_lm_head_workspace_bytes(void);
+XL_API int xl_op_lm_head(const float* x, const float* gamma, const float* table, float* logits,
+                         const uint8_t* rep_flags, float repetition_penalty, int vocab, int k, int* argmax_out,
+                         void* workspace, void* stream);
+
+/* sample_cpu (src/inference.cu:69-114) on the device with the uniform r
+ * supplied: top-1024 by value, / (T + 0.001), softmax, top-p prefix, draw.
+ * logits must already carry the repetition penalty.  workspace:
+ * xl_op_sample_workspace_bytes(vocab) bytes; synchronous (the id is
+ * returned in *token_out). */
+XL_API size_t xl_op_sample_workspace_bytes(int vocab);
+XL_API int xl_op_sample(const float* logits, int vocab, float temperature, float top_p, float r, int* token_out,
+                        void* workspace, void* stream);
+
+/* Linear::forward (src/linear.cu:197-253): Y[n][m] = X[n][k] . W[m][k]^T + b
+ * with the same three modes as xl_op_norm_gemv (SwiGLU writes [n][m/2]). */
+XL_API int xl_op_linear(int mode, const float* x, const float* w, const float* b, float* y, int n, int m, int k,
+                        void* stream);
+
+/* RMSNorm::forward on [n][k] rows (out may alias x). */
+XL_API int xl_op_rmsnorm(const float* x, const float* gamma, float* out, int n, int k, void* stream);
+
+/* Embedding::forward (src/embedding.cu:75-110): out[i] = table[ids[i]]
+ * (ids on the device, validated by the caller). */
+XL_API int xl_op_embedding(const float* table, const int* ids, float* out, int n, int k, void* stream);
+
+/* RoPE::forward on q and k (src/rope.cu:70-106) + KV-cache fill +
+ * MultiHeadAttention::prefill (src/attn.cu:319-365): qkv is [n][3*heads*64]
+ * (q rotated in place), out is [n][heads*64]. */
+XL_API int xl_op_attn_prefill(float* qkv, const float* rope, float* kc, float* vc, float* out, int n, int heads,
+                              int max_ctx, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XL_ENGINE_H */

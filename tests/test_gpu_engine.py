@@ -1,0 +1,156 @@
+"""Engine-level parity: llm_cpp_engine.InferenceEngine (through libxl_engine.so)
+against the oracle port on the same seeded weight tree and prompts.
+
+Bar (see the module docstring of xl_synth for the workload):
+* logits within 1e-3 x (max - min) of the oracle's, every step;
+* greedy tokens identical except where the oracle's top-2 gap is below that;
+* KV cache within 1e-5 abs of the oracle's; V rows bit-exact is not required
+  (they come out of a GEMV), the KV position counter is exact;
+* sampled steps teacher-forced: the oracle's token history is fed to both and
+  the chosen ids must agree wherever the decision is not within tolerance.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+import xl_synth as S
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def eng_mod(built):
+    import llm_cpp_engine
+
+    return llm_cpp_engine
+
+
+def logits_of(eng):
+    return np.frombuffer(eng.last_logits(), dtype=np.float32)
+
+
+def assert_logits_close(got, ref, frac=1e-3):
+    span = float(ref.max() - ref.min())
+    err = float(np.abs(got - ref).max())
+    assert err <= frac * span, f"max |dlogit| {err:.3e} > {frac} x range {span:.3f}"
+
+
+def top2_gap(ref):
+    a = np.partition(ref, -2)[-2:]
+    return float(a[1] - a[0])
+
+
+def check_token(tok_got, tok_ref, ref_logits, frac=1e-3):
+    if tok_got != tok_ref:
+        gap = top2_gap(ref_logits)
+        span = float(ref_logits.max() - ref_logits.min())
+        assert gap < frac * span, f"token {tok_got} != oracle {tok_ref} with top-2 gap {gap:.3e}"
+
+
+def run_greedy(eng, port, ids, steps):
+    tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
+    ref = port.prefill(ids)
+    assert_logits_close(logits_of(eng), ref)
+    check_token(tok, int(np.argmax(ref)), ref)
+    tok_ref = int(np.argmax(ref))
+    toks = [tok]
+    for _ in range(steps):
+        tok = eng.next_token(tok_ref, top_p=0.0, repetition_penalty=1.0)  # teacher-forced on the oracle
+        ref = port.decode(tok_ref)
+        assert_logits_close(logits_of(eng), ref)
+        check_token(tok, int(np.argmax(ref)), ref)
+        tok_ref = int(np.argmax(ref))
+        toks.append(tok)
+    return toks
+
+
+def test_tiny_greedy_and_kv(eng_mod, tiny_weights):
+    sh = S.TINY
+    eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
+    eng.load(tiny_weights)
+    port = O.Port(sh)
+    port.load(tiny_weights)
+    ids = S.prompt_ids(0, 37, sh.vocab)
+    run_greedy(eng, port, ids, 12)
+    assert eng.ctx_len() == port.n == 37 + 12
+    for layer in range(sh.layers):
+        kb, vb = eng.kv(layer, eng.ctx_len(), sh.heads)
+        k = np.frombuffer(kb, np.float32).reshape(-1, sh.heads, 64)
+        v = np.frombuffer(vb, np.float32).reshape(-1, sh.heads, 64)
+        kr, vr = port.kv(layer, port.n)
+        assert np.abs(k - kr).max() < 1e-5 and np.abs(v - vr).max() < 1e-5
+
+
+def test_tiny_kv_reset_rounds(eng_mod, tiny_weights):
+    """Prefill resets the cache; decode appends (tests/test_transformer.cu:100-129)."""
+    sh = S.TINY
+    eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
+    eng.load(tiny_weights)
+    rng = np.random.default_rng(777)
+    for rnd in range(3):
+        n = 5 + 4 * rnd
+        ids = [int(t) for t in rng.integers(0, sh.vocab, n)]
+        t = eng.next_token(ids)
+        assert eng.ctx_len() == n
+        for _ in range(2):
+            t = eng.next_token(t)
+        assert eng.ctx_len() == n + 2
+
+
+def test_tiny_context_limit_and_errors(eng_mod, tiny_weights):
+    sh = S.ModelShape(layers=2, hidden=256, heads=4, ffn=512, vocab=2048, max_ctx=40)
+    eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
+    eng.load(tiny_weights)
+    with pytest.raises(RuntimeError):
+        eng.next_token(5)  # decode before any prefill
+    with pytest.raises(ValueError):
+        eng.next_token([1, 2, sh.vocab])  # bad id
+    with pytest.raises(RuntimeError):
+        eng.next_token(list(range(41)))  # longer than the context
+    t = eng.next_token(list(range(38)))
+    t = eng.next_token(t)
+    t = eng.next_token(t)  # fills position 39
+    assert eng.ctx_len() == 40
+    with pytest.raises(RuntimeError):
+        eng.next_token(t)  # the reference exits here (src/attn.cu:506-515)
+    with pytest.raises(ValueError):
+        eng_mod.InferenceEngine("cpu")
+
+
+def test_tiny_sampled_teacher_forced(eng_mod, tiny_weights):
+    sh = S.TINY
+    eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
+    eng.load(tiny_weights)
+    port = O.Port(sh)
+    port.load(tiny_weights)
+    T, P, RP = 0.7, 0.9, 1.1
+    u = S.philox_uniforms(3, 40)
+    eng.set_uniforms([float(x) for x in u])
+    ids = S.prompt_ids(2, 50, sh.vocab)
+    rep: list[int] = []
+    tok = eng.next_token(ids, temperature=T, top_p=P, repetition_penalty=RP)
+    ref = port.prefill(ids)
+    mismatches = 0
+    for step in range(30):
+        assert_logits_close(logits_of(eng), O.apply_penalty(ref, rep, RP))
+        tok_ref = O.sample(ref, T, P, RP, rep, float(u[step]))
+        mismatches += tok != tok_ref
+        rep.append(tok_ref)
+        # teacher-force the oracle's choice; keep the engine's repetition set in step
+        if tok != tok_ref:
+            pytest.fail(f"step {step}: engine sampled {tok}, oracle {tok_ref}")
+        tok = eng.next_token(tok_ref, temperature=T, top_p=P, repetition_penalty=RP)
+        ref = port.decode(tok_ref)
+    assert mismatches == 0
+
+
+def test_full_greedy_prompt32(eng_mod, full_weights):
+    """XingLing-0.68B, prompt of 32 ids (seed 0), greedy: prefill + 16 decode steps vs the oracle."""
+    sh = S.FULL
+    eng = eng_mod.InferenceEngine("cuda")
+    eng.load(full_weights)
+    port = O.Port(sh)
+    port.load(full_weights)
+    ids = S.prompt_ids(0, 32, sh.vocab)
+    run_greedy(eng, port, ids, 16)
+    assert eng.ctx_len() == 48

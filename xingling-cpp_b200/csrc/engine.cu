@@ -1,0 +1,735 @@
+// Host side of the XingLing engine: weights and KV cache resident in HBM,
+// one CUDA graph per decode step, direct launches for prefill, NCCL for
+// tensor parallelism.  Mirrors the reference's InferenceEngine / Transformer
+// (src/inference.cu:18-151, src/transformer.cu:107-186) with status codes
+// instead of exit(1).
+#include <sys/stat.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <string>
+#include <utility>
+
+#include "engine.h"
+
+namespace xl {
+
+namespace {
+thread_local std::string g_err;
+constexpr double kEps = 1e-6;  // RMSNorm eps, src/rmsnorm.cu:72,100
+constexpr size_t kStagingBytes = 64u << 20;
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct PinnedBuf {
+    void* p = nullptr;
+    ~PinnedBuf() {
+        if (p) cudaFreeHost(p);
+    }
+};
+}  // namespace
+
+void set_error(const std::string& msg) { g_err = msg; }
+const char* last_error() { return g_err.c_str(); }
+void clear_error() { g_err.clear(); }
+
+// ---------------------------------------------------------------------------
+uint32_t philox4x32_10_x0(uint64_t ctr, uint64_t seed) {
+    uint32_t c0 = static_cast<uint32_t>(ctr), c1 = static_cast<uint32_t>(ctr >> 32), c2 = 0, c3 = 0;
+    uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
+    for (int round = 0; round < 10; ++round) {
+        const uint64_t p0 = static_cast<uint64_t>(0xD2511F53u) * c0;
+        const uint64_t p1 = static_cast<uint64_t>(0xCD9E8D57u) * c2;
+        const uint32_t hi0 = static_cast<uint32_t>(p0 >> 32), lo0 = static_cast<uint32_t>(p0);
+        const uint32_t hi1 = static_cast<uint32_t>(p1 >> 32), lo1 = static_cast<uint32_t>(p1);
+        c0 = hi1 ^ c1 ^ k0;
+        c1 = lo1;
+        c2 = hi0 ^ c3 ^ k1;
+        c3 = lo0;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    return c0;
+}
+
+float philox_uniform(uint64_t ctr, uint64_t seed) {
+    return static_cast<float>(philox4x32_10_x0(ctr, seed) >> 8) * (1.0f / 16777216.0f);
+}
+
+void fill_rope_table(float base, int max_ctx, float* out) {
+    for (int pos = 0; pos < max_ctx; ++pos) {
+        for (int j = 0; j < kHalfHead; ++j) {
+            // theta formed in fp32 as src/rope.cu:57 (powf, then * pos).
+            const float theta = std::pow(base, -2.0f * j / 64) * static_cast<float>(pos);
+            out[(pos * kHalfHead + j) * 2 + 0] = std::cos(theta);
+            out[(pos * kHalfHead + j) * 2 + 1] = std::sin(theta);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+int Engine::cuda_fail(cudaError_t e, const char* what) {
+    set_error(std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e));
+    return XL_ERR_CUDA;
+}
+
+int Engine::nccl_fail(ncclResult_t r, const char* what) {
+    set_error(std::string("NCCL error in ") + what + ": " + ncclGetErrorString(r));
+    return XL_ERR_NCCL;
+}
+
+#define XL_CUDA(call)                                        \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call);  \
+    } while (0)
+
+#define XL_NCCL(call)                                        \
+    do {                                                     \
+        ncclResult_t r_ = (call);                            \
+        if (r_ != ncclSuccess) return nccl_fail(r_, #call);  \
+    } while (0)
+
+int make_tp_plan(const xl_config& cfg, int tp, int rank, TpPlan* out) {
+    if (tp < 1 || rank < 0 || rank >= tp || cfg.heads % tp || cfg.ffn % tp) {
+        set_error("tensor parallel: tp_size must divide heads and ffn, 0 <= rank < tp_size");
+        return XL_ERR_ARG;
+    }
+    if (cfg.hidden % 8 || (cfg.ffn / tp) % 8) {
+        set_error("config: hidden and the per-rank ffn width must be multiples of 8");
+        return XL_ERR_ARG;
+    }
+    const int vper = (cfg.vocab + tp - 1) / tp;
+    out->heads = cfg.heads / tp;
+    out->hidden = out->heads * kHeadDim;
+    out->ffn = cfg.ffn / tp;
+    out->vocab_begin = rank * vper;
+    out->vocab_count = std::max(0, std::min(vper, cfg.vocab - rank * vper));
+    if (out->vocab_count <= 0) {
+        set_error("tensor parallel: empty vocab shard");
+        return XL_ERR_ARG;
+    }
+    return XL_OK;
+}
+
+int Engine::create(const xl_config& cfg, int device, int tp_size, int tp_rank, const void* nccl_id, Engine** out) {
+    *out = nullptr;
+    Engine* e = new Engine();
+    int rc = e->init(cfg, device, tp_size, tp_rank, nccl_id);
+    if (rc != XL_OK) {
+        delete e;
+        return rc;
+    }
+    *out = e;
+    return XL_OK;
+}
+
+int Engine::init(const xl_config& cfg, int device, int tp_size, int tp_rank, const void* nccl_id) {
+    if (cfg.layers <= 0 || cfg.hidden <= 0 || cfg.heads <= 0 || cfg.ffn <= 0 || cfg.vocab <= 0 || cfg.max_ctx <= 0) {
+        set_error("config: every size must be positive");
+        return XL_ERR_ARG;
+    }
+    if (cfg.hidden != cfg.heads * kHeadDim) {
+        set_error("config: hidden must equal heads * 64");
+        return XL_ERR_ARG;
+    }
+    TpPlan plan;
+    const int prc = make_tp_plan(cfg, tp_size, tp_rank, &plan);
+    if (prc != XL_OK) return prc;
+    cfg_ = cfg;
+    device_ = device;
+    tp_ = tp_size;
+    rank_ = tp_rank;
+    H_ = cfg.hidden;
+    heads_l_ = plan.heads;
+    Hl_ = plan.hidden;
+    F_ = cfg.ffn;
+    Fl_ = plan.ffn;
+    V_ = cfg.vocab;
+    T_ = cfg.max_ctx;
+    v0_ = plan.vocab_begin;
+    vl_ = plan.vocab_count;
+    int ndev = 0;
+    XL_CUDA(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) {
+        set_error("device ordinal out of range");
+        return XL_ERR_ARG;
+    }
+    XL_CUDA(cudaSetDevice(device_));
+    XL_CUDA(cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, device_));
+    XL_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    XL_CUDA(cudaEventCreate(&ev0_));
+    XL_CUDA(cudaEventCreate(&ev1_));
+    XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_in_), sizeof(DevState), cudaHostAllocDefault));
+    XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_out_), sizeof(DevState), cudaHostAllocDefault));
+    XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_ids_), sizeof(int) * (T_ + 1), cudaHostAllocDefault));
+    std::random_device rd;
+    philox_seed_ = (static_cast<uint64_t>(rd()) << 32) ^ rd();
+    int rc = alloc_all();
+    if (rc != XL_OK) return rc;
+    if (tp_ > 1) {
+        if (nccl_id == nullptr) {
+            set_error("tensor parallel: nccl_id is required when tp_size > 1");
+            return XL_ERR_ARG;
+        }
+        ncclUniqueId id;
+        std::memcpy(&id, nccl_id, sizeof(id));
+        XL_NCCL(ncclCommInitRank(&comm_, tp_, id, rank_));
+    }
+    return XL_OK;
+}
+
+int Engine::alloc_all() {
+    const size_t H = H_, Hl = Hl_, Fl = Fl_, T = T_, V = V_, vl = vl_;
+    const int maxs = attn_max_splits(T_);
+    std::vector<std::pair<void**, size_t>> plan;
+    auto add = [&](void* slot, size_t bytes) { plan.emplace_back(reinterpret_cast<void**>(slot), bytes); };
+    add(&emb_, V * H * 4);
+    add(&gnorm_, H * 4);
+    add(&rope_, T * kHalfHead * 8);
+    layers_.assign(cfg_.layers, LayerWeights{});
+    for (auto& L : layers_) {
+        add(&L.wqkv, 3 * Hl * H * 4);
+        add(&L.bqkv, 3 * Hl * 4);
+        add(&L.wo, H * Hl * 4);
+        add(&L.bo, H * 4);
+        add(&L.w13, 2 * Fl * H * 4);
+        add(&L.b13, 2 * Fl * 4);
+        add(&L.w2, H * Fl * 4);
+        add(&L.b2, H * 4);
+        add(&L.g1, H * 4);
+        add(&L.g2, H * 4);
+        add(&L.kc, heads_l_ * T * kHeadDim * 4);
+        add(&L.vc, heads_l_ * T * kHeadDim * 4);
+    }
+    add(&xa_, H * 4);
+    add(&xb_, H * 4);
+    add(&qkv_, 3 * Hl * 4);
+    add(&att_, Hl * 4);
+    add(&ffh_, Fl * 4);
+    add(&part_, H * 4);
+    add(&logits_, vl * 4);
+    add(&attn_ws_, static_cast<size_t>(heads_l_) * maxs * (kHeadDim + 2) * 4);
+    add(&attn_cnt_, heads_l_ * 4);
+    add(&rep_flags_, vl);
+    add(&st_, sizeof(DevState));
+    add(&px_, T * H * 4);
+    add(&pxn_, T * H * 4);
+    add(&pqkv_, T * 3 * Hl * 4);
+    add(&patt_, T * H * 4);
+    add(&pffh_, T * Fl * 4);
+    add(&pids_, T * 4);
+    size_t total = 0;
+    for (auto& pr : plan) total += align_up(pr.second, 256);
+    XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&arena_), total));
+    arena_bytes_ = total;
+    XL_CUDA(cudaMemset(arena_, 0, total));
+    size_t off = 0;
+    for (auto& pr : plan) {
+        *pr.first = arena_ + off;
+        off += align_up(pr.second, 256);
+    }
+    std::vector<float> table(static_cast<size_t>(T_) * kHalfHead * 2);
+    fill_rope_table(cfg_.rope_base, T_, table.data());
+    XL_CUDA(cudaMemcpy(rope_, table.data(), table.size() * 4, cudaMemcpyHostToDevice));
+    return XL_OK;
+}
+
+Engine::~Engine() {
+    cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
+    if (comm_) ncclCommDestroy(comm_);
+    if (arena_) cudaFree(arena_);
+    if (h_in_) cudaFreeHost(h_in_);
+    if (h_out_) cudaFreeHost(h_out_);
+    if (h_ids_) cudaFreeHost(h_ids_);
+    if (ev0_) cudaEventDestroy(ev0_);
+    if (ev1_) cudaEventDestroy(ev1_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+// ---------------------------------------------------------------------------
+// Weight loading: Tensor::load (src/tensor.cu:113-126) reads raw fp32 and
+// fails on a short file.  Rows [r0, r1) x columns [c0, c1) of a [rows][cols]
+// file go to dst with a destination pitch, through pinned staging.
+namespace {
+struct Loader {
+    std::string dir;
+    char* staging = nullptr;
+    cudaStream_t stream = nullptr;
+    std::string err;
+
+    int copy(const std::string& rel, size_t rows, size_t cols, size_t r0, size_t r1, size_t c0, size_t c1, void* dst,
+             size_t dpitch_bytes, size_t elem_pitch_bytes = 0) {
+        const std::string path = dir + "/" + rel;
+        struct stat sb;
+        if (stat(path.c_str(), &sb) != 0) {
+            err = "cannot open weight file " + path;
+            return XL_ERR_IO;
+        }
+        if (static_cast<size_t>(sb.st_size) < rows * cols * 4) {
+            err = "weight file too short: " + path + " (" + std::to_string(sb.st_size) + " bytes, need " +
+                  std::to_string(rows * cols * 4) + ")";
+            return XL_ERR_IO;
+        }
+        FILE* f = std::fopen(path.c_str(), "rb");
+        if (!f) {
+            err = "cannot open weight file " + path;
+            return XL_ERR_IO;
+        }
+        const size_t row_bytes = cols * 4;
+        const size_t chunk_rows = std::max<size_t>(1, kStagingBytes / row_bytes);
+        int rc = XL_OK;
+        for (size_t r = r0; r < r1 && rc == XL_OK; r += chunk_rows) {
+            const size_t nr = std::min(chunk_rows, r1 - r);
+            if (std::fseek(f, static_cast<long>(r * row_bytes), SEEK_SET) != 0 ||
+                std::fread(staging, row_bytes, nr, f) != nr) {
+                err = "read failed: " + path;
+                rc = XL_ERR_IO;
+                break;
+            }
+            char* d = static_cast<char*>(dst) + (r - r0) * dpitch_bytes;
+            const size_t width = elem_pitch_bytes ? 4 : (c1 - c0) * 4;
+            cudaError_t ce;
+            if (elem_pitch_bytes) {
+                // scatter single elements with a pitch (bias interleave); rows == 1
+                ce = cudaMemcpy2DAsync(d, elem_pitch_bytes, staging + c0 * 4, 4, width, c1 - c0,
+                                       cudaMemcpyHostToDevice, stream);
+            } else {
+                ce = cudaMemcpy2DAsync(d, dpitch_bytes, staging + c0 * 4, row_bytes, width, nr, cudaMemcpyHostToDevice,
+                                       stream);
+            }
+            if (ce == cudaSuccess) ce = cudaStreamSynchronize(stream);
+            if (ce != cudaSuccess) {
+                err = std::string("H2D copy failed for ") + path + ": " + cudaGetErrorString(ce);
+                rc = XL_ERR_CUDA;
+            }
+        }
+        std::fclose(f);
+        return rc;
+    }
+};
+}  // namespace
+
+int Engine::load(const char* dir) {
+    XL_CUDA(cudaSetDevice(device_));
+    if (dir == nullptr) {
+        set_error("load: null path");
+        return XL_ERR_ARG;
+    }
+    PinnedBuf pin;
+    XL_CUDA(cudaHostAlloc(&pin.p, kStagingBytes, cudaHostAllocDefault));
+    Loader ld;
+    ld.dir = dir;
+    ld.staging = static_cast<char*>(pin.p);
+    ld.stream = stream_;
+    const size_t H = H_, Hl = Hl_, Fl = Fl_, F = F_;
+    const size_t hq0 = static_cast<size_t>(rank_) * Hl, hq1 = hq0 + Hl;
+    const size_t f0 = static_cast<size_t>(rank_) * Fl, f1 = f0 + Fl;
+    int rc = XL_OK;
+    auto chk = [&](int r) {
+        if (rc == XL_OK && r != XL_OK) rc = r;
+    };
+    // Embedding (full table: the decode gather may need any row) and final norm.
+    chk(ld.copy("embedding/weight.bin", V_, H, 0, V_, 0, H, emb_, H * 4));
+    chk(ld.copy("norm/weight.bin", 1, H, 0, 1, 0, H, gnorm_, H * 4));
+    for (int l = 0; l < cfg_.layers && rc == XL_OK; ++l) {
+        const std::string b = "blocks/" + std::to_string(l) + "/";
+        LayerWeights& L = layers_[l];
+        const char* qkv_names[3] = {"attn/Q", "attn/K", "attn/V"};
+        for (int i = 0; i < 3; ++i) {
+            chk(ld.copy(b + qkv_names[i] + "/weight.bin", H, H, hq0, hq1, 0, H, L.wqkv + i * Hl * H, H * 4));
+            chk(ld.copy(b + qkv_names[i] + "/bias.bin", 1, H, 0, 1, hq0, hq1, L.bqkv + i * Hl, Hl * 4));
+        }
+        chk(ld.copy(b + "attn/W/weight.bin", H, H, 0, H, hq0, hq1, L.wo, Hl * 4));
+        if (rank_ == 0) chk(ld.copy(b + "attn/W/bias.bin", 1, H, 0, 1, 0, H, L.bo, H * 4));
+        chk(ld.copy(b + "ffn/W1/weight.bin", F, H, f0, f1, 0, H, L.w13, 2 * H * 4));
+        chk(ld.copy(b + "ffn/V/weight.bin", F, H, f0, f1, 0, H, L.w13 + H, 2 * H * 4));
+        chk(ld.copy(b + "ffn/W1/bias.bin", 1, F, 0, 1, f0, f1, L.b13, 0, 8));
+        chk(ld.copy(b + "ffn/V/bias.bin", 1, F, 0, 1, f0, f1, L.b13 + 1, 0, 8));
+        chk(ld.copy(b + "ffn/W2/weight.bin", H, F, 0, H, f0, f1, L.w2, Fl * 4));
+        if (rank_ == 0) chk(ld.copy(b + "ffn/W2/bias.bin", 1, H, 0, 1, 0, H, L.b2, H * 4));
+        chk(ld.copy(b + "norm1/weight.bin", 1, H, 0, 1, 0, H, L.g1, H * 4));
+        chk(ld.copy(b + "norm2/weight.bin", 1, H, 0, 1, 0, H, L.g2, H * 4));
+    }
+    if (rc != XL_OK) {
+        set_error(ld.err);
+        return rc;
+    }
+    loaded_ = true;
+    has_seq_ = false;
+    n_ = 0;
+    rc = capture_decode_graph();
+    return rc;
+}
+
+// ---------------------------------------------------------------------------
+// One decode step, Transformer::forward(int) (src/transformer.cu:180-186):
+// gather -> 16 x [norm1+QKV, RoPE+KV append+attention, out-proj+residual,
+// norm2+W1/V+SwiGLU, W2+residual] -> final norm + LM head -> sampler.
+int Engine::enqueue_decode(cudaStream_t s) {
+    float* cur = xa_;
+    float* other = xb_;
+    bool pending = false;  // TP: part_ holds a reduced delta not yet added to cur
+    for (int l = 0; l < cfg_.layers; ++l) {
+        const LayerWeights& L = layers_[l];
+        NormGemvParams p{};
+        p.gamma = L.g1;
+        p.eps = kEps;
+        p.W = L.wqkv;
+        p.bias = L.bqkv;
+        p.y = qkv_;
+        p.M = 3 * Hl_;
+        p.K = H_;
+        if (l == 0) {
+            p.table = emb_;
+            p.token = &st_->in.token_in;
+            p.x_out = cur;
+        } else if (pending) {
+            p.x = cur;
+            p.delta = part_;
+            p.x_out = other;
+            std::swap(cur, other);
+            pending = false;
+        } else {
+            p.x = cur;
+        }
+        XL_CUDA(launch_norm_gemv(kGemvPlain, p, num_sms_, true, s));
+
+        AttnDecodeParams a{};
+        a.qkv = qkv_;
+        a.rope = rope_;
+        a.kc = L.kc;
+        a.vc = L.vc;
+        a.out = att_;
+        a.part = attn_ws_;
+        a.counters = attn_cnt_;
+        a.pos = &st_->pos;
+        a.heads = heads_l_;
+        a.max_ctx = T_;
+        XL_CUDA(launch_attn_decode(a, true, s));
+
+        NormGemvParams o{};
+        o.x = att_;
+        o.W = L.wo;
+        o.bias = L.bo;
+        o.M = H_;
+        o.K = Hl_;
+        if (tp_ == 1) {
+            o.y = cur;
+            XL_CUDA(launch_norm_gemv(kGemvResidual, o, num_sms_, true, s));
+        } else {
+            o.y = part_;
+            XL_CUDA(launch_norm_gemv(kGemvPlain, o, num_sms_, true, s));
+            XL_NCCL(ncclAllReduce(part_, part_, H_, ncclFloat, ncclSum, comm_, s));
+            pending = true;
+        }
+
+        NormGemvParams f{};
+        f.gamma = L.g2;
+        f.eps = kEps;
+        f.W = L.w13;
+        f.bias = L.b13;
+        f.y = ffh_;
+        f.M = 2 * Fl_;
+        f.K = H_;
+        f.x = cur;
+        if (pending) {
+            f.delta = part_;
+            f.x_out = other;
+            std::swap(cur, other);
+            pending = false;
+        }
+        XL_CUDA(launch_norm_gemv(kGemvSwiGLU, f, num_sms_, true, s));
+
+        NormGemvParams d{};
+        d.x = ffh_;
+        d.W = L.w2;
+        d.bias = L.b2;
+        d.M = H_;
+        d.K = Fl_;
+        if (tp_ == 1) {
+            d.y = cur;
+            XL_CUDA(launch_norm_gemv(kGemvResidual, d, num_sms_, true, s));
+        } else {
+            d.y = part_;
+            XL_CUDA(launch_norm_gemv(kGemvPlain, d, num_sms_, true, s));
+            XL_NCCL(ncclAllReduce(part_, part_, H_, ncclFloat, ncclSum, comm_, s));
+            pending = true;
+        }
+    }
+    lm_x_ = cur;
+    return run_lm_head_and_sample(cur, pending ? part_ : nullptr, s);
+}
+
+// Final norm + tied LM head (Embedding::inverse, src/embedding.cu:173-205)
+// over this rank's vocab shard, argmax merge across ranks, then the sampler.
+int Engine::launch_lm_head(const float* x_last, const float* delta, bool pdl, cudaStream_t s) {
+    NormGemvParams h{};
+    h.x = x_last;
+    h.delta = delta;
+    h.gamma = gnorm_;
+    h.eps = kEps;
+    h.W = emb_ + static_cast<size_t>(v0_) * H_;
+    h.y = logits_;
+    h.M = vl_;
+    h.K = H_;
+    h.rep_flags = rep_flags_;
+    h.st = st_;
+    h.row_offset = v0_;
+    XL_CUDA(launch_norm_gemv(kGemvLogits, h, num_sms_, pdl, s));
+    return XL_OK;
+}
+
+int Engine::run_lm_head_and_sample(const float* x_last, const float* delta, cudaStream_t s) {
+    const int rc = launch_lm_head(x_last, delta, true, s);
+    if (rc != XL_OK) return rc;
+    if (tp_ > 1) XL_NCCL(ncclAllReduce(&st_->argmax_final, &st_->argmax_final, 1, ncclUint64, ncclMax, comm_, s));
+    SampleParams sp{};
+    sp.logits = logits_;
+    sp.V = vl_;
+    sp.v0 = v0_;
+    sp.st = st_;
+    sp.rep_flags = rep_flags_;
+    sp.full = 0;
+    XL_CUDA(launch_sample(sp, true, s));
+    return XL_OK;
+}
+
+int Engine::capture_decode_graph() {
+    if (decode_exec_) {
+        cudaGraphExecDestroy(decode_exec_);
+        decode_exec_ = nullptr;
+    }
+    cudaGraph_t g = nullptr;
+    XL_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_decode(stream_);
+    cudaError_t ce = cudaStreamEndCapture(stream_, &g);
+    if (rc != XL_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+    ce = cudaGraphInstantiate(&decode_exec_, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
+    return XL_OK;
+}
+
+float Engine::next_uniform() {
+    if (!uniforms_.empty()) {
+        const float u = uniforms_.front();
+        uniforms_.pop_front();
+        return u;
+    }
+    return philox_uniform(philox_ctr_++, philox_seed_);
+}
+
+int Engine::finish_step(int* token_out) {
+    XL_CUDA(cudaEventRecord(ev1_, stream_));
+    XL_CUDA(cudaMemcpyAsync(h_out_, st_, sizeof(DevState), cudaMemcpyDeviceToHost, stream_));
+    XL_CUDA(cudaStreamSynchronize(stream_));
+    XL_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
+    const DevState* hs = reinterpret_cast<const DevState*>(h_out_);
+    if (hs->err != 0) {
+        set_error("device error word " + std::to_string(hs->err));
+        return XL_ERR_DEVICE;
+    }
+    *token_out = hs->token_out;
+    return XL_OK;
+}
+
+// InferenceEngine::next_token(vector), src/inference.cu:116-136.
+int Engine::prefill(const int* ids, int n, float temperature, float top_p, float rp, int* token_out) {
+    XL_CUDA(cudaSetDevice(device_));
+    if (!loaded_) {
+        set_error("prefill before load");
+        return XL_ERR_STATE;
+    }
+    if (ids == nullptr || n <= 0) {
+        set_error("prefill: empty prompt");
+        return XL_ERR_ARG;
+    }
+    if (n > T_) {
+        set_error("Input sequence length exceeds max_seq_len (" + std::to_string(n) + " > " + std::to_string(T_) + ")");
+        return XL_ERR_CTX;
+    }
+    if (tp_ > 1 && top_p > 0.0f) {
+        set_error("tensor-parallel engines sample greedily only (top_p <= 0)");
+        return XL_ERR_ARG;
+    }
+    for (int i = 0; i < n; ++i) {
+        if (ids[i] < 0 || ids[i] >= V_) {
+            set_error("Embedding : Invalid token: " + std::to_string(ids[i]) + " ( i = " + std::to_string(i) +
+                      " ), vocabulary size = " + std::to_string(V_));
+            return XL_ERR_TOKEN;
+        }
+    }
+    std::memcpy(h_ids_, ids, sizeof(int) * n);
+    StepIn in{};
+    in.token_in = 0;
+    in.temperature = temperature;
+    in.top_p = top_p;
+    in.rp = rp;
+    in.uniform = next_uniform();
+    in.decode_mode = 0;
+    DevState* hs = reinterpret_cast<DevState*>(h_in_);
+    std::memset(hs, 0, sizeof(DevState));
+    hs->in = in;
+    hs->pos = n;
+    cudaStream_t s = stream_;
+    XL_CUDA(cudaMemcpyAsync(pids_, h_ids_, sizeof(int) * n, cudaMemcpyHostToDevice, s));
+    // in + pos: the first 36 bytes of DevState
+    XL_CUDA(cudaMemcpyAsync(st_, hs, offsetof(DevState, pos) + sizeof(int), cudaMemcpyHostToDevice, s));
+    XL_CUDA(cudaMemsetAsync(rep_flags_, 0, vl_, s));
+    XL_CUDA(cudaEventRecord(ev0_, s));
+
+    const size_t H = H_;
+    XL_CUDA(launch_embed_gather(emb_, pids_, px_, n, H_, s));
+    for (int l = 0; l < cfg_.layers; ++l) {
+        const LayerWeights& L = layers_[l];
+        XL_CUDA(launch_rmsnorm_rows(px_, L.g1, pxn_, n, H_, 1e-6f, s));
+        XL_CUDA(launch_linear_prefill(kGemvPlain, pxn_, L.wqkv, L.bqkv, pqkv_, n, 3 * Hl_, H_, s));
+        XL_CUDA(launch_rope_kv_prefill(pqkv_, rope_, L.kc, L.vc, n, heads_l_, T_, s));
+        XL_CUDA(launch_attn_prefill(pqkv_, L.kc, L.vc, patt_, n, heads_l_, T_, s));
+        if (tp_ == 1) {
+            XL_CUDA(launch_linear_prefill(kGemvResidual, patt_, L.wo, L.bo, px_, n, H_, Hl_, s));
+        } else {
+            XL_CUDA(launch_linear_prefill(kGemvPlain, patt_, L.wo, L.bo, pxn_, n, H_, Hl_, s));
+            XL_NCCL(ncclAllReduce(pxn_, pxn_, n * H, ncclFloat, ncclSum, comm_, s));
+            XL_CUDA(launch_add_rows(px_, pxn_, n * H_, s));
+        }
+        XL_CUDA(launch_rmsnorm_rows(px_, L.g2, pxn_, n, H_, 1e-6f, s));
+        XL_CUDA(launch_linear_prefill(kGemvSwiGLU, pxn_, L.w13, L.b13, pffh_, n, 2 * Fl_, H_, s));
+        if (tp_ == 1) {
+            XL_CUDA(launch_linear_prefill(kGemvResidual, pffh_, L.w2, L.b2, px_, n, H_, Fl_, s));
+        } else {
+            XL_CUDA(launch_linear_prefill(kGemvPlain, pffh_, L.w2, L.b2, pxn_, n, H_, Fl_, s));
+            XL_NCCL(ncclAllReduce(pxn_, pxn_, n * H, ncclFloat, ncclSum, comm_, s));
+            XL_CUDA(launch_add_rows(px_, pxn_, n * H_, s));
+        }
+    }
+    int rc = run_lm_head_and_sample(px_ + static_cast<size_t>(n - 1) * H, nullptr, s);
+    if (rc != XL_OK) return rc;
+    rc = finish_step(token_out);
+    if (rc != XL_OK) return rc;
+    n_ = n;
+    has_seq_ = true;
+    return XL_OK;
+}
+
+// InferenceEngine::next_token(int), src/inference.cu:138-151.
+int Engine::decode(int token, float temperature, float top_p, float rp, int* token_out) {
+    XL_CUDA(cudaSetDevice(device_));
+    if (!loaded_) {
+        set_error("decode before load");
+        return XL_ERR_STATE;
+    }
+    if (!has_seq_) {
+        set_error("decode before any prefill: the KV cache is empty");
+        return XL_ERR_STATE;
+    }
+    if (token < 0 || token >= V_) {
+        set_error("Embedding : Invalid token: " + std::to_string(token));
+        return XL_ERR_TOKEN;
+    }
+    if (n_ >= T_) {
+        set_error("KV cache full: position " + std::to_string(n_) + " of max_seq_len " + std::to_string(T_));
+        return XL_ERR_CTX;
+    }
+    if (tp_ > 1 && top_p > 0.0f) {
+        set_error("tensor-parallel engines sample greedily only (top_p <= 0)");
+        return XL_ERR_ARG;
+    }
+    StepIn* in = h_in_;
+    std::memset(in, 0, sizeof(StepIn));
+    in->token_in = token;
+    in->temperature = temperature;
+    in->top_p = top_p;
+    in->rp = rp;
+    in->uniform = next_uniform();
+    in->decode_mode = 1;
+    XL_CUDA(cudaMemcpyAsync(&st_->in, in, sizeof(StepIn), cudaMemcpyHostToDevice, stream_));
+    XL_CUDA(cudaEventRecord(ev0_, stream_));
+    XL_CUDA(cudaGraphLaunch(decode_exec_, stream_));
+    const int rc = finish_step(token_out);
+    if (rc != XL_OK) return rc;
+    n_ += 1;
+    return XL_OK;
+}
+
+int Engine::profile_lm_head(int iters, float* avg_ms) {
+    XL_CUDA(cudaSetDevice(device_));
+    if (!loaded_ || iters <= 0 || avg_ms == nullptr) {
+        set_error("profile_lm_head: needs a loaded engine and iters > 0");
+        return XL_ERR_ARG;
+    }
+    if (tp_ > 1) {
+        set_error("profile_lm_head: single-rank engines only");
+        return XL_ERR_ARG;
+    }
+    // Same kernel, same arguments as the decode graph's LM head (its residual
+    // stream, final norm, full tied table), without PDL.
+    int rc = launch_lm_head(lm_x_, nullptr, false, stream_);
+    if (rc != XL_OK) return rc;
+    XL_CUDA(cudaEventRecord(ev0_, stream_));
+    for (int i = 0; i < iters && rc == XL_OK; ++i) rc = launch_lm_head(lm_x_, nullptr, false, stream_);
+    if (rc != XL_OK) return rc;
+    XL_CUDA(cudaEventRecord(ev1_, stream_));
+    XL_CUDA(cudaEventSynchronize(ev1_));
+    float ms = 0.0f;
+    XL_CUDA(cudaEventElapsedTime(&ms, ev0_, ev1_));
+    *avg_ms = ms / static_cast<float>(iters);
+    return XL_OK;
+}
+
+int Engine::set_uniforms(const float* u, int n) {
+    if (n < 0 || (n > 0 && u == nullptr)) {
+        set_error("set_uniforms: bad array");
+        return XL_ERR_ARG;
+    }
+    uniforms_.assign(u, u + n);
+    return XL_OK;
+}
+
+int Engine::seed(uint64_t s) {
+    philox_seed_ = s;
+    philox_ctr_ = 0;
+    uniforms_.clear();
+    return XL_OK;
+}
+
+int Engine::last_logits(float* out, int n) {
+    XL_CUDA(cudaSetDevice(device_));
+    if (n != vl_ || out == nullptr) {
+        set_error("last_logits: n must equal the vocab shard size " + std::to_string(vl_));
+        return XL_ERR_ARG;
+    }
+    XL_CUDA(cudaMemcpyAsync(out, logits_, sizeof(float) * vl_, cudaMemcpyDeviceToHost, stream_));
+    XL_CUDA(cudaStreamSynchronize(stream_));
+    return XL_OK;
+}
+
+int Engine::kv_copy(int layer, int npos, float* k_out, float* v_out) {
+    XL_CUDA(cudaSetDevice(device_));
+    if (layer < 0 || layer >= cfg_.layers || npos < 0 || npos > T_) {
+        set_error("kv_copy: layer or npos out of range");
+        return XL_ERR_ARG;
+    }
+    if (npos == 0) return XL_OK;
+    const LayerWeights& L = layers_[layer];
+    for (int h = 0; h < heads_l_; ++h) {
+        const size_t src_off = static_cast<size_t>(h) * T_ * kHeadDim;
+        XL_CUDA(cudaMemcpy2DAsync(k_out + h * kHeadDim, Hl_ * 4, L.kc + src_off, kHeadDim * 4,
+                                  kHeadDim * 4, npos, cudaMemcpyDeviceToHost, stream_));
+        XL_CUDA(cudaMemcpy2DAsync(v_out + h * kHeadDim, Hl_ * 4, L.vc + src_off, kHeadDim * 4,
+                                  kHeadDim * 4, npos, cudaMemcpyDeviceToHost, stream_));
+    }
+    XL_CUDA(cudaStreamSynchronize(stream_));
+    return XL_OK;
+}
+
+}  // namespace xl

@@ -1,0 +1,128 @@
+// XingLing token-loop engine on one B200 (or one tensor-parallel rank).
+#pragma once
+#include <cuda_runtime.h>
+#include <nccl.h>
+#include <stdint.h>
+
+#include <deque>
+#include <string>
+#include <vector>
+
+#include "../../include/xl_engine.h"
+#include "xl_kernels.h"
+
+namespace xl {
+
+// Thread-local last-error message behind xl_last_error().
+void set_error(const std::string& msg);
+const char* last_error();
+void clear_error();
+
+struct LayerWeights {
+    float* wqkv;  // [3*Hl][H]: this rank's Q rows, then K rows, then V rows
+    float* bqkv;  // [3*Hl]
+    float* wo;    // [H][Hl]: columns of this rank's heads
+    float* bo;    // [H] (zero on ranks > 0)
+    float* w13;   // [2*Fl][H]: rows (W1 j, V j) interleaved
+    float* b13;   // [2*Fl]
+    float* w2;    // [H][Fl]
+    float* b2;    // [H] (zero on ranks > 0)
+    float* g1;    // [H]
+    float* g2;    // [H]
+    float* kc;    // [heads_l][max_ctx][64]
+    float* vc;    // [heads_l][max_ctx][64]
+};
+
+class Engine {
+   public:
+    static int create(const xl_config& cfg, int device, int tp_size, int tp_rank, const void* nccl_id, Engine** out);
+    ~Engine();
+
+    int load(const char* dir);
+    int prefill(const int* ids, int n, float temperature, float top_p, float rp, int* token_out);
+    int decode(int token, float temperature, float top_p, float rp, int* token_out);
+    int set_uniforms(const float* u, int n);
+    int seed(uint64_t s);
+    int last_logits(float* out, int n);
+    int kv_copy(int layer, int npos, float* k_out, float* v_out);
+    int profile_lm_head(int iters, float* avg_ms);
+    int ctx_len() const { return n_; }
+    float last_device_ms() const { return last_ms_; }
+    int vocab_begin() const { return v0_; }
+    int vocab_count() const { return vl_; }
+
+   private:
+    Engine() = default;
+    int init(const xl_config& cfg, int device, int tp_size, int tp_rank, const void* nccl_id);
+    int alloc_all();
+    int capture_decode_graph();
+    int enqueue_decode(cudaStream_t s);
+    int run_lm_head_and_sample(const float* x_last, const float* delta, cudaStream_t s);
+    int launch_lm_head(const float* x_last, const float* delta, bool pdl, cudaStream_t s);
+    const float* lm_x_ = nullptr;  // residual stream the decode graph's LM head reads
+    int finish_step(int* token_out);
+    float next_uniform();
+    int cuda_fail(cudaError_t e, const char* what);
+    int nccl_fail(ncclResult_t r, const char* what);
+
+    xl_config cfg_{};
+    int device_ = 0;
+    int num_sms_ = 148;
+    int tp_ = 1, rank_ = 0;
+    int H_ = 0, Hl_ = 0, heads_l_ = 0, F_ = 0, Fl_ = 0, V_ = 0, v0_ = 0, vl_ = 0, T_ = 0;
+
+    // device memory
+    char* arena_ = nullptr;
+    size_t arena_bytes_ = 0;
+    float* emb_ = nullptr;     // [V][H] (full table: gather needs every row)
+    float* gnorm_ = nullptr;   // [H]
+    float2* rope_ = nullptr;   // [T][32]
+    std::vector<LayerWeights> layers_;
+    float* xa_ = nullptr;      // decode residual stream (ping)
+    float* xb_ = nullptr;      // decode residual stream (pong, TP)
+    float* qkv_ = nullptr;     // [3*Hl]
+    float* att_ = nullptr;     // [Hl]
+    float* ffh_ = nullptr;     // [Fl]
+    float* part_ = nullptr;    // [H] TP partial sums
+    float* logits_ = nullptr;  // [vl]
+    float* attn_ws_ = nullptr; // split-K partials
+    int* attn_cnt_ = nullptr;  // [heads_l] split counters
+    uint8_t* rep_flags_ = nullptr;  // [vl]
+    DevState* st_ = nullptr;
+    // prefill buffers [T][...]
+    float *px_ = nullptr, *pxn_ = nullptr, *pqkv_ = nullptr, *patt_ = nullptr, *pffh_ = nullptr;
+    int* pids_ = nullptr;
+
+    // host
+    StepIn* h_in_ = nullptr;   // pinned
+    int* h_out_ = nullptr;     // pinned: token_out, err
+    int* h_ids_ = nullptr;     // pinned prompt staging
+    cudaStream_t stream_ = nullptr;
+    cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
+    cudaGraphExec_t decode_exec_ = nullptr;
+    ncclComm_t comm_ = nullptr;
+
+    bool loaded_ = false;
+    bool has_seq_ = false;
+    int n_ = 0;
+    float last_ms_ = 0.0f;
+    std::deque<float> uniforms_;
+    uint64_t philox_seed_ = 0;
+    uint64_t philox_ctr_ = 0;
+};
+
+// Tensor-parallel partition of one rank (see xl_tp_plan in xl_engine.h).
+struct TpPlan {
+    int heads, hidden, ffn, vocab_begin, vocab_count;
+};
+int make_tp_plan(const xl_config& cfg, int tp, int rank, TpPlan* out);
+
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11): counter (ctr, 0, 0, 0),
+// key (seed lo, seed hi); returns the first output word.
+uint32_t philox4x32_10_x0(uint64_t ctr, uint64_t seed);
+float philox_uniform(uint64_t ctr, uint64_t seed);
+
+// RoPE angle table of the reference (src/rope.cu:47-68), (cos, sin) pairs.
+void fill_rope_table(float base, int max_ctx, float* out);
+
+}  // namespace xl

@@ -1,0 +1,103 @@
+// Host-side launchers for the XingLing sm_100a kernels.  Every launcher is
+// asynchronous on the given stream and returns the launch status.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace xl {
+
+constexpr int kHeadDim = 64;   // XingLing attention head width (src/inference.cu:19-28: 1536 / 24)
+constexpr int kHalfHead = 32;  // rotate-half RoPE pairs (j, j + 32), src/rope.cu:20-45
+constexpr int kTopK = 1024;    // sampler candidate count, src/inference.cu:66
+
+// Host-written inputs of one step (copied to the device before each call).
+struct StepIn {
+    int token_in;       // decode input id
+    float temperature;  // sample_cpu arguments, src/inference.cu:69-76
+    float top_p;
+    float rp;
+    float uniform;      // the draw r in [0, 1), src/inference.cu:105
+    int decode_mode;    // 1: the sampler also advances pos (decode), 0: prefill
+    int pad[2];
+};
+
+// Device-resident state of one engine (one sequence per GPU).
+struct DevState {
+    StepIn in;
+    int pos;                          // positions in the KV cache (the reference's KVcache::n)
+    int token_out;                    // last sampled id
+    int greedy_token;                 // argmax of the penalised logits of the last LM-head pass
+    int lm_done;                      // scratch: LM-head CTAs finished (zero between steps)
+    unsigned long long argmax_key;    // scratch for the LM-head argmax (zero between steps)
+    unsigned long long argmax_final;  // packed (value, id) of the winning logit
+    int err;                          // device-side error bits (0 = ok)
+    int pad[3];
+};
+
+enum GemvMode : int {
+    kGemvPlain = 0,     // y[m] = W[m].x + b[m]
+    kGemvSwiGLU = 1,    // rows interleaved (W1 row j, V row j): y[j] = silu(a + b1[j]) * (c + bv[j])
+    kGemvResidual = 2,  // y[m] += W[m].x + b[m]   (y is the residual stream)
+    kGemvLogits = 3,    // y[m] = E[m].x with repetition penalty; argmax into DevState
+};
+
+struct NormGemvParams {
+    const float* x;        // input vector [K] (ignored when table != nullptr)
+    const float* table;    // gather source: x = table[*token] (decode embedding)
+    const int* token;      // device token id for the gather
+    const float* delta;    // optional addend: x_eff = x + delta
+    float* x_out;          // optional: block 0 stores x_eff here (residual stream)
+    const float* gamma;    // optional RMSNorm gain (nullptr: no norm)
+    double eps;
+    const float* W;        // [M][K] row-major
+    const float* bias;     // [M] or nullptr
+    float* y;              // output
+    int M, K;
+    // kGemvLogits only
+    const uint8_t* rep_flags;  // [M] 1 = id was sampled since the last prefill
+    DevState* st;
+    int row_offset;        // global id of row 0 (vocab shard start)
+};
+
+cudaError_t launch_norm_gemv(int mode, const NormGemvParams& p, int num_sms, bool pdl, cudaStream_t s);
+
+struct AttnDecodeParams {
+    const float* qkv;      // [3 * heads * 64]: q | k | v of this token (pre-RoPE)
+    const float2* rope;    // [max_ctx][32] (cos, sin)
+    float* kc;             // [heads][max_ctx][64] this layer's key cache
+    float* vc;             // [heads][max_ctx][64]
+    float* out;            // [heads * 64]
+    float* part;           // scratch [heads][max_splits][66]
+    int* counters;         // scratch [heads], zero between calls
+    const int* pos;        // device position n (the new token's slot)
+    int heads, max_ctx;
+};
+constexpr int kAttnChunk = 64;
+__host__ __device__ inline int attn_max_splits(int max_ctx) { return (max_ctx + kAttnChunk - 1) / kAttnChunk; }
+cudaError_t launch_attn_decode(const AttnDecodeParams& p, bool pdl, cudaStream_t s);
+
+struct SampleParams {
+    const float* logits;   // [V] penalised logits of this vocab shard
+    int V;                 // shard size
+    int v0;                // global id of shard row 0
+    DevState* st;
+    uint8_t* rep_flags;    // [V]
+    int full;              // 1: always run the full top-k path (no argmax shortcut)
+};
+cudaError_t launch_sample(const SampleParams& p, bool pdl, cudaStream_t s);
+
+// ---- prefill ----
+cudaError_t launch_embed_gather(const float* table, const int* ids, float* out, int n, int k, cudaStream_t s);
+cudaError_t launch_rmsnorm_rows(const float* x, const float* gamma, float* out, int n, int k, float eps,
+                                cudaStream_t s);
+// Y[N][M] (+)= X[N][K] . W[M][K]^T + b; mode as GemvMode (Plain / SwiGLU / Residual).
+cudaError_t launch_linear_prefill(int mode, const float* X, const float* W, const float* b, float* Y, int n,
+                                  int m, int k, cudaStream_t s);
+cudaError_t launch_rope_kv_prefill(float* qkv, const float2* rope, float* kc, float* vc, int n, int heads,
+                                   int max_ctx, cudaStream_t s);
+// x[i] += d[i] for i < n (tensor-parallel residual add after an all-reduce).
+cudaError_t launch_add_rows(float* x, const float* d, int n, cudaStream_t s);
+cudaError_t launch_attn_prefill(const float* qkv, const float* kc, const float* vc, float* out, int n, int heads,
+                                int max_ctx, cudaStream_t s);
+
+}  // namespace xl
