@@ -433,10 +433,13 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const SampleParams
             const unsigned be = __ballot_sync(0xffffffffu, eq);
             const unsigned long long packed =
                 (static_cast<unsigned long long>(k) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
-            if (gt) cand[off_gt + __popc(bg & lt)] = packed;
+            if (gt) {
+                const int at = off_gt + __popc(bg & lt);
+                if (at < n_gt) cand[at] = packed;
+            }
             if (eq) {
                 const int r = off_eq + __popc(be & lt);
-                if (r < need_eq) cand[n_gt + r] = packed;
+                if (r < need_eq && n_gt + r < kTopK) cand[n_gt + r] = packed;
             }
             off_gt += __popc(bg);
             off_eq += __popc(be);

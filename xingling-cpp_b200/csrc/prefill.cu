@@ -358,13 +358,9 @@ cudaError_t launch_rope_kv_prefill(float* qkv, const float2* rope, float* kc, fl
 cudaError_t launch_attn_prefill(const float* qkv, const float* kc, const float* vc, float* out, int n, int heads,
                                 int max_ctx, cudaStream_t s) {
     if (n <= 0 || n > max_ctx) return cudaErrorInvalidValue;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kAttnPrefillSmem));
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kAttnPrefillSmem));
+    if (e != cudaSuccess) return e;
     attn_prefill_kernel<<<dim3((n + kAT - 1) / kAT, heads), 256, kAttnPrefillSmem, s>>>(qkv, kc, vc, out, n, heads,
                                                                                         max_ctx);
     return cudaGetLastError();
