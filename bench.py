@@ -411,6 +411,29 @@ def tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks) -
             "tokens_per_s": n_dec / (dev / 1e3), "first_tokens": toks[:8]}
 
 
+def ncu_case(args) -> None:
+    """Short fixed workloads for Nsight Compute captures (no timing output):
+    decode-full: XingLing-0.68B, prefill 32 + 4 decode steps;
+    decode-wide: 2 full-width layers, vocab 8192 (weights 276 MB > L2), prefill 32 + 3 decode steps;
+    prefill-512: XingLing-0.68B, one prefill of 512 ids.
+    --decode-path selects the persistent (0) or per-op (1) decode kernels."""
+    import llm_cpp_engine
+
+    shape = S.FULL if args.ncu_case in ("decode-full", "prefill-512") else S.WIDE2
+    wdir = WEIGHT_DIR if shape is S.FULL else WEIGHT_DIR + "_wide2"
+    S.write_weight_tree(wdir, shape)
+    eng = llm_cpp_engine.InferenceEngine("cuda:0", **shape.engine_kwargs())
+    eng.load(wdir)
+    eng.set_option("decode_path", args.decode_path)
+    if args.ncu_case == "prefill-512":
+        eng.next_token(S.prompt_ids(1, PREFILL_N, shape.vocab), top_p=0.0, repetition_penalty=1.0)
+        return
+    tok = eng.next_token(S.prompt_ids(0, PROMPT, shape.vocab), top_p=0.0, repetition_penalty=1.0)
+    for _ in range(4 if args.ncu_case == "decode-full" else 3):
+        tok = eng.next_token(tok, top_p=0.0, repetition_penalty=1.0)
+    print("ncu case done", args.ncu_case, tok)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -418,13 +441,17 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["xl", "reference"], default="xl")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--ncu-case", choices=["decode-full", "decode-wide", "prefill-512"], default=None)
+    ap.add_argument("--decode-path", type=int, default=0, choices=[0, 1])
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--budget", type=float, default=15.0, help=argparse.SUPPRESS)
     ap.add_argument("--weights", default=WEIGHT_DIR, help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.cpu_worker:
+    if args.ncu_case:
+        ncu_case(args)
+    elif args.cpu_worker:
         cpu_worker(args)
     elif args.impl == "reference":
         reference_arm(args)

@@ -126,6 +126,15 @@ XL_API int xl_engine_ctx_len(const xl_engine* e);
  * [npos][heads][64] layout, for this rank's heads. */
 XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, float* v_out);
 
+/* Engine options (no reference counterpart):
+ *   "decode_path" 0  one persistent kernel per decode token (default; single
+ *                    GPU): a TMA weight stream through shared memory across
+ *                    all layers and the LM head, phases gated by grid-wide
+ *                    counters;
+ *                 1  one kernel per fused op (the tensor-parallel path).
+ * Changing an option re-captures the decode graph. */
+XL_API int xl_engine_set_option(xl_engine* e, const char* key, int value);
+
 /* Device time of the last prefill / decode call in milliseconds (CUDA events
  * around the device work, excluding host copies). */
 XL_API int xl_engine_last_device_ms(const xl_engine* e, float* ms);

@@ -25,6 +25,15 @@ def eng_mod(built):
     return llm_cpp_engine
 
 
+PATHS = pytest.mark.parametrize("path", [0, 1], ids=["persistent", "per_op"])
+
+
+def make_engine(mod, path, **kw):
+    eng = mod.InferenceEngine("cuda", **kw)
+    eng.set_option("decode_path", path)
+    return eng
+
+
 def logits_of(eng):
     return np.frombuffer(eng.last_logits(), dtype=np.float32)
 
@@ -64,9 +73,10 @@ def run_greedy(eng, port, ids, steps):
     return toks
 
 
-def test_tiny_greedy_and_kv(eng_mod, tiny_weights):
+@PATHS
+def test_tiny_greedy_and_kv(eng_mod, tiny_weights, path):
     sh = S.TINY
-    eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
+    eng = make_engine(eng_mod, path, **sh.engine_kwargs())
     eng.load(tiny_weights)
     port = O.Port(sh)
     port.load(tiny_weights)
@@ -81,10 +91,11 @@ def test_tiny_greedy_and_kv(eng_mod, tiny_weights):
         assert np.abs(k - kr).max() < 1e-5 and np.abs(v - vr).max() < 1e-5
 
 
-def test_tiny_kv_reset_rounds(eng_mod, tiny_weights):
+@PATHS
+def test_tiny_kv_reset_rounds(eng_mod, tiny_weights, path):
     """Prefill resets the cache; decode appends (tests/test_transformer.cu:100-129)."""
     sh = S.TINY
-    eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
+    eng = make_engine(eng_mod, path, **sh.engine_kwargs())
     eng.load(tiny_weights)
     rng = np.random.default_rng(777)
     for rnd in range(3):
@@ -97,9 +108,10 @@ def test_tiny_kv_reset_rounds(eng_mod, tiny_weights):
         assert eng.ctx_len() == n + 2
 
 
-def test_tiny_context_limit_and_errors(eng_mod, tiny_weights):
+@PATHS
+def test_tiny_context_limit_and_errors(eng_mod, tiny_weights, path):
     sh = S.ModelShape(layers=2, hidden=256, heads=4, ffn=512, vocab=2048, max_ctx=40)
-    eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
+    eng = make_engine(eng_mod, path, **sh.engine_kwargs())
     eng.load(tiny_weights)
     with pytest.raises(RuntimeError):
         eng.next_token(5)  # decode before any prefill
@@ -117,9 +129,10 @@ def test_tiny_context_limit_and_errors(eng_mod, tiny_weights):
         eng_mod.InferenceEngine("cpu")
 
 
-def test_tiny_sampled_teacher_forced(eng_mod, tiny_weights):
+@PATHS
+def test_tiny_sampled_teacher_forced(eng_mod, tiny_weights, path):
     sh = S.TINY
-    eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
+    eng = make_engine(eng_mod, path, **sh.engine_kwargs())
     eng.load(tiny_weights)
     port = O.Port(sh)
     port.load(tiny_weights)
@@ -144,13 +157,45 @@ def test_tiny_sampled_teacher_forced(eng_mod, tiny_weights):
     assert mismatches == 0
 
 
-def test_full_greedy_prompt32(eng_mod, full_weights):
+@PATHS
+def test_full_greedy_prompt32(eng_mod, full_weights, path):
     """XingLing-0.68B, prompt of 32 ids (seed 0), greedy: prefill + 16 decode steps vs the oracle."""
     sh = S.FULL
-    eng = eng_mod.InferenceEngine("cuda")
+    eng = make_engine(eng_mod, path)
     eng.load(full_weights)
     port = O.Port(sh)
     port.load(full_weights)
     ids = S.prompt_ids(0, 32, sh.vocab)
     run_greedy(eng, port, ids, 16)
     assert eng.ctx_len() == 48
+
+
+@PATHS
+def test_full_long_context_sampled(eng_mod, full_weights, path):
+    """Long context: prompt of 700 ids (seed 2), decode to the 768-position limit with T 0.7, top_p 0.9,
+    repetition penalty 1.1 and Philox (seed 3) uniforms, teacher-forced on the oracle every 4th step
+    (the oracle's CPU decode is the slow part); the 69th decode call must fail (context full)."""
+    sh = S.FULL
+    eng = make_engine(eng_mod, path)
+    eng.load(full_weights)
+    port = O.Port(sh)
+    port.load(full_weights)
+    T, P, RP = 0.7, 0.9, 1.1
+    u = S.philox_uniforms(3, 69)
+    eng.set_uniforms([float(x) for x in u])
+    ids = S.prompt_ids(2, 700, sh.vocab)
+    rep: list[int] = []
+    tok = eng.next_token(ids, temperature=T, top_p=P, repetition_penalty=RP)
+    ref = port.prefill(ids)
+    for step in range(68):
+        got = logits_of(eng)
+        if step % 4 == 0 or step == 67:
+            assert_logits_close(got, O.apply_penalty(ref, rep, RP))
+        tok_ref = O.sample(ref, T, P, RP, rep, float(u[step]))
+        assert tok == tok_ref, f"step {step}: engine {tok}, oracle {tok_ref}"
+        rep.append(tok_ref)
+        tok = eng.next_token(tok_ref, temperature=T, top_p=P, repetition_penalty=RP)
+        ref = port.decode(tok_ref)
+    assert eng.ctx_len() == 768
+    with pytest.raises(RuntimeError):
+        eng.next_token(tok, temperature=T, top_p=P, repetition_penalty=RP)

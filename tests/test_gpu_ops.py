@@ -26,6 +26,8 @@ def torch_cuda(built):
 
 
 def dev(torch, a):
+    """A device copy; callers keep the returned tensor referenced until the
+    kernel that reads it has finished (the caching allocator reuses freed blocks)."""
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
@@ -76,8 +78,9 @@ def test_norm_gemv_swiglu_and_residual(torch_cuda):
     b13 = np.empty(2 * F, np.float32)
     b13[0::2], b13[1::2] = b1, bv
     y = torch.empty(F, device="cuda")
-    X.check(X.lib().xl_op_norm_gemv(1, X.ptr(dev(torch, x)), X.ptr(dev(torch, gamma)), X.ptr(dev(torch, w13)),
-                                    X.ptr(dev(torch, b13)), X.ptr(y), 2 * F, H, X.stream()))
+    dx, dg, dw13, db13 = dev(torch, x), dev(torch, gamma), dev(torch, w13), dev(torch, b13)
+    X.check(X.lib().xl_op_norm_gemv(1, X.ptr(dx), X.ptr(dg), X.ptr(dw13), X.ptr(db13), X.ptr(y), 2 * F, H,
+                                    X.stream()))
     torch.cuda.synchronize()
     xn = O.rmsnorm(x[None], gamma)
     ref = O.silu_mul(O.linear(xn, w1, b1), O.linear(xn, v, bv))[0]
@@ -86,9 +89,8 @@ def test_norm_gemv_swiglu_and_residual(torch_cuda):
     w2 = g.uniform(-0.02, 0.02, (H, F)).astype(np.float32)
     b2 = g.uniform(-0.02, 0.02, H).astype(np.float32)
     resid = g.uniform(-1, 1, H).astype(np.float32)
-    yr = dev(torch, resid)
-    X.check(X.lib().xl_op_norm_gemv(2, X.ptr(y), None, X.ptr(dev(torch, w2)), X.ptr(dev(torch, b2)), X.ptr(yr), H,
-                                    F, X.stream()))
+    yr, dw2, db2 = dev(torch, resid), dev(torch, w2), dev(torch, b2)
+    X.check(X.lib().xl_op_norm_gemv(2, X.ptr(y), None, X.ptr(dw2), X.ptr(db2), X.ptr(yr), H, F, X.stream()))
     torch.cuda.synchronize()
     close(host(yr), resid + O.linear(ref[None], w2, b2)[0], 1e-5, 1e-4)
 
@@ -149,8 +151,9 @@ def test_lm_head(torch_cuda, vocab, rp):
     logits = torch.empty(vocab, device="cuda")
     ws = torch.zeros(X.lib().xl_op_lm_head_workspace_bytes(), dtype=torch.uint8, device="cuda")
     arg = C.c_int(-1)
-    X.check(X.lib().xl_op_lm_head(X.ptr(dx), X.ptr(dgm), X.ptr(dt), X.ptr(logits), X.ptr(dev(torch, flags)), rp, vocab,
-                                  H, C.byref(arg), X.ptr(ws), X.stream()))
+    dflags = dev(torch, flags)
+    X.check(X.lib().xl_op_lm_head(X.ptr(dx), X.ptr(dgm), X.ptr(dt), X.ptr(logits), X.ptr(dflags), rp, vocab, H,
+                                  C.byref(arg), X.ptr(ws), X.stream()))
     torch.cuda.synchronize()
     ref = O.apply_penalty(O.lm_head(table, O.rmsnorm(x[None], gamma)[0]), rep, rp)
     got = host(logits)
@@ -183,9 +186,8 @@ def test_linear_prefill(torch_cuda, mode, n, m, k):
     b = g.uniform(-0.02, 0.02, m).astype(np.float32)
     width = m // 2 if mode == 1 else m
     init = g.uniform(-1, 1, (n, width)).astype(np.float32)
-    y = dev(torch, init)
-    X.check(X.lib().xl_op_linear(mode, X.ptr(dev(torch, x)), X.ptr(dev(torch, w)), X.ptr(dev(torch, b)), X.ptr(y), n,
-                                 m, k, X.stream()))
+    y, dx, dw, db = dev(torch, init), dev(torch, x), dev(torch, w), dev(torch, b)
+    X.check(X.lib().xl_op_linear(mode, X.ptr(dx), X.ptr(dw), X.ptr(db), X.ptr(y), n, m, k, X.stream()))
     torch.cuda.synchronize()
     full = O.linear(x, w, b)
     if mode == 0:
@@ -202,15 +204,16 @@ def test_rmsnorm_rows_and_embedding(torch_cuda):
     g = rng(123)
     x = g.uniform(-0.1, 0.1, (37, H)).astype(np.float32)
     gamma = g.uniform(0.8, 1.2, H).astype(np.float32)
-    out = torch.empty_like(dev(torch, x))
-    X.check(X.lib().xl_op_rmsnorm(X.ptr(dev(torch, x)), X.ptr(dev(torch, gamma)), X.ptr(out), 37, H, X.stream()))
+    dx, dg = dev(torch, x), dev(torch, gamma)
+    out = torch.empty_like(dx)
+    X.check(X.lib().xl_op_rmsnorm(X.ptr(dx), X.ptr(dg), X.ptr(out), 37, H, X.stream()))
     torch.cuda.synchronize()
     close(host(out), O.rmsnorm(x, gamma), 1e-6, 1e-5)
     table = g.uniform(-0.02, 0.02, (5000, H)).astype(np.float32)
     ids = g.integers(0, 5000, 37).astype(np.int32)
     rows = torch.empty((37, H), device="cuda")
-    X.check(X.lib().xl_op_embedding(X.ptr(dev(torch, table)), X.ptr(dev(torch, ids)), X.ptr(rows), 37, H,
-                                    X.stream()))
+    dtab, dids = dev(torch, table), dev(torch, ids)
+    X.check(X.lib().xl_op_embedding(X.ptr(dtab), X.ptr(dids), X.ptr(rows), 37, H, X.stream()))
     torch.cuda.synchronize()
     assert np.array_equal(host(rows), table[ids])  # gather is bit-exact
 
@@ -226,8 +229,9 @@ def test_attn_prefill(torch_cuda, n):
     kc = torch.zeros((HEADS, T, 64), device="cuda")
     vc = torch.zeros((HEADS, T, 64), device="cuda")
     out = torch.empty((n, H), device="cuda")
-    X.check(X.lib().xl_op_attn_prefill(X.ptr(qkv), X.ptr(_rope_dev(torch)), X.ptr(kc), X.ptr(vc), X.ptr(out), n, HEADS,
-                                       T, X.stream()))
+    rope = _rope_dev(torch)
+    X.check(X.lib().xl_op_attn_prefill(X.ptr(qkv), X.ptr(rope), X.ptr(kc), X.ptr(vc), X.ptr(out), n, HEADS, T,
+                                       X.stream()))
     torch.cuda.synchronize()
     close(host(out).reshape(n, HEADS, 64), out_ref, 2e-6, 1e-4)
     close(host(kc).transpose(1, 0, 2)[:n], kc_ref[:n], 1e-6, 1e-5)

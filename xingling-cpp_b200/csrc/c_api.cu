@@ -139,6 +139,12 @@ int xl_engine_last_device_ms(const xl_engine* e, float* ms) {
     return XL_OK;
 }
 
+int xl_engine_set_option(xl_engine* e, const char* key, int value) {
+    xl::clear_error();
+    if (!e) return bad("null engine");
+    return e->impl->set_option(key, value);
+}
+
 int xl_philox_uniforms(uint64_t seed, uint64_t start, int n, float* out) {
     if (n < 0 || (n > 0 && !out)) return bad("xl_philox_uniforms: bad arguments");
     for (int i = 0; i < n; ++i) out[i] = xl::philox_uniform(start + static_cast<uint64_t>(i), seed);

@@ -213,6 +213,7 @@ int Engine::alloc_all() {
     add(&logits_, vl * 4);
     add(&attn_ws_, static_cast<size_t>(heads_l_) * maxs * (kHeadDim + 2) * 4);
     add(&attn_cnt_, heads_l_ * 4);
+    add(&done_, (5 * static_cast<size_t>(cfg_.layers) + 1) * 4);
     add(&rep_flags_, vl);
     add(&st_, sizeof(DevState));
     add(&px_, T * H * 4);
@@ -370,7 +371,52 @@ int Engine::load(const char* dir) {
 // One decode step, Transformer::forward(int) (src/transformer.cu:180-186):
 // gather -> 16 x [norm1+QKV, RoPE+KV append+attention, out-proj+residual,
 // norm2+W1/V+SwiGLU, W2+residual] -> final norm + LM head -> sampler.
+// Single-GPU decode step: zero the phase counters, one persistent kernel for
+// all 16 layers and the LM head, then the sampler.
+int Engine::enqueue_decode_persistent(cudaStream_t s) {
+    PersistentParams p{};
+    if (cfg_.layers > kMaxLayers) {
+        set_error("persistent decode supports at most 32 layers");
+        return XL_ERR_ARG;
+    }
+    for (int l = 0; l < cfg_.layers; ++l) {
+        const LayerWeights& L = layers_[l];
+        p.layer[l] = LayerPtrs{L.wqkv, L.bqkv, L.wo, L.bo, L.w13, L.b13, L.w2, L.b2, L.g1, L.g2, L.kc, L.vc};
+    }
+    p.layers = cfg_.layers;
+    p.emb = emb_;
+    p.gnorm = gnorm_;
+    p.rope = rope_;
+    p.x = xa_;
+    p.qkv = qkv_;
+    p.part = attn_ws_;
+    p.ffh = ffh_;
+    p.logits = logits_;
+    p.rep_flags = rep_flags_;
+    p.st = st_;
+    p.done = done_;
+    p.H = H_;
+    p.Hl = Hl_;
+    p.heads = heads_l_;
+    p.Fl = Fl_;
+    p.V = V_;
+    p.T = T_;
+    XL_CUDA(cudaMemsetAsync(done_, 0, (5 * static_cast<size_t>(cfg_.layers) + 1) * sizeof(int), s));
+    XL_CUDA(launch_decode_persistent(p, num_sms_, s));
+    lm_x_ = xa_;
+    SampleParams sp{};
+    sp.logits = logits_;
+    sp.V = vl_;
+    sp.v0 = v0_;
+    sp.st = st_;
+    sp.rep_flags = rep_flags_;
+    sp.full = 0;
+    XL_CUDA(launch_sample(sp, true, s));
+    return XL_OK;
+}
+
 int Engine::enqueue_decode(cudaStream_t s) {
+    if (tp_ == 1 && decode_path_ == 0) return enqueue_decode_persistent(s);
     float* cur = xa_;
     float* other = xb_;
     bool pending = false;  // TP: part_ holds a reduced delta not yet added to cur
@@ -684,6 +730,21 @@ int Engine::profile_lm_head(int iters, float* avg_ms) {
     XL_CUDA(cudaEventElapsedTime(&ms, ev0_, ev1_));
     *avg_ms = ms / static_cast<float>(iters);
     return XL_OK;
+}
+
+int Engine::set_option(const char* key, int value) {
+    XL_CUDA(cudaSetDevice(device_));
+    const std::string k = key ? key : "";
+    if (k == "decode_path") {
+        if (value != 0 && value != 1) {
+            set_error("decode_path must be 0 (persistent kernel) or 1 (per-op kernels)");
+            return XL_ERR_ARG;
+        }
+        decode_path_ = value;
+        return loaded_ ? capture_decode_graph() : XL_OK;
+    }
+    set_error("unknown option: " + k);
+    return XL_ERR_ARG;
 }
 
 int Engine::set_uniforms(const float* u, int n) {

@@ -46,6 +46,7 @@ class Engine {
     int last_logits(float* out, int n);
     int kv_copy(int layer, int npos, float* k_out, float* v_out);
     int profile_lm_head(int iters, float* avg_ms);
+    int set_option(const char* key, int value);
     int ctx_len() const { return n_; }
     float last_device_ms() const { return last_ms_; }
     int vocab_begin() const { return v0_; }
@@ -57,6 +58,7 @@ class Engine {
     int alloc_all();
     int capture_decode_graph();
     int enqueue_decode(cudaStream_t s);
+    int enqueue_decode_persistent(cudaStream_t s);
     int run_lm_head_and_sample(const float* x_last, const float* delta, cudaStream_t s);
     int launch_lm_head(const float* x_last, const float* delta, bool pdl, cudaStream_t s);
     const float* lm_x_ = nullptr;  // residual stream the decode graph's LM head reads
@@ -87,6 +89,7 @@ class Engine {
     float* logits_ = nullptr;  // [vl]
     float* attn_ws_ = nullptr; // split-K partials
     int* attn_cnt_ = nullptr;  // [heads_l] split counters
+    int* done_ = nullptr;      // [5*layers + 1] phase counters of the persistent decode kernel
     uint8_t* rep_flags_ = nullptr;  // [vl]
     DevState* st_ = nullptr;
     // prefill buffers [T][...]
@@ -102,6 +105,7 @@ class Engine {
     cudaGraphExec_t decode_exec_ = nullptr;
     ncclComm_t comm_ = nullptr;
 
+    int decode_path_ = 0;      // 0: persistent kernel (single GPU), 1: per-op kernels
     bool loaded_ = false;
     bool has_seq_ = false;
     int n_ = 0;

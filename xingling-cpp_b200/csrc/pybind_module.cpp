@@ -147,6 +147,15 @@ class InferenceEngine {
         return ms;
     }
 
+    void set_option(const std::string& key, int value) {
+        int rc;
+        {
+            py::gil_scoped_release nogil;
+            rc = xl_engine_set_option(e_, key.c_str(), value);
+        }
+        check(rc);
+    }
+
     float profile_lm_head(int iters) {
         float ms = 0.0f;
         int rc;
@@ -200,6 +209,7 @@ PYBIND11_MODULE(llm_cpp_engine, m) {
         .def("kv", &InferenceEngine::kv, py::arg("layer"), py::arg("npos"), py::arg("heads_local"))
         .def("ctx_len", &InferenceEngine::ctx_len)
         .def("last_device_ms", &InferenceEngine::last_device_ms)
+        .def("set_option", &InferenceEngine::set_option, py::arg("key"), py::arg("value"))
         .def("profile_lm_head", &InferenceEngine::profile_lm_head, py::arg("iters") = 20)
         .def_readwrite("im_start_id", &InferenceEngine::im_start_id)
         .def_readwrite("im_end_id", &InferenceEngine::im_end_id)

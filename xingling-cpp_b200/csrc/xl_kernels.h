@@ -76,6 +76,31 @@ constexpr int kAttnChunk = 64;
 __host__ __device__ inline int attn_max_splits(int max_ctx) { return (max_ctx + kAttnChunk - 1) / kAttnChunk; }
 cudaError_t launch_attn_decode(const AttnDecodeParams& p, bool pdl, cudaStream_t s);
 
+// Persistent decode step (decode_persistent.cu): one cooperative launch per token.
+constexpr int kMaxLayers = 32;
+struct LayerPtrs {
+    const float *wqkv, *bqkv, *wo, *bo, *w13, *b13, *w2, *b2, *g1, *g2;
+    float *kc, *vc;
+};
+struct PersistentParams {
+    LayerPtrs layer[kMaxLayers];
+    int layers;
+    const float* emb;       // [V][H] tied embedding / LM head
+    const float* gnorm;     // [H] final RMSNorm gain
+    const float2* rope;     // [T][32]
+    float* x;               // [H] residual stream
+    float* qkv;             // [3*Hl]
+    float* part;            // attention partials [heads][max_splits][66]
+    float* ffh;             // [Fl] SwiGLU activations
+    float* logits;          // [V]
+    const uint8_t* rep_flags;
+    DevState* st;
+    int* done;              // [5*layers + 1] phase counters, zeroed before each launch
+    int H, Hl, heads, Fl, V, T;
+};
+size_t persistent_smem_bytes();
+cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cudaStream_t s);
+
 struct SampleParams {
     const float* logits;   // [V] penalised logits of this vocab shard
     int V;                 // shard size
