@@ -39,7 +39,8 @@ constexpr int kTileK = 384;                     // floats of a row per tile
 constexpr int kSlotBytes = kTileRows * kTileK * 4;  // 24 KB
 constexpr int kSlots = 8;                       // 192 KB ring
 constexpr int kMaxK = 4096;
-constexpr size_t kSmemBytes = static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 + 2 * kSlots * 8 + 256;
+constexpr size_t kSmemBytes =
+    static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 + 2 * kSlots * 8 + 256 + kConsumerWarps * 64 * 4;
 constexpr uint32_t kMbarSpinLimit = 1u << 24;
 constexpr uint32_t kFlagSpinLimit = 1u << 23;
 constexpr int kErrMbar = 1, kErrFlag = 2;
@@ -146,20 +147,70 @@ __device__ __forceinline__ void my_groups(int M, int& g0, int& g1) {
 
 // ---------------------------------------------------------------------------
 // Producer: the whole token's weight stream for this CTA.
+//
+// A unit is one 16-row group of one GEMV phase; its rows are contiguous in
+// HBM.  Besides the ring copies, the producer keeps an L2 prefetch cursor
+// kPrefetchUnits units ahead, so that HBM keeps streaming into L2 while the
+// ring is full (consumers waiting at a phase boundary or in attention); the
+// ring copies then hit L2.
+constexpr int kPrefetchUnits = 4;
+constexpr uint32_t kPrefetchPiece = 32768;
+
+struct Unit {
+    int ph, g, g1;
+};
+
+// First unit at or after phase ph (ph beyond the schedule: none).
+__device__ bool unit_first(const PersistentParams& p, int ph, Unit& u) {
+    const int last = 5 * p.layers;
+    for (; ph <= last; ++ph) {
+        if (phase_kind(ph, p.layers) == kAttn) continue;
+        int g0, g1;
+        my_groups(gemv_of(p, ph).M, g0, g1);
+        if (g0 < g1) {
+            u = Unit{ph, g0, g1};
+            return true;
+        }
+    }
+    return false;
+}
+
+__device__ bool unit_next(const PersistentParams& p, Unit& u) {
+    if (++u.g < u.g1) return true;
+    return unit_first(p, u.ph + 1, u);
+}
+
+__device__ void prefetch_unit(const PersistentParams& p, const Unit& u) {
+    const Gemv d = gemv_of(p, u.ph);
+    const int rows = min(kTileRows, d.M - u.g * kTileRows);
+    const char* src = reinterpret_cast<const char*>(d.W + static_cast<size_t>(u.g) * kTileRows * d.K);
+    uint32_t bytes = static_cast<uint32_t>(rows) * d.K * 4;
+    for (uint32_t off = 0; off < bytes; off += kPrefetchPiece)
+        prefetch_l2_bulk(src + off, min(kPrefetchPiece, bytes - off));
+}
+
 __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, uint64_t* empty) {
     DevState* st = p.st;
     int slot = 0;
     uint32_t par = 0;
     int issued = 0;
     bool ok = true;
-    const int last = 5 * p.layers;
-    for (int ph = 0; ph <= last && ok; ++ph) {
-        if (phase_kind(ph, p.layers) == kAttn) continue;
-        const Gemv d = gemv_of(p, ph);
-        int g0, g1;
-        my_groups(d.M, g0, g1);
+    Unit cu, pu;
+    bool have = unit_first(p, 0, cu);
+    bool pf = unit_first(p, 0, pu);
+    for (int i = 0; i < kPrefetchUnits && pf; ++i) {
+        prefetch_unit(p, pu);
+        pf = unit_next(p, pu);
+    }
+    for (; have && ok; have = unit_next(p, cu)) {
+        if (pf) {
+            prefetch_unit(p, pu);
+            pf = unit_next(p, pu);
+        }
+        const Gemv d = gemv_of(p, cu.ph);
         const int nkt = (d.K + kTileK - 1) / kTileK;
-        for (int g = g0; g < g1 && ok; ++g) {
+        const int g = cu.g;
+        {
             const int rows = min(kTileRows, d.M - g * kTileRows);
             for (int kt = 0; kt < nkt; ++kt) {
                 if (!wait_parity(&empty[slot], par ^ 1u, st)) {
@@ -278,7 +329,7 @@ __device__ void stage_copy(const float* src, int K, float* xs) {
 // Merge the split-K attention partials (m, l, o[64]) of every head into xs.
 __device__ void stage_attn_combine(const PersistentParams& p, int nsplit, float* xs) {
     const int t = threadIdx.x - 32;
-    const int maxs = attn_max_splits(p.T);
+    const int maxs = persistent_max_splits(p.T);
     for (int i = t; i < p.Hl; i += kConsumerThreads) {
         const int h = i >> 6, d = i & 63;
         const float* base = p.part + static_cast<size_t>(h) * maxs * (kHeadDim + 2);
@@ -299,13 +350,14 @@ __device__ void stage_attn_combine(const PersistentParams& p, int nsplit, float*
     }
 }
 
-// One (head, 64-position chunk) of the decode attention on one warp:
-// RoPE at position n (src/rope.cu:20-45), KV append when the chunk holds n,
-// scores, softmax and P.V; writes the (max, sum, o) partial.
-__device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int h, int s, int n) {
+// One (head, 32-position chunk) of the decode attention on one warp, lane j
+// owning position t0 + j: RoPE at position n (src/rope.cu:20-45), KV append
+// when the chunk holds n, scores, softmax and P.V; writes the (max, sum, o)
+// partial.  All 16 K-row loads of a lane are in flight together.
+__device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int h, int s, int n, float* qsh) {
     const int lane = threadIdx.x & 31;
-    const int t0 = s * kAttnChunk;
-    const int cnt = min(kAttnChunk, n + 1 - t0);
+    const int t0 = s * kPersistChunk;
+    const int cnt = min(kPersistChunk, n + 1 - t0);
     const float* q = p.qkv + h * kHeadDim;
     const float* kn = p.qkv + p.Hl + h * kHeadDim;
     const float* vn = p.qkv + 2 * p.Hl + h * kHeadDim;
@@ -313,8 +365,8 @@ __device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int 
     float* vc = y.vc + static_cast<size_t>(h) * p.T * kHeadDim;
     const float2 cs = p.rope[n * kHalfHead + lane];
     const float qa = __ldcg(q + lane), qb = __ldcg(q + lane + kHalfHead);
-    const float qra = (qa * cs.x + qb * cs.y) * 0.125f;  // 1/sqrt(64) is exact
-    const float qrb = (-qa * cs.y + qb * cs.x) * 0.125f;
+    qsh[lane] = (qa * cs.x + qb * cs.y) * 0.125f;  // 1/sqrt(64) is exact
+    qsh[lane + kHalfHead] = (-qa * cs.y + qb * cs.x) * 0.125f;
     if (n >= t0 && n < t0 + cnt) {
         const float ka = __ldcg(kn + lane), kb = __ldcg(kn + lane + kHalfHead);
         kc[n * kHeadDim + lane] = ka * cs.x + kb * cs.y;
@@ -323,45 +375,46 @@ __device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int 
         vc[n * kHeadDim + lane + kHalfHead] = __ldcg(vn + lane + kHalfHead);
     }
     __syncwarp();
-    // scores: position j's score ends in lane j % 32, slot j / 32
-    float sc0 = -INFINITY, sc1 = -INFINITY;
-#pragma unroll 4
-    for (int j = 0; j < cnt; ++j) {
-        const float* kr = kc + static_cast<size_t>(t0 + j) * kHeadDim;
-        const float d = warp_sum(fmaf(__ldcg(kr + lane), qra, __ldcg(kr + lane + kHalfHead) * qrb));
-        if ((j & 31) == lane) {
-            if (j < 32) sc0 = d;
-            else sc1 = d;
-        }
+    float sc = -INFINITY;
+    if (lane < cnt) {
+        const float4* kr = reinterpret_cast<const float4*>(kc + static_cast<size_t>(t0 + lane) * kHeadDim);
+        float4 kv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) kv[i] = __ldcg(kr + i);
+        const float4* q4 = reinterpret_cast<const float4*>(qsh);
+        float d = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) d = dot4(kv[i], q4[i], d);
+        sc = d;
     }
-    const float m = warp_max(fmaxf(sc0, sc1));
-    const float e0 = (sc0 == -INFINITY) ? 0.0f : expf(sc0 - m);
-    const float e1 = (sc1 == -INFINITY) ? 0.0f : expf(sc1 - m);
-    const float l = warp_sum(e0 + e1);
+    const float m = warp_max(sc);
+    const float e = lane < cnt ? expf(sc - m) : 0.0f;
+    const float l = warp_sum(e);
     float oa = 0.0f, ob = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
     for (int j = 0; j < cnt; ++j) {
-        const float pj = __shfl_sync(0xffffffffu, j < 32 ? e0 : e1, j & 31);
+        const float pj = __shfl_sync(0xffffffffu, e, j);
         const float* vr = vc + static_cast<size_t>(t0 + j) * kHeadDim;
         oa = fmaf(pj, __ldcg(vr + lane), oa);
         ob = fmaf(pj, __ldcg(vr + lane + kHalfHead), ob);
     }
-    float* pp = p.part + (static_cast<size_t>(h) * attn_max_splits(p.T) + s) * (kHeadDim + 2);
+    float* pp = p.part + (static_cast<size_t>(h) * persistent_max_splits(p.T) + s) * (kHeadDim + 2);
     pp[2 + lane] = oa;
     pp[2 + lane + kHalfHead] = ob;
     if (lane == 0) {
         pp[0] = m;
         pp[1] = l;
     }
+    __syncwarp();
 }
 
 __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint64_t* full, uint64_t* empty,
-                          float* red, unsigned long long* best_s) {
+                          float* red, unsigned long long* best_s, float* qbuf) {
     DevState* st = p.st;
     const int t = threadIdx.x - 32;
     const int warp = t >> 5, lane = t & 31;
     const int n = st->pos;
-    const int nsplit = (n + kAttnChunk) / kAttnChunk;  // chunks of 0..n
+    const int nsplit = (n + kPersistChunk) / kPersistChunk;  // chunks of positions 0..n
     const float rp = st->in.rp;
     int slot = 0;
     uint32_t par = 0;
@@ -375,8 +428,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
         const LayerPtrs* y = ph < last ? &p.layer[ph / 5] : nullptr;
         if (kind == kAttn) {
             const int items = p.heads * nsplit;
-            for (int it = blockIdx.x * kConsumerWarps + warp; it < items; it += gridDim.x * kConsumerWarps)
-                attend_chunk(p, *y, it / nsplit, it % nsplit, n);
+            for (int it = blockIdx.x + gridDim.x * warp; it < items; it += gridDim.x * kConsumerWarps)
+                attend_chunk(p, *y, it / nsplit, it % nsplit, n, qbuf + warp * kHeadDim);
             signal_phase(p, ph);
             continue;
         }
@@ -502,6 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     uint64_t* empty = full + kSlots;
     float* red = reinterpret_cast<float*>(empty + kSlots);
     unsigned long long* best_s = reinterpret_cast<unsigned long long*>(red + 16);
+    float* qbuf = reinterpret_cast<float*>(best_s + kConsumerWarps + 8);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
@@ -516,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) producer(p, ring, full, empty);
     } else {
-        consumers(p, ring, xs, full, empty, red, best_s);
+        consumers(p, ring, xs, full, empty, red, best_s, qbuf);
     }
 }
 

@@ -183,7 +183,7 @@ int Engine::init(const xl_config& cfg, int device, int tp_size, int tp_rank, con
 
 int Engine::alloc_all() {
     const size_t H = H_, Hl = Hl_, Fl = Fl_, T = T_, V = V_, vl = vl_;
-    const int maxs = attn_max_splits(T_);
+    const int maxs = std::max(attn_max_splits(T_), persistent_max_splits(T_));
     std::vector<std::pair<void**, size_t>> plan;
     auto add = [&](void* slot, size_t bytes) { plan.emplace_back(reinterpret_cast<void**>(slot), bytes); };
     add(&emb_, V * H * 4);

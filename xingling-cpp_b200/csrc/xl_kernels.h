@@ -78,6 +78,10 @@ cudaError_t launch_attn_decode(const AttnDecodeParams& p, bool pdl, cudaStream_t
 
 // Persistent decode step (decode_persistent.cu): one cooperative launch per token.
 constexpr int kMaxLayers = 32;
+constexpr int kPersistChunk = 32;  // attention positions per warp item
+__host__ __device__ inline int persistent_max_splits(int max_ctx) {
+    return (max_ctx + kPersistChunk - 1) / kPersistChunk;
+}
 struct LayerPtrs {
     const float *wqkv, *bqkv, *wo, *bo, *w13, *b13, *w2, *b2, *g1, *g2;
     float *kc, *vc;
@@ -90,7 +94,7 @@ struct PersistentParams {
     const float2* rope;     // [T][32]
     float* x;               // [H] residual stream
     float* qkv;             // [3*Hl]
-    float* part;            // attention partials [heads][max_splits][66]
+    float* part;            // attention partials [heads][persistent_max_splits][66]
     float* ffh;             // [Fl] SwiGLU activations
     float* logits;          // [V]
     const uint8_t* rep_flags;
