@@ -132,8 +132,18 @@ XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, fl
  *                    all layers and the LM head, phases gated by grid-wide
  *                    counters;
  *                 1  one kernel per fused op (the tensor-parallel path).
+ *   "phase_trace" 1  the persistent kernel stamps %globaltimer (ns) per CTA
+ *                    and phase: consumer start (after the grid-wide wait),
+ *                    input staged, phase done, producer first and last issue;
+ *                    read with xl_engine_phase_trace (a profiling aid);
+ *   "prefill_gemm" 0  prefill projections on tcgen05 with the 3xTF32 split
+ *                     (default); 1  fp32 FMA tiles.
  * Changing an option re-captures the decode graph. */
 XL_API int xl_engine_set_option(xl_engine* e, const char* key, int value);
+/* The last decode step's phase timeline: n = SMs x (5 x layers + 1) x 5
+ * values, [cta][phase][field], phases ordered QKV, attention, out-proj,
+ * W1/V, W2 per layer, then the LM head. */
+XL_API int xl_engine_phase_trace(xl_engine* e, unsigned long long* out, int n);
 
 /* Device time of the last prefill / decode call in milliseconds (CUDA events
  * around the device work, excluding host copies). */
@@ -193,9 +203,17 @@ XL_API int xl_op_sample(const float* logits, int vocab, float temperature, float
                         void* workspace, void* stream);
 
 /* Linear::forward (src/linear.cu:197-253): Y[n][m] = X[n][k] . W[m][k]^T + b
- * with the same three modes as xl_op_norm_gemv (SwiGLU writes [n][m/2]). */
-XL_API int xl_op_linear(int mode, const float* x, const float* w, const float* b, float* y, int n, int m, int k,
-                        void* stream);
+ * with the same three modes as xl_op_norm_gemv (SwiGLU writes [n][m/2]).
+ * With x_lo and w_lo (the TF32 residuals from xl_op_split_lo) the product
+ * runs on the tcgen05 tensor cores as X.W_hi + X_lo.W_hi + X_hi.W_lo
+ * (3xTF32, fp32-level accuracy; k % 32 == 0; SwiGLU also writes y_lo);
+ * with x_lo or w_lo NULL it runs as fp32 FMA tiles. */
+XL_API int xl_op_linear(int mode, const float* x, const float* x_lo, const float* w, const float* w_lo,
+                        const float* b, float* y, float* y_lo, int n, int m, int k, void* stream);
+
+/* lo[i] = x[i] - (x[i] with its 13 low mantissa bits cleared): the part of
+ * an fp32 value a TF32 tensor-core operand drops. */
+XL_API int xl_op_split_lo(const float* x, float* lo, size_t n, void* stream);
 
 /* RMSNorm::forward on [n][k] rows (out may alias x). */
 XL_API int xl_op_rmsnorm(const float* x, const float* gamma, float* out, int n, int k, void* stream);

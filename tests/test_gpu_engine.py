@@ -74,9 +74,11 @@ def run_greedy(eng, port, ids, steps):
 
 
 @PATHS
-def test_tiny_greedy_and_kv(eng_mod, tiny_weights, path):
+@pytest.mark.parametrize("prefill_gemm", [0, 1], ids=["tcgen05", "fma"])
+def test_tiny_greedy_and_kv(eng_mod, tiny_weights, path, prefill_gemm):
     sh = S.TINY
     eng = make_engine(eng_mod, path, **sh.engine_kwargs())
+    eng.set_option("prefill_gemm", prefill_gemm)
     eng.load(tiny_weights)
     port = O.Port(sh)
     port.load(tiny_weights)

@@ -175,10 +175,12 @@ def test_sample(torch_cuda, temperature, top_p, r):
     assert tok.value == O.sample(logits, temperature, top_p, 1.0, [], r)
 
 
+@pytest.mark.parametrize("tensor_cores", [True, False], ids=["tcgen05_3xtf32", "fp32_fma"])
 @pytest.mark.parametrize("mode,n,m,k", [(0, 37, H, H), (0, 512, 3 * H, H), (2, 37, H, F), (1, 77, 2 * F, H),
-                                        (0, 5, 576, 192)])
-def test_linear_prefill(torch_cuda, mode, n, m, k):
-    """Linear::forward at N=37 as tests/test_linear.cu:32-54, plus the fused epilogues."""
+                                        (0, 5, 576, 192), (2, 130, 200, 64)])
+def test_linear_prefill(torch_cuda, mode, n, m, k, tensor_cores):
+    """Linear::forward at N=37 as tests/test_linear.cu:32-54, plus the fused epilogues; the
+    tensor-core path (3xTF32) must keep fp32-level accuracy."""
     torch = torch_cuda
     g = rng(123 + n)
     x = g.uniform(-0.1, 0.1, (n, k)).astype(np.float32)
@@ -187,7 +189,14 @@ def test_linear_prefill(torch_cuda, mode, n, m, k):
     width = m // 2 if mode == 1 else m
     init = g.uniform(-1, 1, (n, width)).astype(np.float32)
     y, dx, dw, db = dev(torch, init), dev(torch, x), dev(torch, w), dev(torch, b)
-    X.check(X.lib().xl_op_linear(mode, X.ptr(dx), X.ptr(dw), X.ptr(db), X.ptr(y), n, m, k, X.stream()))
+    x_lo = w_lo = y_lo = None
+    if tensor_cores:
+        x_lo, w_lo = torch.empty_like(dx), torch.empty_like(dw)
+        y_lo = torch.full_like(y, np.nan)
+        X.check(X.lib().xl_op_split_lo(X.ptr(dx), X.ptr(x_lo), dx.numel(), X.stream()))
+        X.check(X.lib().xl_op_split_lo(X.ptr(dw), X.ptr(w_lo), dw.numel(), X.stream()))
+    X.check(X.lib().xl_op_linear(mode, X.ptr(dx), X.ptr(x_lo), X.ptr(dw), X.ptr(w_lo), X.ptr(db), X.ptr(y),
+                                 X.ptr(y_lo), n, m, k, X.stream()))
     torch.cuda.synchronize()
     full = O.linear(x, w, b)
     if mode == 0:
@@ -196,7 +205,11 @@ def test_linear_prefill(torch_cuda, mode, n, m, k):
         ref = init + full
     else:
         ref = O.silu_mul(full[:, 0::2], full[:, 1::2])
-    close(host(y), ref, 1e-5, 1e-4)
+    close(host(y), ref, 2e-6, 1e-4)
+    if tensor_cores and mode == 1:
+        hy = host(y)
+        trunc = (hy.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+        assert np.array_equal(host(y_lo), hy - trunc)
 
 
 def test_rmsnorm_rows_and_embedding(torch_cuda):

@@ -19,7 +19,8 @@ _SIGS = {
     "xl_op_lm_head": ([VP, VP, VP, VP, VP, F, I, I, C.POINTER(C.c_int), VP, VP], I),
     "xl_op_sample_workspace_bytes": ([I], SZ),
     "xl_op_sample": ([VP, I, F, F, F, C.POINTER(C.c_int), VP, VP], I),
-    "xl_op_linear": ([I, VP, VP, VP, VP, I, I, I, VP], I),
+    "xl_op_linear": ([I, VP, VP, VP, VP, VP, VP, VP, I, I, I, VP], I),
+    "xl_op_split_lo": ([VP, VP, SZ, VP], I),
     "xl_op_rmsnorm": ([VP, VP, VP, I, I, VP], I),
     "xl_op_embedding": ([VP, VP, VP, I, I, VP], I),
     "xl_op_attn_prefill": ([VP, VP, VP, VP, VP, I, I, I, VP], I),

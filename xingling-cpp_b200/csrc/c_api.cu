@@ -145,6 +145,12 @@ int xl_engine_set_option(xl_engine* e, const char* key, int value) {
     return e->impl->set_option(key, value);
 }
 
+int xl_engine_phase_trace(xl_engine* e, unsigned long long* out, int n) {
+    xl::clear_error();
+    if (!e) return bad("null engine");
+    return e->impl->phase_trace(out, n);
+}
+
 int xl_philox_uniforms(uint64_t seed, uint64_t start, int n, float* out) {
     if (n < 0 || (n > 0 && !out)) return bad("xl_philox_uniforms: bad arguments");
     for (int i = 0; i < n; ++i) out[i] = xl::philox_uniform(start + static_cast<uint64_t>(i), seed);
@@ -299,18 +305,37 @@ int xl_op_sample(const float* logits, int vocab, float temperature, float top_p,
     return XL_OK;
 }
 
-int xl_op_linear(int mode, const float* x, const float* w, const float* b, float* y, int n, int m, int k,
-                 void* stream) {
+int xl_op_linear(int mode, const float* x, const float* x_lo, const float* w, const float* w_lo, const float* b,
+                 float* y, float* y_lo, int n, int m, int k, void* stream) {
     xl::clear_error();
     if (!x || !w || !y || n <= 0 || m <= 0 || k <= 0 || k % 8) return bad("xl_op_linear: bad arguments");
+    if (mode != xl::kGemvPlain && mode != xl::kGemvSwiGLU && mode != xl::kGemvResidual)
+        return bad("xl_op_linear: mode must be 0, 1 or 2");
     if (mode == xl::kGemvSwiGLU && (m % 2 || !b)) return bad("xl_op_linear: SwiGLU needs even m and a bias");
-    return cuda_status(xl::launch_linear_prefill(mode, x, w, b, y, n, m, k, as_stream(stream)), "xl_op_linear");
+    cudaStream_t s = as_stream(stream);
+    if (!x_lo || !w_lo)
+        return cuda_status(xl::launch_linear_prefill(mode, x, w, b, y, n, m, k, s), "xl_op_linear");
+    if (k % 32) return bad("xl_op_linear: the tensor-core path needs k % 32 == 0");
+    if (mode == xl::kGemvSwiGLU && !y_lo) return bad("xl_op_linear: the tensor-core SwiGLU path writes y_lo");
+    xl::TcOperands o;
+    int rc = cuda_status(xl::make_tile_map(&o.w, w, m, k), "make_tile_map");
+    if (rc == XL_OK) rc = cuda_status(xl::make_tile_map(&o.w_lo, w_lo, m, k), "make_tile_map");
+    if (rc == XL_OK) rc = cuda_status(xl::make_tile_map(&o.x, x, n, k), "make_tile_map");
+    if (rc == XL_OK) rc = cuda_status(xl::make_tile_map(&o.x_lo, x_lo, n, k), "make_tile_map");
+    if (rc != XL_OK) return rc;
+    return cuda_status(xl::launch_gemm_tc(mode, o, b, y, y_lo, n, m, k, nullptr, s), "xl_op_linear (tcgen05)");
+}
+
+int xl_op_split_lo(const float* x, float* lo, size_t n, void* stream) {
+    xl::clear_error();
+    if (!x || !lo) return bad("xl_op_split_lo: null pointer");
+    return cuda_status(xl::launch_split_lo(x, lo, n, as_stream(stream)), "xl_op_split_lo");
 }
 
 int xl_op_rmsnorm(const float* x, const float* gamma, float* out, int n, int k, void* stream) {
     xl::clear_error();
     if (!x || !gamma || !out || n <= 0 || k <= 0 || k % 4) return bad("xl_op_rmsnorm: bad arguments");
-    return cuda_status(xl::launch_rmsnorm_rows(x, gamma, out, n, k, 1e-6f, as_stream(stream)), "xl_op_rmsnorm");
+    return cuda_status(xl::launch_rmsnorm_rows(x, gamma, out, nullptr, n, k, as_stream(stream)), "xl_op_rmsnorm");
 }
 
 int xl_op_embedding(const float* table, const int* ids, float* out, int n, int k, void* stream) {
@@ -328,7 +353,7 @@ int xl_op_attn_prefill(float* qkv, const float* rope, float* kc, float* vc, floa
     const float2* r2 = reinterpret_cast<const float2*>(rope);
     int rc = cuda_status(xl::launch_rope_kv_prefill(qkv, r2, kc, vc, n, heads, max_ctx, s), "rope_kv_prefill");
     if (rc != XL_OK) return rc;
-    return cuda_status(xl::launch_attn_prefill(qkv, kc, vc, out, n, heads, max_ctx, s), "attn_prefill");
+    return cuda_status(xl::launch_attn_prefill(qkv, kc, vc, out, nullptr, n, heads, max_ctx, s), "attn_prefill");
 }
 
 }  // extern "C"

@@ -86,6 +86,17 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 }
 __device__ __forceinline__ bool aborted(const DevState* st) { return *reinterpret_cast<const volatile int*>(&st->err); }
 
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Optional phase timeline: trace[(cta * phases + ph) * kTraceFields + field] (ns).
+enum TraceField : int { kTrConsStart = 0, kTrConsStaged = 1, kTrConsEnd = 2, kTrProdFirst = 3, kTrProdLast = 4 };
+__device__ __forceinline__ void trace_at(const PersistentParams& p, int ph, int field) {
+    if (p.trace) p.trace[(static_cast<size_t>(blockIdx.x) * (5 * p.layers + 1) + ph) * kTraceFields + field] = globaltimer();
+}
+
 // Bounded wait on an mbarrier phase; false (and the error bit) on timeout or abort.
 __device__ bool wait_parity(uint64_t* bar, uint32_t parity, DevState* st) {
     uint32_t it = 0;
@@ -180,6 +191,12 @@ __device__ bool unit_next(const PersistentParams& p, Unit& u) {
     return unit_first(p, u.ph + 1, u);
 }
 
+__device__ __forceinline__ int cu_first_group(const PersistentParams& p, const Unit& u) {
+    int g0, g1;
+    my_groups(gemv_of(p, u.ph).M, g0, g1);
+    return g0;
+}
+
 __device__ void prefetch_unit(const PersistentParams& p, const Unit& u) {
     const Gemv d = gemv_of(p, u.ph);
     const int rows = min(kTileRows, d.M - u.g * kTileRows);
@@ -210,6 +227,7 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
         const Gemv d = gemv_of(p, cu.ph);
         const int nkt = (d.K + kTileK - 1) / kTileK;
         const int g = cu.g;
+        if (g == cu_first_group(p, cu)) trace_at(p, cu.ph, kTrProdFirst);
         {
             const int rows = min(kTileRows, d.M - g * kTileRows);
             for (int kt = 0; kt < nkt; ++kt) {
@@ -232,6 +250,7 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
                 }
             }
         }
+        if (g + 1 == cu.g1) trace_at(p, cu.ph, kTrProdLast);
     }
     if (!ok) {
         // Drain: every copy already issued must land before this CTA exits.
@@ -424,13 +443,16 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
     const int last = 5 * p.layers;
     for (int ph = 0; ph <= last; ++ph) {
         if (ph > 0 && !wait_phase(p, ph - 1)) return;
+        if (t == 0) trace_at(p, ph, kTrConsStart);
         const int kind = phase_kind(ph, p.layers);
         const LayerPtrs* y = ph < last ? &p.layer[ph / 5] : nullptr;
         if (kind == kAttn) {
             const int items = p.heads * nsplit;
             for (int it = blockIdx.x + gridDim.x * warp; it < items; it += gridDim.x * kConsumerWarps)
                 attend_chunk(p, *y, it / nsplit, it % nsplit, n, qbuf + warp * kHeadDim);
+            if (t == 0) trace_at(p, ph, kTrConsStaged);
             signal_phase(p, ph);
+            if (t == 0) trace_at(p, ph, kTrConsEnd);
             continue;
         }
         const Gemv d = gemv_of(p, ph);
@@ -452,6 +474,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
             stage_norm(p.x, p.gnorm, p.H, xs, red, nullptr);
         }
         consumer_sync();
+        if (t == 0) trace_at(p, ph, kTrConsStaged);
         int g0, g1;
         my_groups(d.M, g0, g1);
         const int nkt = (d.K + kTileK - 1) / kTileK;
@@ -527,6 +550,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
             }
         }
         if (kind != kLM) signal_phase(p, ph);
+        if (t == 0) trace_at(p, ph, kTrConsEnd);
     }
     // LM head: CTA argmax -> global max; the last CTA publishes the winner.
     if (lane == 0) best_s[warp] = best_i >= 0 ? pack_argmax(best_v, best_i) : 0ull;

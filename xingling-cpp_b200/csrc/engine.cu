@@ -203,6 +203,10 @@ int Engine::alloc_all() {
         add(&L.g2, H * 4);
         add(&L.kc, heads_l_ * T * kHeadDim * 4);
         add(&L.vc, heads_l_ * T * kHeadDim * 4);
+        add(&L.wqkv_lo, 3 * Hl * H * 4);
+        add(&L.wo_lo, H * Hl * 4);
+        add(&L.w13_lo, 2 * Fl * H * 4);
+        add(&L.w2_lo, H * Fl * 4);
     }
     add(&xa_, H * 4);
     add(&xb_, H * 4);
@@ -221,6 +225,9 @@ int Engine::alloc_all() {
     add(&pqkv_, T * 3 * Hl * 4);
     add(&patt_, T * H * 4);
     add(&pffh_, T * Fl * 4);
+    add(&pxn_lo_, T * H * 4);
+    add(&patt_lo_, T * H * 4);
+    add(&pffh_lo_, T * Fl * 4);
     add(&pids_, T * 4);
     size_t total = 0;
     for (auto& pr : plan) total += align_up(pr.second, 256);
@@ -247,6 +254,7 @@ Engine::~Engine() {
     if (h_in_) cudaFreeHost(h_in_);
     if (h_out_) cudaFreeHost(h_out_);
     if (h_ids_) cudaFreeHost(h_ids_);
+    if (trace_) cudaFree(trace_);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
     if (stream_) cudaStreamDestroy(stream_);
@@ -360,11 +368,54 @@ int Engine::load(const char* dir) {
         set_error(ld.err);
         return rc;
     }
+    rc = prepare_prefill_operands();
+    if (rc != XL_OK) return rc;
     loaded_ = true;
     has_seq_ = false;
     n_ = 0;
     rc = capture_decode_graph();
     return rc;
+}
+
+// TF32 residuals of the projection weights and the TMA maps of every prefill
+// GEMM operand (weights, their residuals, the fixed activation buffers).
+int Engine::prepare_prefill_operands() {
+    const size_t H = H_, Hl = Hl_, Fl = Fl_;
+    for (auto& L : layers_) {
+        XL_CUDA(launch_split_lo(L.wqkv, L.wqkv_lo, 3 * Hl * H, stream_));
+        XL_CUDA(launch_split_lo(L.wo, L.wo_lo, H * Hl, stream_));
+        XL_CUDA(launch_split_lo(L.w13, L.w13_lo, 2 * Fl * H, stream_));
+        XL_CUDA(launch_split_lo(L.w2, L.w2_lo, H * Fl, stream_));
+        XL_CUDA(make_tile_map(&L.tc_qkv.w, L.wqkv, 3 * Hl_, H_));
+        XL_CUDA(make_tile_map(&L.tc_qkv.w_lo, L.wqkv_lo, 3 * Hl_, H_));
+        XL_CUDA(make_tile_map(&L.tc_qkv.x, pxn_, T_, H_));
+        XL_CUDA(make_tile_map(&L.tc_qkv.x_lo, pxn_lo_, T_, H_));
+        XL_CUDA(make_tile_map(&L.tc_wo.w, L.wo, H_, Hl_));
+        XL_CUDA(make_tile_map(&L.tc_wo.w_lo, L.wo_lo, H_, Hl_));
+        XL_CUDA(make_tile_map(&L.tc_wo.x, patt_, T_, Hl_));
+        XL_CUDA(make_tile_map(&L.tc_wo.x_lo, patt_lo_, T_, Hl_));
+        XL_CUDA(make_tile_map(&L.tc_w13.w, L.w13, 2 * Fl_, H_));
+        XL_CUDA(make_tile_map(&L.tc_w13.w_lo, L.w13_lo, 2 * Fl_, H_));
+        XL_CUDA(make_tile_map(&L.tc_w13.x, pxn_, T_, H_));
+        XL_CUDA(make_tile_map(&L.tc_w13.x_lo, pxn_lo_, T_, H_));
+        XL_CUDA(make_tile_map(&L.tc_w2.w, L.w2, H_, Fl_));
+        XL_CUDA(make_tile_map(&L.tc_w2.w_lo, L.w2_lo, H_, Fl_));
+        XL_CUDA(make_tile_map(&L.tc_w2.x, pffh_, T_, Fl_));
+        XL_CUDA(make_tile_map(&L.tc_w2.x_lo, pffh_lo_, T_, Fl_));
+    }
+    XL_CUDA(cudaStreamSynchronize(stream_));
+    return XL_OK;
+}
+
+int Engine::prefill_linear(int mode, const TcOperands& o, const float* x, const float* w, const float* b, float* y,
+                           float* y_lo, int n, int m, int k, cudaStream_t s) {
+    if (prefill_gemm_ == 0) {
+        XL_CUDA(launch_gemm_tc(mode, o, b, y, y_lo, n, m, k, &st_->err, s));
+    } else {
+        XL_CUDA(launch_linear_prefill(mode, x, w, b, y, n, m, k, s));
+        if (y_lo) XL_CUDA(launch_split_lo(y, y_lo, static_cast<size_t>(n) * (mode == kGemvSwiGLU ? m / 2 : m), s));
+    }
+    return XL_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -395,6 +446,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     p.rep_flags = rep_flags_;
     p.st = st_;
     p.done = done_;
+    p.trace = trace_;
     p.H = H_;
     p.Hl = Hl_;
     p.heads = heads_l_;
@@ -635,30 +687,40 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
 
     const size_t H = H_;
     XL_CUDA(launch_embed_gather(emb_, pids_, px_, n, H_, s));
-    for (int l = 0; l < cfg_.layers; ++l) {
+    int rc = XL_OK;
+    for (int l = 0; l < cfg_.layers && rc == XL_OK; ++l) {
         const LayerWeights& L = layers_[l];
-        XL_CUDA(launch_rmsnorm_rows(px_, L.g1, pxn_, n, H_, 1e-6f, s));
-        XL_CUDA(launch_linear_prefill(kGemvPlain, pxn_, L.wqkv, L.bqkv, pqkv_, n, 3 * Hl_, H_, s));
+        XL_CUDA(launch_rmsnorm_rows(px_, L.g1, pxn_, pxn_lo_, n, H_, s));
+        rc = prefill_linear(kGemvPlain, L.tc_qkv, pxn_, L.wqkv, L.bqkv, pqkv_, nullptr, n, 3 * Hl_, H_, s);
+        if (rc != XL_OK) break;
         XL_CUDA(launch_rope_kv_prefill(pqkv_, rope_, L.kc, L.vc, n, heads_l_, T_, s));
-        XL_CUDA(launch_attn_prefill(pqkv_, L.kc, L.vc, patt_, n, heads_l_, T_, s));
+        XL_CUDA(launch_attn_prefill(pqkv_, L.kc, L.vc, patt_, patt_lo_, n, heads_l_, T_, s));
         if (tp_ == 1) {
-            XL_CUDA(launch_linear_prefill(kGemvResidual, patt_, L.wo, L.bo, px_, n, H_, Hl_, s));
+            rc = prefill_linear(kGemvResidual, L.tc_wo, patt_, L.wo, L.bo, px_, nullptr, n, H_, Hl_, s);
         } else {
-            XL_CUDA(launch_linear_prefill(kGemvPlain, patt_, L.wo, L.bo, pxn_, n, H_, Hl_, s));
-            XL_NCCL(ncclAllReduce(pxn_, pxn_, n * H, ncclFloat, ncclSum, comm_, s));
-            XL_CUDA(launch_add_rows(px_, pxn_, n * H_, s));
+            // partial sums into pxn_ (free until the next norm), reduced over ranks, then added
+            rc = prefill_linear(kGemvPlain, L.tc_wo, patt_, L.wo, L.bo, pxn_, nullptr, n, H_, Hl_, s);
+            if (rc == XL_OK) {
+                XL_NCCL(ncclAllReduce(pxn_, pxn_, n * H, ncclFloat, ncclSum, comm_, s));
+                XL_CUDA(launch_add_rows(px_, pxn_, n * H_, s));
+            }
         }
-        XL_CUDA(launch_rmsnorm_rows(px_, L.g2, pxn_, n, H_, 1e-6f, s));
-        XL_CUDA(launch_linear_prefill(kGemvSwiGLU, pxn_, L.w13, L.b13, pffh_, n, 2 * Fl_, H_, s));
+        if (rc != XL_OK) break;
+        XL_CUDA(launch_rmsnorm_rows(px_, L.g2, pxn_, pxn_lo_, n, H_, s));
+        rc = prefill_linear(kGemvSwiGLU, L.tc_w13, pxn_, L.w13, L.b13, pffh_, pffh_lo_, n, 2 * Fl_, H_, s);
+        if (rc != XL_OK) break;
         if (tp_ == 1) {
-            XL_CUDA(launch_linear_prefill(kGemvResidual, pffh_, L.w2, L.b2, px_, n, H_, Fl_, s));
+            rc = prefill_linear(kGemvResidual, L.tc_w2, pffh_, L.w2, L.b2, px_, nullptr, n, H_, Fl_, s);
         } else {
-            XL_CUDA(launch_linear_prefill(kGemvPlain, pffh_, L.w2, L.b2, pxn_, n, H_, Fl_, s));
-            XL_NCCL(ncclAllReduce(pxn_, pxn_, n * H, ncclFloat, ncclSum, comm_, s));
-            XL_CUDA(launch_add_rows(px_, pxn_, n * H_, s));
+            rc = prefill_linear(kGemvPlain, L.tc_w2, pffh_, L.w2, L.b2, pxn_, nullptr, n, H_, Fl_, s);
+            if (rc == XL_OK) {
+                XL_NCCL(ncclAllReduce(pxn_, pxn_, n * H, ncclFloat, ncclSum, comm_, s));
+                XL_CUDA(launch_add_rows(px_, pxn_, n * H_, s));
+            }
         }
     }
-    int rc = run_lm_head_and_sample(px_ + static_cast<size_t>(n - 1) * H, nullptr, s);
+    if (rc != XL_OK) return rc;
+    rc = run_lm_head_and_sample(px_ + static_cast<size_t>(n - 1) * H, nullptr, s);
     if (rc != XL_OK) return rc;
     rc = finish_step(token_out);
     if (rc != XL_OK) return rc;
@@ -743,8 +805,40 @@ int Engine::set_option(const char* key, int value) {
         decode_path_ = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
+    if (k == "prefill_gemm") {
+        if (value != 0 && value != 1) {
+            set_error("prefill_gemm must be 0 (tcgen05 3xTF32) or 1 (fp32 SIMT tiles)");
+            return XL_ERR_ARG;
+        }
+        prefill_gemm_ = value;
+        return XL_OK;
+    }
+    if (k == "phase_trace") {
+        if (value && !trace_) {
+            const size_t n = static_cast<size_t>(num_sms_) * (5 * cfg_.layers + 1) * kTraceFields;
+            XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&trace_), n * sizeof(unsigned long long)));
+            XL_CUDA(cudaMemset(trace_, 0, n * sizeof(unsigned long long)));
+        } else if (!value && trace_) {
+            XL_CUDA(cudaStreamSynchronize(stream_));
+            XL_CUDA(cudaFree(trace_));
+            trace_ = nullptr;
+        }
+        return loaded_ ? capture_decode_graph() : XL_OK;
+    }
     set_error("unknown option: " + k);
     return XL_ERR_ARG;
+}
+
+int Engine::phase_trace(unsigned long long* out, int n) {
+    XL_CUDA(cudaSetDevice(device_));
+    const int need = num_sms_ * (5 * cfg_.layers + 1) * kTraceFields;
+    if (!trace_ || !out || n != need) {
+        set_error("phase_trace: enable the phase_trace option; n must be " + std::to_string(need));
+        return XL_ERR_ARG;
+    }
+    XL_CUDA(cudaMemcpyAsync(out, trace_, sizeof(unsigned long long) * n, cudaMemcpyDeviceToHost, stream_));
+    XL_CUDA(cudaStreamSynchronize(stream_));
+    return XL_OK;
 }
 
 int Engine::set_uniforms(const float* u, int n) {

@@ -31,6 +31,9 @@ struct LayerWeights {
     float* g2;    // [H]
     float* kc;    // [heads_l][max_ctx][64]
     float* vc;    // [heads_l][max_ctx][64]
+    // TF32 residuals (w - trunc19(w)) of the four projections, for the 3xTF32 prefill GEMMs
+    float *wqkv_lo, *wo_lo, *w13_lo, *w2_lo;
+    TcOperands tc_qkv, tc_wo, tc_w13, tc_w2;  // TMA maps of the prefill GEMM operands
 };
 
 class Engine {
@@ -47,6 +50,7 @@ class Engine {
     int kv_copy(int layer, int npos, float* k_out, float* v_out);
     int profile_lm_head(int iters, float* avg_ms);
     int set_option(const char* key, int value);
+    int phase_trace(unsigned long long* out, int n);
     int ctx_len() const { return n_; }
     float last_device_ms() const { return last_ms_; }
     int vocab_begin() const { return v0_; }
@@ -59,6 +63,9 @@ class Engine {
     int capture_decode_graph();
     int enqueue_decode(cudaStream_t s);
     int enqueue_decode_persistent(cudaStream_t s);
+    int prepare_prefill_operands();
+    int prefill_linear(int mode, const TcOperands& o, const float* x, const float* w, const float* b, float* y,
+                       float* y_lo, int n, int m, int k, cudaStream_t s);
     int run_lm_head_and_sample(const float* x_last, const float* delta, cudaStream_t s);
     int launch_lm_head(const float* x_last, const float* delta, bool pdl, cudaStream_t s);
     const float* lm_x_ = nullptr;  // residual stream the decode graph's LM head reads
@@ -90,10 +97,12 @@ class Engine {
     float* attn_ws_ = nullptr; // split-K partials
     int* attn_cnt_ = nullptr;  // [heads_l] split counters
     int* done_ = nullptr;      // [5*layers + 1] phase counters of the persistent decode kernel
+    unsigned long long* trace_ = nullptr;  // optional phase timeline of the persistent kernel
     uint8_t* rep_flags_ = nullptr;  // [vl]
     DevState* st_ = nullptr;
     // prefill buffers [T][...]
     float *px_ = nullptr, *pxn_ = nullptr, *pqkv_ = nullptr, *patt_ = nullptr, *pffh_ = nullptr;
+    float *pxn_lo_ = nullptr, *patt_lo_ = nullptr, *pffh_lo_ = nullptr;
     int* pids_ = nullptr;
 
     // host
@@ -106,6 +115,7 @@ class Engine {
     ncclComm_t comm_ = nullptr;
 
     int decode_path_ = 0;      // 0: persistent kernel (single GPU), 1: per-op kernels
+    int prefill_gemm_ = 0;     // 0: tcgen05 3xTF32, 1: fp32 SIMT tiles
     bool loaded_ = false;
     bool has_seq_ = false;
     int n_ = 0;

@@ -26,8 +26,11 @@ __global__ void __launch_bounds__(256) embed_gather_kernel(const float* __restri
     for (int i = threadIdx.x; i < (k >> 2); i += blockDim.x) dst[i] = src[i];
 }
 
+__device__ __forceinline__ float lo19(float v) { return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
+
 __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
-                                                           float* __restrict__ out, int k, double eps) {
+                                                           float* __restrict__ out, float* __restrict__ out_lo, int k,
+                                                           double eps) {
     __shared__ float red[8];
     const int row = blockIdx.x;
     const float4* x4 = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * k);
@@ -50,6 +53,9 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const float* __restri
         v.z = v.z * inv * g.z;
         v.w = v.w * inv * g.w;
         o4[i] = v;
+        if (out_lo)
+            reinterpret_cast<float4*>(out_lo + static_cast<size_t>(row) * k)[i] =
+                make_float4(lo19(v.x), lo19(v.y), lo19(v.z), lo19(v.w));
     }
 }
 
@@ -187,8 +193,8 @@ constexpr int kAT = 64;
 constexpr int kAP = kAT + 4;
 
 __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
-                                                           const float* __restrict__ vc, float* __restrict__ out, int N,
-                                                           int heads, int max_ctx) {
+                                                           const float* __restrict__ vc, float* __restrict__ out,
+                                                           float* __restrict__ out_lo, int N, int heads, int max_ctx) {
     extern __shared__ __align__(16) float smem[];
     float* Qt = smem;              // [64 dims][kAP] (q scaled by 1/8, transposed)
     float* Kt = Qt + kAT * kAP;    // [64 dims][kAP] (transposed)
@@ -292,8 +298,10 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
         const int qi = q0 + ty * 4 + i;
         if (qi < N) {
             const float inv = 1.0f / l_run[i];
-            *reinterpret_cast<float4*>(out + static_cast<size_t>(qi) * HL + h * kHeadDim + tx * 4) =
-                make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+            const float4 r = make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+            const size_t off = static_cast<size_t>(qi) * HL + h * kHeadDim + tx * 4;
+            *reinterpret_cast<float4*>(out + off) = r;
+            if (out_lo) *reinterpret_cast<float4*>(out_lo + off) = make_float4(lo19(r.x), lo19(r.y), lo19(r.z), lo19(r.w));
         }
     }
 }
@@ -313,11 +321,10 @@ cudaError_t launch_embed_gather(const float* table, const int* ids, float* out, 
     return cudaGetLastError();
 }
 
-cudaError_t launch_rmsnorm_rows(const float* x, const float* gamma, float* out, int n, int k, float eps,
+cudaError_t launch_rmsnorm_rows(const float* x, const float* gamma, float* out, float* out_lo, int n, int k,
                                 cudaStream_t s) {
     if (n <= 0 || k % 4) return cudaErrorInvalidValue;
-    (void)eps;
-    rmsnorm_rows_kernel<<<n, 256, 0, s>>>(x, gamma, out, k, 1e-6);
+    rmsnorm_rows_kernel<<<n, 256, 0, s>>>(x, gamma, out, out_lo, k, 1e-6);
     return cudaGetLastError();
 }
 
@@ -355,14 +362,14 @@ cudaError_t launch_rope_kv_prefill(float* qkv, const float2* rope, float* kc, fl
     return cudaGetLastError();
 }
 
-cudaError_t launch_attn_prefill(const float* qkv, const float* kc, const float* vc, float* out, int n, int heads,
-                                int max_ctx, cudaStream_t s) {
+cudaError_t launch_attn_prefill(const float* qkv, const float* kc, const float* vc, float* out, float* out_lo, int n,
+                                int heads, int max_ctx, cudaStream_t s) {
     if (n <= 0 || n > max_ctx) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kAttnPrefillSmem));
     if (e != cudaSuccess) return e;
-    attn_prefill_kernel<<<dim3((n + kAT - 1) / kAT, heads), 256, kAttnPrefillSmem, s>>>(qkv, kc, vc, out, n, heads,
-                                                                                        max_ctx);
+    attn_prefill_kernel<<<dim3((n + kAT - 1) / kAT, heads), 256, kAttnPrefillSmem, s>>>(qkv, kc, vc, out, out_lo, n,
+                                                                                        heads, max_ctx);
     return cudaGetLastError();
 }
 

@@ -156,6 +156,12 @@ class InferenceEngine {
         check(rc);
     }
 
+    py::bytes phase_trace(int n) {
+        std::string buf(static_cast<size_t>(n) * 8, '\0');
+        check(xl_engine_phase_trace(e_, reinterpret_cast<unsigned long long*>(&buf[0]), n));
+        return py::bytes(buf);
+    }
+
     float profile_lm_head(int iters) {
         float ms = 0.0f;
         int rc;
@@ -210,6 +216,7 @@ PYBIND11_MODULE(llm_cpp_engine, m) {
         .def("ctx_len", &InferenceEngine::ctx_len)
         .def("last_device_ms", &InferenceEngine::last_device_ms)
         .def("set_option", &InferenceEngine::set_option, py::arg("key"), py::arg("value"))
+        .def("phase_trace", &InferenceEngine::phase_trace, py::arg("n"))
         .def("profile_lm_head", &InferenceEngine::profile_lm_head, py::arg("iters") = 20)
         .def_readwrite("im_start_id", &InferenceEngine::im_start_id)
         .def_readwrite("im_end_id", &InferenceEngine::im_end_id)

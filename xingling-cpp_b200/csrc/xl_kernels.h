@@ -1,6 +1,7 @@
 // Host-side launchers for the XingLing sm_100a kernels.  Every launcher is
 // asynchronous on the given stream and returns the launch status.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -100,8 +101,10 @@ struct PersistentParams {
     const uint8_t* rep_flags;
     DevState* st;
     int* done;              // [5*layers + 1] phase counters, zeroed before each launch
+    unsigned long long* trace;  // optional [grid][5*layers + 1][kTraceFields] timestamps (ns), or nullptr
     int H, Hl, heads, Fl, V, T;
 };
+constexpr int kTraceFields = 5;
 size_t persistent_smem_bytes();
 cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cudaStream_t s);
 
@@ -115,9 +118,24 @@ struct SampleParams {
 };
 cudaError_t launch_sample(const SampleParams& p, bool pdl, cudaStream_t s);
 
+// ---- prefill on tcgen05 (gemm_tc.cu) ----
+// Operand maps of one projection: W and W_lo ([M][K]), X and X_lo ([rows][K]),
+// each a 2D TMA map with {32, 128} boxes and 128B swizzle (make_tile_map).
+struct TcOperands {
+    CUtensorMap w, w_lo, x, x_lo;
+};
+cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int cols);
+// C[N][M] (+)= X[N][K] . W[M][K]^T + b with the 3xTF32 split; SwiGLU writes C and C_lo as [N][M/2].
+cudaError_t launch_gemm_tc(int mode, const TcOperands& o, const float* bias, float* C, float* C_lo, int n, int m,
+                           int k, int* err, cudaStream_t s);
+// lo[i] = x[i] - (x[i] with its 13 low mantissa bits cleared): the TF32 residual.
+cudaError_t launch_split_lo(const float* x, float* lo, size_t n, cudaStream_t s);
+size_t gemm_tc_smem_bytes();
+
 // ---- prefill ----
 cudaError_t launch_embed_gather(const float* table, const int* ids, float* out, int n, int k, cudaStream_t s);
-cudaError_t launch_rmsnorm_rows(const float* x, const float* gamma, float* out, int n, int k, float eps,
+// out_lo (optional) receives the TF32 residual of out for the 3xTF32 GEMMs.
+cudaError_t launch_rmsnorm_rows(const float* x, const float* gamma, float* out, float* out_lo, int n, int k,
                                 cudaStream_t s);
 // Y[N][M] (+)= X[N][K] . W[M][K]^T + b; mode as GemvMode (Plain / SwiGLU / Residual).
 cudaError_t launch_linear_prefill(int mode, const float* X, const float* W, const float* b, float* Y, int n,
@@ -126,7 +144,7 @@ cudaError_t launch_rope_kv_prefill(float* qkv, const float2* rope, float* kc, fl
                                    int max_ctx, cudaStream_t s);
 // x[i] += d[i] for i < n (tensor-parallel residual add after an all-reduce).
 cudaError_t launch_add_rows(float* x, const float* d, int n, cudaStream_t s);
-cudaError_t launch_attn_prefill(const float* qkv, const float* kc, const float* vc, float* out, int n, int heads,
-                                int max_ctx, cudaStream_t s);
+cudaError_t launch_attn_prefill(const float* qkv, const float* kc, const float* vc, float* out, float* out_lo, int n,
+                                int heads, int max_ctx, cudaStream_t s);
 
 }  // namespace xl
