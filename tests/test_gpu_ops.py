@@ -205,7 +205,9 @@ def test_linear_prefill(torch_cuda, mode, n, m, k, tensor_cores):
         ref = init + full
     else:
         ref = O.silu_mul(full[:, 0::2], full[:, 1::2])
-    close(host(y), ref, 2e-6, 1e-4)
+    # 3xTF32 keeps the products to ~2^-21 relative; the tensor core's fp32
+    # accumulation over K terms adds ~1e-6 x sqrt(K / 1536) absolute here.
+    close(host(y), ref, 2e-5 if tensor_cores else 2e-6, 1e-4)
     if tensor_cores and mode == 1:
         hy = host(y)
         trunc = (hy.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
