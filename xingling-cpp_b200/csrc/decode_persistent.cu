@@ -3,14 +3,17 @@
 // One CTA per SM (cooperative launch, so every CTA is resident).  Warp 0 is a
 // producer: one lane streams every weight tile this CTA needs for the whole
 // token (16 x [QKV, out-proj, W1/V, W2] and the tied LM head) from HBM into a
-// shared-memory ring with cp.async.bulk (TMA engine), gated only by free ring
-// slots.  Warps 1..8 consume: per phase they wait for the previous phase of
-// every CTA (a global counter), stage the phase's input vector in shared
-// memory (residual update, RMSNorm, attention combine or SwiGLU input), take
-// ring tiles, reduce with warp shuffles and apply the epilogue.  Because the
+// shared-memory ring with 2D TMA tile loads (cp.async.bulk.tensor, one 16 KB
+// [16 rows][256 floats] box per instruction), gated only by free ring slots,
+// and keeps an L2 bulk-prefetch cursor a few row groups ahead.  Warps 1..8
+// consume: per phase they wait for the previous phase of every CTA (a global
+// counter), stage the phase's input vector in shared memory (embedding
+// gather, residual stream, RMSNorm, attention combine or SwiGLU input), take
+// ring tiles (two rows per warp), reduce with warp shuffles and apply the
+// epilogue, whose operands (bias, residual, repetition flags) are loaded
+// before the unit's tiles so their latency overlaps the stream.  Because the
 // producer never waits on activations, HBM keeps streaming across phase
-// boundaries; the only per-phase cost is the consumers' barrier latency,
-// hidden behind the ring.
+// boundaries.
 //
 // Replaces, for one decode token, the reference's Transformer::forward(int)
 // (src/transformer.cu:180-186) with TransformerBlock::forward
@@ -34,16 +37,19 @@ namespace {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kTileRows = 2 * kConsumerWarps;   // each consumer warp owns two rows of a tile
-constexpr int kTileK = 384;                     // floats of a row per tile
-constexpr int kSlotBytes = kTileRows * kTileK * 4;  // 24 KB
-constexpr int kSlots = 8;                       // 192 KB ring
+constexpr int kSlotBytes = kPersistTileRows * kPersistTileK * 4;  // 16 KB
+constexpr int kSlots = 12;                                       // 192 KB ring
 constexpr int kMaxK = 4096;
-constexpr size_t kSmemBytes =
-    static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 + 2 * kSlots * 8 + 256 + kConsumerWarps * 64 * 4;
+constexpr int kCombineFloats = 2048;  // (weight, sum) per (head, split): 24 heads x 24 splits at most
+constexpr size_t kSmemBytes = static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 + 2 * kSlots * 8 + 512 +
+                              kConsumerWarps * 64 * 4 + kCombineFloats * 4;
 constexpr uint32_t kMbarSpinLimit = 1u << 24;
-constexpr uint32_t kFlagSpinLimit = 1u << 23;
+constexpr uint32_t kFlagSpinLimit = 1u << 24;
 constexpr int kErrMbar = 1, kErrFlag = 2;
+constexpr int kPrefetchUnits = 4;
+constexpr uint32_t kPrefetchPiece = 32768;
+
+static_assert(kPersistTileRows == 2 * kConsumerWarps, "each consumer warp owns two rows of a tile");
 
 enum PhaseKind : int { kQKV = 0, kAttn = 1, kWo = 2, kW13 = 3, kW2 = 4, kLM = 5 };
 
@@ -71,12 +77,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Global -> shared bulk copy (no multicast) completing on a CTA-local mbarrier.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
+// 2D TMA tile load (no multicast) of one [16 rows][256 floats] box at (x, y).
+__device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerThreads) : "memory"); }
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -112,6 +119,7 @@ __device__ bool wait_parity(uint64_t* bar, uint32_t parity, DevState* st) {
 struct Gemv {
     const float* W;
     const float* bias;
+    const CUtensorMap* map;
     int M, K, kind;
 };
 
@@ -121,27 +129,24 @@ __device__ __forceinline__ Gemv gemv_of(const PersistentParams& p, int ph) {
     Gemv g{};
     const int L = p.layers;
     if (ph == 5 * L) {
-        g.W = p.emb;
-        g.bias = nullptr;
-        g.M = p.V;
-        g.K = p.H;
-        g.kind = kLM;
+        g.W = p.emb, g.bias = nullptr, g.map = &p.maps[kPersistMaps - 1], g.M = p.V, g.K = p.H, g.kind = kLM;
         return g;
     }
-    const LayerPtrs& y = p.layer[ph / 5];
+    const int l = ph / 5;
+    const LayerPtrs& y = p.layer[l];
     g.kind = ph % 5;
     switch (g.kind) {
         case kQKV:
-            g.W = y.wqkv, g.bias = y.bqkv, g.M = 3 * p.Hl, g.K = p.H;
+            g.W = y.wqkv, g.bias = y.bqkv, g.map = &p.maps[4 * l + 0], g.M = 3 * p.Hl, g.K = p.H;
             break;
         case kWo:
-            g.W = y.wo, g.bias = y.bo, g.M = p.H, g.K = p.Hl;
+            g.W = y.wo, g.bias = y.bo, g.map = &p.maps[4 * l + 1], g.M = p.H, g.K = p.Hl;
             break;
         case kW13:
-            g.W = y.w13, g.bias = y.b13, g.M = 2 * p.Fl, g.K = p.H;
+            g.W = y.w13, g.bias = y.b13, g.map = &p.maps[4 * l + 2], g.M = 2 * p.Fl, g.K = p.H;
             break;
         case kW2:
-            g.W = y.w2, g.bias = y.b2, g.M = p.H, g.K = p.Fl;
+            g.W = y.w2, g.bias = y.b2, g.map = &p.maps[4 * l + 3], g.M = p.H, g.K = p.Fl;
             break;
         default:
             break;
@@ -151,27 +156,18 @@ __device__ __forceinline__ Gemv gemv_of(const PersistentParams& p, int ph) {
 
 // This CTA's row groups (16 rows each) of an M-row matrix: a balanced split.
 __device__ __forceinline__ void my_groups(int M, int& g0, int& g1) {
-    const int groups = (M + kTileRows - 1) / kTileRows;
+    const int groups = (M + kPersistTileRows - 1) / kPersistTileRows;
     g0 = static_cast<int>((static_cast<long long>(blockIdx.x) * groups) / gridDim.x);
     g1 = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * groups) / gridDim.x);
 }
 
 // ---------------------------------------------------------------------------
-// Producer: the whole token's weight stream for this CTA.
-//
-// A unit is one 16-row group of one GEMV phase; its rows are contiguous in
-// HBM.  Besides the ring copies, the producer keeps an L2 prefetch cursor
-// kPrefetchUnits units ahead, so that HBM keeps streaming into L2 while the
-// ring is full (consumers waiting at a phase boundary or in attention); the
-// ring copies then hit L2.
-constexpr int kPrefetchUnits = 4;
-constexpr uint32_t kPrefetchPiece = 32768;
-
+// Producer.  A unit is one 16-row group of one GEMV phase; its rows are
+// contiguous in HBM, which the L2 prefetch cursor uses.
 struct Unit {
-    int ph, g, g1;
+    int ph, g, g0, g1;
 };
 
-// First unit at or after phase ph (ph beyond the schedule: none).
 __device__ bool unit_first(const PersistentParams& p, int ph, Unit& u) {
     const int last = 5 * p.layers;
     for (; ph <= last; ++ph) {
@@ -179,7 +175,7 @@ __device__ bool unit_first(const PersistentParams& p, int ph, Unit& u) {
         int g0, g1;
         my_groups(gemv_of(p, ph).M, g0, g1);
         if (g0 < g1) {
-            u = Unit{ph, g0, g1};
+            u = Unit{ph, g0, g0, g1};
             return true;
         }
     }
@@ -191,17 +187,11 @@ __device__ bool unit_next(const PersistentParams& p, Unit& u) {
     return unit_first(p, u.ph + 1, u);
 }
 
-__device__ __forceinline__ int cu_first_group(const PersistentParams& p, const Unit& u) {
-    int g0, g1;
-    my_groups(gemv_of(p, u.ph).M, g0, g1);
-    return g0;
-}
-
 __device__ void prefetch_unit(const PersistentParams& p, const Unit& u) {
     const Gemv d = gemv_of(p, u.ph);
-    const int rows = min(kTileRows, d.M - u.g * kTileRows);
-    const char* src = reinterpret_cast<const char*>(d.W + static_cast<size_t>(u.g) * kTileRows * d.K);
-    uint32_t bytes = static_cast<uint32_t>(rows) * d.K * 4;
+    const int rows = min(kPersistTileRows, d.M - u.g * kPersistTileRows);
+    const char* src = reinterpret_cast<const char*>(d.W + static_cast<size_t>(u.g) * kPersistTileRows * d.K);
+    const uint32_t bytes = static_cast<uint32_t>(rows) * d.K * 4;
     for (uint32_t off = 0; off < bytes; off += kPrefetchPiece)
         prefetch_l2_bulk(src + off, min(kPrefetchPiece, bytes - off));
 }
@@ -225,38 +215,31 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
             pf = unit_next(p, pu);
         }
         const Gemv d = gemv_of(p, cu.ph);
-        const int nkt = (d.K + kTileK - 1) / kTileK;
-        const int g = cu.g;
-        if (g == cu_first_group(p, cu)) trace_at(p, cu.ph, kTrProdFirst);
-        {
-            const int rows = min(kTileRows, d.M - g * kTileRows);
-            for (int kt = 0; kt < nkt; ++kt) {
-                if (!wait_parity(&empty[slot], par ^ 1u, st)) {
-                    ok = false;
-                    break;
-                }
-                const int k0 = kt * kTileK;
-                const int kc = min(kTileK, d.K - k0);
-                mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(rows * kc * 4));
-                char* dst = ring + static_cast<size_t>(slot) * kSlotBytes;
-                const float* src = d.W + static_cast<size_t>(g) * kTileRows * d.K + k0;
-                for (int r = 0; r < rows; ++r)
-                    bulk_g2s(dst + r * kTileK * 4, src + static_cast<size_t>(r) * d.K, static_cast<uint32_t>(kc * 4),
-                             &full[slot]);
-                ++issued;
-                if (++slot == kSlots) {
-                    slot = 0;
-                    par ^= 1u;
-                }
+        const int nkt = (d.K + kPersistTileK - 1) / kPersistTileK;
+        if (cu.g == cu.g0) trace_at(p, cu.ph, kTrProdFirst);
+        for (int kt = 0; kt < nkt; ++kt) {
+            if (!wait_parity(&empty[slot], par ^ 1u, st)) {
+                ok = false;
+                break;
+            }
+            // Rows past M and columns past K of the box are zero-filled by TMA and
+            // still counted in the transaction bytes.
+            mbar_arrive_expect_tx(&full[slot], kSlotBytes);
+            tma_tile(ring + static_cast<size_t>(slot) * kSlotBytes, d.map, kt * kPersistTileK,
+                     cu.g * kPersistTileRows, &full[slot]);
+            ++issued;
+            if (++slot == kSlots) {
+                slot = 0;
+                par ^= 1u;
             }
         }
-        if (g + 1 == cu.g1) trace_at(p, cu.ph, kTrProdLast);
+        if (cu.g + 1 == cu.g1) trace_at(p, cu.ph, kTrProdLast);
     }
     if (!ok) {
         // Drain: every copy already issued must land before this CTA exits.
         const int pending = issued < kSlots ? issued : kSlots;
         for (int i = 1; i <= pending; ++i) {
-            const int k = issued - i;  // tile index k went to slot k % kSlots with parity (k / kSlots) & 1
+            const int k = issued - i;  // tile k went to slot k % kSlots with parity (k / kSlots) & 1
             const int s = k % kSlots;
             const uint32_t pp = static_cast<uint32_t>((k / kSlots) & 1);
             uint32_t it = 0;
@@ -270,8 +253,7 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
 // Consumer helpers (256 threads, named barrier 1).
 
 // Wait until every CTA finished phase ph (counter == gridDim.x).
-__device__ bool wait_phase(const PersistentParams& p, int ph) {
-    __shared__ int s_ok;
+__device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
     if (threadIdx.x == 32) {
         const int* c = p.done + ph;
         uint32_t it = 0;
@@ -282,13 +264,12 @@ __device__ bool wait_phase(const PersistentParams& p, int ph) {
                 ok = 0;
                 break;
             }
-            __nanosleep(32);
         }
         __threadfence();
-        s_ok = ok;
+        *s_ok = ok;
     }
     consumer_sync();
-    return s_ok != 0;
+    return *s_ok != 0;
 }
 
 __device__ void signal_phase(const PersistentParams& p, int ph) {
@@ -316,6 +297,7 @@ __device__ float consumer_sum(float v, float* red) {
 __device__ void stage_norm(const float* src, const float* gamma, int K, float* xs, float* red, float* x_out) {
     const int t = threadIdx.x - 32;
     const float4* s4 = reinterpret_cast<const float4*>(src);
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
     float4* x4 = reinterpret_cast<float4*>(xs);
     float ss = 0.0f;
     for (int i = t; i < (K >> 2); i += kConsumerThreads) {
@@ -327,7 +309,6 @@ __device__ void stage_norm(const float* src, const float* gamma, int K, float* x
     const float tot = consumer_sum(ss, red);
     // RMSNorm of src/rmsnorm.cu:99-101: 1 / sqrt(mean + 1e-6), in double.
     const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(tot / static_cast<float>(K)) + 1e-6));
-    const float4* g4 = reinterpret_cast<const float4*>(gamma);
     for (int i = t; i < (K >> 2); i += kConsumerThreads) {
         float4 v = x4[i];
         const float4 g = g4[i];
@@ -345,34 +326,59 @@ __device__ void stage_copy(const float* src, int K, float* xs) {
         reinterpret_cast<float4*>(xs)[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
 }
 
-// Merge the split-K attention partials (m, l, o[64]) of every head into xs.
-__device__ void stage_attn_combine(const PersistentParams& p, int nsplit, float* xs) {
+// Merge the split-K attention partials (m, l, o[64]) of every head into xs:
+// per-split weights exp(m_s - M) / L first (smem), then every output with its
+// loads all in flight.
+__device__ void stage_attn_combine(const PersistentParams& p, int nsplit, float* xs, float* wsm) {
     const int t = threadIdx.x - 32;
     const int maxs = persistent_max_splits(p.T);
+    const int heads = p.Hl >> 6;
+    for (int i = t; i < heads * nsplit; i += kConsumerThreads) {
+        const int h = i / nsplit, s = i % nsplit;
+        const float* ps = p.part + (static_cast<size_t>(h) * maxs + s) * (kHeadDim + 2);
+        wsm[2 * i] = __ldcg(ps);
+        wsm[2 * i + 1] = __ldcg(ps + 1);
+    }
+    consumer_sync();
+    for (int h = t; h < heads; h += kConsumerThreads) {
+        float M = -INFINITY;
+        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, wsm[2 * (h * nsplit + s)]);
+        float L = 0.0f;
+        for (int s = 0; s < nsplit; ++s) L = fmaf(wsm[2 * (h * nsplit + s) + 1], expf(wsm[2 * (h * nsplit + s)] - M), L);
+        for (int s = 0; s < nsplit; ++s) wsm[2 * (h * nsplit + s)] = expf(wsm[2 * (h * nsplit + s)] - M) / L;
+    }
+    consumer_sync();
     for (int i = t; i < p.Hl; i += kConsumerThreads) {
         const int h = i >> 6, d = i & 63;
-        const float* base = p.part + static_cast<size_t>(h) * maxs * (kHeadDim + 2);
-        if (nsplit == 1) {
-            xs[i] = __ldcg(base + 2 + d) / __ldcg(base + 1);
-            continue;
-        }
-        float M = -INFINITY;
-        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(base + s * (kHeadDim + 2)));
-        float Ls = 0.0f, O = 0.0f;
-        for (int s = 0; s < nsplit; ++s) {
-            const float* ps = base + s * (kHeadDim + 2);
-            const float w = expf(__ldcg(ps) - M);
-            Ls = fmaf(__ldcg(ps + 1), w, Ls);
-            O = fmaf(__ldcg(ps + 2 + d), w, O);
-        }
-        xs[i] = O / Ls;
+        float o = 0.0f;
+        for (int s = 0; s < nsplit; ++s)
+            o = fmaf(__ldcg(p.part + (static_cast<size_t>(h) * maxs + s) * (kHeadDim + 2) + 2 + d),
+                     wsm[2 * (h * nsplit + s)], o);
+        xs[i] = o;
     }
+}
+
+// Butterfly reduce-scatter of a 64-float vector held by every lane: afterwards
+// lane l holds the warp-wide sums of elements 2l and 2l+1.
+__device__ __forceinline__ float2 warp_reduce_scatter64(float (&v)[64]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int half = 32, off = 16; off > 0; half >>= 1, off >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+    return make_float2(v[0], v[1]);
 }
 
 // One (head, 32-position chunk) of the decode attention on one warp, lane j
 // owning position t0 + j: RoPE at position n (src/rope.cu:20-45), KV append
 // when the chunk holds n, scores, softmax and P.V; writes the (max, sum, o)
-// partial.  All 16 K-row loads of a lane are in flight together.
+// partial.  Each lane's K and V rows (32 x 16 B loads) are in flight together.
 __device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int h, int s, int n, float* qsh) {
     const int lane = threadIdx.x & 31;
     const int t0 = s * kPersistChunk;
@@ -394,32 +400,33 @@ __device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int 
         vc[n * kHeadDim + lane + kHalfHead] = __ldcg(vn + lane + kHalfHead);
     }
     __syncwarp();
-    float sc = -INFINITY;
-    if (lane < cnt) {
-        const float4* kr = reinterpret_cast<const float4*>(kc + static_cast<size_t>(t0 + lane) * kHeadDim);
-        float4 kv[16];
+    const bool mine = lane < cnt;
+    const float4* kr = reinterpret_cast<const float4*>(kc + static_cast<size_t>(t0 + (mine ? lane : 0)) * kHeadDim);
+    const float4* vr = reinterpret_cast<const float4*>(vc + static_cast<size_t>(t0 + (mine ? lane : 0)) * kHeadDim);
+    float4 kv[16], vv[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) kv[i] = __ldcg(kr + i);
-        const float4* q4 = reinterpret_cast<const float4*>(qsh);
-        float d = 0.0f;
+    for (int i = 0; i < 16; ++i) kv[i] = __ldcg(kr + i);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) d = dot4(kv[i], q4[i], d);
-        sc = d;
-    }
+    for (int i = 0; i < 16; ++i) vv[i] = __ldcg(vr + i);
+    const float4* q4 = reinterpret_cast<const float4*>(qsh);
+    float d = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) d = dot4(kv[i], q4[i], d);
+    const float sc = mine ? d : -INFINITY;
     const float m = warp_max(sc);
-    const float e = lane < cnt ? expf(sc - m) : 0.0f;
+    const float e = mine ? expf(sc - m) : 0.0f;
     const float l = warp_sum(e);
-    float oa = 0.0f, ob = 0.0f;
-#pragma unroll 8
-    for (int j = 0; j < cnt; ++j) {
-        const float pj = __shfl_sync(0xffffffffu, e, j);
-        const float* vr = vc + static_cast<size_t>(t0 + j) * kHeadDim;
-        oa = fmaf(pj, __ldcg(vr + lane), oa);
-        ob = fmaf(pj, __ldcg(vr + lane + kHalfHead), ob);
+    float w[64];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        w[4 * i + 0] = e * vv[i].x;
+        w[4 * i + 1] = e * vv[i].y;
+        w[4 * i + 2] = e * vv[i].z;
+        w[4 * i + 3] = e * vv[i].w;
     }
+    const float2 o = warp_reduce_scatter64(w);
     float* pp = p.part + (static_cast<size_t>(h) * persistent_max_splits(p.T) + s) * (kHeadDim + 2);
-    pp[2 + lane] = oa;
-    pp[2 + lane + kHalfHead] = ob;
+    reinterpret_cast<float2*>(pp + 2)[lane] = o;
     if (lane == 0) {
         pp[0] = m;
         pp[1] = l;
@@ -428,7 +435,7 @@ __device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int 
 }
 
 __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint64_t* full, uint64_t* empty,
-                          float* red, unsigned long long* best_s, float* qbuf) {
+                          float* red, unsigned long long* best_s, float* qbuf, float* wsm, int* s_ok) {
     DevState* st = p.st;
     const int t = threadIdx.x - 32;
     const int warp = t >> 5, lane = t & 31;
@@ -442,7 +449,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
     bool ok = true;
     const int last = 5 * p.layers;
     for (int ph = 0; ph <= last; ++ph) {
-        if (ph > 0 && !wait_phase(p, ph - 1)) return;
+        if (ph > 0 && !wait_phase(p, ph - 1, s_ok)) return;
         if (t == 0) trace_at(p, ph, kTrConsStart);
         const int kind = phase_kind(ph, p.layers);
         const LayerPtrs* y = ph < last ? &p.layer[ph / 5] : nullptr;
@@ -465,7 +472,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 stage_norm(p.x, y->g1, p.H, xs, red, nullptr);
             }
         } else if (kind == kWo) {
-            stage_attn_combine(p, nsplit, xs);
+            stage_attn_combine(p, nsplit, xs, wsm);
         } else if (kind == kW13) {
             stage_norm(p.x, y->g2, p.H, xs, red, nullptr);
         } else if (kind == kW2) {
@@ -477,41 +484,52 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
         if (t == 0) trace_at(p, ph, kTrConsStaged);
         int g0, g1;
         my_groups(d.M, g0, g1);
-        const int nkt = (d.K + kTileK - 1) / kTileK;
+        const int nkt = (d.K + kPersistTileK - 1) / kPersistTileK;
         const float4* x4 = reinterpret_cast<const float4*>(xs);
+        const int ra = 2 * warp, rb = ra + 1;
         for (int g = g0; g < g1; ++g) {
-            const int rows = min(kTileRows, d.M - g * kTileRows);
-            const int ra = 2 * warp, rb = 2 * warp + 1;
+            const int rows = min(kPersistTileRows, d.M - g * kPersistTileRows);
             const bool va = ra < rows, vb = rb < rows;
+            const int Ra = g * kPersistTileRows + ra, Rb = Ra + 1;
+            // Epilogue operands, loaded now so that their latency overlaps the tiles.
+            float ea = 0.0f, eb = 0.0f;  // bias, or the repetition flag in the LM head
+            float xa = 0.0f, xb = 0.0f;  // residual stream
+            if (kind == kLM) {
+                if (va) ea = p.rep_flags[Ra] ? 1.0f : 0.0f;
+                if (vb) eb = p.rep_flags[Rb] ? 1.0f : 0.0f;
+            } else {
+                if (va) ea = d.bias[Ra];
+                if (vb) eb = d.bias[Rb];
+                if (kind == kWo || kind == kW2) {
+                    if (va) xa = __ldcg(p.x + Ra);
+                    if (vb) xb = __ldcg(p.x + Rb);
+                }
+            }
             float acc_a = 0.0f, acc_b = 0.0f;
             for (int kt = 0; kt < nkt; ++kt) {
                 // After a failed wait this warp only walks the schedule so that it
                 // meets the other consumer warps at every named barrier.
                 if (ok && !wait_parity(&full[slot], par, st)) ok = false;
-                if (!ok) {
-                    if (++slot == kSlots) {
-                        slot = 0;
-                        par ^= 1u;
-                    }
-                    continue;
-                }
-                const int k0 = kt * kTileK;
-                const int kc4 = min(kTileK, d.K - k0) >> 2;
-                const float4* tile = reinterpret_cast<const float4*>(ring + static_cast<size_t>(slot) * kSlotBytes);
-                const float4* wa = tile + ra * (kTileK / 4);
-                const float4* wb = tile + rb * (kTileK / 4);
-                const float4* xk = x4 + (k0 >> 2);
+                if (ok) {
+                    const int k0 = kt * kPersistTileK;
+                    const int kc4 = min(kPersistTileK, d.K - k0) >> 2;
+                    const float4* tile =
+                        reinterpret_cast<const float4*>(ring + static_cast<size_t>(slot) * kSlotBytes);
+                    const float4* wa = tile + ra * (kPersistTileK / 4);
+                    const float4* wb = tile + rb * (kPersistTileK / 4);
+                    const float4* xk = x4 + (k0 >> 2);
 #pragma unroll
-                for (int j0 = 0; j0 < kTileK / 4; j0 += 32) {
-                    const int j = j0 + lane;
-                    if (j < kc4) {
-                        const float4 xv = xk[j];
-                        if (va) acc_a = dot4(wa[j], xv, acc_a);
-                        if (vb) acc_b = dot4(wb[j], xv, acc_b);
+                    for (int j0 = 0; j0 < kPersistTileK / 4; j0 += 32) {
+                        const int j = j0 + lane;
+                        if (j < kc4) {
+                            const float4 xv = xk[j];
+                            acc_a = dot4(wa[j], xv, acc_a);
+                            acc_b = dot4(wb[j], xv, acc_b);
+                        }
                     }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[slot]);
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[slot]);
                 if (++slot == kSlots) {
                     slot = 0;
                     par ^= 1u;
@@ -519,30 +537,29 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
             }
             acc_a = warp_sum(acc_a);
             acc_b = warp_sum(acc_b);
-            const int Ra = g * kTileRows + ra, Rb = Ra + 1;
             switch (kind) {
                 case kQKV:
-                    if (lane == 0 && va) p.qkv[Ra] = acc_a + d.bias[Ra];
-                    if (lane == 1 && vb) p.qkv[Rb] = acc_b + d.bias[Rb];
+                    if (lane == 0 && va) p.qkv[Ra] = acc_a + ea;
+                    if (lane == 1 && vb) p.qkv[Rb] = acc_b + eb;
                     break;
                 case kWo:
                 case kW2:
-                    if (lane == 0 && va) p.x[Ra] = __ldcg(p.x + Ra) + (acc_a + d.bias[Ra]);
-                    if (lane == 1 && vb) p.x[Rb] = __ldcg(p.x + Rb) + (acc_b + d.bias[Rb]);
+                    if (lane == 0 && va) p.x[Ra] = xa + (acc_a + ea);
+                    if (lane == 1 && vb) p.x[Rb] = xb + (acc_b + eb);
                     break;
                 case kW13:
-                    if (lane == 0 && vb) p.ffh[Ra >> 1] = silu(acc_a + d.bias[Ra]) * (acc_b + d.bias[Rb]);
+                    if (lane == 0 && vb) p.ffh[Ra >> 1] = silu(acc_a + ea) * (acc_b + eb);
                     break;
                 default: {  // kLM: logits with the repetition penalty, running argmax
                     if (va) {
                         float v = acc_a;
-                        if (p.rep_flags[Ra]) v = rep_penalty(v, rp);
+                        if (ea != 0.0f) v = rep_penalty(v, rp);
                         if (lane == 0) p.logits[Ra] = v;
                         if (v > best_v) best_v = v, best_i = Ra;
                     }
                     if (vb) {
                         float v = acc_b;
-                        if (p.rep_flags[Rb]) v = rep_penalty(v, rp);
+                        if (eb != 0.0f) v = rep_penalty(v, rp);
                         if (lane == 1) p.logits[Rb] = v;
                         if (v > best_v) best_v = v, best_i = Rb;
                     }
@@ -577,9 +594,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     float* xs = reinterpret_cast<float*>(smem + static_cast<size_t>(kSlots) * kSlotBytes);
     uint64_t* full = reinterpret_cast<uint64_t*>(xs + kMaxK);
     uint64_t* empty = full + kSlots;
-    float* red = reinterpret_cast<float*>(empty + kSlots);
-    unsigned long long* best_s = reinterpret_cast<unsigned long long*>(red + 16);
-    float* qbuf = reinterpret_cast<float*>(best_s + kConsumerWarps + 8);
+    float* red = reinterpret_cast<float*>(empty + kSlots);                  // 16 floats
+    unsigned long long* best_s = reinterpret_cast<unsigned long long*>(red + 16);  // 8
+    int* s_ok = reinterpret_cast<int*>(best_s + kConsumerWarps);            // 1 (+pad)
+    float* qbuf = reinterpret_cast<float*>(smem + static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 +
+                                           2 * kSlots * 8 + 512);           // 8 x 64
+    float* wsm = qbuf + kConsumerWarps * kHeadDim;                          // kCombineFloats
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
@@ -594,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) producer(p, ring, full, empty);
     } else {
-        consumers(p, ring, xs, full, empty, red, best_s, qbuf);
+        consumers(p, ring, xs, full, empty, red, best_s, qbuf, wsm, s_ok);
     }
 }
 
@@ -604,6 +624,7 @@ size_t persistent_smem_bytes() { return kSmemBytes; }
 
 cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cudaStream_t s) {
     if (p.H > kMaxK || p.Hl > kMaxK || p.Fl > kMaxK || p.H % 4 || p.Hl % 4 || p.Fl % 4) return cudaErrorInvalidValue;
+    if (2 * (p.Hl >> 6) * persistent_max_splits(p.T) > kCombineFloats) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;

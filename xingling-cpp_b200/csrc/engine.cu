@@ -433,7 +433,12 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     for (int l = 0; l < cfg_.layers; ++l) {
         const LayerWeights& L = layers_[l];
         p.layer[l] = LayerPtrs{L.wqkv, L.bqkv, L.wo, L.bo, L.w13, L.b13, L.w2, L.b2, L.g1, L.g2, L.kc, L.vc};
+        XL_CUDA(make_stream_map(&p.maps[4 * l + 0], L.wqkv, 3 * Hl_, H_));
+        XL_CUDA(make_stream_map(&p.maps[4 * l + 1], L.wo, H_, Hl_));
+        XL_CUDA(make_stream_map(&p.maps[4 * l + 2], L.w13, 2 * Fl_, H_));
+        XL_CUDA(make_stream_map(&p.maps[4 * l + 3], L.w2, H_, Fl_));
     }
+    XL_CUDA(make_stream_map(&p.maps[kPersistMaps - 1], emb_, V_, H_));
     p.layers = cfg_.layers;
     p.emb = emb_;
     p.gnorm = gnorm_;

@@ -79,7 +79,10 @@ cudaError_t launch_attn_decode(const AttnDecodeParams& p, bool pdl, cudaStream_t
 
 // Persistent decode step (decode_persistent.cu): one cooperative launch per token.
 constexpr int kMaxLayers = 32;
-constexpr int kPersistChunk = 32;  // attention positions per warp item
+constexpr int kPersistChunk = 32;     // attention positions per warp item
+constexpr int kPersistTileRows = 16;  // weight tile streamed per TMA load: 16 rows x 256 floats
+constexpr int kPersistTileK = 256;
+constexpr int kPersistMaps = 4 * kMaxLayers + 1;  // QKV, Wo, W1/V, W2 per layer, then the LM head
 __host__ __device__ inline int persistent_max_splits(int max_ctx) {
     return (max_ctx + kPersistChunk - 1) / kPersistChunk;
 }
@@ -88,6 +91,7 @@ struct LayerPtrs {
     float *kc, *vc;
 };
 struct PersistentParams {
+    CUtensorMap maps[kPersistMaps];  // [16 rows][256 floats] box maps of every streamed matrix
     LayerPtrs layer[kMaxLayers];
     int layers;
     const float* emb;       // [V][H] tied embedding / LM head
@@ -106,6 +110,8 @@ struct PersistentParams {
 };
 constexpr int kTraceFields = 5;
 size_t persistent_smem_bytes();
+// The [16 rows][256 floats] TMA box map (no swizzle) of a row-major [rows][cols] weight.
+cudaError_t make_stream_map(CUtensorMap* map, const float* base, int rows, int cols);
 cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cudaStream_t s);
 
 struct SampleParams {
