@@ -136,6 +136,8 @@ XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, fl
  *                    and phase: consumer start (after the grid-wide wait),
  *                    input staged, phase done, producer first and last issue;
  *                    read with xl_engine_phase_trace (a profiling aid);
+ *   "prefetch_units" n  L2 prefetch distance of the persistent kernel's
+ *                    weight stream, in 16-row groups (0 = none);
  *   "prefill_gemm" 0  prefill projections on tcgen05 with the 3xTF32 split
  *                     (default); 1  fp32 FMA tiles.
  * Changing an option re-captures the decode graph. */

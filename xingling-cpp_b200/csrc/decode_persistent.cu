@@ -46,7 +46,6 @@ constexpr size_t kSmemBytes = static_cast<size_t>(kSlots) * kSlotBytes + kMaxK *
 constexpr uint32_t kMbarSpinLimit = 1u << 24;
 constexpr uint32_t kFlagSpinLimit = 1u << 24;
 constexpr int kErrMbar = 1, kErrFlag = 2;
-constexpr int kPrefetchUnits = 4;
 constexpr uint32_t kPrefetchPiece = 32768;
 
 static_assert(kPersistTileRows == 2 * kConsumerWarps, "each consumer warp owns two rows of a tile");
@@ -163,7 +162,8 @@ __device__ __forceinline__ void my_groups(int M, int& g0, int& g1) {
 
 // ---------------------------------------------------------------------------
 // Producer.  A unit is one 16-row group of one GEMV phase; its rows are
-// contiguous in HBM, which the L2 prefetch cursor uses.
+// contiguous in HBM, which the L2 prefetch cursor (p.prefetch_units units
+// ahead of the ring copies, 0 = off) uses.
 struct Unit {
     int ph, g, g0, g1;
 };
@@ -205,12 +205,12 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
     Unit cu, pu;
     bool have = unit_first(p, 0, cu);
     bool pf = unit_first(p, 0, pu);
-    for (int i = 0; i < kPrefetchUnits && pf; ++i) {
+    for (int i = 0; i < p.prefetch_units && pf; ++i) {
         prefetch_unit(p, pu);
         pf = unit_next(p, pu);
     }
     for (; have && ok; have = unit_next(p, cu)) {
-        if (pf) {
+        if (pf && p.prefetch_units > 0) {
             prefetch_unit(p, pu);
             pf = unit_next(p, pu);
         }

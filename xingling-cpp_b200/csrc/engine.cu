@@ -452,6 +452,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     p.st = st_;
     p.done = done_;
     p.trace = trace_;
+    p.prefetch_units = prefetch_units_;
     p.H = H_;
     p.Hl = Hl_;
     p.heads = heads_l_;
@@ -817,6 +818,14 @@ int Engine::set_option(const char* key, int value) {
         }
         prefill_gemm_ = value;
         return XL_OK;
+    }
+    if (k == "prefetch_units") {
+        if (value < 0 || value > 64) {
+            set_error("prefetch_units must be in [0, 64]");
+            return XL_ERR_ARG;
+        }
+        prefetch_units_ = value;
+        return loaded_ ? capture_decode_graph() : XL_OK;
     }
     if (k == "phase_trace") {
         if (value && !trace_) {

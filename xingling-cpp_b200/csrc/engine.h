@@ -116,6 +116,7 @@ class Engine {
 
     int decode_path_ = 0;      // 0: persistent kernel (single GPU), 1: per-op kernels
     int prefill_gemm_ = 0;     // 0: tcgen05 3xTF32, 1: fp32 SIMT tiles
+    int prefetch_units_ = 4;   // persistent decode: L2 prefetch distance in 16-row groups
     bool loaded_ = false;
     bool has_seq_ = false;
     int n_ = 0;

@@ -106,6 +106,7 @@ struct PersistentParams {
     DevState* st;
     int* done;              // [5*layers + 1] phase counters, zeroed before each launch
     unsigned long long* trace;  // optional [grid][5*layers + 1][kTraceFields] timestamps (ns), or nullptr
+    int prefetch_units;         // L2 prefetch distance of the weight stream in 16-row groups (0 = off)
     int H, Hl, heads, Fl, V, T;
 };
 constexpr int kTraceFields = 5;
