@@ -184,6 +184,23 @@ XL_API size_t xl_op_attn_decode_workspace_bytes(int heads, int max_ctx);
 XL_API int xl_op_attn_decode(const float* qkv, const float* rope, float* kc, float* vc, float* out, const int* pos,
                              int heads, int max_ctx, void* workspace, void* stream);
 
+/* xl_op_attn_decode for callers that cannot allocate device memory.  No
+ * counterpart in the reference.  Some hosts cannot call cudaMalloc on the
+ * decode path: an embedder whose device memory is owned by a pool it must not
+ * bypass, or a latency-critical caller for whom a cudaMalloc (which may
+ * synchronize the device) is not acceptable.  This entry point needs no
+ * workspace: its split-K scratch is a static device array of about 132 KB
+ * inside the library, which every GPU that loads the library holds until the
+ * process exits.  Limits: heads <= 32, max_ctx <= 1024; larger sizes return
+ * XL_ERR_ARG (use xl_op_attn_decode with a workspace).  It allocates nothing
+ * and calls no allocating routine.  The first call on each device looks up
+ * the array's device address with that device current; make that first call
+ * before any stream capture.  All calls share the one array: calls that
+ * overlap on the GPU (other streams, other threads) race on it, so order them
+ * on one stream.  Same arguments and results as xl_op_attn_decode. */
+XL_API int xl_op_attn_decode_noalloc(const float* qkv, const float* rope, float* kc, float* vc, float* out,
+                                     const int* pos, int heads, int max_ctx, void* stream);
+
 /* Embedding::inverse (src/embedding.cu:173-205) fused with the final RMSNorm
  * (gamma may be NULL) and the repetition penalty of sample_cpu
  * (src/inference.cu:71-74): logits[v] = E[v].x, penalised where

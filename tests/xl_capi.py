@@ -15,6 +15,7 @@ _SIGS = {
     "xl_rope_table": ([F, I, VP], I),
     "xl_op_attn_decode_workspace_bytes": ([I, I], SZ),
     "xl_op_attn_decode": ([VP, VP, VP, VP, VP, VP, I, I, VP, VP], I),
+    "xl_op_attn_decode_noalloc": ([VP, VP, VP, VP, VP, VP, I, I, VP], I),
     "xl_op_lm_head_workspace_bytes": ([], SZ),
     "xl_op_lm_head": ([VP, VP, VP, VP, VP, F, I, I, C.POINTER(C.c_int), VP, VP], I),
     "xl_op_sample_workspace_bytes": ([I], SZ),

@@ -15,7 +15,11 @@
 //                     (src/inference.cu:58-114).
 #include <math.h>
 
+#include <mutex>
+#include <string>
+
 #include "xl_device.cuh"
+#include "xl_engine.h"
 #include "xl_kernels.h"
 
 namespace xl {
@@ -555,4 +559,85 @@ cudaError_t launch_sample(const SampleParams& p, bool pdl, cudaStream_t s) {
     return launch_ex(sample_kernel, dim3(1), dim3(kSampThreads), 0, pdl, s, p);
 }
 
+void set_error(const std::string& msg);
+
+// ---------------------------------------------------------------------------
+// Decode attention without a caller workspace.
+//
+// The split-K partials and the per-head split counters live in this
+// file-scope device array instead of caller memory.  Every GPU that loads the
+// library holds the array until the process exits.  Its device address is
+// looked up once per device (cudaGetSymbolAddress with that device current)
+// by the first call on that device; in host code the symbol itself is only a
+// host-side stand-in and is never passed to a kernel.
+namespace {
+constexpr int kStaticMaxHeads = 32;
+constexpr int kStaticMaxCtx = 1024;
+constexpr size_t kStaticPartBytes =
+    static_cast<size_t>(kStaticMaxHeads) * ((kStaticMaxCtx + kAttnChunk - 1) / kAttnChunk) * (kHeadDim + 2) * 4;
+constexpr size_t kStaticScratchBytes = kStaticPartBytes + kStaticMaxHeads * 4;  // partials, then counters
+static __device__ __align__(256) unsigned char g_attn_scratch[kStaticScratchBytes];
+constexpr int kMaxDevices = 64;
+void* g_scratch_addr[kMaxDevices] = {};
+std::mutex g_scratch_mu;
+}  // namespace
+
 }  // namespace xl
+
+extern "C" XL_API int xl_op_attn_decode_noalloc(const float* qkv, const float* rope, float* kc, float* vc, float* out,
+                                                const int* pos, int heads, int max_ctx, void* stream) {
+    if (!qkv || !rope || !kc || !vc || !out || !pos || heads <= 0 || max_ctx <= 0) {
+        xl::set_error("xl_op_attn_decode_noalloc: bad arguments");
+        return XL_ERR_ARG;
+    }
+    if (heads > xl::kStaticMaxHeads || max_ctx > xl::kStaticMaxCtx) {
+        xl::set_error("xl_op_attn_decode_noalloc: heads must be <= 32 and max_ctx <= 1024 (the static scratch limit); "
+                      "use xl_op_attn_decode with a workspace for larger sizes");
+        return XL_ERR_ARG;
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= xl::kMaxDevices) {
+        xl::set_error(std::string("xl_op_attn_decode_noalloc: no usable current device: ") + cudaGetErrorString(e));
+        return XL_ERR_CUDA;
+    }
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(xl::g_scratch_mu);
+        if (!xl::g_scratch_addr[dev]) {
+            e = cudaGetSymbolAddress(&xl::g_scratch_addr[dev], xl::g_attn_scratch);
+            if (e != cudaSuccess) {
+                xl::g_scratch_addr[dev] = nullptr;
+                xl::set_error(std::string("xl_op_attn_decode_noalloc: cudaGetSymbolAddress failed: ") +
+                              cudaGetErrorString(e));
+                return XL_ERR_CUDA;
+            }
+        }
+        base = xl::g_scratch_addr[dev];
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // The counters must start at zero; the partials need no clearing.
+    int* counters = reinterpret_cast<int*>(static_cast<unsigned char*>(base) + xl::kStaticPartBytes);
+    e = cudaMemsetAsync(counters, 0, sizeof(int) * heads, s);
+    if (e != cudaSuccess) {
+        xl::set_error(std::string("xl_op_attn_decode_noalloc: clearing the counters failed: ") + cudaGetErrorString(e));
+        return XL_ERR_CUDA;
+    }
+    xl::AttnDecodeParams a{};
+    a.qkv = qkv;
+    a.rope = reinterpret_cast<const float2*>(rope);
+    a.kc = kc;
+    a.vc = vc;
+    a.out = out;
+    a.part = static_cast<float*>(base);  // laid out for max_ctx up to kStaticMaxCtx
+    a.counters = counters;
+    a.pos = pos;
+    a.heads = heads;
+    a.max_ctx = max_ctx;
+    e = xl::launch_attn_decode(a, false, s);
+    if (e != cudaSuccess) {
+        xl::set_error(std::string("xl_op_attn_decode_noalloc: ") + cudaGetErrorString(e));
+        return XL_ERR_CUDA;
+    }
+    return XL_OK;
+}
