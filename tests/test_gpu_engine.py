@@ -6,8 +6,10 @@ Bar (see the module docstring of xl_synth for the workload):
 * greedy tokens identical except where the oracle's top-2 gap is below that;
 * KV cache within 1e-5 abs of the oracle's; V rows bit-exact is not required
   (they come out of a GEMV), the KV position counter is exact;
-* sampled steps teacher-forced: the oracle's token history is fed to both and
-  the chosen ids must agree wherever the decision is not within tolerance.
+* sampled steps teacher-forced: the oracle's token history is fed to both; the
+  device sampler must reproduce sample_cpu exactly on the engine's logits, and
+  any id that differs from the oracle's is explained by the measured logit
+  difference moving r * total across a cumulative-probability boundary.
 """
 import numpy as np
 import pytest
@@ -131,14 +133,41 @@ def test_tiny_context_limit_and_errors(eng_mod, tiny_weights, path):
         eng_mod.InferenceEngine("cpu")
 
 
+def divergence_explained(ref_pen, got, T, P, r, tok) -> bool:
+    """True when the engine's id is what sample_cpu could pick from the oracle's
+    logits moved by at most the measured logit difference: r * total lies within
+    eps of the engine id's cumulative-probability interval in the oracle's
+    candidate order.  The sums are formed as sample_cpu forms them (fp32,
+    sequential, src/inference.cu:87-111); eps is the largest shift the measured
+    logit difference can cause in a cumulative sum (2 * delta / (T + 0.001))
+    plus the fp32 rounding of ~1000 sequential additions."""
+    delta = float(np.abs(got - ref_pen).max())
+    order = np.lexsort((np.arange(ref_pen.size), -ref_pen))[:1024]
+    v = ref_pen[order].astype(np.float32) / np.float32(T + 0.001)
+    e = np.exp(v - v[0]).astype(np.float32)
+    p = (e / np.cumsum(e, dtype=np.float32)[-1]).astype(np.float32)
+    c = np.cumsum(p, dtype=np.float32)
+    total = c[min(int(np.searchsorted(c, np.float32(P))), c.size - 1)]
+    target = r * float(total)
+    hit = np.nonzero(order == tok)[0]
+    if hit.size == 0:
+        return False
+    k = int(hit[0])
+    eps = 2.0 * delta / (T + 0.001) + 1.5e-4
+    lo = float(c[k - 1]) if k > 0 else 0.0
+    return lo - eps <= target <= float(c[k]) + eps
+
+
 def run_sampled(eng, port, ids, steps, T, P, RP, u, check_every=1):
-    """Teacher-forced sampled decode.  Every checked step: the engine's logits
-    (which carry the penalty of the ids the engine sampled) are within the
-    tolerance of the oracle's; the engine's id equals the oracle sampler run on
-    the engine's own logits with the same uniform (the device sampler is exact
-    given its logits).  Where the engine's id differs from the oracle's, the
-    difference comes only from logits within tolerance moving r * total across
-    a cumulative-probability boundary; such steps are counted and returned."""
+    """Teacher-forced sampled decode (the oracle's ids are fed back to both).
+    Every checked step: the engine's logits, which carry the penalty of the ids
+    the engine itself sampled, are within tolerance of the oracle's logits with
+    that same penalty set; and every step the engine's id equals the oracle
+    sampler run on the engine's own logits with the same uniform (the device
+    sampler is exact).  Where the engine's id differs from the oracle's pick for
+    the same history, the difference must be explained by the measured logit
+    difference (divergence_explained).  Returns the last id and the number of
+    explained divergences."""
     rep_ref: list[int] = []
     rep_eng: list[int] = []
     tok = eng.next_token(ids, temperature=T, top_p=P, repetition_penalty=RP)
@@ -146,11 +175,16 @@ def run_sampled(eng, port, ids, steps, T, P, RP, u, check_every=1):
     diverged = 0
     for step in range(steps):
         got = logits_of(eng)
+        ref_pen = O.apply_penalty(ref, rep_eng, RP)
         if step % check_every == 0 or step == steps - 1:
-            assert_logits_close(got, O.apply_penalty(ref, rep_eng, RP))
-        assert tok == O.sample(got, T, P, 1.0, [], float(u[step])), f"step {step}: device sampler"
-        tok_ref = O.sample(ref, T, P, RP, rep_ref, float(u[step]))
-        diverged += tok != tok_ref
+            assert_logits_close(got, ref_pen)
+        r = float(u[step])
+        assert tok == O.sample(got, T, P, 1.0, [], r), f"step {step}: device sampler"
+        tok_same_history = O.sample(ref, T, P, RP, rep_eng, r)
+        if tok != tok_same_history:
+            diverged += 1
+            assert divergence_explained(ref_pen, got, T, P, r, tok), f"step {step}: {tok} vs {tok_same_history}"
+        tok_ref = O.sample(ref, T, P, RP, rep_ref, r)
         rep_ref.append(tok_ref)
         rep_eng.append(tok)
         tok = eng.next_token(tok_ref, temperature=T, top_p=P, repetition_penalty=RP)  # teacher-forced
@@ -167,8 +201,7 @@ def test_tiny_sampled_teacher_forced(eng_mod, tiny_weights, path):
     port.load(tiny_weights)
     u = S.philox_uniforms(3, 40)
     eng.set_uniforms([float(x) for x in u])
-    _, diverged = run_sampled(eng, port, S.prompt_ids(2, 50, sh.vocab), 30, 0.7, 0.9, 1.1, u)
-    assert diverged <= 3
+    run_sampled(eng, port, S.prompt_ids(2, 50, sh.vocab), 30, 0.7, 0.9, 1.1, u)
 
 
 @PATHS
@@ -197,8 +230,7 @@ def test_full_long_context_sampled(eng_mod, full_weights, path):
     T, P, RP = 0.7, 0.9, 1.1
     u = S.philox_uniforms(3, 69)
     eng.set_uniforms([float(x) for x in u])
-    tok, diverged = run_sampled(eng, port, S.prompt_ids(2, 700, sh.vocab), 68, T, P, RP, u, check_every=4)
-    assert diverged <= 7  # at most ~10% of the steps, each explained by the logit tolerance
+    tok, _ = run_sampled(eng, port, S.prompt_ids(2, 700, sh.vocab), 68, T, P, RP, u, check_every=4)
     assert eng.ctx_len() == 768
     with pytest.raises(RuntimeError):
         eng.next_token(tok, temperature=T, top_p=P, repetition_penalty=RP)

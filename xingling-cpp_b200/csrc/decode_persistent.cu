@@ -40,9 +40,8 @@ constexpr int kThreads = kConsumerThreads + 32;
 constexpr int kSlotBytes = kPersistTileRows * kPersistTileK * 4;  // 16 KB
 constexpr int kSlots = 12;                                       // 192 KB ring
 constexpr int kMaxK = 4096;
-constexpr int kCombineFloats = 2048;  // (weight, sum) per (head, split): 24 heads x 24 splits at most
-constexpr size_t kSmemBytes = static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 + 2 * kSlots * 8 + 512 +
-                              kConsumerWarps * 64 * 4 + kCombineFloats * 4;
+constexpr size_t kSmemBytes =
+    static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 + 2 * kSlots * 8 + 512 + kConsumerWarps * 64 * 4;
 constexpr uint32_t kMbarSpinLimit = 1u << 24;
 constexpr uint32_t kFlagSpinLimit = 1u << 24;
 constexpr int kErrMbar = 1, kErrFlag = 2;
@@ -265,7 +264,6 @@ __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
                 break;
             }
         }
-        __threadfence();
         *s_ok = ok;
     }
     consumer_sync();
@@ -274,10 +272,7 @@ __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
 
 __device__ void signal_phase(const PersistentParams& p, int ph) {
     consumer_sync();
-    if (threadIdx.x == 32) {
-        __threadfence();
-        atomicAdd(p.done + ph, 1);
-    }
+    if (threadIdx.x == 32) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.done + ph) : "memory");
 }
 
 // Block-wide (consumers) sum of one float per thread.
@@ -326,38 +321,6 @@ __device__ void stage_copy(const float* src, int K, float* xs) {
         reinterpret_cast<float4*>(xs)[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
 }
 
-// Merge the split-K attention partials (m, l, o[64]) of every head into xs:
-// per-split weights exp(m_s - M) / L first (smem), then every output with its
-// loads all in flight.
-__device__ void stage_attn_combine(const PersistentParams& p, int nsplit, float* xs, float* wsm) {
-    const int t = threadIdx.x - 32;
-    const int maxs = persistent_max_splits(p.T);
-    const int heads = p.Hl >> 6;
-    for (int i = t; i < heads * nsplit; i += kConsumerThreads) {
-        const int h = i / nsplit, s = i % nsplit;
-        const float* ps = p.part + (static_cast<size_t>(h) * maxs + s) * (kHeadDim + 2);
-        wsm[2 * i] = __ldcg(ps);
-        wsm[2 * i + 1] = __ldcg(ps + 1);
-    }
-    consumer_sync();
-    for (int h = t; h < heads; h += kConsumerThreads) {
-        float M = -INFINITY;
-        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, wsm[2 * (h * nsplit + s)]);
-        float L = 0.0f;
-        for (int s = 0; s < nsplit; ++s) L = fmaf(wsm[2 * (h * nsplit + s) + 1], expf(wsm[2 * (h * nsplit + s)] - M), L);
-        for (int s = 0; s < nsplit; ++s) wsm[2 * (h * nsplit + s)] = expf(wsm[2 * (h * nsplit + s)] - M) / L;
-    }
-    consumer_sync();
-    for (int i = t; i < p.Hl; i += kConsumerThreads) {
-        const int h = i >> 6, d = i & 63;
-        float o = 0.0f;
-        for (int s = 0; s < nsplit; ++s)
-            o = fmaf(__ldcg(p.part + (static_cast<size_t>(h) * maxs + s) * (kHeadDim + 2) + 2 + d),
-                     wsm[2 * (h * nsplit + s)], o);
-        xs[i] = o;
-    }
-}
-
 // Butterfly reduce-scatter of a 64-float vector held by every lane: afterwards
 // lane l holds the warp-wide sums of elements 2l and 2l+1.
 __device__ __forceinline__ float2 warp_reduce_scatter64(float (&v)[64]) {
@@ -377,9 +340,12 @@ __device__ __forceinline__ float2 warp_reduce_scatter64(float (&v)[64]) {
 
 // One (head, 32-position chunk) of the decode attention on one warp, lane j
 // owning position t0 + j: RoPE at position n (src/rope.cu:20-45), KV append
-// when the chunk holds n, scores, softmax and P.V; writes the (max, sum, o)
-// partial.  Each lane's K and V rows (32 x 16 B loads) are in flight together.
-__device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int h, int s, int n, float* qsh) {
+// when the chunk holds n, scores, softmax and P.V.  Each lane's K and V rows
+// (32 x 16 B loads) are in flight together.  With one chunk the warp writes the
+// head's output; otherwise it writes its (max, sum, o) partial and the last
+// chunk of the head to finish (a per-head ticket) merges the partials.
+__device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int layer, int h, int s, int nsplit, int n,
+                             float* qsh) {
     const int lane = threadIdx.x & 31;
     const int t0 = s * kPersistChunk;
     const int cnt = min(kPersistChunk, n + 1 - t0);
@@ -425,17 +391,46 @@ __device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int 
         w[4 * i + 3] = e * vv[i].w;
     }
     const float2 o = warp_reduce_scatter64(w);
-    float* pp = p.part + (static_cast<size_t>(h) * persistent_max_splits(p.T) + s) * (kHeadDim + 2);
+    float2* out = reinterpret_cast<float2*>(p.att + h * kHeadDim);
+    if (nsplit == 1) {
+        out[lane] = make_float2(o.x / l, o.y / l);
+        return;
+    }
+    const int maxs = persistent_max_splits(p.T);
+    float* base = p.part + static_cast<size_t>(h) * maxs * (kHeadDim + 2);
+    float* pp = base + s * (kHeadDim + 2);
     reinterpret_cast<float2*>(pp + 2)[lane] = o;
     if (lane == 0) {
         pp[0] = m;
         pp[1] = l;
     }
     __syncwarp();
+    int ticket = 0;
+    if (lane == 0) {
+        __threadfence();
+        ticket = atomicAdd(p.head_done + layer * p.heads + h, 1);
+    }
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (ticket != nsplit - 1) return;
+    __threadfence();
+    // Merge: lane s holds split s's (max, sum); every lane its two output dims.
+    const float ms = lane < nsplit ? __ldcg(base + lane * (kHeadDim + 2)) : -INFINITY;
+    const float ls = lane < nsplit ? __ldcg(base + lane * (kHeadDim + 2) + 1) : 0.0f;
+    const float M = warp_max(ms);
+    const float ws = lane < nsplit ? expf(ms - M) : 0.0f;
+    const float L = warp_sum(ls * ws);
+    float2 acc = make_float2(0.0f, 0.0f);
+    for (int k = 0; k < nsplit; ++k) {
+        const float wk = __shfl_sync(0xffffffffu, ws, k);
+        const float2 ok = __ldcg(reinterpret_cast<const float2*>(base + k * (kHeadDim + 2) + 2) + lane);
+        acc.x = fmaf(wk, ok.x, acc.x);
+        acc.y = fmaf(wk, ok.y, acc.y);
+    }
+    out[lane] = make_float2(acc.x / L, acc.y / L);
 }
 
 __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint64_t* full, uint64_t* empty,
-                          float* red, unsigned long long* best_s, float* qbuf, float* wsm, int* s_ok) {
+                          float* red, unsigned long long* best_s, float* qbuf, int* s_ok) {
     DevState* st = p.st;
     const int t = threadIdx.x - 32;
     const int warp = t >> 5, lane = t & 31;
@@ -456,7 +451,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
         if (kind == kAttn) {
             const int items = p.heads * nsplit;
             for (int it = blockIdx.x + gridDim.x * warp; it < items; it += gridDim.x * kConsumerWarps)
-                attend_chunk(p, *y, it / nsplit, it % nsplit, n, qbuf + warp * kHeadDim);
+                attend_chunk(p, *y, ph / 5, it / nsplit, it % nsplit, nsplit, n, qbuf + warp * kHeadDim);
             if (t == 0) trace_at(p, ph, kTrConsStaged);
             signal_phase(p, ph);
             if (t == 0) trace_at(p, ph, kTrConsEnd);
@@ -472,7 +467,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 stage_norm(p.x, y->g1, p.H, xs, red, nullptr);
             }
         } else if (kind == kWo) {
-            stage_attn_combine(p, nsplit, xs, wsm);
+            stage_copy(p.att, p.Hl, xs);
         } else if (kind == kW13) {
             stage_norm(p.x, y->g2, p.H, xs, red, nullptr);
         } else if (kind == kW2) {
@@ -599,7 +594,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     int* s_ok = reinterpret_cast<int*>(best_s + kConsumerWarps);            // 1 (+pad)
     float* qbuf = reinterpret_cast<float*>(smem + static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 +
                                            2 * kSlots * 8 + 512);           // 8 x 64
-    float* wsm = qbuf + kConsumerWarps * kHeadDim;                          // kCombineFloats
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
@@ -614,7 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) producer(p, ring, full, empty);
     } else {
-        consumers(p, ring, xs, full, empty, red, best_s, qbuf, wsm, s_ok);
+        consumers(p, ring, xs, full, empty, red, best_s, qbuf, s_ok);
     }
 }
 
@@ -624,7 +618,7 @@ size_t persistent_smem_bytes() { return kSmemBytes; }
 
 cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cudaStream_t s) {
     if (p.H > kMaxK || p.Hl > kMaxK || p.Fl > kMaxK || p.H % 4 || p.Hl % 4 || p.Fl % 4) return cudaErrorInvalidValue;
-    if (2 * (p.Hl >> 6) * persistent_max_splits(p.T) > kCombineFloats) return cudaErrorInvalidValue;
+    if (persistent_max_splits(p.T) > 32) return cudaErrorInvalidValue;  // one lane per split in the merge
     cudaError_t e = cudaFuncSetAttribute(decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;

@@ -217,7 +217,7 @@ int Engine::alloc_all() {
     add(&logits_, vl * 4);
     add(&attn_ws_, static_cast<size_t>(heads_l_) * maxs * (kHeadDim + 2) * 4);
     add(&attn_cnt_, heads_l_ * 4);
-    add(&done_, (5 * static_cast<size_t>(cfg_.layers) + 1) * 4);
+    add(&done_, (5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_) * 4);
     add(&rep_flags_, vl);
     add(&st_, sizeof(DevState));
     add(&px_, T * H * 4);
@@ -225,6 +225,8 @@ int Engine::alloc_all() {
     add(&pqkv_, T * 3 * Hl * 4);
     add(&patt_, T * H * 4);
     add(&pffh_, T * Fl * 4);
+    splitk_floats_ = static_cast<size_t>(16) << 20;  // 64 MB
+    add(&splitk_ws_, splitk_floats_ * 4);
     add(&pxn_lo_, T * H * 4);
     add(&patt_lo_, T * H * 4);
     add(&pffh_lo_, T * Fl * 4);
@@ -410,7 +412,7 @@ int Engine::prepare_prefill_operands() {
 int Engine::prefill_linear(int mode, const TcOperands& o, const float* x, const float* w, const float* b, float* y,
                            float* y_lo, int n, int m, int k, cudaStream_t s) {
     if (prefill_gemm_ == 0) {
-        XL_CUDA(launch_gemm_tc(mode, o, b, y, y_lo, n, m, k, &st_->err, s));
+        XL_CUDA(launch_gemm_tc(mode, o, b, y, y_lo, n, m, k, &st_->err, s, splitk_ws_, splitk_floats_, num_sms_));
     } else {
         XL_CUDA(launch_linear_prefill(mode, x, w, b, y, n, m, k, s));
         if (y_lo) XL_CUDA(launch_split_lo(y, y_lo, static_cast<size_t>(n) * (mode == kGemvSwiGLU ? m / 2 : m), s));
@@ -451,6 +453,8 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     p.rep_flags = rep_flags_;
     p.st = st_;
     p.done = done_;
+    p.head_done = done_ + 5 * cfg_.layers + 1;
+    p.att = att_;
     p.trace = trace_;
     p.prefetch_units = prefetch_units_;
     p.H = H_;
@@ -459,7 +463,9 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     p.Fl = Fl_;
     p.V = V_;
     p.T = T_;
-    XL_CUDA(cudaMemsetAsync(done_, 0, (5 * static_cast<size_t>(cfg_.layers) + 1) * sizeof(int), s));
+    XL_CUDA(cudaMemsetAsync(
+        done_, 0, (5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_) * sizeof(int),
+        s));
     XL_CUDA(launch_decode_persistent(p, num_sms_, s));
     lm_x_ = xa_;
     SampleParams sp{};

@@ -103,6 +103,8 @@ class Engine {
     // prefill buffers [T][...]
     float *px_ = nullptr, *pxn_ = nullptr, *pqkv_ = nullptr, *patt_ = nullptr, *pffh_ = nullptr;
     float *pxn_lo_ = nullptr, *patt_lo_ = nullptr, *pffh_lo_ = nullptr;
+    float* splitk_ws_ = nullptr;  // split-K partial sums of the prefill GEMMs
+    size_t splitk_floats_ = 0;
     int* pids_ = nullptr;
 
     // host
@@ -116,7 +118,7 @@ class Engine {
 
     int decode_path_ = 0;      // 0: persistent kernel (single GPU), 1: per-op kernels
     int prefill_gemm_ = 0;     // 0: tcgen05 3xTF32, 1: fp32 SIMT tiles
-    int prefetch_units_ = 4;   // persistent decode: L2 prefetch distance in 16-row groups
+    int prefetch_units_ = 0;   // persistent decode: L2 prefetch distance in 16-row groups (off: measured slower)
     bool loaded_ = false;
     bool has_seq_ = false;
     int n_ = 0;

@@ -41,6 +41,7 @@ constexpr int kStageBytes = 4 * kTileBytes;  // W, W_lo, X, X_lo
 constexpr int kGemmThreads = 192;
 constexpr size_t kGemmSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
 constexpr uint32_t kSpinLimit = 1u << 26;
+constexpr int kGemmPartial = 4;  // epilogue: raw slice accumulator into the split-K workspace
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -125,7 +126,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
-    const int nkb = K / kBK;
+    // split-K: this CTA's K-blocks [kb0, kb1) of blockIdx.z of gridDim.z slices
+    const int nkb_all = K / kBK;
+    const int kb0 = static_cast<int>(static_cast<long long>(blockIdx.z) * nkb_all / gridDim.z);
+    const int kb1 = static_cast<int>(static_cast<long long>(blockIdx.z + 1) * nkb_all / gridDim.z);
+    const int nkb = kb1 - kb0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -153,11 +158,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const uint32_t ph = static_cast<uint32_t>(kb / kStages) & 1u;
                 if (!wait_bar(&empty[s], ph ^ 1u, err)) break;
                 char* st = smem + s * kStageBytes;
+                const int kx = (kb0 + kb) * kBK;
                 mbar_expect_tx(&full[s], kStageBytes);
-                tma_load_2d(st, &tm_w, kb * kBK, m0, &full[s]);
-                tma_load_2d(st + kTileBytes, &tm_wlo, kb * kBK, m0, &full[s]);
-                tma_load_2d(st + 2 * kTileBytes, &tm_x, kb * kBK, n0, &full[s]);
-                tma_load_2d(st + 3 * kTileBytes, &tm_xlo, kb * kBK, n0, &full[s]);
+                tma_load_2d(st, &tm_w, kx, m0, &full[s]);
+                tma_load_2d(st + kTileBytes, &tm_wlo, kx, m0, &full[s]);
+                tma_load_2d(st + 2 * kTileBytes, &tm_x, kx, n0, &full[s]);
+                tma_load_2d(st + 3 * kTileBytes, &tm_xlo, kx, n0, &full[s]);
             }
         }
     } else if (warp == 1) {
@@ -186,7 +192,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int q = warp & 3;
         const int f = m0 + 32 * q + lane;
         const bool fok = f < M;
-        const float bf = (fok && bias) ? bias[f] : 0.0f;
+        const float bf = (fok && bias && MODE != kGemmPartial) ? bias[f] : 0.0f;
         if (wait_bar(accum, 0, err)) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll 1
@@ -208,7 +214,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int j = 0; j < 32; ++j) {
                     const int n = n0 + c0 + j;
                     const float v = __uint_as_float(r[j]) + bf;
-                    if (MODE == kGemvSwiGLU) {
+                    if (MODE == kGemmPartial) {
+                        // raw accumulator of this K slice: C is the workspace [slices][N][M]
+                        if (fok && n < N) C[(static_cast<size_t>(blockIdx.z) * N + n) * M + f] = v;
+                    } else if (MODE == kGemvSwiGLU) {
                         // features (2i, 2i+1) = (W1 row i, V row i) sit in adjacent lanes
                         const float partner = __shfl_xor_sync(0xffffffffu, v, 1);
                         if ((lane & 1) == 0 && fok && n < N) {
@@ -231,6 +240,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN) : "memory");
+    }
+}
+
+// Sum of the split-K slices in slice order, then the mode's epilogue.
+template <int MODE>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, int slices,
+                                                            const float* __restrict__ bias, float* __restrict__ C,
+                                                            float* __restrict__ C_lo, int N, int M) {
+    const size_t total = static_cast<size_t>(N) * (MODE == kGemvSwiGLU ? M / 2 : M);
+    const size_t plane = static_cast<size_t>(N) * M;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        if (MODE == kGemvSwiGLU) {
+            const size_t n = i / (M / 2), j = i % (M / 2);
+            const size_t ia = n * M + 2 * j;
+            float a = 0.0f, c = 0.0f;
+            for (int z = 0; z < slices; ++z) {
+                a += ws[z * plane + ia];
+                c += ws[z * plane + ia + 1];
+            }
+            const float h = silu(a + bias[2 * j]) * (c + bias[2 * j + 1]);
+            C[i] = h;
+            C_lo[i] = tf32_lo(h);
+        } else {
+            const int m = static_cast<int>(i % M);
+            float a = 0.0f;
+            for (int z = 0; z < slices; ++z) a += ws[z * plane + i];
+            const float v = a + (bias ? bias[m] : 0.0f);
+            if (MODE == kGemvResidual) C[i] += v;
+            else C[i] = v;
+        }
     }
 }
 
@@ -289,37 +329,60 @@ cudaError_t make_stream_map(CUtensorMap* map, const float* base, int rows, int c
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+template <int MODE>
+cudaError_t launch_tc(dim3 grid, const TcOperands& o, const float* bias, float* C, float* C_lo, int m, int n, int k,
+                      int* err, cudaStream_t s) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kGemmSmem));
+    if (e != cudaSuccess) return e;
+    gemm_tc_kernel<MODE><<<grid, kGemmThreads, kGemmSmem, s>>>(o.w, o.w_lo, o.x, o.x_lo, bias, C, C_lo, m, n, k, err);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_gemm_tc(int mode, const TcOperands& o, const float* bias, float* C, float* C_lo, int n, int m,
-                           int k, int* err, cudaStream_t s) {
+                           int k, int* err, cudaStream_t s, float* ws, size_t ws_floats, int num_sms) {
     if (n <= 0 || m <= 0 || k <= 0 || k % kBK || (mode == kGemvSwiGLU && (m % 2 || !C_lo))) return cudaErrorInvalidValue;
-    dim3 grid((m + kBM - 1) / kBM, (n + kBN - 1) / kBN);
+    const int tiles = ((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
+    const int nkb = k / kBK;
+    // K slices so that the grid covers the SMs, each slice keeping >= 4 K-blocks
+    int slices = 1;
+    if (ws && tiles < num_sms) {
+        slices = std::min(num_sms / tiles, std::max(1, nkb / 4));
+        const size_t plane = static_cast<size_t>(n) * m;
+        while (slices > 1 && static_cast<size_t>(slices) * plane > ws_floats) --slices;
+    }
+    dim3 grid((m + kBM - 1) / kBM, (n + kBN - 1) / kBN, slices);
     cudaError_t e;
+    if (slices > 1) {
+        e = launch_tc<kGemmPartial>(grid, o, nullptr, ws, nullptr, m, n, k, err, s);
+        if (e != cudaSuccess) return e;
+        const size_t total = static_cast<size_t>(n) * (mode == kGemvSwiGLU ? m / 2 : m);
+        const unsigned blocks = static_cast<unsigned>(std::min<size_t>((total + 255) / 256, 148 * 8));
+        switch (mode) {
+            case kGemvPlain:
+                splitk_reduce_kernel<kGemvPlain><<<blocks, 256, 0, s>>>(ws, slices, bias, C, C_lo, n, m);
+                break;
+            case kGemvSwiGLU:
+                splitk_reduce_kernel<kGemvSwiGLU><<<blocks, 256, 0, s>>>(ws, slices, bias, C, C_lo, n, m);
+                break;
+            case kGemvResidual:
+                splitk_reduce_kernel<kGemvResidual><<<blocks, 256, 0, s>>>(ws, slices, bias, C, C_lo, n, m);
+                break;
+            default:
+                return cudaErrorInvalidValue;
+        }
+        return cudaGetLastError();
+    }
     switch (mode) {
         case kGemvPlain:
-            e = cudaFuncSetAttribute(gemm_tc_kernel<kGemvPlain>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(kGemmSmem));
-            if (e != cudaSuccess) return e;
-            gemm_tc_kernel<kGemvPlain><<<grid, kGemmThreads, kGemmSmem, s>>>(o.w, o.w_lo, o.x, o.x_lo, bias, C, C_lo,
-                                                                            m, n, k, err);
-            break;
+            return launch_tc<kGemvPlain>(grid, o, bias, C, C_lo, m, n, k, err, s);
         case kGemvSwiGLU:
-            e = cudaFuncSetAttribute(gemm_tc_kernel<kGemvSwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(kGemmSmem));
-            if (e != cudaSuccess) return e;
-            gemm_tc_kernel<kGemvSwiGLU><<<grid, kGemmThreads, kGemmSmem, s>>>(o.w, o.w_lo, o.x, o.x_lo, bias, C, C_lo,
-                                                                             m, n, k, err);
-            break;
+            return launch_tc<kGemvSwiGLU>(grid, o, bias, C, C_lo, m, n, k, err, s);
         case kGemvResidual:
-            e = cudaFuncSetAttribute(gemm_tc_kernel<kGemvResidual>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(kGemmSmem));
-            if (e != cudaSuccess) return e;
-            gemm_tc_kernel<kGemvResidual><<<grid, kGemmThreads, kGemmSmem, s>>>(o.w, o.w_lo, o.x, o.x_lo, bias, C,
-                                                                               C_lo, m, n, k, err);
-            break;
+            return launch_tc<kGemvResidual>(grid, o, bias, C, C_lo, m, n, k, err, s);
         default:
             return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 cudaError_t launch_split_lo(const float* x, float* lo, size_t n, cudaStream_t s) {

@@ -199,8 +199,9 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
     float* Qt = smem;              // [64 dims][kAP] (q scaled by 1/8, transposed)
     float* Kt = Qt + kAT * kAP;    // [64 dims][kAP] (transposed)
     float* Vs = Kt + kAT * kAP;    // [64 keys][kAP]
-    float* Ps = Vs + kAT * kAP;    // [64 queries][kAP]
-    const int qt = blockIdx.x, h = blockIdx.y;
+    float* Pt = Vs + kAT * kAP;    // [64 keys][kAP] (probabilities, transposed)
+    // Causal work grows with the query tile: launch the longest tiles first.
+    const int qt = gridDim.x - 1 - blockIdx.x, h = blockIdx.y;
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int HL = heads * kHeadDim;
     const int q0 = qt * kAT;
@@ -224,12 +225,19 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
     for (int kt = 0; kt <= last_kt; ++kt) {
         const int k0 = kt * kAT;
         __syncthreads();
-        for (int e = tid; e < kAT * kHeadDim; e += 256) {
-            const int r = e >> 6, d = e & 63;
+        for (int e = tid; e < kAT * kHeadDim / 4; e += 256) {
+            const int r = e >> 4, d4 = (e & 15) * 4;
             const int t = k0 + r;
             const bool ok = t < N;
-            Kt[d * kAP + r] = ok ? kh[static_cast<size_t>(t) * kHeadDim + d] : 0.0f;
-            Vs[r * kAP + d] = ok ? vh[static_cast<size_t>(t) * kHeadDim + d] : 0.0f;
+            const float4 kv = ok ? *reinterpret_cast<const float4*>(kh + static_cast<size_t>(t) * kHeadDim + d4)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 vv = ok ? *reinterpret_cast<const float4*>(vh + static_cast<size_t>(t) * kHeadDim + d4)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            Kt[(d4 + 0) * kAP + r] = kv.x;
+            Kt[(d4 + 1) * kAP + r] = kv.y;
+            Kt[(d4 + 2) * kAP + r] = kv.z;
+            Kt[(d4 + 3) * kAP + r] = kv.w;
+            *reinterpret_cast<float4*>(&Vs[r * kAP + d4]) = vv;
         }
         __syncthreads();
         float s[4][4];
@@ -277,19 +285,21 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
             m_run[i] = m_new;
 #pragma unroll
             for (int j = 0; j < 4; ++j) o[i][j] *= scale;
-            *reinterpret_cast<float4*>(&Ps[(ty * 4 + i) * kAP + tx * 4]) = make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) Pt[(tx * 4 + j) * kAP + ty * 4 + i] = s[i][j];
         }
         __syncthreads();
 #pragma unroll 8
         for (int j = 0; j < kAT; ++j) {
             const float4 v = *reinterpret_cast<const float4*>(&Vs[j * kAP + tx * 4]);
+            const float4 pq = *reinterpret_cast<const float4*>(&Pt[j * kAP + ty * 4]);
+            const float pv[4] = {pq.x, pq.y, pq.z, pq.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const float pj = Ps[(ty * 4 + i) * kAP + j];
-                o[i][0] = fmaf(pj, v.x, o[i][0]);
-                o[i][1] = fmaf(pj, v.y, o[i][1]);
-                o[i][2] = fmaf(pj, v.z, o[i][2]);
-                o[i][3] = fmaf(pj, v.w, o[i][3]);
+                o[i][0] = fmaf(pv[i], v.x, o[i][0]);
+                o[i][1] = fmaf(pv[i], v.y, o[i][1]);
+                o[i][2] = fmaf(pv[i], v.z, o[i][2]);
+                o[i][3] = fmaf(pv[i], v.w, o[i][3]);
             }
         }
     }

@@ -100,11 +100,13 @@ struct PersistentParams {
     float* x;               // [H] residual stream
     float* qkv;             // [3*Hl]
     float* part;            // attention partials [heads][persistent_max_splits][66]
+    float* att;             // [Hl] attention output (merged per head)
+    int* head_done;         // [layers][heads] split tickets, zeroed before each launch
     float* ffh;             // [Fl] SwiGLU activations
     float* logits;          // [V]
     const uint8_t* rep_flags;
     DevState* st;
-    int* done;              // [5*layers + 1] phase counters, zeroed before each launch
+    int* done;              // [5*layers + 1] phase counters, zeroed before each launch (with head_done)
     unsigned long long* trace;  // optional [grid][5*layers + 1][kTraceFields] timestamps (ns), or nullptr
     int prefetch_units;         // L2 prefetch distance of the weight stream in 16-row groups (0 = off)
     int H, Hl, heads, Fl, V, T;
@@ -133,8 +135,11 @@ struct TcOperands {
 };
 cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int cols);
 // C[N][M] (+)= X[N][K] . W[M][K]^T + b with the 3xTF32 split; SwiGLU writes C and C_lo as [N][M/2].
+// With a workspace (ws, ws_floats) and fewer output tiles than SMs, K is split
+// into slices whose partial sums are added in slice order by a second kernel.
 cudaError_t launch_gemm_tc(int mode, const TcOperands& o, const float* bias, float* C, float* C_lo, int n, int m,
-                           int k, int* err, cudaStream_t s);
+                           int k, int* err, cudaStream_t s, float* ws = nullptr, size_t ws_floats = 0,
+                           int num_sms = 148);
 // lo[i] = x[i] - (x[i] with its 13 low mantissa bits cleared): the TF32 residual.
 cudaError_t launch_split_lo(const float* x, float* lo, size_t n, cudaStream_t s);
 size_t gemm_tc_smem_bytes();
