@@ -136,8 +136,10 @@ XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, fl
  *                    and phase: consumer start (after the grid-wide wait),
  *                    input staged, phase done, producer first and last issue;
  *                    read with xl_engine_phase_trace (a profiling aid);
- *   "prefetch_units" n  L2 prefetch distance of the persistent kernel's
- *                    weight stream, in 16-row groups (0 = none);
+ *   "tma_inflight" n  weight boxes (32 KB) each SM of the persistent kernel
+ *                    keeps requested but not landed, in [1, 6] (default 2):
+ *                    enough to keep HBM busy, few enough that other memory
+ *                    accesses do not queue behind the stream;
  *   "prefill_gemm" 0  prefill projections on tcgen05 with the 3xTF32 split
  *                     (default); 1  fp32 FMA tiles.
  * Changing an option re-captures the decode graph. */

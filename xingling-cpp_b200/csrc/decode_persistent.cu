@@ -1,19 +1,32 @@
 // Persistent decode-step kernel for sm_100a: one launch per token.
 //
 // One CTA per SM (cooperative launch, so every CTA is resident).  Warp 0 is a
-// producer: one lane streams every weight tile this CTA needs for the whole
+// producer: one lane streams every weight box this CTA needs for the whole
 // token (16 x [QKV, out-proj, W1/V, W2] and the tied LM head) from HBM into a
-// shared-memory ring with 2D TMA tile loads (cp.async.bulk.tensor, one 16 KB
-// [16 rows][256 floats] box per instruction), gated only by free ring slots,
-// and keeps an L2 bulk-prefetch cursor a few row groups ahead.  Warps 1..8
-// consume: per phase they wait for the previous phase of every CTA (a global
-// counter), stage the phase's input vector in shared memory (embedding
-// gather, residual stream, RMSNorm, attention combine or SwiGLU input), take
-// ring tiles (two rows per warp), reduce with warp shuffles and apply the
-// epilogue, whose operands (bias, residual, repetition flags) are loaded
-// before the unit's tiles so their latency overlaps the stream.  Because the
-// producer never waits on activations, HBM keeps streaming across phase
-// boundaries.
+// shared-memory ring with 3D TMA loads (cp.async.bulk.tensor, one 32 KB
+// [16 rows][512 floats] box per instruction: a single SM sustains ~70 GB/s
+// with 16 KB boxes and ~90 GB/s with 32 KB ones), gated by free ring slots and
+// by a cap on boxes in flight (requested, not landed), so HBM keeps streaming
+// across phase boundaries without queueing more requests than it needs to
+// stay busy.  Warps 1..8 consume: per phase they wait for the previous phase
+// of every CTA (a global counter), stage the phase's input vector in shared
+// memory, take ring boxes (two rows per warp) and reduce with warp shuffles.
+//
+// Work split.  QKV, W1/V and the LM head go to the CTAs in whole 16-row
+// groups (bias / SwiGLU / penalty epilogues in place).  The out-projection and
+// W2 (1536 rows = 96 groups, fewer than the 148 SMs) are split evenly by
+// boxes instead; each CTA writes the partial row sums of the groups it
+// touches, and the next RMSNorm staging, which reads the residual stream
+// anyway, adds x + bias + the partials in CTA order (deterministic).  The
+// residual stream ping-pongs between xa (entering a layer) and xb (after the
+// out-projection); each CTA stores one slice of it.
+//
+// Attention.  Head h runs on one CTA (three at most, at 768 positions); its
+// warps take one 32-position chunk each.  Each warp prefetches its chunk's
+// cached K/V rows into L2 (two bulk prefetches) before the wait for the QKV
+// phase, so their HBM latency overlaps the grid barrier; the chunks merge in
+// shared memory, and only a head split over several CTAs merges through
+// global memory (ticket).
 //
 // Replaces, for one decode token, the reference's Transformer::forward(int)
 // (src/transformer.cu:180-186) with TransformerBlock::forward
@@ -34,20 +47,26 @@ namespace xl {
 
 namespace {
 
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = kPersistWarps;
 constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kSlotBytes = kPersistTileRows * kPersistTileK * 4;  // 16 KB
-constexpr int kSlots = 12;                                       // 192 KB ring
+constexpr int kBoxK = kPersistBoxTiles * kPersistTileK;        // 512 floats of K per box
+constexpr int kSlotBytes = kPersistTileRows * kBoxK * 4;         // 32 KB
+constexpr int kSlots = kPersistSlots;                            // 192 KB ring
 constexpr int kMaxK = 4096;
-constexpr size_t kSmemBytes =
-    static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 + 2 * kSlots * 8 + 512 + kConsumerWarps * 64 * 4;
+constexpr size_t kSmemBytes = static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 + 2 * kSlots * 8 + 512;
 constexpr uint32_t kMbarSpinLimit = 1u << 24;
 constexpr uint32_t kFlagSpinLimit = 1u << 24;
 constexpr int kErrMbar = 1, kErrFlag = 2;
-constexpr uint32_t kPrefetchPiece = 32768;
+// Attention scratch inside the staging buffer xs (free between the QKV and
+// out-projection stagings): per warp the rotated q (64 floats), then per warp
+// (max, sum, o[64]) partials.
+constexpr int kAttnWarpScratch = kHeadDim;
+constexpr int kAttnPartStride = kHeadDim + 4;
+constexpr int kStageQuads = kMaxK / 4 / kConsumerThreads;  // float4 of a staged vector per consumer thread
 
-static_assert(kPersistTileRows == 2 * kConsumerWarps, "each consumer warp owns two rows of a tile");
+static_assert(kPersistTileRows == 2 * kConsumerWarps, "each consumer warp owns two rows of a box");
+static_assert(kConsumerWarps * (kAttnWarpScratch + kAttnPartStride) <= kMaxK, "attention scratch fits in xs");
 
 enum PhaseKind : int { kQKV = 0, kAttn = 1, kWo = 2, kW13 = 3, kW2 = 4, kLM = 5 };
 
@@ -75,12 +94,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// 2D TMA tile load (no multicast) of one [16 rows][256 floats] box at (x, y).
-__device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+// 3D TMA load (no multicast) of one [16 rows][kd k-tiles][256 floats] box whose
+// first k-tile is kt and first row is row; the map views W[rows][K] as
+// [rows][K/256][256].
+__device__ __forceinline__ void tma_box(void* dst, const CUtensorMap* map, int kt, int row, uint64_t* bar) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(0), "r"(kt), "r"(row), "r"(smem_u32(bar))
         : "memory");
 }
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerThreads) : "memory"); }
@@ -152,47 +173,51 @@ __device__ __forceinline__ Gemv gemv_of(const PersistentParams& p, int ph) {
     return g;
 }
 
-// This CTA's row groups (16 rows each) of an M-row matrix: a balanced split.
-__device__ __forceinline__ void my_groups(int M, int& g0, int& g1) {
-    const int groups = (M + kPersistTileRows - 1) / kPersistTileRows;
-    g0 = static_cast<int>((static_cast<long long>(blockIdx.x) * groups) / gridDim.x);
-    g1 = static_cast<int>((static_cast<long long>(blockIdx.x + 1) * groups) / gridDim.x);
+// This CTA's boxes [t0, t1) of a phase, nb boxes of kd k-tiles per 16-row
+// group, T boxes in all: whole groups (a balanced split of the groups) for
+// QKV, W1/V and the LM head; an even split of the boxes for the residual
+// projections.
+struct Boxes {
+    int t0, t1, nb, kd, T;
+};
+__device__ __forceinline__ Boxes boxes_of(const Gemv& d) {
+    Boxes r;
+    r.kd = persist_box_tiles(d.K);
+    r.nb = persist_boxes_per_group(d.K);
+    const int groups = (d.M + kPersistTileRows - 1) / kPersistTileRows;
+    r.T = groups * r.nb;
+    if (d.kind == kWo || d.kind == kW2) {
+        r.t0 = static_cast<int>(static_cast<long long>(blockIdx.x) * r.T / gridDim.x);
+        r.t1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * r.T / gridDim.x);
+    } else {
+        r.t0 = static_cast<int>(static_cast<long long>(blockIdx.x) * groups / gridDim.x) * r.nb;
+        r.t1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * groups / gridDim.x) * r.nb;
+    }
+    return r;
 }
 
 // ---------------------------------------------------------------------------
-// Producer.  A unit is one 16-row group of one GEMV phase; its rows are
-// contiguous in HBM, which the L2 prefetch cursor (p.prefetch_units units
-// ahead of the ring copies, 0 = off) uses.
-struct Unit {
-    int ph, g, g0, g1;
+// Producer: walks this CTA's boxes of every GEMV phase in order.
+struct Cursor {
+    const CUtensorMap* map;
+    int ph, tau, t1, t0, nb, kd;
+    bool valid;
 };
 
-__device__ bool unit_first(const PersistentParams& p, int ph, Unit& u) {
+__device__ void cursor_first(const PersistentParams& p, int ph, Cursor& c) {
     const int last = 5 * p.layers;
     for (; ph <= last; ++ph) {
         if (phase_kind(ph, p.layers) == kAttn) continue;
-        int g0, g1;
-        my_groups(gemv_of(p, ph).M, g0, g1);
-        if (g0 < g1) {
-            u = Unit{ph, g0, g0, g1};
-            return true;
+        const Gemv d = gemv_of(p, ph);
+        const Boxes r = boxes_of(d);
+        if (r.t0 < r.t1) {
+            c.map = d.map;
+            c.ph = ph, c.tau = r.t0, c.t0 = r.t0, c.t1 = r.t1, c.nb = r.nb, c.kd = r.kd;
+            c.valid = true;
+            return;
         }
     }
-    return false;
-}
-
-__device__ bool unit_next(const PersistentParams& p, Unit& u) {
-    if (++u.g < u.g1) return true;
-    return unit_first(p, u.ph + 1, u);
-}
-
-__device__ void prefetch_unit(const PersistentParams& p, const Unit& u) {
-    const Gemv d = gemv_of(p, u.ph);
-    const int rows = min(kPersistTileRows, d.M - u.g * kPersistTileRows);
-    const char* src = reinterpret_cast<const char*>(d.W + static_cast<size_t>(u.g) * kPersistTileRows * d.K);
-    const uint32_t bytes = static_cast<uint32_t>(rows) * d.K * 4;
-    for (uint32_t off = 0; off < bytes; off += kPrefetchPiece)
-        prefetch_l2_bulk(src + off, min(kPrefetchPiece, bytes - off));
+    c.valid = false;
 }
 
 __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, uint64_t* empty) {
@@ -201,44 +226,43 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
     uint32_t par = 0;
     int issued = 0;
     bool ok = true;
-    Unit cu, pu;
-    bool have = unit_first(p, 0, cu);
-    bool pf = unit_first(p, 0, pu);
-    for (int i = 0; i < p.prefetch_units && pf; ++i) {
-        prefetch_unit(p, pu);
-        pf = unit_next(p, pu);
-    }
-    for (; have && ok; have = unit_next(p, cu)) {
-        if (pf && p.prefetch_units > 0) {
-            prefetch_unit(p, pu);
-            pf = unit_next(p, pu);
+    const int inflight = p.inflight;
+    Cursor c;
+    for (cursor_first(p, 0, c); c.valid;) {
+        if (!wait_parity(&empty[slot], par ^ 1u, st)) {
+            ok = false;
+            break;
         }
-        const Gemv d = gemv_of(p, cu.ph);
-        const int nkt = (d.K + kPersistTileK - 1) / kPersistTileK;
-        if (cu.g == cu.g0) trace_at(p, cu.ph, kTrProdFirst);
-        for (int kt = 0; kt < nkt; ++kt) {
-            if (!wait_parity(&empty[slot], par ^ 1u, st)) {
+        // At most `inflight` boxes requested but not landed: a deeper queue only
+        // adds latency to every other memory access once HBM is saturated.
+        if (issued >= inflight) {
+            const int k = issued - inflight;
+            if (!wait_parity(&full[k % kSlots], static_cast<uint32_t>((k / kSlots) & 1), st)) {
                 ok = false;
                 break;
             }
-            // Rows past M and columns past K of the box are zero-filled by TMA and
-            // still counted in the transaction bytes.
-            mbar_arrive_expect_tx(&full[slot], kSlotBytes);
-            tma_tile(ring + static_cast<size_t>(slot) * kSlotBytes, d.map, kt * kPersistTileK,
-                     cu.g * kPersistTileRows, &full[slot]);
-            ++issued;
-            if (++slot == kSlots) {
-                slot = 0;
-                par ^= 1u;
-            }
         }
-        if (cu.g + 1 == cu.g1) trace_at(p, cu.ph, kTrProdLast);
+        if (c.tau == c.t0) trace_at(p, c.ph, kTrProdFirst);
+        const int g = c.tau / c.nb, bi = c.tau % c.nb;
+        // Rows past M and k-tiles past K of the box are zero-filled by TMA and
+        // still counted in the transaction bytes.
+        mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(kPersistTileRows * kPersistTileK * 4 * c.kd));
+        tma_box(ring + static_cast<size_t>(slot) * kSlotBytes, c.map, bi * c.kd, g * kPersistTileRows, &full[slot]);
+        ++issued;
+        if (++slot == kSlots) {
+            slot = 0;
+            par ^= 1u;
+        }
+        if (++c.tau == c.t1) {
+            trace_at(p, c.ph, kTrProdLast);
+            cursor_first(p, c.ph + 1, c);
+        }
     }
     if (!ok) {
         // Drain: every copy already issued must land before this CTA exits.
         const int pending = issued < kSlots ? issued : kSlots;
         for (int i = 1; i <= pending; ++i) {
-            const int k = issued - i;  // tile k went to slot k % kSlots with parity (k / kSlots) & 1
+            const int k = issued - i;  // box k went to slot k % kSlots with parity (k / kSlots) & 1
             const int s = k % kSlots;
             const uint32_t pp = static_cast<uint32_t>((k / kSlots) & 1);
             uint32_t it = 0;
@@ -288,30 +312,79 @@ __device__ float consumer_sum(float v, float* red) {
     return s;
 }
 
-// xs = rmsnorm(src) * gamma (src read through L2); optionally store src to x_out.
-__device__ void stage_norm(const float* src, const float* gamma, int K, float* xs, float* red, float* x_out) {
+// Residual rows 4q .. 4q+3 (within one 16-row group) after a split
+// projection: x_old + (the partial row sums of the CTAs that own the group's
+// boxes, in CTA order, + bias).
+__device__ __forceinline__ float4 residual_quad(const float* x_old, const float* bias, const float* cres, int q, int nb,
+                                                int T) {
+    const int g = (4 * q) / kPersistTileRows;
+    const int G = gridDim.x;
+    const int c0 = ((g * nb + 1) * G - 1) / T;            // persist_owner_cta of the group's first box
+    const int nc = ((g * nb + nb) * G - 1) / T - c0 + 1;  // ... through its last box
+    const float4* part = reinterpret_cast<const float4*>(cres + g * (kPersistMaxContrib * kPersistTileRows)) +
+                         (q % (kPersistTileRows / 4));
+    float4 v[kPersistMaxContrib];
+#pragma unroll
+    for (int c = 0; c < kPersistMaxContrib; ++c)
+        v[c] = c < nc ? __ldcg(part + c * (kPersistTileRows / 4)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float4 xo = __ldcg(reinterpret_cast<const float4*>(x_old) + q);
+    const float4 b = reinterpret_cast<const float4*>(bias)[q];
+    float4 s = v[0];
+#pragma unroll
+    for (int c = 1; c < kPersistMaxContrib; ++c) {
+        if (c < nc) {
+            s.x += v[c].x;
+            s.y += v[c].y;
+            s.z += v[c].z;
+            s.w += v[c].w;
+        }
+    }
+    return make_float4(xo.x + (s.x + b.x), xo.y + (s.y + b.y), xo.z + (s.z + b.z), xo.w + (s.w + b.w));
+}
+
+// xs = rmsnorm(x) * gamma, where x is the embedding row (cres == nullptr) or
+// the residual after a split projection of nb boxes per group; this CTA stores
+// its slice of x to x_out.  float4 accesses; gamma is loaded with x.
+__device__ void stage_norm(const PersistentParams& p, const float* x_old, const float* bias, const float* cres,
+                           int nb, const float* gamma, float* xs, float* red, float* x_out) {
     const int t = threadIdx.x - 32;
-    const float4* s4 = reinterpret_cast<const float4*>(src);
-    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+    const int K = p.H;
+    const int T = (K / kPersistTileRows) * nb;
+    const int s0 = static_cast<int>(static_cast<long long>(blockIdx.x) * K / gridDim.x);
+    const int s1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * K / gridDim.x);
     float4* x4 = reinterpret_cast<float4*>(xs);
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+    float4 gk[kStageQuads];
     float ss = 0.0f;
-    for (int i = t; i < (K >> 2); i += kConsumerThreads) {
-        const float4 v = __ldcg(s4 + i);
-        x4[i] = v;
-        if (x_out) reinterpret_cast<float4*>(x_out)[i] = v;
-        ss = dot4(v, v, ss);
+#pragma unroll
+    for (int k = 0; k < kStageQuads; ++k) {
+        const int q = t + k * kConsumerThreads;
+        if (q < (K >> 2)) {
+            gk[k] = g4[q];
+            const float4 v =
+                cres ? residual_quad(x_old, bias, cres, q, nb, T) : __ldcg(reinterpret_cast<const float4*>(x_old) + q);
+            x4[q] = v;
+            const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (4 * q + u >= s0 && 4 * q + u < s1) x_out[4 * q + u] = e[u];
+            ss = dot4(v, v, ss);
+        }
     }
     const float tot = consumer_sum(ss, red);
     // RMSNorm of src/rmsnorm.cu:99-101: 1 / sqrt(mean + 1e-6), in double.
     const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(tot / static_cast<float>(K)) + 1e-6));
-    for (int i = t; i < (K >> 2); i += kConsumerThreads) {
-        float4 v = x4[i];
-        const float4 g = g4[i];
-        v.x = v.x * inv * g.x;
-        v.y = v.y * inv * g.y;
-        v.z = v.z * inv * g.z;
-        v.w = v.w * inv * g.w;
-        x4[i] = v;
+#pragma unroll
+    for (int k = 0; k < kStageQuads; ++k) {
+        const int q = t + k * kConsumerThreads;
+        if (q < (K >> 2)) {
+            float4 v = x4[q];
+            v.x = v.x * inv * gk[k].x;
+            v.y = v.y * inv * gk[k].y;
+            v.z = v.z * inv * gk[k].z;
+            v.w = v.w * inv * gk[k].w;
+            x4[q] = v;
+        }
     }
 }
 
@@ -338,71 +411,125 @@ __device__ __forceinline__ float2 warp_reduce_scatter64(float (&v)[64]) {
     return make_float2(v[0], v[1]);
 }
 
-// One (head, 32-position chunk) of the decode attention on one warp, lane j
-// owning position t0 + j: RoPE at position n (src/rope.cu:20-45), KV append
-// when the chunk holds n, scores, softmax and P.V.  Each lane's K and V rows
-// (32 x 16 B loads) are in flight together.  With one chunk the warp writes the
-// head's output; otherwise it writes its (max, sum, o) partial and the last
-// chunk of the head to finish (a per-head ticket) merges the partials.
-__device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int layer, int h, int s, int nsplit, int n,
-                             float* qsh) {
-    const int lane = threadIdx.x & 31;
+// This CTA's attention item of the token: head h, CTA j of the head's nct;
+// the heads * nct items are spread evenly over the grid, one per CTA at most.
+__device__ __forceinline__ bool attn_item(int heads, int nct, int& h, int& j) {
+    const int items = heads * nct, G = gridDim.x, b = blockIdx.x;
+    const int i = (b * items + G - 1) / G;
+    if (i >= items || (i * G) / items != b) return false;
+    h = i / nct;
+    j = i % nct;
+    return true;
+}
+
+// The attention phase of one layer on this CTA (all consumer warps enter).
+// Per warp: chunk s = j * 8 + warp of positions [32 s, 32 s + 32) ∩ [0, n],
+// lane l owning position 32 s + l: RoPE at position n (src/rope.cu:20-45), KV
+// append, scores, softmax and P.V (src/attn.cu:490-547).  Returns false if the
+// wait for the QKV phase failed.
+__device__ bool attention_phase(const PersistentParams& p, int layer, int ph, int n, float* xs, int* s_ok) {
+    const int t = threadIdx.x - 32;
+    const int warp = t >> 5, lane = t & 31;
+    const int nsplit = n / kPersistChunk + 1;
+    const int nct = (nsplit + kConsumerWarps - 1) / kConsumerWarps;
+    int h = 0, j = 0;
+    const bool has = attn_item(p.heads, nct, h, j);
+    const LayerPtrs& y = p.layer[layer];
+    const int s = j * kConsumerWarps + warp;
+    const bool active = has && s < nsplit;
     const int t0 = s * kPersistChunk;
-    const int cnt = min(kPersistChunk, n + 1 - t0);
-    const float* q = p.qkv + h * kHeadDim;
-    const float* kn = p.qkv + p.Hl + h * kHeadDim;
-    const float* vn = p.qkv + 2 * p.Hl + h * kHeadDim;
+    const int pos = t0 + lane;
+    const bool mine = active && pos <= n;
     float* kc = y.kc + static_cast<size_t>(h) * p.T * kHeadDim;
     float* vc = y.vc + static_cast<size_t>(h) * p.T * kHeadDim;
-    const float2 cs = p.rope[n * kHalfHead + lane];
-    const float qa = __ldcg(q + lane), qb = __ldcg(q + lane + kHalfHead);
-    qsh[lane] = (qa * cs.x + qb * cs.y) * 0.125f;  // 1/sqrt(64) is exact
-    qsh[lane + kHalfHead] = (-qa * cs.y + qb * cs.x) * 0.125f;
-    if (n >= t0 && n < t0 + cnt) {
-        const float ka = __ldcg(kn + lane), kb = __ldcg(kn + lane + kHalfHead);
-        kc[n * kHeadDim + lane] = ka * cs.x + kb * cs.y;
-        kc[n * kHeadDim + lane + kHalfHead] = -ka * cs.y + kb * cs.x;
-        vc[n * kHeadDim + lane] = __ldcg(vn + lane);
-        vc[n * kHeadDim + lane + kHalfHead] = __ldcg(vn + lane + kHalfHead);
+    // Cached rows t0 .. min(t0 + 32, n) - 1 of this chunk (rows are 256 B, contiguous per head).
+    const int cached = active ? min(kPersistChunk, n - t0) : 0;
+    if (lane == 0 && cached > 0) {
+        prefetch_l2_bulk(kc + static_cast<size_t>(t0) * kHeadDim, static_cast<uint32_t>(cached) * kHeadDim * 4);
+        prefetch_l2_bulk(vc + static_cast<size_t>(t0) * kHeadDim, static_cast<uint32_t>(cached) * kHeadDim * 4);
     }
-    __syncwarp();
-    const bool mine = lane < cnt;
-    const float4* kr = reinterpret_cast<const float4*>(kc + static_cast<size_t>(t0 + (mine ? lane : 0)) * kHeadDim);
-    const float4* vr = reinterpret_cast<const float4*>(vc + static_cast<size_t>(t0 + (mine ? lane : 0)) * kHeadDim);
-    float4 kv[16], vv[16];
+    if (!wait_phase(p, ph - 1, s_ok)) return false;
+    if (t == 0) trace_at(p, ph, kTrConsStart);
+    if (!has) return true;
+    float* qsh = xs + warp * kAttnWarpScratch;
+    float* apart = xs + kConsumerWarps * kAttnWarpScratch;  // [8][68]
+    if (active) {
+        const float2 cs = p.rope[n * kHalfHead + lane];
+        const float* q = p.qkv + h * kHeadDim;
+        const float qa = __ldcg(q + lane), qb = __ldcg(q + lane + kHalfHead);
+        qsh[lane] = (qa * cs.x + qb * cs.y) * 0.125f;  // 1/sqrt(64) is exact
+        qsh[lane + kHalfHead] = (-qa * cs.y + qb * cs.x) * 0.125f;
+        if (n >= t0 && n < t0 + kPersistChunk) {
+            const float* kn = p.qkv + p.Hl + h * kHeadDim;
+            const float* vn = p.qkv + 2 * p.Hl + h * kHeadDim;
+            const float ka = __ldcg(kn + lane), kb = __ldcg(kn + lane + kHalfHead);
+            const float va = __ldcg(vn + lane), vb = __ldcg(vn + lane + kHalfHead);
+            kc[n * kHeadDim + lane] = ka * cs.x + kb * cs.y;
+            kc[n * kHeadDim + lane + kHalfHead] = -ka * cs.y + kb * cs.x;
+            vc[n * kHeadDim + lane] = va;
+            vc[n * kHeadDim + lane + kHalfHead] = vb;
+        }
+        __syncwarp();  // orders the row-n stores before the lane that owns position n reads them
+        const float4* kr = reinterpret_cast<const float4*>(kc + static_cast<size_t>(mine ? pos : t0) * kHeadDim);
+        const float4* vr = reinterpret_cast<const float4*>(vc + static_cast<size_t>(mine ? pos : t0) * kHeadDim);
+        float4 kv[16], vv[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) kv[i] = __ldcg(kr + i);
+        for (int i = 0; i < 16; ++i) kv[i] = __ldcg(kr + i);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) vv[i] = __ldcg(vr + i);
-    const float4* q4 = reinterpret_cast<const float4*>(qsh);
-    float d = 0.0f;
+        for (int i = 0; i < 16; ++i) vv[i] = __ldcg(vr + i);
+        const float4* q4 = reinterpret_cast<const float4*>(qsh);
+        float d = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) d = dot4(kv[i], q4[i], d);
-    const float sc = mine ? d : -INFINITY;
-    const float m = warp_max(sc);
-    const float e = mine ? expf(sc - m) : 0.0f;
-    const float l = warp_sum(e);
-    float w[64];
+        for (int i = 0; i < 16; ++i) d = dot4(kv[i], q4[i], d);
+        const float sc = mine ? d : -INFINITY;
+        const float m = warp_max(sc);
+        const float e = mine ? expf(sc - m) : 0.0f;
+        const float l = warp_sum(e);
+        float w[64];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        w[4 * i + 0] = e * vv[i].x;
-        w[4 * i + 1] = e * vv[i].y;
-        w[4 * i + 2] = e * vv[i].z;
-        w[4 * i + 3] = e * vv[i].w;
+        for (int i = 0; i < 16; ++i) {
+            w[4 * i + 0] = e * vv[i].x;
+            w[4 * i + 1] = e * vv[i].y;
+            w[4 * i + 2] = e * vv[i].z;
+            w[4 * i + 3] = e * vv[i].w;
+        }
+        const float2 o = warp_reduce_scatter64(w);
+        float* ap = apart + warp * kAttnPartStride;
+        reinterpret_cast<float2*>(ap + 4)[lane] = o;
+        if (lane == 0) {
+            ap[0] = m;
+            ap[1] = l;
+        }
     }
-    const float2 o = warp_reduce_scatter64(w);
+    consumer_sync();
+    if (warp != 0) return true;
+    // Merge this CTA's chunks: lane k holds chunk k's (max, sum); every lane
+    // two output dims.
+    const int nw = min(kConsumerWarps, nsplit - j * kConsumerWarps);
+    const float mk = lane < nw ? apart[lane * kAttnPartStride] : -INFINITY;
+    const float lk = lane < nw ? apart[lane * kAttnPartStride + 1] : 0.0f;
+    const float M = warp_max(mk);
+    const float wk = lane < nw ? expf(mk - M) : 0.0f;
+    const float L = warp_sum(lk * wk);
+    float2 acc = make_float2(0.0f, 0.0f);
+    for (int k = 0; k < nw; ++k) {
+        const float wt = __shfl_sync(0xffffffffu, wk, k);
+        const float2 ok = reinterpret_cast<const float2*>(apart + k * kAttnPartStride + 4)[lane];
+        acc.x = fmaf(wt, ok.x, acc.x);
+        acc.y = fmaf(wt, ok.y, acc.y);
+    }
     float2* out = reinterpret_cast<float2*>(p.att + h * kHeadDim);
-    if (nsplit == 1) {
-        out[lane] = make_float2(o.x / l, o.y / l);
-        return;
+    if (nct == 1) {
+        out[lane] = make_float2(acc.x / L, acc.y / L);
+        return true;
     }
-    const int maxs = persistent_max_splits(p.T);
-    float* base = p.part + static_cast<size_t>(h) * maxs * (kHeadDim + 2);
-    float* pp = base + s * (kHeadDim + 2);
-    reinterpret_cast<float2*>(pp + 2)[lane] = o;
+    // A head split over nct CTAs: the last CTA to finish merges their partials.
+    float* base = p.part + static_cast<size_t>(h) * persistent_max_splits(p.T) * (kHeadDim + 2);
+    float* pp = base + j * (kHeadDim + 2);
+    reinterpret_cast<float2*>(pp + 2)[lane] = acc;
     if (lane == 0) {
-        pp[0] = m;
-        pp[1] = l;
+        pp[0] = M;
+        pp[1] = L;
     }
     __syncwarp();
     int ticket = 0;
@@ -411,32 +538,32 @@ __device__ void attend_chunk(const PersistentParams& p, const LayerPtrs& y, int 
         ticket = atomicAdd(p.head_done + layer * p.heads + h, 1);
     }
     ticket = __shfl_sync(0xffffffffu, ticket, 0);
-    if (ticket != nsplit - 1) return;
+    if (ticket != nct - 1) return true;
     __threadfence();
-    // Merge: lane s holds split s's (max, sum); every lane its two output dims.
-    const float ms = lane < nsplit ? __ldcg(base + lane * (kHeadDim + 2)) : -INFINITY;
-    const float ls = lane < nsplit ? __ldcg(base + lane * (kHeadDim + 2) + 1) : 0.0f;
-    const float M = warp_max(ms);
-    const float ws = lane < nsplit ? expf(ms - M) : 0.0f;
-    const float L = warp_sum(ls * ws);
-    float2 acc = make_float2(0.0f, 0.0f);
-    for (int k = 0; k < nsplit; ++k) {
-        const float wk = __shfl_sync(0xffffffffu, ws, k);
+    const float mc = lane < nct ? __ldcg(base + lane * (kHeadDim + 2)) : -INFINITY;
+    const float lc = lane < nct ? __ldcg(base + lane * (kHeadDim + 2) + 1) : 0.0f;
+    const float M2 = warp_max(mc);
+    const float wc = lane < nct ? expf(mc - M2) : 0.0f;
+    const float L2 = warp_sum(lc * wc);
+    float2 acc2 = make_float2(0.0f, 0.0f);
+    for (int k = 0; k < nct; ++k) {
+        const float wt = __shfl_sync(0xffffffffu, wc, k);
         const float2 ok = __ldcg(reinterpret_cast<const float2*>(base + k * (kHeadDim + 2) + 2) + lane);
-        acc.x = fmaf(wk, ok.x, acc.x);
-        acc.y = fmaf(wk, ok.y, acc.y);
+        acc2.x = fmaf(wt, ok.x, acc2.x);
+        acc2.y = fmaf(wt, ok.y, acc2.y);
     }
-    out[lane] = make_float2(acc.x / L, acc.y / L);
+    out[lane] = make_float2(acc2.x / L2, acc2.y / L2);
+    return true;
 }
 
 __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint64_t* full, uint64_t* empty,
-                          float* red, unsigned long long* best_s, float* qbuf, int* s_ok) {
+                          float* red, unsigned long long* best_s, int* s_ok) {
     DevState* st = p.st;
     const int t = threadIdx.x - 32;
     const int warp = t >> 5, lane = t & 31;
     const int n = st->pos;
-    const int nsplit = (n + kPersistChunk) / kPersistChunk;  // chunks of positions 0..n
     const float rp = st->in.rp;
+    const int nb_wo = persist_boxes_per_group(p.Hl), nb_w2 = persist_boxes_per_group(p.Fl);
     int slot = 0;
     uint32_t par = 0;
     float best_v = -INFINITY;
@@ -444,77 +571,72 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
     bool ok = true;
     const int last = 5 * p.layers;
     for (int ph = 0; ph <= last; ++ph) {
-        if (ph > 0 && !wait_phase(p, ph - 1, s_ok)) return;
-        if (t == 0) trace_at(p, ph, kTrConsStart);
         const int kind = phase_kind(ph, p.layers);
-        const LayerPtrs* y = ph < last ? &p.layer[ph / 5] : nullptr;
         if (kind == kAttn) {
-            const int items = p.heads * nsplit;
-            for (int it = blockIdx.x + gridDim.x * warp; it < items; it += gridDim.x * kConsumerWarps)
-                attend_chunk(p, *y, ph / 5, it / nsplit, it % nsplit, nsplit, n, qbuf + warp * kHeadDim);
+            if (!attention_phase(p, ph / 5, ph, n, xs, s_ok)) return;
             if (t == 0) trace_at(p, ph, kTrConsStaged);
             signal_phase(p, ph);
             if (t == 0) trace_at(p, ph, kTrConsEnd);
             continue;
         }
+        if (ph > 0 && !wait_phase(p, ph - 1, s_ok)) return;
+        if (t == 0) trace_at(p, ph, kTrConsStart);
+        const int l = ph / 5;
+        const LayerPtrs* y = ph < last ? &p.layer[l] : nullptr;
         const Gemv d = gemv_of(p, ph);
-        // stage this phase's input vector
+        // Stage this phase's input vector.
         if (kind == kQKV) {
-            if (ph == 0) {
-                const float* row = p.emb + static_cast<size_t>(st->in.token_in) * p.H;
-                stage_norm(row, y->g1, p.H, xs, red, blockIdx.x == 0 ? p.x : nullptr);
-            } else {
-                stage_norm(p.x, y->g1, p.H, xs, red, nullptr);
-            }
+            if (l == 0)
+                stage_norm(p, p.emb + static_cast<size_t>(st->in.token_in) * p.H, nullptr, nullptr, 0, y->g1, xs, red,
+                           p.xa);
+            else
+                stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, y->g1, xs, red, p.xa);
         } else if (kind == kWo) {
             stage_copy(p.att, p.Hl, xs);
         } else if (kind == kW13) {
-            stage_norm(p.x, y->g2, p.H, xs, red, nullptr);
+            stage_norm(p, p.xa, y->bo, p.cres, nb_wo, y->g2, xs, red, p.xb);
         } else if (kind == kW2) {
             stage_copy(p.ffh, p.Fl, xs);
         } else {  // kLM
-            stage_norm(p.x, p.gnorm, p.H, xs, red, nullptr);
+            stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, p.gnorm, xs, red, p.xa);
         }
         consumer_sync();
         if (t == 0) trace_at(p, ph, kTrConsStaged);
-        int g0, g1;
-        my_groups(d.M, g0, g1);
-        const int nkt = (d.K + kPersistTileK - 1) / kPersistTileK;
+        const Boxes r = boxes_of(d);
+        const int rs4 = r.kd * (kPersistTileK / 4);  // float4 per row of a box
         const float4* x4 = reinterpret_cast<const float4*>(xs);
         const int ra = 2 * warp, rb = ra + 1;
-        for (int g = g0; g < g1; ++g) {
+        const bool split = kind == kWo || kind == kW2;
+        for (int tau = r.t0; tau < r.t1;) {
+            const int g = tau / r.nb;
+            const int bi0 = tau % r.nb, bi1 = min(r.nb, bi0 + (r.t1 - tau));
             const int rows = min(kPersistTileRows, d.M - g * kPersistTileRows);
             const bool va = ra < rows, vb = rb < rows;
             const int Ra = g * kPersistTileRows + ra, Rb = Ra + 1;
-            // Epilogue operands, loaded now so that their latency overlaps the tiles.
+            // Epilogue operands, loaded now so that their latency overlaps the boxes.
             float ea = 0.0f, eb = 0.0f;  // bias, or the repetition flag in the LM head
-            float xa = 0.0f, xb = 0.0f;  // residual stream
             if (kind == kLM) {
                 if (va) ea = p.rep_flags[Ra] ? 1.0f : 0.0f;
                 if (vb) eb = p.rep_flags[Rb] ? 1.0f : 0.0f;
-            } else {
+            } else if (!split) {
                 if (va) ea = d.bias[Ra];
                 if (vb) eb = d.bias[Rb];
-                if (kind == kWo || kind == kW2) {
-                    if (va) xa = __ldcg(p.x + Ra);
-                    if (vb) xb = __ldcg(p.x + Rb);
-                }
             }
             float acc_a = 0.0f, acc_b = 0.0f;
-            for (int kt = 0; kt < nkt; ++kt) {
+            for (int bi = bi0; bi < bi1; ++bi) {
                 // After a failed wait this warp only walks the schedule so that it
                 // meets the other consumer warps at every named barrier.
                 if (ok && !wait_parity(&full[slot], par, st)) ok = false;
                 if (ok) {
-                    const int k0 = kt * kPersistTileK;
-                    const int kc4 = min(kPersistTileK, d.K - k0) >> 2;
+                    const int k0 = bi * r.kd * kPersistTileK;
+                    const int kc4 = min(r.kd * kPersistTileK, d.K - k0) >> 2;
                     const float4* tile =
                         reinterpret_cast<const float4*>(ring + static_cast<size_t>(slot) * kSlotBytes);
-                    const float4* wa = tile + ra * (kPersistTileK / 4);
-                    const float4* wb = tile + rb * (kPersistTileK / 4);
+                    const float4* wa = tile + ra * rs4;
+                    const float4* wb = tile + rb * rs4;
                     const float4* xk = x4 + (k0 >> 2);
 #pragma unroll
-                    for (int j0 = 0; j0 < kPersistTileK / 4; j0 += 32) {
+                    for (int j0 = 0; j0 < kBoxK / 4; j0 += 32) {
                         const int j = j0 + lane;
                         if (j < kc4) {
                             const float4 xv = xk[j];
@@ -530,6 +652,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                     par ^= 1u;
                 }
             }
+            tau += bi1 - bi0;
             acc_a = warp_sum(acc_a);
             acc_b = warp_sum(acc_b);
             switch (kind) {
@@ -538,10 +661,13 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                     if (lane == 1 && vb) p.qkv[Rb] = acc_b + eb;
                     break;
                 case kWo:
-                case kW2:
-                    if (lane == 0 && va) p.x[Ra] = xa + (acc_a + ea);
-                    if (lane == 1 && vb) p.x[Rb] = xb + (acc_b + eb);
+                case kW2: {  // partial row sums of this CTA's boxes of group g
+                    const int c = blockIdx.x - persist_owner_cta(static_cast<long long>(g) * r.nb, r.T, gridDim.x);
+                    float* q = p.cres + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows;
+                    if (lane == 0) q[ra] = acc_a;
+                    if (lane == 1) q[rb] = acc_b;
                     break;
+                }
                 case kW13:
                     if (lane == 0 && vb) p.ffh[Ra >> 1] = silu(acc_a + ea) * (acc_b + eb);
                     break;
@@ -592,8 +718,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     float* red = reinterpret_cast<float*>(empty + kSlots);                  // 16 floats
     unsigned long long* best_s = reinterpret_cast<unsigned long long*>(red + 16);  // 8
     int* s_ok = reinterpret_cast<int*>(best_s + kConsumerWarps);            // 1 (+pad)
-    float* qbuf = reinterpret_cast<float*>(smem + static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 +
-                                           2 * kSlots * 8 + 512);           // 8 x 64
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
@@ -608,7 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) producer(p, ring, full, empty);
     } else {
-        consumers(p, ring, xs, full, empty, red, best_s, qbuf, s_ok);
+        consumers(p, ring, xs, full, empty, red, best_s, s_ok);
     }
 }
 
@@ -617,8 +741,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
 size_t persistent_smem_bytes() { return kSmemBytes; }
 
 cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cudaStream_t s) {
-    if (p.H > kMaxK || p.Hl > kMaxK || p.Fl > kMaxK || p.H % 4 || p.Hl % 4 || p.Fl % 4) return cudaErrorInvalidValue;
-    if (persistent_max_splits(p.T) > 32) return cudaErrorInvalidValue;  // one lane per split in the merge
+    if (p.H > kMaxK || p.Hl > kMaxK || p.Fl > kMaxK || p.H % kPersistTileK || p.Hl % kPersistTileK ||
+        p.Fl % kPersistTileK)
+        return cudaErrorInvalidValue;
+    // Attention: at most one item per CTA, at most 32 CTAs per head (one lane each in the merge).
+    const int nct = persist_attn_ctas_per_head(p.T);
+    if (p.heads * nct > num_sms || nct > 32) return cudaErrorInvalidValue;
+    if (p.inflight < 1 || p.inflight > kSlots) return cudaErrorInvalidValue;
+    if (persist_max_contrib(p.H, p.Hl, num_sms) > kPersistMaxContrib ||
+        persist_max_contrib(p.H, p.Fl, num_sms) > kPersistMaxContrib)
+        return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;

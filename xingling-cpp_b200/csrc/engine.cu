@@ -214,6 +214,7 @@ int Engine::alloc_all() {
     add(&att_, Hl * 4);
     add(&ffh_, Fl * 4);
     add(&part_, H * 4);
+    add(&cres_, H / kPersistTileRows * kPersistMaxContrib * kPersistTileRows * 4);
     add(&logits_, vl * 4);
     add(&attn_ws_, static_cast<size_t>(heads_l_) * maxs * (kHeadDim + 2) * 4);
     add(&attn_cnt_, heads_l_ * 4);
@@ -445,7 +446,9 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     p.emb = emb_;
     p.gnorm = gnorm_;
     p.rope = rope_;
-    p.x = xa_;
+    p.xa = xa_;
+    p.xb = xb_;
+    p.cres = cres_;
     p.qkv = qkv_;
     p.part = attn_ws_;
     p.ffh = ffh_;
@@ -456,7 +459,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     p.head_done = done_ + 5 * cfg_.layers + 1;
     p.att = att_;
     p.trace = trace_;
-    p.prefetch_units = prefetch_units_;
+    p.inflight = inflight_;
     p.H = H_;
     p.Hl = Hl_;
     p.heads = heads_l_;
@@ -480,7 +483,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
 }
 
 int Engine::enqueue_decode(cudaStream_t s) {
-    if (tp_ == 1 && decode_path_ == 0) return enqueue_decode_persistent(s);
+    if (tp_ == 1 && decode_path_ == 0 && persistent_fits()) return enqueue_decode_persistent(s);
     float* cur = xa_;
     float* other = xb_;
     bool pending = false;  // TP: part_ holds a reduced delta not yet added to cur
@@ -825,12 +828,12 @@ int Engine::set_option(const char* key, int value) {
         prefill_gemm_ = value;
         return XL_OK;
     }
-    if (k == "prefetch_units") {
-        if (value < 0 || value > 64) {
-            set_error("prefetch_units must be in [0, 64]");
+    if (k == "tma_inflight") {
+        if (value < 1 || value > kPersistSlots) {
+            set_error("tma_inflight must be in [1, 6]");
             return XL_ERR_ARG;
         }
-        prefetch_units_ = value;
+        inflight_ = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
     if (k == "phase_trace") {

@@ -63,6 +63,16 @@ class Engine {
     int capture_decode_graph();
     int enqueue_decode(cudaStream_t s);
     int enqueue_decode_persistent(cudaStream_t s);
+    // The persistent kernel streams K in 256-float tiles of at most 4096 floats,
+    // runs at most one attention item per SM and lets at most
+    // kPersistMaxContrib SMs share a row group of the residual projections.
+    bool persistent_fits() const {
+        return cfg_.layers <= kMaxLayers && H_ % kPersistTileK == 0 && Hl_ % kPersistTileK == 0 &&
+               Fl_ % kPersistTileK == 0 && H_ <= 4096 && Hl_ <= 4096 && Fl_ <= 4096 &&
+               heads_l_ * persist_attn_ctas_per_head(T_) <= num_sms_ &&
+               persist_max_contrib(H_, Hl_, num_sms_) <= kPersistMaxContrib &&
+               persist_max_contrib(H_, Fl_, num_sms_) <= kPersistMaxContrib;
+    }
     int prepare_prefill_operands();
     int prefill_linear(int mode, const TcOperands& o, const float* x, const float* w, const float* b, float* y,
                        float* y_lo, int n, int m, int k, cudaStream_t s);
@@ -88,7 +98,8 @@ class Engine {
     float2* rope_ = nullptr;   // [T][32]
     std::vector<LayerWeights> layers_;
     float* xa_ = nullptr;      // decode residual stream (ping)
-    float* xb_ = nullptr;      // decode residual stream (pong, TP)
+    float* xb_ = nullptr;      // decode residual stream (pong)
+    float* cres_ = nullptr;    // persistent decode: partial row sums of the residual projections
     float* qkv_ = nullptr;     // [3*Hl]
     float* att_ = nullptr;     // [Hl]
     float* ffh_ = nullptr;     // [Fl]
@@ -118,7 +129,7 @@ class Engine {
 
     int decode_path_ = 0;      // 0: persistent kernel (single GPU), 1: per-op kernels
     int prefill_gemm_ = 0;     // 0: tcgen05 3xTF32, 1: fp32 SIMT tiles
-    int prefetch_units_ = 0;   // persistent decode: L2 prefetch distance in 16-row groups (off: measured slower)
+    int inflight_ = 2;  // persistent decode: weight boxes requested but not landed, per SM
     bool loaded_ = false;
     bool has_seq_ = false;
     int n_ = 0;

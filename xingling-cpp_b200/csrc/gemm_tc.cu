@@ -318,12 +318,16 @@ cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int col
 cudaError_t make_stream_map(CUtensorMap* map, const float* base, int rows, int cols) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
-    if (reinterpret_cast<uintptr_t>(base) % 16 || (cols * 4) % 16) return cudaErrorInvalidValue;
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kPersistTileK), static_cast<cuuint32_t>(kPersistTileRows)};
-    const cuuint32_t elem[2] = {1, 1};
-    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, elem,
+    if (reinterpret_cast<uintptr_t>(base) % 16 || cols % kPersistTileK) return cudaErrorInvalidValue;
+    const int nkt = cols / kPersistTileK;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kPersistTileK), static_cast<cuuint64_t>(nkt),
+                                static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kPersistTileK) * 4, static_cast<cuuint64_t>(cols) * 4};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kPersistTileK),
+                               static_cast<cuuint32_t>(persist_box_tiles(cols)),
+                               static_cast<cuuint32_t>(kPersistTileRows)};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, elem,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;

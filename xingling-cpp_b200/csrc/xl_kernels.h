@@ -79,41 +79,77 @@ cudaError_t launch_attn_decode(const AttnDecodeParams& p, bool pdl, cudaStream_t
 
 // Persistent decode step (decode_persistent.cu): one cooperative launch per token.
 constexpr int kMaxLayers = 32;
-constexpr int kPersistChunk = 32;     // attention positions per warp item
-constexpr int kPersistTileRows = 16;  // weight tile streamed per TMA load: 16 rows x 256 floats
+constexpr int kPersistChunk = 32;     // attention positions per warp
+constexpr int kPersistTileRows = 16;  // weight box streamed per TMA load: 16 rows x 2 k-tiles x 256 floats
 constexpr int kPersistTileK = 256;
+constexpr int kPersistBoxTiles = 2;
+constexpr int kPersistSlots = 6;      // 32 KB ring slots per CTA
+constexpr int kPersistWarps = 8;      // consumer warps per CTA (attention: one chunk each)
+constexpr int kPersistMaxContrib = 4; // CTAs that may share one 16-row group of a residual projection
 constexpr int kPersistMaps = 4 * kMaxLayers + 1;  // QKV, Wo, W1/V, W2 per layer, then the LM head
 __host__ __device__ inline int persistent_max_splits(int max_ctx) {
     return (max_ctx + kPersistChunk - 1) / kPersistChunk;
+}
+// k-tiles per box and boxes per 16-row group of a K-column weight (K % 256 == 0).
+__host__ __device__ inline int persist_box_tiles(int K) {
+    return K / kPersistTileK < kPersistBoxTiles ? K / kPersistTileK : kPersistBoxTiles;
+}
+__host__ __device__ inline int persist_boxes_per_group(int K) {
+    const int kd = persist_box_tiles(K);
+    return (K / kPersistTileK + kd - 1) / kd;
+}
+// The residual projections (out-proj, W2) are split evenly by boxes: CTA b of
+// G takes boxes [b*T/G, (b+1)*T/G) of T = (M/16) * nb; box tau belongs to
+// persist_owner_cta(tau).  A group's partial row sums come from the CTAs that
+// own its first to last box.
+__host__ __device__ inline int persist_owner_cta(long long tau, long long T, int G) {
+    return static_cast<int>(((tau + 1) * G - 1) / T);
+}
+inline int persist_max_contrib(int M, int K, int G) {
+    const long long nb = persist_boxes_per_group(K), T = static_cast<long long>(M / kPersistTileRows) * nb;
+    int c = 0;
+    for (long long g = 0; g < M / kPersistTileRows; ++g) {
+        const int n = persist_owner_cta(g * nb + nb - 1, T, G) - persist_owner_cta(g * nb, T, G) + 1;
+        c = n > c ? n : c;
+    }
+    return c;
+}
+// Attention: CTAs per head, each taking up to kPersistWarps chunks of 32 positions.
+__host__ __device__ inline int persist_attn_ctas_per_head(int max_ctx) {
+    return (persistent_max_splits(max_ctx) + kPersistWarps - 1) / kPersistWarps;
 }
 struct LayerPtrs {
     const float *wqkv, *bqkv, *wo, *bo, *w13, *b13, *w2, *b2, *g1, *g2;
     float *kc, *vc;
 };
 struct PersistentParams {
-    CUtensorMap maps[kPersistMaps];  // [16 rows][256 floats] box maps of every streamed matrix
+    CUtensorMap maps[kPersistMaps];  // 3D box maps (make_stream_map) of every streamed matrix
     LayerPtrs layer[kMaxLayers];
     int layers;
     const float* emb;       // [V][H] tied embedding / LM head
     const float* gnorm;     // [H] final RMSNorm gain
     const float2* rope;     // [T][32]
-    float* x;               // [H] residual stream
+    float* xa;              // [H] residual stream entering a layer (and the LM head's input)
+    float* xb;              // [H] residual stream after the out-projection
+    float* cres;            // [H/16][kPersistMaxContrib][16] partial row sums of out-proj / W2
     float* qkv;             // [3*Hl]
-    float* part;            // attention partials [heads][persistent_max_splits][66]
+    float* part;            // attention partials across CTAs [heads][persistent_max_splits][66]
     float* att;             // [Hl] attention output (merged per head)
-    int* head_done;         // [layers][heads] split tickets, zeroed before each launch
+    int* head_done;         // [layers][heads] CTA tickets of the cross-CTA attention merge
     float* ffh;             // [Fl] SwiGLU activations
     float* logits;          // [V]
     const uint8_t* rep_flags;
     DevState* st;
-    int* done;              // [5*layers + 1] phase counters, zeroed before each launch (with head_done)
+    int* done;              // [5*layers + 1] phase counters (then head_done), zeroed before each launch
     unsigned long long* trace;  // optional [grid][5*layers + 1][kTraceFields] timestamps (ns), or nullptr
-    int prefetch_units;         // L2 prefetch distance of the weight stream in 16-row groups (0 = off)
+    int inflight;               // weight boxes requested but not landed, per CTA (1 .. kPersistSlots)
     int H, Hl, heads, Fl, V, T;
 };
 constexpr int kTraceFields = 5;
 size_t persistent_smem_bytes();
-// The [16 rows][256 floats] TMA box map (no swizzle) of a row-major [rows][cols] weight.
+// The TMA map (no swizzle) of a row-major [rows][cols] weight viewed as
+// [rows][cols/256][256], box [16 rows][min(2, cols/256) k-tiles][256 floats];
+// cols must be a multiple of 256.
 cudaError_t make_stream_map(CUtensorMap* map, const float* base, int rows, int cols);
 cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cudaStream_t s);
 
