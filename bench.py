@@ -9,9 +9,14 @@ weights 2.75 GB per token, far above the 126 MB L2, so no flush is needed);
 `e2e` is the same metric through the public API (llm_cpp_engine
 next_token(int)), wall clock, including the per-token host->device copy of
 the step inputs from pinned memory and the device->host read of the result.
-Also reported: prefill of a 512-id prompt (seed 1), the LM-head kernel's
-roofline, the reference's own CPU path on the host cores, and at N > 1 the
-tensor-parallel decode latency (prompt 64, seed 4, greedy 256).
+`roofline` is the dominant kernel, the persistent decode kernel (one launch
+per token, >99% of a decode step's kernel time), timed by CUDA event nodes
+around it inside the decode graph in one more step right after the timed
+region (the nodes cost the sampler its early launch, so the timed steps run
+without them).  Also reported: the whole decode
+step against the same roofline, prefill of a 512-id prompt (seed 1), the
+reference's own CPU path on the host cores, and at N > 1 the tensor-parallel
+decode latency (prompt 64, seed 4, greedy 256).
 
   python bench.py [--gpus N --steps K --warmup W]          # this engine
   python bench.py --impl reference [...]                   # reference CPU path
@@ -72,6 +77,21 @@ def decode_bytes_per_token(shape: S.ModelShape, ctx: float) -> float:
     H, F, V, L = shape.hidden, shape.ffn, shape.vocab, shape.layers
     per_layer = 4 * (4 * H * H + 4 * H + 3 * F * H + 2 * F + H + 2 * H)
     return L * per_layer + 4 * V * H + 4 * H + 4 * H + 2 * L * 4 * H * ctx
+
+
+def traffic_per_launch() -> float | None:
+    """DRAM bytes (read + write) of one persistent decode launch at the bench's
+    workload, from the Nsight Compute capture summarised in
+    profiles/decode_persistent_kernel.md (its `traffic_per_launch_full` line)."""
+    p = os.path.join(ROOT, "profiles", "decode_persistent_kernel.md")
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.startswith("traffic_per_launch_full:"):
+                    return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
 
 
 def prefill_flops(shape: S.ModelShape, n: int) -> float:
@@ -282,12 +302,13 @@ def xl_arm(args) -> None:
         tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
         pre_dev = eng.last_device_ms()
         w1 = time.perf_counter()
-        dec_dev = 0.0
+        dec_dev, kern = 0.0, []
         for _ in range(DECODE):
             tok = eng.next_token(tok, top_p=0.0, repetition_penalty=1.0)
             dec_dev += eng.last_device_ms()
+            kern.append(eng.last_kernel_ms())
         w2 = time.perf_counter()
-        return pre_dev, dec_dev, w1 - w0, w2 - w1
+        return pre_dev, dec_dev, w1 - w0, w2 - w1, kern
 
     for _ in range(args.warmup):
         step()
@@ -299,11 +320,13 @@ def xl_arm(args) -> None:
     with Clocks(uuid) as clk:
         barrier()
         torch.cuda.synchronize()
+        launches0 = llm_cpp_engine.kernel_launches()
         t0 = time.perf_counter()
         res = [step() for _ in range(args.steps)]
         torch.cuda.synchronize()
         barrier()
         wall = time.perf_counter() - t0
+        launches = llm_cpp_engine.kernel_launches() - launches0
     clocks = clk.summary()
 
     dec_dev_s = max_over_ranks(sum(r[1] for r in res) / 1e3)
@@ -321,10 +344,19 @@ def xl_arm(args) -> None:
     step_bytes = decode_bytes_per_token(shape, ctx_mean)
     step_gbs = step_bytes * (args.steps * DECODE) / (sum(r[1] for r in res) / 1e3) / 1e9
 
-    # the dominant kernel: fused final norm + tied LM head (streams the 932 MB table)
-    lm_ms = eng.profile_lm_head(20)
-    lm_bytes = 4.0 * shape.vocab * shape.hidden + shape.vocab + 4.0 * shape.vocab + 8.0 * shape.hidden
-    lm_gbs = lm_bytes / (lm_ms / 1e3) / 1e9
+    # the dominant kernel: the persistent decode kernel, one launch per token at
+    # context PROMPT + i, timed by event nodes around it in the decode graph
+    # (a separate pass: the nodes cost the sampler its early launch, so the
+    # headline steps above run without them)
+    eng.set_option("kernel_events", 1)
+    kres = [step() for _ in range(2)][1:]
+    eng.set_option("kernel_events", 0)
+    kern_ms = [k for r in kres for k in r[4]]
+    if min(kern_ms) <= 0:
+        raise RuntimeError("persistent decode kernel times missing (decode path not persistent?)")
+    kern_bytes = [decode_bytes_per_token(shape, PROMPT + i) for _ in kres for i in range(DECODE)]
+    kern_avg_ms = sum(kern_ms) / len(kern_ms)
+    kern_gbs = sum(kern_bytes) / (sum(kern_ms) / 1e3) / 1e9
 
     # prefill of the 512-id prompt (seed 1)
     pids = S.prompt_ids(1, PREFILL_N, shape.vocab)
@@ -349,7 +381,6 @@ def xl_arm(args) -> None:
     cpu = run_cpu_baseline(args.cpu_budget) if world == 1 else None
     h2d = 4 * PROMPT + 36 + DECODE * 32
     d2h = (DECODE + 1) * 80
-    per_step_launches = (1 + 8 * shape.layers + 2) + DECODE * (5 * shape.layers + 2)
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * step_dev_s / args.steps, "higher_is_better": True,
@@ -360,9 +391,10 @@ def xl_arm(args) -> None:
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (2.75 GB of weights per token vs 126 MB L2)",
                    "value_timing": "CUDA events on the engine stream around each decode step; max over ranks"},
-        "roofline": {"bound": "hbm", "kernel": "norm_gemv_kernel<kGemvLogits> (final norm + tied LM head)",
-                     "achieved": lm_gbs, "peak": hbm, "unit": "GB/s", "frac": lm_gbs / hbm, "traffic": None,
-                     "peak_kind": pk_kind, "bytes_per_launch": lm_bytes, "avg_launch_ms": lm_ms},
+        "roofline": {"bound": "hbm", "kernel": "decode_persistent_kernel (16 layers + LM head, one launch per token)",
+                     "achieved": kern_gbs, "peak": hbm, "unit": "GB/s", "frac": kern_gbs / hbm,
+                     "traffic": traffic_per_launch(), "peak_kind": pk_kind,
+                     "bytes_per_launch": sum(kern_bytes) / len(kern_bytes), "avg_launch_ms": kern_avg_ms},
         "step_roofline": {"bound": "hbm", "achieved": step_gbs, "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm,
                           "bytes_per_token": step_bytes, "mean_ctx": ctx_mean,
                           "ms_per_token": 1e3 * (sum(r[1] for r in res) / 1e3) / (args.steps * DECODE)},
@@ -374,7 +406,7 @@ def xl_arm(args) -> None:
         "cpu_baseline": cpu,
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "llm_cpp_engine.InferenceEngine.next_token"},
-        "gpu_launches": per_step_launches * args.steps,
+        "gpu_launches": launches,
         "clocks": clocks,
     }
     if tp_info is not None:

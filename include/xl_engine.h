@@ -140,6 +140,9 @@ XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, fl
  *                    keeps requested but not landed, in [1, 6] (default 2):
  *                    enough to keep HBM busy, few enough that other memory
  *                    accesses do not queue behind the stream;
+ *   "kernel_events" 1  event-record nodes around the persistent kernel in the
+ *                    decode graph, so xl_engine_last_kernel_ms reports its
+ *                    own duration (costs the sampler its early launch);
  *   "prefill_gemm" 0  prefill projections on tcgen05 with the 3xTF32 split
  *                     (default); 1  fp32 FMA tiles.
  * Changing an option re-captures the decode graph. */
@@ -152,6 +155,16 @@ XL_API int xl_engine_phase_trace(xl_engine* e, unsigned long long* out, int n);
 /* Device time of the last prefill / decode call in milliseconds (CUDA events
  * around the device work, excluding host copies). */
 XL_API int xl_engine_last_device_ms(const xl_engine* e, float* ms);
+
+/* Duration of the persistent decode kernel alone in the last decode step
+ * (CUDA events in the decode graph; needs option "kernel_events" = 1 and the
+ * persistent path), else -1.  No reference counterpart: a profiling aid. */
+XL_API int xl_engine_last_kernel_ms(const xl_engine* e, float* ms);
+
+/* Kernels this library has run in this process, every engine and op entry
+ * point included (a decode graph's kernels count at each replay).  No
+ * reference counterpart: lets a caller check that the GPU path ran. */
+XL_API long long xl_kernel_launches(void);
 
 /* Launches the engine's fused final-norm + LM-head kernel (the largest single
  * kernel of a decode step: it streams the whole tied embedding table) `iters`

@@ -110,6 +110,19 @@ def test_module_reports_missing_gpu_as_error(built):
         m.InferenceEngine("cuda")
 
 
+def test_kernel_launch_counter(built):
+    import ctypes as C
+
+    import llm_cpp_engine as m
+
+    lib = C.CDLL(X.LIB_PATH)
+    lib.xl_kernel_launches.restype = C.c_longlong
+    n = lib.xl_kernel_launches()
+    assert n >= 0 and m.kernel_launches() >= 0
+    # launches are only counted by launchers: nothing ran here, so nothing changed
+    assert lib.xl_kernel_launches() == n
+
+
 def test_weight_tree_is_deterministic(tmp_path):
     sh = S.ModelShape(layers=1, hidden=64, heads=1, ffn=64, vocab=100, max_ctx=16)
     a = S.write_weight_tree(str(tmp_path / "a"), sh)

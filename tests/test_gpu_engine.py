@@ -112,6 +112,33 @@ def test_tiny_kv_reset_rounds(eng_mod, tiny_weights, path):
         assert eng.ctx_len() == n + 2
 
 
+def test_tiny_kernel_events_and_launch_count(eng_mod, tiny_weights):
+    """Event nodes around the persistent kernel time it alone (within the step),
+    change no token, and the library counts the decode graph's two kernels
+    (persistent step + sampler) at every replay."""
+    sh = S.TINY
+    ids = [int(t) for t in np.random.default_rng(5).integers(0, sh.vocab, 9)]
+    toks = {}
+    for ev in (0, 1):
+        eng = make_engine(eng_mod, 0, **sh.engine_kwargs())
+        eng.load(tiny_weights)
+        eng.set_option("kernel_events", ev)
+        t = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
+        seq = [t]
+        for _ in range(4):
+            n0 = eng_mod.kernel_launches()
+            t = eng.next_token(t, top_p=0.0, repetition_penalty=1.0)
+            assert eng_mod.kernel_launches() - n0 == 2
+            seq.append(t)
+            k = eng.last_kernel_ms()
+            if ev:
+                assert 0.0 < k <= eng.last_device_ms()
+            else:
+                assert k == -1.0
+        toks[ev] = seq
+    assert toks[0] == toks[1]
+
+
 @PATHS
 def test_tiny_context_limit_and_errors(eng_mod, tiny_weights, path):
     sh = S.ModelShape(layers=2, hidden=256, heads=4, ffn=512, vocab=2048, max_ctx=40)

@@ -139,6 +139,14 @@ int xl_engine_last_device_ms(const xl_engine* e, float* ms) {
     return XL_OK;
 }
 
+int xl_engine_last_kernel_ms(const xl_engine* e, float* ms) {
+    if (!e || !ms) return bad("null argument");
+    *ms = e->impl->last_kernel_ms();
+    return XL_OK;
+}
+
+long long xl_kernel_launches(void) { return xl::launch_count(); }
+
 int xl_engine_set_option(xl_engine* e, const char* key, int value) {
     xl::clear_error();
     if (!e) return bad("null engine");

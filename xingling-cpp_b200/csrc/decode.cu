@@ -15,6 +15,8 @@
 //                     (src/inference.cu:58-114).
 #include <math.h>
 
+#include <atomic>
+
 #include <mutex>
 #include <string>
 
@@ -525,6 +527,7 @@ cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, bool pdl, c
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
+    count_launch();
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
@@ -581,6 +584,16 @@ constexpr int kMaxDevices = 64;
 void* g_scratch_addr[kMaxDevices] = {};
 std::mutex g_scratch_mu;
 }  // namespace
+
+namespace {
+std::atomic<long long> g_launches{0};  // kernels enqueued or recorded by the launchers
+std::atomic<long long> g_graphs{0};    // kernels run by graph replays, less those recorded at capture
+}  // namespace
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void count_graph_kernels(long long n) { g_graphs.fetch_add(n, std::memory_order_relaxed); }
+long long launch_count() {
+    return g_launches.load(std::memory_order_relaxed) + g_graphs.load(std::memory_order_relaxed);
+}
 
 }  // namespace xl
 

@@ -764,6 +764,7 @@ cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cud
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    count_launch();
     return cudaLaunchKernelEx(&cfg, decode_persistent_kernel, p);
 }
 

@@ -162,6 +162,8 @@ int Engine::init(const xl_config& cfg, int device, int tp_size, int tp_rank, con
     XL_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     XL_CUDA(cudaEventCreate(&ev0_));
     XL_CUDA(cudaEventCreate(&ev1_));
+    XL_CUDA(cudaEventCreate(&kev0_));
+    XL_CUDA(cudaEventCreate(&kev1_));
     XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_in_), sizeof(DevState), cudaHostAllocDefault));
     XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_out_), sizeof(DevState), cudaHostAllocDefault));
     XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_ids_), sizeof(int) * (T_ + 1), cudaHostAllocDefault));
@@ -260,6 +262,8 @@ Engine::~Engine() {
     if (trace_) cudaFree(trace_);
     if (ev0_) cudaEventDestroy(ev0_);
     if (ev1_) cudaEventDestroy(ev1_);
+    if (kev0_) cudaEventDestroy(kev0_);
+    if (kev1_) cudaEventDestroy(kev1_);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -469,7 +473,11 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     XL_CUDA(cudaMemsetAsync(
         done_, 0, (5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_) * sizeof(int),
         s));
+    // Optional event-record nodes around the kernel (kernel_events): its own
+    // duration, read back by last_kernel_ms.
+    if (kernel_events_) XL_CUDA(cudaEventRecordWithFlags(kev0_, s, cudaEventRecordExternal));
     XL_CUDA(launch_decode_persistent(p, num_sms_, s));
+    if (kernel_events_) XL_CUDA(cudaEventRecordWithFlags(kev1_, s, cudaEventRecordExternal));
     lm_x_ = xa_;
     SampleParams sp{};
     sp.logits = logits_;
@@ -483,7 +491,8 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
 }
 
 int Engine::enqueue_decode(cudaStream_t s) {
-    if (tp_ == 1 && decode_path_ == 0 && persistent_fits()) return enqueue_decode_persistent(s);
+    persistent_graph_ = tp_ == 1 && decode_path_ == 0 && persistent_fits();
+    if (persistent_graph_) return enqueue_decode_persistent(s);
     float* cur = xa_;
     float* other = xb_;
     bool pending = false;  // TP: part_ holds a reduced delta not yet added to cur
@@ -619,7 +628,10 @@ int Engine::capture_decode_graph() {
     }
     cudaGraph_t g = nullptr;
     XL_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    const long long recorded0 = launch_count();
     int rc = enqueue_decode(stream_);
+    decode_graph_kernels_ = launch_count() - recorded0;
+    count_graph_kernels(-decode_graph_kernels_);  // recorded, not run; each replay adds them
     cudaError_t ce = cudaStreamEndCapture(stream_, &g);
     if (rc != XL_OK) {
         if (g) cudaGraphDestroy(g);
@@ -778,8 +790,11 @@ int Engine::decode(int token, float temperature, float top_p, float rp, int* tok
     XL_CUDA(cudaMemcpyAsync(&st_->in, in, sizeof(StepIn), cudaMemcpyHostToDevice, stream_));
     XL_CUDA(cudaEventRecord(ev0_, stream_));
     XL_CUDA(cudaGraphLaunch(decode_exec_, stream_));
+    count_graph_kernels(decode_graph_kernels_);
     const int rc = finish_step(token_out);
     if (rc != XL_OK) return rc;
+    last_kernel_ms_ = -1.0f;
+    if (kernel_events_ && persistent_graph_) XL_CUDA(cudaEventElapsedTime(&last_kernel_ms_, kev0_, kev1_));
     n_ += 1;
     return XL_OK;
 }
@@ -834,6 +849,14 @@ int Engine::set_option(const char* key, int value) {
             return XL_ERR_ARG;
         }
         inflight_ = value;
+        return loaded_ ? capture_decode_graph() : XL_OK;
+    }
+    if (k == "kernel_events") {
+        if (value != 0 && value != 1) {
+            set_error("kernel_events must be 0 or 1");
+            return XL_ERR_ARG;
+        }
+        kernel_events_ = value != 0;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
     if (k == "phase_trace") {

@@ -53,6 +53,7 @@ class Engine {
     int phase_trace(unsigned long long* out, int n);
     int ctx_len() const { return n_; }
     float last_device_ms() const { return last_ms_; }
+    float last_kernel_ms() const { return last_kernel_ms_; }
     int vocab_begin() const { return v0_; }
     int vocab_count() const { return vl_; }
 
@@ -129,11 +130,16 @@ class Engine {
 
     int decode_path_ = 0;      // 0: persistent kernel (single GPU), 1: per-op kernels
     int prefill_gemm_ = 0;     // 0: tcgen05 3xTF32, 1: fp32 SIMT tiles
+    long long decode_graph_kernels_ = 0;  // kernels recorded in the decode graph
     int inflight_ = 2;  // persistent decode: weight boxes requested but not landed, per SM
     bool loaded_ = false;
     bool has_seq_ = false;
     int n_ = 0;
     float last_ms_ = 0.0f;
+    float last_kernel_ms_ = -1.0f;     // persistent kernel of the last decode step (kernel_events), or -1
+    bool kernel_events_ = false;       // event-record nodes around the persistent kernel in the decode graph
+    bool persistent_graph_ = false;    // the decode graph runs the persistent kernel
+    cudaEvent_t kev0_ = nullptr, kev1_ = nullptr;
     std::deque<float> uniforms_;
     uint64_t philox_seed_ = 0;
     uint64_t philox_ctr_ = 0;

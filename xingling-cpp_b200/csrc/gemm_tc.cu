@@ -339,6 +339,7 @@ cudaError_t launch_tc(dim3 grid, const TcOperands& o, const float* bias, float* 
     cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kGemmSmem));
     if (e != cudaSuccess) return e;
+    count_launch();
     gemm_tc_kernel<MODE><<<grid, kGemmThreads, kGemmSmem, s>>>(o.w, o.w_lo, o.x, o.x_lo, bias, C, C_lo, m, n, k, err);
     return cudaGetLastError();
 }
@@ -362,6 +363,7 @@ cudaError_t launch_gemm_tc(int mode, const TcOperands& o, const float* bias, flo
         if (e != cudaSuccess) return e;
         const size_t total = static_cast<size_t>(n) * (mode == kGemvSwiGLU ? m / 2 : m);
         const unsigned blocks = static_cast<unsigned>(std::min<size_t>((total + 255) / 256, 148 * 8));
+        count_launch();
         switch (mode) {
             case kGemvPlain:
                 splitk_reduce_kernel<kGemvPlain><<<blocks, 256, 0, s>>>(ws, slices, bias, C, C_lo, n, m);
@@ -392,6 +394,7 @@ cudaError_t launch_gemm_tc(int mode, const TcOperands& o, const float* bias, flo
 cudaError_t launch_split_lo(const float* x, float* lo, size_t n, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
     const size_t blocks = std::min<size_t>((n + 255) / 256, 148 * 16);
+    count_launch();
     split_lo_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, lo, n);
     return cudaGetLastError();
 }

@@ -327,6 +327,7 @@ constexpr size_t kAttnPrefillSmem = 4 * kAT * kAP * sizeof(float);
 
 cudaError_t launch_embed_gather(const float* table, const int* ids, float* out, int n, int k, cudaStream_t s) {
     if (n <= 0 || k % 4) return cudaErrorInvalidValue;
+    count_launch();
     embed_gather_kernel<<<n, 256, 0, s>>>(table, ids, out, k);
     return cudaGetLastError();
 }
@@ -334,6 +335,7 @@ cudaError_t launch_embed_gather(const float* table, const int* ids, float* out, 
 cudaError_t launch_rmsnorm_rows(const float* x, const float* gamma, float* out, float* out_lo, int n, int k,
                                 cudaStream_t s) {
     if (n <= 0 || k % 4) return cudaErrorInvalidValue;
+    count_launch();
     rmsnorm_rows_kernel<<<n, 256, 0, s>>>(x, gamma, out, out_lo, k, 1e-6);
     return cudaGetLastError();
 }
@@ -342,6 +344,7 @@ cudaError_t launch_linear_prefill(int mode, const float* X, const float* W, cons
                                   int k, cudaStream_t s) {
     if (n <= 0 || m <= 0 || k % kBK) return cudaErrorInvalidValue;
     dim3 grid((m + kBN - 1) / kBN, (n + kBM - 1) / kBM);
+    count_launch();
     switch (mode) {
         case kGemvPlain:
             sgemm_tn_kernel<kGemvPlain><<<grid, 256, 0, s>>>(X, W, b, Y, n, m, k);
@@ -361,6 +364,7 @@ cudaError_t launch_linear_prefill(int mode, const float* X, const float* W, cons
 
 cudaError_t launch_add_rows(float* x, const float* d, int n, cudaStream_t s) {
     if (n <= 0) return cudaErrorInvalidValue;
+    count_launch();
     add_rows_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, d, n);
     return cudaGetLastError();
 }
@@ -368,6 +372,7 @@ cudaError_t launch_add_rows(float* x, const float* d, int n, cudaStream_t s) {
 cudaError_t launch_rope_kv_prefill(float* qkv, const float2* rope, float* kc, float* vc, int n, int heads,
                                    int max_ctx, cudaStream_t s) {
     if (n <= 0 || n > max_ctx) return cudaErrorInvalidValue;
+    count_launch();
     rope_kv_prefill_kernel<<<dim3(n, heads), 32, 0, s>>>(qkv, rope, kc, vc, heads, max_ctx);
     return cudaGetLastError();
 }
@@ -378,6 +383,7 @@ cudaError_t launch_attn_prefill(const float* qkv, const float* kc, const float* 
     cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kAttnPrefillSmem));
     if (e != cudaSuccess) return e;
+    count_launch();
     attn_prefill_kernel<<<dim3((n + kAT - 1) / kAT, heads), 256, kAttnPrefillSmem, s>>>(qkv, kc, vc, out, out_lo, n,
                                                                                         heads, max_ctx);
     return cudaGetLastError();

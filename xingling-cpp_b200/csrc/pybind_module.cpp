@@ -147,6 +147,12 @@ class InferenceEngine {
         return ms;
     }
 
+    float last_kernel_ms() const {
+        float ms = 0.0f;
+        check(xl_engine_last_kernel_ms(e_, &ms));
+        return ms;
+    }
+
     void set_option(const std::string& key, int value) {
         int rc;
         {
@@ -190,6 +196,8 @@ class InferenceEngine {
 PYBIND11_MODULE(llm_cpp_engine, m) {
     m.doc() = "XingLing-0.68B token loop on NVIDIA B200 (sm_100a), drop-in for the reference's llm_cpp_engine";
 
+    m.def("kernel_launches", []() { return xl_kernel_launches(); },
+          "Kernels this library has run in this process (decode-graph kernels count at each replay).");
     m.def("nccl_unique_id", []() {
         std::string id(XL_NCCL_ID_BYTES, '\0');
         check(xl_nccl_unique_id(&id[0], XL_NCCL_ID_BYTES));
@@ -215,6 +223,7 @@ PYBIND11_MODULE(llm_cpp_engine, m) {
         .def("kv", &InferenceEngine::kv, py::arg("layer"), py::arg("npos"), py::arg("heads_local"))
         .def("ctx_len", &InferenceEngine::ctx_len)
         .def("last_device_ms", &InferenceEngine::last_device_ms)
+        .def("last_kernel_ms", &InferenceEngine::last_kernel_ms)
         .def("set_option", &InferenceEngine::set_option, py::arg("key"), py::arg("value"))
         .def("phase_trace", &InferenceEngine::phase_trace, py::arg("n"))
         .def("profile_lm_head", &InferenceEngine::profile_lm_head, py::arg("iters") = 20)

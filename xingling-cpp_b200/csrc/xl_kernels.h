@@ -77,6 +77,13 @@ constexpr int kAttnChunk = 64;
 __host__ __device__ inline int attn_max_splits(int max_ctx) { return (max_ctx + kAttnChunk - 1) / kAttnChunk; }
 cudaError_t launch_attn_decode(const AttnDecodeParams& p, bool pdl, cudaStream_t s);
 
+// Kernels this library ran, process-wide: each launcher counts the kernel it
+// enqueues (or records, during a stream capture); a graph's owner subtracts
+// the recorded kernels once and adds them back at every replay.
+void count_launch();
+void count_graph_kernels(long long n);
+long long launch_count();
+
 // Persistent decode step (decode_persistent.cu): one cooperative launch per token.
 constexpr int kMaxLayers = 32;
 constexpr int kPersistChunk = 32;     // attention positions per warp
