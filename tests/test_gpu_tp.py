@@ -1,11 +1,20 @@
 """Tensor-parallel decode on two GPUs (skipped with fewer): two spawned ranks,
 each one shard of the engine on its own GPU with the engine's own NCCL
 communicator (rank 0's id handed over through a queue), against the oracle
-port on the same weight tree.  Greedy and teacher-forced on the oracle's ids;
-the ranks' vocab shards, concatenated, must match the oracle's logits within
-1e-3 of their range, and every rank must return the same id (the greedy merge
-of per-shard (value, id) maxima).  NVLS stays off: a rank that fails must not
-leave memory bound to an NVLink multicast object."""
+port on the same weight tree.
+
+* Greedy, teacher-forced on the oracle's ids: the ranks' vocab shards,
+  concatenated, match the oracle's logits within 1e-3 of their range, and
+  every rank returns the same id (the greedy merge of per-shard maxima).
+* Sampled (temperature 0.7, top_p 0.9, repetition penalty 1.1, the same
+  Philox uniforms queued on both ranks), free-running: every rank returns the
+  same id, which is exactly sample_cpu's draw on the concatenated penalised
+  logits (the all-gather merge of per-shard top-1024 lists), and those logits
+  match the oracle's, penalised with the engine's own history, within 1e-3 of
+  their range.
+
+NVLS stays off: a rank that fails must not leave memory bound to an NVLink
+multicast object."""
 import os
 import queue
 import sys
@@ -28,7 +37,7 @@ def _gpus() -> int:
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _rank(rank, world, wdir, shape_kw, ids, teach, q_id, q_out):
+def _rank(rank, world, wdir, shape_kw, ids, teach, q_id, q_out, sampled=None):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     sys.path[:0] = [os.path.join(ROOT, "xingling-cpp_b200")]
     try:
@@ -43,24 +52,35 @@ def _rank(rank, world, wdir, shape_kw, ids, teach, q_id, q_out):
         eng = m.InferenceEngine(f"cuda:{rank}", tp=world, rank=rank, nccl_id=ident, **shape_kw)
         eng.load(wdir)
         toks, logits = [], []
-        tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
-        toks.append(tok)
-        logits.append(np.frombuffer(eng.last_logits(), np.float32).copy())
-        for t in teach:
-            tok = eng.next_token(int(t), top_p=0.0, repetition_penalty=1.0)
+        if sampled is None:
+            tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
             toks.append(tok)
             logits.append(np.frombuffer(eng.last_logits(), np.float32).copy())
+            for t in teach:
+                tok = eng.next_token(int(t), top_p=0.0, repetition_penalty=1.0)
+                toks.append(tok)
+                logits.append(np.frombuffer(eng.last_logits(), np.float32).copy())
+        else:
+            T, P, RP, uniforms = sampled
+            eng.set_uniforms([float(u) for u in uniforms])
+            tok = eng.next_token(ids, temperature=T, top_p=P, repetition_penalty=RP)
+            toks.append(tok)
+            logits.append(np.frombuffer(eng.last_logits(), np.float32).copy())
+            for _ in range(len(uniforms) - 1):
+                tok = eng.next_token(tok, temperature=T, top_p=P, repetition_penalty=RP)
+                toks.append(tok)
+                logits.append(np.frombuffer(eng.last_logits(), np.float32).copy())
         q_out.put((rank, "ok", toks, logits, eng.vocab_shard()))
     except Exception as e:  # noqa: BLE001
         q_out.put((rank, "error", repr(e)[:400], None, None))
 
 
-def _run_tp(wdir, shape, ids, teach):
+def _run_tp(wdir, shape, ids, teach, sampled=None):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q_id, q_out = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, WORLD, wdir, shape.engine_kwargs(), ids, teach, q_id, q_out))
+    procs = [ctx.Process(target=_rank, args=(r, WORLD, wdir, shape.engine_kwargs(), ids, teach, q_id, q_out, sampled))
              for r in range(WORLD)]
     for p in procs:
         p.start()
@@ -113,3 +133,41 @@ def test_tp2_greedy_matches_oracle(built, shape_name):
         if tok != want:
             a = np.partition(ref, -2)[-2:]
             assert a[1] - a[0] < 1e-3 * span, f"step {step}: token {tok} != oracle {want}"
+
+
+def _check_ranks(out, shape):
+    assert sorted(out) == list(range(WORLD)), f"ranks missing: {out}"
+    for r in range(WORLD):
+        assert out[r][1] == "ok", out[r][2]
+    shards = [out[r][4] for r in range(WORLD)]
+    assert shards[0][0] == 0 and shards[-1][0] + shards[-1][1] == shape.vocab
+    for r in range(1, WORLD):
+        assert shards[r][0] == shards[r - 1][0] + shards[r - 1][1]
+
+
+@pytest.mark.parametrize("shape_name", ["TINY", "WIDE2"])
+def test_tp2_sampled_merge_matches_sample_cpu(built, shape_name):
+    if _gpus() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    shape = getattr(S, shape_name)
+    wdir = S.write_weight_tree(os.path.join("/tmp/xl_weights", shape_name.lower()), shape)
+    T, P, RP = 0.7, 0.9, 1.1
+    uniforms = S.philox_uniforms(3, 12)
+    ids = S.prompt_ids(2, 41, shape.vocab)
+    out = _run_tp(wdir, shape, ids, [], sampled=(T, P, RP, uniforms))
+    _check_ranks(out, shape)
+    port = O.Port(shape)
+    port.load(wdir)
+    history = []
+    for step, r in enumerate(uniforms):
+        toks = {out[q][2][step] for q in range(WORLD)}
+        assert len(toks) == 1, f"step {step}: ranks disagree {toks}"
+        tok = toks.pop()
+        got = np.concatenate([out[q][3][step] for q in range(WORLD)])
+        assert tok == O.sample(got, T, P, 1.0, [], float(r)), f"step {step}: merged draw differs from sample_cpu"
+        ref = port.prefill(ids) if step == 0 else port.decode(out[0][2][step - 1])
+        ref_pen = O.apply_penalty(ref, history, RP)
+        span = float(ref_pen.max() - ref_pen.min())
+        err = float(np.abs(got - ref_pen).max())
+        assert err <= 1e-3 * span, f"step {step}: max |dlogit| {err:.3e} > 1e-3 x {span:.3f}"
+        history.append(tok)

@@ -349,6 +349,46 @@ __device__ int block_inclusive_scan(int v, int* warp_tot) {
     return v + add;
 }
 
+// Temperature, softmax over the kc sorted candidates (packed (key, ~global
+// id)), top-p and the draw with the step's uniform: the arithmetic of
+// src/inference.cu:87-111, sequential float sums in candidate order on one
+// thread.  All threads of the block call it; thread 0 writes *s_token.
+__device__ void draw_token(const unsigned long long* cand, int kc, float* prob, const DevState* st, int* s_token) {
+    const int tid = threadIdx.x;
+    const float top_p = st->in.top_p;
+    const float inv_t_den = st->in.temperature + 0.001f;
+    const float v0 = key_float(static_cast<uint32_t>(cand[0] >> 32)) / inv_t_den;
+    float e = 0.0f;
+    if (tid < kc) {
+        const float v = key_float(static_cast<uint32_t>(cand[tid] >> 32)) / inv_t_den;
+        e = expf(v - v0);
+    }
+    prob[tid] = e;
+    __syncthreads();
+    if (tid == 0) {
+        float sum_exp = 1.0f;
+        for (int i = 1; i < kc; ++i) sum_exp += prob[i];
+        prob[0] = prob[0] / sum_exp;
+        for (int i = 1; i < kc; ++i) prob[i] = prob[i] / sum_exp;
+        float total = 0.0f;
+        for (int i = 0; i < kc; ++i) {
+            total += prob[i];
+            if (total >= top_p) break;
+        }
+        const float r = st->in.uniform;
+        float acc = 0.0f;
+        int pick = kc - 1;
+        for (int i = 0; i < kc; ++i) {
+            acc += prob[i];
+            if (acc > r * total) {
+                pick = i;
+                break;
+            }
+        }
+        *s_token = static_cast<int>(0xffffffffu - static_cast<uint32_t>(cand[pick] & 0xffffffffull));
+    }
+}
+
 __global__ void __launch_bounds__(kSampThreads) sample_kernel(const SampleParams p) {
     __shared__ unsigned int hist[2048];
     __shared__ unsigned long long cand[kTopK];
@@ -438,7 +478,7 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const SampleParams
             const unsigned bg = __ballot_sync(0xffffffffu, gt);
             const unsigned be = __ballot_sync(0xffffffffu, eq);
             const unsigned long long packed =
-                (static_cast<unsigned long long>(k) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
+                (static_cast<unsigned long long>(k) << 32) | (0xffffffffu - static_cast<uint32_t>(p.v0 + i));
             if (gt) {
                 const int at = off_gt + __popc(bg & lt);
                 if (at < n_gt) cand[at] = packed;
@@ -468,40 +508,60 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const SampleParams
                 __syncthreads();
             }
         }
+        if (p.cand_out) {
+            // Tensor-parallel select: this shard's sorted top-kc, merged across ranks by sample_merge_kernel.
+            for (int i = tid; i < kTopK; i += kSampThreads) p.cand_out[i] = cand[i];
+            return;
+        }
         // --- temperature, softmax over the candidates, top-p, draw ---
-        const float inv_t_den = st->in.temperature + 0.001f;
-        const float v0 = key_float(static_cast<uint32_t>(cand[0] >> 32)) / inv_t_den;
-        float e = 0.0f;
-        if (tid < kc) {
-            const float v = key_float(static_cast<uint32_t>(cand[tid] >> 32)) / inv_t_den;
-            e = expf(v - v0);
-        }
-        prob[tid] = e;
+        draw_token(cand, kc, prob, st, &s_token);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const int tok = s_token;
+        st->token_out = tok;
+        const int local = tok - p.v0;
+        if (local >= 0 && local < p.V) p.rep_flags[local] = 1;
+        if (st->in.decode_mode) st->pos += 1;
+    }
+}
+
+// Tensor-parallel merge of sample_cpu (src/inference.cu:58-114) over vocab
+// shards: every rank holds the same all-gathered candidate lists (each shard's
+// sorted top-1024, packed (key, ~global id)), sorts their union by value (ties:
+// lower id first), keeps the top min(V, 1024) and draws exactly as the
+// single-GPU sampler does, with the same uniform on every rank, so all ranks
+// agree on the id.  Greedy steps take the all-reduced argmax instead.
+__global__ void __launch_bounds__(kSampThreads) sample_merge_kernel(const SampleMergeParams p) {
+    extern __shared__ unsigned long long all[];  // n_pad packed candidates
+    __shared__ float prob[kTopK];
+    __shared__ int s_token;
+    pdl_launch_dependents();
+    pdl_wait();
+    DevState* st = p.st;
+    const int tid = threadIdx.x;
+    if (!(st->in.top_p > 0.0f)) {
+        if (tid == 0) s_token = unpack_argmax_index(st->argmax_final);
+    } else {
+        for (int i = tid; i < p.n_pad; i += kSampThreads) all[i] = i < p.n ? p.cand[i] : 0ull;
         __syncthreads();
-        if (tid == 0) {
-            // Sequential float sums in candidate order, as src/inference.cu:87-111.
-            float sum_exp = 1.0f;
-            for (int i = 1; i < kc; ++i) sum_exp += prob[i];
-            s_token = 0;
-            prob[0] = prob[0] / sum_exp;
-            for (int i = 1; i < kc; ++i) prob[i] = prob[i] / sum_exp;
-            float total = 0.0f;
-            for (int i = 0; i < kc; ++i) {
-                total += prob[i];
-                if (total >= top_p) break;
-            }
-            const float r = st->in.uniform;
-            float acc = 0.0f;
-            int pick = kc - 1;
-            for (int i = 0; i < kc; ++i) {
-                acc += prob[i];
-                if (acc > r * total) {
-                    pick = i;
-                    break;
+        for (int k = 2; k <= p.n_pad; k <<= 1) {
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                for (int i = tid; i < p.n_pad; i += kSampThreads) {
+                    const int ixj = i ^ j;
+                    if (ixj > i) {
+                        const unsigned long long a = all[i], b = all[ixj];
+                        const bool desc = (i & k) == 0;
+                        if (desc ? (a < b) : (a > b)) {
+                            all[i] = b;
+                            all[ixj] = a;
+                        }
+                    }
                 }
+                __syncthreads();
             }
-            s_token = static_cast<int>(0xffffffffu - static_cast<uint32_t>(cand[pick] & 0xffffffffull));
         }
+        draw_token(all, p.V_total < kTopK ? p.V_total : kTopK, prob, st, &s_token);
     }
     __syncthreads();
     if (tid == 0) {
@@ -560,6 +620,17 @@ cudaError_t launch_attn_decode(const AttnDecodeParams& p, bool pdl, cudaStream_t
 
 cudaError_t launch_sample(const SampleParams& p, bool pdl, cudaStream_t s) {
     return launch_ex(sample_kernel, dim3(1), dim3(kSampThreads), 0, pdl, s, p);
+}
+
+cudaError_t launch_sample_merge(const SampleMergeParams& p, bool pdl, cudaStream_t s) {
+    if (p.n <= 0 || p.n_pad < p.n || p.n_pad > kMaxMergeCandidates || (p.n_pad & (p.n_pad - 1))) {
+        return cudaErrorInvalidValue;
+    }
+    const size_t smem = static_cast<size_t>(p.n_pad) * sizeof(unsigned long long);
+    cudaError_t e = cudaFuncSetAttribute(sample_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    return launch_ex(sample_merge_kernel, dim3(1), dim3(kSampThreads), smem, pdl, s, p);
 }
 
 void set_error(const std::string& msg);

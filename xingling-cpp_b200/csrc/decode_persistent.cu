@@ -64,6 +64,7 @@ constexpr int kErrMbar = 1, kErrFlag = 2;
 constexpr int kAttnWarpScratch = kHeadDim;
 constexpr int kAttnPartStride = kHeadDim + 4;
 constexpr int kStageQuads = kMaxK / 4 / kConsumerThreads;  // float4 of a staged vector per consumer thread
+constexpr int kPreGroups = 4;  // row groups per CTA whose biases are loaded before the phase wait
 
 static_assert(kPersistTileRows == 2 * kConsumerWarps, "each consumer warp owns two rows of a box");
 static_assert(kConsumerWarps * (kAttnWarpScratch + kAttnPartStride) <= kMaxK, "attention scratch fits in xs");
@@ -275,13 +276,14 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
 // ---------------------------------------------------------------------------
 // Consumer helpers (256 threads, named barrier 1).
 
-// Wait until every CTA finished phase ph (counter == gridDim.x).
+// Wait until every consumer warp of every CTA finished phase ph (counter ==
+// 8 x gridDim.x).
 __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
     if (threadIdx.x == 32) {
         const int* c = p.done + ph;
         uint32_t it = 0;
         int ok = 1;
-        while (ld_acquire(c) < static_cast<int>(gridDim.x)) {
+        while (ld_acquire(c) < static_cast<int>(gridDim.x) * kConsumerWarps) {
             if (++it >= kFlagSpinLimit || ((it & 255u) == 0 && aborted(p.st))) {
                 atomicOr(&p.st->err, kErrFlag);
                 ok = 0;
@@ -294,9 +296,12 @@ __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
     return *s_ok != 0;
 }
 
+// Each warp publishes its own stores of phase ph as soon as it has issued
+// them: lane 0 releases (cumulative over the warp's lanes, ordered by the
+// __syncwarp) and adds 1 to the counter, so no warp waits for its CTA.
 __device__ void signal_phase(const PersistentParams& p, int ph) {
-    consumer_sync();
-    if (threadIdx.x == 32) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.done + ph) : "memory");
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.done + ph) : "memory");
 }
 
 // Block-wide (consumers) sum of one float per thread.
@@ -579,11 +584,27 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
             if (t == 0) trace_at(p, ph, kTrConsEnd);
             continue;
         }
-        if (ph > 0 && !wait_phase(p, ph - 1, s_ok)) return;
-        if (t == 0) trace_at(p, ph, kTrConsStart);
         const int l = ph / 5;
         const LayerPtrs* y = ph < last ? &p.layer[l] : nullptr;
         const Gemv d = gemv_of(p, ph);
+        const Boxes r = boxes_of(d);
+        const int ra = 2 * warp, rb = ra + 1;
+        // Biases of this CTA's first groups (QKV, W1/V), loaded before the wait so
+        // that their latency hides behind it.
+        const int g_first = r.t0 / r.nb;
+        float pre_a[kPreGroups], pre_b[kPreGroups];
+        if (kind == kQKV || kind == kW13) {
+#pragma unroll
+            for (int i = 0; i < kPreGroups; ++i) {
+                const int g = g_first + i;
+                if (g * r.nb < r.t1) {
+                    pre_a[i] = d.bias[g * kPersistTileRows + ra];
+                    pre_b[i] = d.bias[g * kPersistTileRows + rb];
+                }
+            }
+        }
+        if (ph > 0 && !wait_phase(p, ph - 1, s_ok)) return;
+        if (t == 0) trace_at(p, ph, kTrConsStart);
         // Stage this phase's input vector.
         if (kind == kQKV) {
             if (l == 0)
@@ -602,10 +623,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
         }
         consumer_sync();
         if (t == 0) trace_at(p, ph, kTrConsStaged);
-        const Boxes r = boxes_of(d);
         const int rs4 = r.kd * (kPersistTileK / 4);  // float4 per row of a box
         const float4* x4 = reinterpret_cast<const float4*>(xs);
-        const int ra = 2 * warp, rb = ra + 1;
         const bool split = kind == kWo || kind == kW2;
         for (int tau = r.t0; tau < r.t1;) {
             const int g = tau / r.nb;
@@ -619,8 +638,14 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 if (va) ea = p.rep_flags[Ra] ? 1.0f : 0.0f;
                 if (vb) eb = p.rep_flags[Rb] ? 1.0f : 0.0f;
             } else if (!split) {
-                if (va) ea = d.bias[Ra];
-                if (vb) eb = d.bias[Rb];
+                const int gi = g - g_first;
+                if (gi < kPreGroups) {
+                    ea = pre_a[gi];
+                    eb = pre_b[gi];
+                } else {
+                    if (va) ea = d.bias[Ra];
+                    if (vb) eb = d.bias[Rb];
+                }
             }
             float acc_a = 0.0f, acc_b = 0.0f;
             for (int bi = bi0; bi < bi1; ++bi) {

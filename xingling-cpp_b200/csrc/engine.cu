@@ -178,6 +178,10 @@ int Engine::init(const xl_config& cfg, int device, int tp_size, int tp_rank, con
         }
         ncclUniqueId id;
         std::memcpy(&id, nccl_id, sizeof(id));
+        // Every rank must draw the same uniforms: seed Philox from the shared id (FNV-1a).
+        uint64_t h = 1469598103934665603ull;
+        for (size_t i = 0; i < sizeof(id); ++i) h = (h ^ static_cast<unsigned char>(id.internal[i])) * 1099511628211ull;
+        philox_seed_ = h;
         XL_NCCL(ncclCommInitRank(&comm_, tp_, id, rank_));
     }
     return XL_OK;
@@ -216,6 +220,8 @@ int Engine::alloc_all() {
     add(&att_, Hl * 4);
     add(&ffh_, Fl * 4);
     add(&part_, H * 4);
+    add(&cand_local_, kTopK * 8);
+    add(&cand_all_, static_cast<size_t>(tp_) * kTopK * 8);
     add(&cres_, H / kPersistTileRows * kPersistMaxContrib * kPersistTileRows * 4);
     add(&logits_, vl * 4);
     add(&attn_ws_, static_cast<size_t>(heads_l_) * maxs * (kHeadDim + 2) * 4);
@@ -254,6 +260,7 @@ Engine::~Engine() {
     cudaSetDevice(device_);
     if (stream_) cudaStreamSynchronize(stream_);
     if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
+    if (decode_exec_s_) cudaGraphExecDestroy(decode_exec_s_);
     if (comm_) ncclCommDestroy(comm_);
     if (arena_) cudaFree(arena_);
     if (h_in_) cudaFreeHost(h_in_);
@@ -490,7 +497,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     return XL_OK;
 }
 
-int Engine::enqueue_decode(cudaStream_t s) {
+int Engine::enqueue_decode(cudaStream_t s, bool sampled) {
     persistent_graph_ = tp_ == 1 && decode_path_ == 0 && persistent_fits();
     if (persistent_graph_) return enqueue_decode_persistent(s);
     float* cur = xa_;
@@ -584,7 +591,7 @@ int Engine::enqueue_decode(cudaStream_t s) {
         }
     }
     lm_x_ = cur;
-    return run_lm_head_and_sample(cur, pending ? part_ : nullptr, s);
+    return run_lm_head_and_sample(cur, pending ? part_ : nullptr, s, sampled);
 }
 
 // Final norm + tied LM head (Embedding::inverse, src/embedding.cu:173-205)
@@ -606,7 +613,7 @@ int Engine::launch_lm_head(const float* x_last, const float* delta, bool pdl, cu
     return XL_OK;
 }
 
-int Engine::run_lm_head_and_sample(const float* x_last, const float* delta, cudaStream_t s) {
+int Engine::run_lm_head_and_sample(const float* x_last, const float* delta, cudaStream_t s, bool sampled) {
     const int rc = launch_lm_head(x_last, delta, true, s);
     if (rc != XL_OK) return rc;
     if (tp_ > 1) XL_NCCL(ncclAllReduce(&st_->argmax_final, &st_->argmax_final, 1, ncclUint64, ncclMax, comm_, s));
@@ -617,30 +624,54 @@ int Engine::run_lm_head_and_sample(const float* x_last, const float* delta, cuda
     sp.st = st_;
     sp.rep_flags = rep_flags_;
     sp.full = 0;
+    if (tp_ > 1 && sampled) {
+        // Sampling merge across vocab shards: local top-1024, all-gather, one draw on every rank.
+        sp.full = 1;
+        sp.cand_out = cand_local_;
+        XL_CUDA(launch_sample(sp, true, s));
+        XL_NCCL(ncclAllGather(cand_local_, cand_all_, kTopK, ncclUint64, comm_, s));
+        SampleMergeParams mp{};
+        mp.cand = cand_all_;
+        mp.n = tp_ * kTopK;
+        mp.n_pad = kTopK;
+        while (mp.n_pad < mp.n) mp.n_pad <<= 1;
+        mp.V_total = V_;
+        mp.st = st_;
+        mp.rep_flags = rep_flags_;
+        mp.V = vl_;
+        mp.v0 = v0_;
+        XL_CUDA(launch_sample_merge(mp, false, s));
+        return XL_OK;
+    }
     XL_CUDA(launch_sample(sp, true, s));
     return XL_OK;
 }
 
 int Engine::capture_decode_graph() {
-    if (decode_exec_) {
-        cudaGraphExecDestroy(decode_exec_);
-        decode_exec_ = nullptr;
+    for (int sampled = 0; sampled < 2; ++sampled) {
+        cudaGraphExec_t& exec = sampled ? decode_exec_s_ : decode_exec_;
+        long long& kernels = sampled ? decode_graph_kernels_s_ : decode_graph_kernels_;
+        if (exec) {
+            cudaGraphExecDestroy(exec);
+            exec = nullptr;
+        }
+        if (sampled && tp_ == 1) break;  // one graph serves both on a single GPU
+        cudaGraph_t g = nullptr;
+        XL_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+        const long long recorded0 = launch_count();
+        int rc = enqueue_decode(stream_, sampled != 0);
+        kernels = launch_count() - recorded0;
+        count_graph_kernels(-kernels);  // recorded, not run; each replay adds them
+        cudaError_t ce = cudaStreamEndCapture(stream_, &g);
+        if (rc != XL_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+        ce = cudaGraphInstantiate(&exec, g, 0);
+        cudaGraphDestroy(g);
+        if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
     }
-    cudaGraph_t g = nullptr;
-    XL_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
-    const long long recorded0 = launch_count();
-    int rc = enqueue_decode(stream_);
-    decode_graph_kernels_ = launch_count() - recorded0;
-    count_graph_kernels(-decode_graph_kernels_);  // recorded, not run; each replay adds them
-    cudaError_t ce = cudaStreamEndCapture(stream_, &g);
-    if (rc != XL_OK) {
-        if (g) cudaGraphDestroy(g);
-        return rc;
-    }
-    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
-    ce = cudaGraphInstantiate(&decode_exec_, g, 0);
-    cudaGraphDestroy(g);
-    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
     return XL_OK;
 }
 
@@ -681,10 +712,6 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
     if (n > T_) {
         set_error("Input sequence length exceeds max_seq_len (" + std::to_string(n) + " > " + std::to_string(T_) + ")");
         return XL_ERR_CTX;
-    }
-    if (tp_ > 1 && top_p > 0.0f) {
-        set_error("tensor-parallel engines sample greedily only (top_p <= 0)");
-        return XL_ERR_ARG;
     }
     for (int i = 0; i < n; ++i) {
         if (ids[i] < 0 || ids[i] >= V_) {
@@ -747,7 +774,7 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
         }
     }
     if (rc != XL_OK) return rc;
-    rc = run_lm_head_and_sample(px_ + static_cast<size_t>(n - 1) * H, nullptr, s);
+    rc = run_lm_head_and_sample(px_ + static_cast<size_t>(n - 1) * H, nullptr, s, top_p > 0.0f);
     if (rc != XL_OK) return rc;
     rc = finish_step(token_out);
     if (rc != XL_OK) return rc;
@@ -775,10 +802,6 @@ int Engine::decode(int token, float temperature, float top_p, float rp, int* tok
         set_error("KV cache full: position " + std::to_string(n_) + " of max_seq_len " + std::to_string(T_));
         return XL_ERR_CTX;
     }
-    if (tp_ > 1 && top_p > 0.0f) {
-        set_error("tensor-parallel engines sample greedily only (top_p <= 0)");
-        return XL_ERR_ARG;
-    }
     StepIn* in = h_in_;
     std::memset(in, 0, sizeof(StepIn));
     in->token_in = token;
@@ -789,8 +812,9 @@ int Engine::decode(int token, float temperature, float top_p, float rp, int* tok
     in->decode_mode = 1;
     XL_CUDA(cudaMemcpyAsync(&st_->in, in, sizeof(StepIn), cudaMemcpyHostToDevice, stream_));
     XL_CUDA(cudaEventRecord(ev0_, stream_));
-    XL_CUDA(cudaGraphLaunch(decode_exec_, stream_));
-    count_graph_kernels(decode_graph_kernels_);
+    const bool use_sampled = tp_ > 1 && top_p > 0.0f;
+    XL_CUDA(cudaGraphLaunch(use_sampled ? decode_exec_s_ : decode_exec_, stream_));
+    count_graph_kernels(use_sampled ? decode_graph_kernels_s_ : decode_graph_kernels_);
     const int rc = finish_step(token_out);
     if (rc != XL_OK) return rc;
     last_kernel_ms_ = -1.0f;

@@ -62,7 +62,7 @@ class Engine {
     int init(const xl_config& cfg, int device, int tp_size, int tp_rank, const void* nccl_id);
     int alloc_all();
     int capture_decode_graph();
-    int enqueue_decode(cudaStream_t s);
+    int enqueue_decode(cudaStream_t s, bool sampled);
     int enqueue_decode_persistent(cudaStream_t s);
     // The persistent kernel streams K in 256-float tiles of at most 4096 floats,
     // runs at most one attention item per SM and lets at most
@@ -77,7 +77,7 @@ class Engine {
     int prepare_prefill_operands();
     int prefill_linear(int mode, const TcOperands& o, const float* x, const float* w, const float* b, float* y,
                        float* y_lo, int n, int m, int k, cudaStream_t s);
-    int run_lm_head_and_sample(const float* x_last, const float* delta, cudaStream_t s);
+    int run_lm_head_and_sample(const float* x_last, const float* delta, cudaStream_t s, bool sampled);
     int launch_lm_head(const float* x_last, const float* delta, bool pdl, cudaStream_t s);
     const float* lm_x_ = nullptr;  // residual stream the decode graph's LM head reads
     int finish_step(int* token_out);
@@ -126,6 +126,9 @@ class Engine {
     cudaStream_t stream_ = nullptr;
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
     cudaGraphExec_t decode_exec_ = nullptr;
+    cudaGraphExec_t decode_exec_s_ = nullptr;  // tensor parallel: the sampled step (candidate merge)
+    long long decode_graph_kernels_s_ = 0;
+    unsigned long long *cand_local_ = nullptr, *cand_all_ = nullptr;  // tensor-parallel sampling merge
     ncclComm_t comm_ = nullptr;
 
     int decode_path_ = 0;      // 0: persistent kernel (single GPU), 1: per-op kernels

@@ -167,8 +167,24 @@ struct SampleParams {
     DevState* st;
     uint8_t* rep_flags;    // [V]
     int full;              // 1: always run the full top-k path (no argmax shortcut)
+    unsigned long long* cand_out;  // tensor parallel: write the shard's sorted top-1024 here, draw nothing
 };
 cudaError_t launch_sample(const SampleParams& p, bool pdl, cudaStream_t s);
+
+// Tensor-parallel sampling merge: the all-gathered per-shard candidate lists
+// (packed (value key, ~global id), n = tp x 1024), sorted as one; draws as
+// sample_kernel does.  n_pad: n rounded up to a power of two.
+constexpr int kMaxMergeCandidates = 8 * kTopK;
+struct SampleMergeParams {
+    const unsigned long long* cand;
+    int n, n_pad;
+    int V_total;           // full vocabulary (the candidate count is min(V_total, 1024))
+    DevState* st;
+    uint8_t* rep_flags;    // [V] this rank's shard
+    int V;                 // shard size
+    int v0;                // global id of shard row 0
+};
+cudaError_t launch_sample_merge(const SampleMergeParams& p, bool pdl, cudaStream_t s);
 
 // ---- prefill on tcgen05 (gemm_tc.cu) ----
 // Operand maps of one projection: W and W_lo ([M][K]), X and X_lo ([rows][K]),
