@@ -372,6 +372,7 @@ def xl_arm(args) -> None:
     flops = prefill_flops(shape, PREFILL_N)
     tf32_peak = float(pk.get("bf16_tflops", 1590.0)) / 2.0
 
+    batch_info = replica_batch(eng, rank, world, max_over_ranks, barrier)
     tp_info = None
     if world > 1:
         tp_info = tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks)
@@ -409,6 +410,7 @@ def xl_arm(args) -> None:
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    line["replica_batch"] = batch_info
     if tp_info is not None:
         line["tp"] = tp_info
     print(json.dumps(line))
@@ -441,6 +443,35 @@ def tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks) -
     del eng
     return {"tp": world, "prompt": 64, "decode_tokens": n_dec, "ms_per_token": dev / n_dec,
             "tokens_per_s": n_dec / (dev / 1e3), "first_tokens": toks[:8]}
+
+
+def replica_batch(eng, rank, world, max_over_ranks, barrier) -> dict:
+    """64 independent sequences over the ranks' replicas: prompt lengths uniform
+    in [16, 512] and ids uniform (seed 5), 128 sampled tokens each (T 0.7,
+    top_p 0.9, repetition penalty 1.1, Philox seed 5000 + sequence).  Reports
+    the box's aggregate decode tokens/s over prefill + decode time."""
+    import numpy as np
+
+    rng = np.random.default_rng(5)
+    lens = rng.integers(16, 513, size=64)
+    seqs = [[int(t) for t in rng.integers(0, S.FULL.vocab, size=int(n))] for n in lens]
+    mine = list(range(rank, 64, world))
+    barrier()
+    dev_ms, w0 = 0.0, time.perf_counter()
+    for j in mine:
+        eng.seed(5000 + j)
+        tok = eng.next_token(seqs[j], temperature=0.7, top_p=0.9, repetition_penalty=1.1)
+        dev_ms += eng.last_device_ms()
+        for _ in range(DECODE):
+            tok = eng.next_token(tok, temperature=0.7, top_p=0.9, repetition_penalty=1.1)
+            dev_ms += eng.last_device_ms()
+    wall = time.perf_counter() - w0
+    dev_s = max_over_ranks(dev_ms / 1e3)
+    wall = max_over_ranks(wall)
+    tokens = 64 * DECODE
+    return {"sequences": 64, "prompt_len": "uniform [16, 512], seed 5", "decode_tokens_each": DECODE,
+            "sampling": "T 0.7, top_p 0.9, rp 1.1", "replicas": world, "tokens_per_s": tokens / dev_s,
+            "e2e_tokens_per_s": tokens / wall, "timing": "device time of every prefill and decode step; max over ranks"}
 
 
 def ncu_case(args) -> None:

@@ -145,6 +145,9 @@ XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, fl
  *                    own duration (costs the sampler its early launch);
  *   "prefill_gemm" 0  prefill projections on tcgen05 with the 3xTF32 split
  *                     (default); 1  fp32 FMA tiles.
+ *   "prefill_attn" 0  prefill attention on tcgen05 with the 3xTF32 split:
+ *                     S = q k^T per head, causal row softmax, P v (default);
+ *                  1  fp32 FMA flash-style tiles with online softmax.
  * Changing an option re-captures the decode graph. */
 XL_API int xl_engine_set_option(xl_engine* e, const char* key, int value);
 /* The last decode step's phase timeline: n = SMs x (5 x layers + 1) x 5

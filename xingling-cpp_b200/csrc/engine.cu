@@ -240,6 +240,15 @@ int Engine::alloc_all() {
     add(&patt_lo_, T * H * 4);
     add(&pffh_lo_, T * Fl * 4);
     add(&pids_, T * 4);
+    // tensor-core prefill attention (transient, shared by the layers)
+    add(&aq_, T * Hl * 4);
+    add(&aq_lo_, T * Hl * 4);
+    add(&ak_, T * Hl * 4);
+    add(&ak_lo_, T * Hl * 4);
+    add(&avt_, T * Hl * 4);
+    add(&avt_lo_, T * Hl * 4);
+    add(&ap_, static_cast<size_t>(heads_l_) * T * T * 4);
+    add(&ap_lo_, static_cast<size_t>(heads_l_) * T * T * 4);
     size_t total = 0;
     for (auto& pr : plan) total += align_up(pr.second, 256);
     XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&arena_), total));
@@ -416,6 +425,17 @@ int Engine::prepare_prefill_operands() {
         XL_CUDA(make_tile_map(&L.tc_w2.w_lo, L.w2_lo, H_, Fl_));
         XL_CUDA(make_tile_map(&L.tc_w2.x, pffh_, T_, Fl_));
         XL_CUDA(make_tile_map(&L.tc_w2.x_lo, pffh_lo_, T_, Fl_));
+    }
+    // tensor-core prefill attention: S = (q/8) k^T, then P v (its key blocks need T % 32 == 0)
+    if (T_ % 32 == 0) {
+        XL_CUDA(make_tile_map(&tc_attn_s_.x, aq_, T_, Hl_));
+        XL_CUDA(make_tile_map(&tc_attn_s_.x_lo, aq_lo_, T_, Hl_));
+        XL_CUDA(make_tile_map(&tc_attn_s_.w, ak_, heads_l_ * T_, kHeadDim));
+        XL_CUDA(make_tile_map(&tc_attn_s_.w_lo, ak_lo_, heads_l_ * T_, kHeadDim));
+        XL_CUDA(make_tile_map(&tc_attn_pv_.x, ap_, heads_l_ * T_, T_));
+        XL_CUDA(make_tile_map(&tc_attn_pv_.x_lo, ap_lo_, heads_l_ * T_, T_));
+        XL_CUDA(make_tile_map(&tc_attn_pv_.w, avt_, heads_l_ * kHeadDim, T_));
+        XL_CUDA(make_tile_map(&tc_attn_pv_.w_lo, avt_lo_, heads_l_ * kHeadDim, T_));
     }
     XL_CUDA(cudaStreamSynchronize(stream_));
     return XL_OK;
@@ -748,7 +768,15 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
         rc = prefill_linear(kGemvPlain, L.tc_qkv, pxn_, L.wqkv, L.bqkv, pqkv_, nullptr, n, 3 * Hl_, H_, s);
         if (rc != XL_OK) break;
         XL_CUDA(launch_rope_kv_prefill(pqkv_, rope_, L.kc, L.vc, n, heads_l_, T_, s));
-        XL_CUDA(launch_attn_prefill(pqkv_, L.kc, L.vc, patt_, patt_lo_, n, heads_l_, T_, s));
+        if (prefill_attn_ == 0 && T_ % 32 == 0) {
+            XL_CUDA(launch_attn_operands(pqkv_, L.kc, L.vc, aq_, aq_lo_, ak_, ak_lo_, avt_, avt_lo_, n, heads_l_, T_,
+                                         s));
+            XL_CUDA(launch_attn_scores_tc(tc_attn_s_, ap_, n, heads_l_, T_, &st_->err, s));
+            XL_CUDA(launch_attn_softmax(ap_, ap_lo_, n, heads_l_, T_, s));
+            XL_CUDA(launch_attn_pv_tc(tc_attn_pv_, patt_, patt_lo_, n, heads_l_, T_, &st_->err, s));
+        } else {
+            XL_CUDA(launch_attn_prefill(pqkv_, L.kc, L.vc, patt_, patt_lo_, n, heads_l_, T_, s));
+        }
         if (tp_ == 1) {
             rc = prefill_linear(kGemvResidual, L.tc_wo, patt_, L.wo, L.bo, px_, nullptr, n, H_, Hl_, s);
         } else {
@@ -865,6 +893,14 @@ int Engine::set_option(const char* key, int value) {
             return XL_ERR_ARG;
         }
         prefill_gemm_ = value;
+        return XL_OK;
+    }
+    if (k == "prefill_attn") {
+        if (value != 0 && value != 1) {
+            set_error("prefill_attn must be 0 (tcgen05 3xTF32) or 1 (fp32 FMA tiles)");
+            return XL_ERR_ARG;
+        }
+        prefill_attn_ = value;
         return XL_OK;
     }
     if (k == "tma_inflight") {

@@ -133,6 +133,11 @@ class Engine {
 
     int decode_path_ = 0;      // 0: persistent kernel (single GPU), 1: per-op kernels
     int prefill_gemm_ = 0;     // 0: tcgen05 3xTF32, 1: fp32 SIMT tiles
+    int prefill_attn_ = 0;     // 0: tcgen05 3xTF32 (S GEMM, softmax, PV GEMM), 1: fp32 FMA flash tiles
+    // tensor-core prefill attention: q/8 [T][Hl], k [heads][T][64], v^T [heads*64][T], S/P [heads][T][T]
+    float *aq_ = nullptr, *aq_lo_ = nullptr, *ak_ = nullptr, *ak_lo_ = nullptr, *avt_ = nullptr, *avt_lo_ = nullptr;
+    float *ap_ = nullptr, *ap_lo_ = nullptr;
+    TcOperands tc_attn_s_{}, tc_attn_pv_{};
     long long decode_graph_kernels_ = 0;  // kernels recorded in the decode graph
     int inflight_ = 2;  // persistent decode: weight boxes requested but not landed, per SM
     bool loaded_ = false;

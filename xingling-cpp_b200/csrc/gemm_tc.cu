@@ -42,6 +42,8 @@ constexpr int kGemmThreads = 192;
 constexpr size_t kGemmSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
 constexpr uint32_t kSpinLimit = 1u << 26;
 constexpr int kGemmPartial = 4;  // epilogue: raw slice accumulator into the split-K workspace
+constexpr int kGemmScores = 5;   // attention: S[z][n][m] = q_n . k_m per head z (tiles above the diagonal skipped)
+constexpr int kGemmPV = 6;       // attention: O[n][z*64 + f] (+ lo) = P[z][n][:] . V[:][f], keys up to the tile's last query
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -116,8 +118,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wlo,
                    const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_xlo,
                    const float* __restrict__ bias, float* __restrict__ C, float* __restrict__ C_lo, int M, int N,
-                   int K, int* err) {
+                   int K, int* err, const GemmBatch bt) {
     extern __shared__ __align__(1024) char smem_raw[];
+    constexpr bool kBatched = MODE == kGemmScores || MODE == kGemmPV;
+    // Scores: a tile whose first key follows its last query is fully masked (causal).
+    if (MODE == kGemmScores && static_cast<int>(blockIdx.x) * kBM >= static_cast<int>(blockIdx.y + 1) * kBN) return;
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
     uint64_t* empty = full + kStages;
@@ -126,11 +131,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
-    // split-K: this CTA's K-blocks [kb0, kb1) of blockIdx.z of gridDim.z slices
+    // split-K: this CTA's K-blocks [kb0, kb1) of blockIdx.z of gridDim.z slices;
+    // batched (attention) modes: blockIdx.z is the head and K is whole, or for
+    // P.V cut at the tile's last query (P is zero past it).
     const int nkb_all = K / kBK;
-    const int kb0 = static_cast<int>(static_cast<long long>(blockIdx.z) * nkb_all / gridDim.z);
-    const int kb1 = static_cast<int>(static_cast<long long>(blockIdx.z + 1) * nkb_all / gridDim.z);
+    int kb0 = 0, kb1 = nkb_all;
+    if (!kBatched) {
+        kb0 = static_cast<int>(static_cast<long long>(blockIdx.z) * nkb_all / gridDim.z);
+        kb1 = static_cast<int>(static_cast<long long>(blockIdx.z + 1) * nkb_all / gridDim.z);
+    } else if (MODE == kGemmPV) {
+        kb1 = min(nkb_all, (min(N, n0 + kBN) + kBK - 1) / kBK);
+    }
     const int nkb = kb1 - kb0;
+    const int bz = kBatched ? static_cast<int>(blockIdx.z) : 0;
+    const int wx0 = bz * bt.w_x, wy0 = bz * bt.w_y, xx0 = bz * bt.x_x, xy0 = bz * bt.x_y;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -160,10 +174,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 char* st = smem + s * kStageBytes;
                 const int kx = (kb0 + kb) * kBK;
                 mbar_expect_tx(&full[s], kStageBytes);
-                tma_load_2d(st, &tm_w, kx, m0, &full[s]);
-                tma_load_2d(st + kTileBytes, &tm_wlo, kx, m0, &full[s]);
-                tma_load_2d(st + 2 * kTileBytes, &tm_x, kx, n0, &full[s]);
-                tma_load_2d(st + 3 * kTileBytes, &tm_xlo, kx, n0, &full[s]);
+                tma_load_2d(st, &tm_w, kx + wx0, m0 + wy0, &full[s]);
+                tma_load_2d(st + kTileBytes, &tm_wlo, kx + wx0, m0 + wy0, &full[s]);
+                tma_load_2d(st + 2 * kTileBytes, &tm_x, kx + xx0, n0 + xy0, &full[s]);
+                tma_load_2d(st + 3 * kTileBytes, &tm_xlo, kx + xx0, n0 + xy0, &full[s]);
             }
         }
     } else if (warp == 1) {
@@ -192,7 +206,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int q = warp & 3;
         const int f = m0 + 32 * q + lane;
         const bool fok = f < M;
-        const float bf = (fok && bias && MODE != kGemmPartial) ? bias[f] : 0.0f;
+        const float bf = (fok && bias && MODE != kGemmPartial && !kBatched) ? bias[f] : 0.0f;
         if (wait_bar(accum, 0, err)) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll 1
@@ -214,7 +228,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int j = 0; j < 32; ++j) {
                     const int n = n0 + c0 + j;
                     const float v = __uint_as_float(r[j]) + bf;
-                    if (MODE == kGemmPartial) {
+                    if (MODE == kGemmScores) {
+                        if (fok && n < N) C[(static_cast<size_t>(bz) * bt.c_rows + n) * bt.ldc + f] = v;
+                    } else if (MODE == kGemmPV) {
+                        if (fok && n < N) {
+                            const size_t o = static_cast<size_t>(n) * bt.ldc + bz * bt.c_col + f;
+                            C[o] = v;
+                            C_lo[o] = tf32_lo(v);
+                        }
+                    } else if (MODE == kGemmPartial) {
                         // raw accumulator of this K slice: C is the workspace [slices][N][M]
                         if (fok && n < N) C[(static_cast<size_t>(blockIdx.z) * N + n) * M + f] = v;
                     } else if (MODE == kGemvSwiGLU) {
@@ -335,12 +357,13 @@ cudaError_t make_stream_map(CUtensorMap* map, const float* base, int rows, int c
 
 template <int MODE>
 cudaError_t launch_tc(dim3 grid, const TcOperands& o, const float* bias, float* C, float* C_lo, int m, int n, int k,
-                      int* err, cudaStream_t s) {
+                      int* err, cudaStream_t s, const GemmBatch& bt = GemmBatch{}) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kGemmSmem));
     if (e != cudaSuccess) return e;
     count_launch();
-    gemm_tc_kernel<MODE><<<grid, kGemmThreads, kGemmSmem, s>>>(o.w, o.w_lo, o.x, o.x_lo, bias, C, C_lo, m, n, k, err);
+    gemm_tc_kernel<MODE><<<grid, kGemmThreads, kGemmSmem, s>>>(o.w, o.w_lo, o.x, o.x_lo, bias, C, C_lo, m, n, k, err,
+                                                                bt);
     return cudaGetLastError();
 }
 
@@ -389,6 +412,31 @@ cudaError_t launch_gemm_tc(int mode, const TcOperands& o, const float* bias, flo
         default:
             return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_attn_scores_tc(const TcOperands& o, float* S, int n, int heads, int max_ctx, int* err,
+                                  cudaStream_t s) {
+    if (n <= 0 || n > max_ctx || heads <= 0) return cudaErrorInvalidValue;
+    GemmBatch bt{};
+    bt.w_y = max_ctx;
+    bt.x_x = kHeadDim;
+    bt.c_rows = max_ctx;
+    bt.ldc = max_ctx;
+    const unsigned t = static_cast<unsigned>((n + kBM - 1) / kBM);
+    return launch_tc<kGemmScores>(dim3(t, t, heads), o, nullptr, S, nullptr, n, n, kHeadDim, err, s, bt);
+}
+
+cudaError_t launch_attn_pv_tc(const TcOperands& o, float* out, float* out_lo, int n, int heads, int max_ctx, int* err,
+                              cudaStream_t s) {
+    if (n <= 0 || n > max_ctx || heads <= 0 || max_ctx % kBK) return cudaErrorInvalidValue;
+    GemmBatch bt{};
+    bt.w_y = kHeadDim;
+    bt.x_y = max_ctx;
+    bt.ldc = heads * kHeadDim;
+    bt.c_col = kHeadDim;
+    const int k = ((n + kBK - 1) / kBK) * kBK;
+    const unsigned t = static_cast<unsigned>((n + kBN - 1) / kBN);
+    return launch_tc<kGemmPV>(dim3(1, t, heads), o, nullptr, out, out_lo, kHeadDim, n, k, err, s, bt);
 }
 
 cudaError_t launch_split_lo(const float* x, float* lo, size_t n, cudaStream_t s) {

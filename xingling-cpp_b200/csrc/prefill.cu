@@ -187,6 +187,54 @@ __global__ void __launch_bounds__(32) rope_kv_prefill_kernel(float* __restrict__
     vd[j + kHalfHead] = v[j + kHalfHead];
 }
 
+// Operands of the tensor-core attention for one (row t, head h), after
+// rope_kv_prefill: q/8 (the exact 1/sqrt(64) scale) into q8[t][h*64 + d], the
+// rotated k into kq[h][t][d] and v transposed into vt[h*64 + d][t], each with
+// its tf32 lo half for the 3xTF32 products.
+__global__ void __launch_bounds__(64) attn_operands_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
+                                                           const float* __restrict__ vc, float* __restrict__ q8,
+                                                           float* __restrict__ q8_lo, float* __restrict__ kq,
+                                                           float* __restrict__ kq_lo, float* __restrict__ vt,
+                                                           float* __restrict__ vt_lo, int heads, int max_ctx) {
+    const int t = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+    const int HL = heads * kHeadDim;
+    const float q = qkv[static_cast<size_t>(t) * 3 * HL + h * kHeadDim + d] * 0.125f;
+    const size_t qi = static_cast<size_t>(t) * HL + h * kHeadDim + d;
+    q8[qi] = q;
+    q8_lo[qi] = lo19(q);
+    const size_t ci = (static_cast<size_t>(h) * max_ctx + t) * kHeadDim + d;
+    const float k = kc[ci], v = vc[ci];
+    kq[ci] = k;
+    kq_lo[ci] = lo19(k);
+    const size_t vi = (static_cast<size_t>(h) * kHeadDim + d) * max_ctx + t;
+    vt[vi] = v;
+    vt_lo[vi] = lo19(v);
+}
+
+// Causal softmax of one score row per warp: P[h][q][k] = exp(s - max) / sum for
+// k <= q (the online-softmax result of src/attn.cu:47-167 written out), zero
+// for q < k < kpad (the P.V GEMM reads keys up to kpad), plus the lo half.
+__global__ void __launch_bounds__(256) attn_softmax_kernel(float* __restrict__ S, float* __restrict__ P_lo, int n,
+                                                           int heads, int max_ctx, int kpad) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= n * heads) return;
+    const int h = row / n, q = row % n;
+    float* s = S + (static_cast<size_t>(h) * max_ctx + q) * max_ctx;
+    float* pl = P_lo + (static_cast<size_t>(h) * max_ctx + q) * max_ctx;
+    float m = -INFINITY;
+    for (int k = lane; k <= q; k += 32) m = fmaxf(m, s[k]);
+    m = warp_max(m);
+    float l = 0.0f;
+    for (int k = lane; k <= q; k += 32) l += expf(s[k] - m);
+    l = warp_sum(l);
+    const float inv = 1.0f / l;
+    for (int k = lane; k < kpad; k += 32) {
+        const float p = k <= q ? expf(s[k] - m) * inv : 0.0f;
+        s[k] = p;
+        pl[k] = lo19(p);
+    }
+}
+
 // Causal attention for one (64-query tile, head); 256 threads as 16 x 16,
 // each owning a 4 x 4 block of the score tile and of the output tile.
 constexpr int kAT = 64;
@@ -386,6 +434,24 @@ cudaError_t launch_attn_prefill(const float* qkv, const float* kc, const float* 
     count_launch();
     attn_prefill_kernel<<<dim3((n + kAT - 1) / kAT, heads), 256, kAttnPrefillSmem, s>>>(qkv, kc, vc, out, out_lo, n,
                                                                                         heads, max_ctx);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attn_operands(const float* qkv, const float* kc, const float* vc, float* q8, float* q8_lo,
+                                 float* kq, float* kq_lo, float* vt, float* vt_lo, int n, int heads, int max_ctx,
+                                 cudaStream_t s) {
+    if (n <= 0 || n > max_ctx) return cudaErrorInvalidValue;
+    count_launch();
+    attn_operands_kernel<<<dim3(n, heads), kHeadDim, 0, s>>>(qkv, kc, vc, q8, q8_lo, kq, kq_lo, vt, vt_lo, heads,
+                                                             max_ctx);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attn_softmax(float* S, float* P_lo, int n, int heads, int max_ctx, cudaStream_t s) {
+    const int kpad = ((n + 31) / 32) * 32;
+    if (n <= 0 || n > max_ctx || kpad > max_ctx) return cudaErrorInvalidValue;
+    count_launch();
+    attn_softmax_kernel<<<(n * heads + 7) / 8, 256, 0, s>>>(S, P_lo, n, heads, max_ctx, kpad);
     return cudaGetLastError();
 }
 

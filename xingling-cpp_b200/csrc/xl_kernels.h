@@ -196,6 +196,28 @@ cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int col
 // C[N][M] (+)= X[N][K] . W[M][K]^T + b with the 3xTF32 split; SwiGLU writes C and C_lo as [N][M/2].
 // With a workspace (ws, ws_floats) and fewer output tiles than SMs, K is split
 // into slices whose partial sums are added in slice order by a second kernel.
+// Tensor-core prefill attention, around the two GEMMs below: the operands
+// (after launch_rope_kv_prefill) and the causal row softmax of S in place.
+cudaError_t launch_attn_operands(const float* qkv, const float* kc, const float* vc, float* q8, float* q8_lo,
+                                 float* kq, float* kq_lo, float* vt, float* vt_lo, int n, int heads, int max_ctx,
+                                 cudaStream_t s);
+cudaError_t launch_attn_softmax(float* S, float* P_lo, int n, int heads, int max_ctx, cudaStream_t s);
+// Prefill attention on tcgen05 (3xTF32), per head z as the grid's third
+// dimension: operand tile coordinates advance by (w_x, w_y) and (x_x, x_y) per
+// head.  Scores: C = S[z][t][ldc] with c_rows rows per head.  P.V: C, C_lo =
+// out[t][ldc] at column z * c_col.
+struct GemmBatch {
+    int w_x, w_y, x_x, x_y;
+    int c_rows, ldc, c_col;
+};
+// S[h][q][k] = (q/8 . k) for q, k < n (tiles above the diagonal are skipped).
+// o.x / o.x_lo: q/8 [T][heads*64]; o.w / o.w_lo: k [heads*T][64] (make_tile_map).
+cudaError_t launch_attn_scores_tc(const TcOperands& o, float* S, int n, int heads, int max_ctx, int* err,
+                                  cudaStream_t s);
+// out[q][h*64 + d] (and its lo half) = sum over keys k <= q of P[h][q][k] v[h][k][d].
+// o.x / o.x_lo: P [heads*T][T]; o.w / o.w_lo: v transposed [heads*64][T].
+cudaError_t launch_attn_pv_tc(const TcOperands& o, float* out, float* out_lo, int n, int heads, int max_ctx, int* err,
+                              cudaStream_t s);
 cudaError_t launch_gemm_tc(int mode, const TcOperands& o, const float* bias, float* C, float* C_lo, int n, int m,
                            int k, int* err, cudaStream_t s, float* ws = nullptr, size_t ws_floats = 0,
                            int num_sms = 148);
