@@ -174,6 +174,8 @@ __device__ __forceinline__ Gemv gemv_of(const PersistentParams& p, int ph) {
     return g;
 }
 
+// Index arithmetic is 32-bit: every product below is at most 148 SMs x 28,440
+// boxes (the LM head), far inside int range.
 // This CTA's boxes [t0, t1) of a phase, nb boxes of kd k-tiles per 16-row
 // group, T boxes in all: whole groups (a balanced split of the groups) for
 // QKV, W1/V and the LM head; an even split of the boxes for the residual
@@ -188,11 +190,11 @@ __device__ __forceinline__ Boxes boxes_of(const Gemv& d) {
     const int groups = (d.M + kPersistTileRows - 1) / kPersistTileRows;
     r.T = groups * r.nb;
     if (d.kind == kWo || d.kind == kW2) {
-        r.t0 = static_cast<int>(static_cast<long long>(blockIdx.x) * r.T / gridDim.x);
-        r.t1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * r.T / gridDim.x);
+        r.t0 = static_cast<int>(blockIdx.x) * r.T / static_cast<int>(gridDim.x);
+        r.t1 = static_cast<int>(blockIdx.x + 1) * r.T / static_cast<int>(gridDim.x);
     } else {
-        r.t0 = static_cast<int>(static_cast<long long>(blockIdx.x) * groups / gridDim.x) * r.nb;
-        r.t1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * groups / gridDim.x) * r.nb;
+        r.t0 = static_cast<int>(blockIdx.x) * groups / static_cast<int>(gridDim.x) * r.nb;
+        r.t1 = static_cast<int>(blockIdx.x + 1) * groups / static_cast<int>(gridDim.x) * r.nb;
     }
     return r;
 }
@@ -350,13 +352,13 @@ __device__ __forceinline__ float4 residual_quad(const float* x_old, const float*
 // xs = rmsnorm(x) * gamma, where x is the embedding row (cres == nullptr) or
 // the residual after a split projection of nb boxes per group; this CTA stores
 // its slice of x to x_out.  float4 accesses; gamma is loaded with x.
-__device__ void stage_norm(const PersistentParams& p, const float* x_old, const float* bias, const float* cres,
+__device__ __noinline__ void stage_norm(const PersistentParams& p, const float* x_old, const float* bias, const float* cres,
                            int nb, const float* gamma, float* xs, float* red, float* x_out) {
     const int t = threadIdx.x - 32;
     const int K = p.H;
     const int T = (K / kPersistTileRows) * nb;
-    const int s0 = static_cast<int>(static_cast<long long>(blockIdx.x) * K / gridDim.x);
-    const int s1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * K / gridDim.x);
+    const int s0 = static_cast<int>(blockIdx.x) * K / static_cast<int>(gridDim.x);
+    const int s1 = static_cast<int>(blockIdx.x + 1) * K / static_cast<int>(gridDim.x);
     float4* x4 = reinterpret_cast<float4*>(xs);
     const float4* g4 = reinterpret_cast<const float4*>(gamma);
     float4 gk[kStageQuads];
@@ -397,23 +399,6 @@ __device__ void stage_copy(const float* src, int K, float* xs) {
     const int t = threadIdx.x - 32;
     for (int i = t; i < (K >> 2); i += kConsumerThreads)
         reinterpret_cast<float4*>(xs)[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
-}
-
-// Butterfly reduce-scatter of a 64-float vector held by every lane: afterwards
-// lane l holds the warp-wide sums of elements 2l and 2l+1.
-__device__ __forceinline__ float2 warp_reduce_scatter64(float (&v)[64]) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int half = 32, off = 16; off > 0; half >>= 1, off >>= 1) {
-        const bool upper = (lane & off) != 0;
-#pragma unroll
-        for (int i = 0; i < half; ++i) {
-            const float send = upper ? v[i] : v[i + half];
-            const float keep = upper ? v[i + half] : v[i];
-            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-        }
-    }
-    return make_float2(v[0], v[1]);
 }
 
 // This CTA's attention item of the token: head h, CTA j of the head's nct;
@@ -476,12 +461,9 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
         }
         __syncwarp();  // orders the row-n stores before the lane that owns position n reads them
         const float4* kr = reinterpret_cast<const float4*>(kc + static_cast<size_t>(mine ? pos : t0) * kHeadDim);
-        const float4* vr = reinterpret_cast<const float4*>(vc + static_cast<size_t>(mine ? pos : t0) * kHeadDim);
-        float4 kv[16], vv[16];
+        float4 kv[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) kv[i] = __ldcg(kr + i);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) vv[i] = __ldcg(vr + i);
         const float4* q4 = reinterpret_cast<const float4*>(qsh);
         float d = 0.0f;
 #pragma unroll
@@ -490,15 +472,21 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
         const float m = warp_max(sc);
         const float e = mine ? expf(sc - m) : 0.0f;
         const float l = warp_sum(e);
-        float w[64];
+        // P.V with lane = output dims (2 lane, 2 lane + 1): every row of the chunk
+        // is read as 32 coalesced float2 (lanes past the chunk's end weigh 0).
+        const int cnt = min(kPersistChunk, n + 1 - t0);
+        const float2* vr = reinterpret_cast<const float2*>(vc + static_cast<size_t>(t0) * kHeadDim) + lane;
+        float2 vrow[kPersistChunk];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            w[4 * i + 0] = e * vv[i].x;
-            w[4 * i + 1] = e * vv[i].y;
-            w[4 * i + 2] = e * vv[i].z;
-            w[4 * i + 3] = e * vv[i].w;
+        for (int jpos = 0; jpos < kPersistChunk; ++jpos)
+            vrow[jpos] = jpos < cnt ? __ldcg(vr + jpos * (kHeadDim / 2)) : make_float2(0.0f, 0.0f);
+        float2 o = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int jpos = 0; jpos < kPersistChunk; ++jpos) {
+            const float ej = __shfl_sync(0xffffffffu, e, jpos);
+            o.x = fmaf(ej, vrow[jpos].x, o.x);
+            o.y = fmaf(ej, vrow[jpos].y, o.y);
         }
-        const float2 o = warp_reduce_scatter64(w);
         float* ap = apart + warp * kAttnPartStride;
         reinterpret_cast<float2*>(ap + 4)[lane] = o;
         if (lane == 0) {
@@ -686,8 +674,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                     if (lane == 1 && vb) p.qkv[Rb] = acc_b + eb;
                     break;
                 case kWo:
-                case kW2: {  // partial row sums of this CTA's boxes of group g
-                    const int c = blockIdx.x - persist_owner_cta(static_cast<long long>(g) * r.nb, r.T, gridDim.x);
+                case kW2: {  // partial row sums of this CTA's boxes of group g (c: this CTA's rank among its owners)
+                    const int c = blockIdx.x - ((g * r.nb + 1) * static_cast<int>(gridDim.x) - 1) / r.T;
                     float* q = p.cres + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows;
                     if (lane == 0) q[ra] = acc_a;
                     if (lane == 1) q[rb] = acc_b;
