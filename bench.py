@@ -13,10 +13,12 @@ the step inputs from pinned memory and the device->host read of the result.
 per token, >99% of a decode step's kernel time), timed by CUDA event nodes
 around it inside the decode graph in one more step right after the timed
 region (the nodes cost the sampler its early launch, so the timed steps run
-without them).  Also reported: the whole decode
-step against the same roofline, prefill of a 512-id prompt (seed 1), the
-reference's own CPU path on the host cores, and at N > 1 the tensor-parallel
-decode latency (prompt 64, seed 4, greedy 256).
+without them).  Also reported: the whole decode step against the same
+roofline, prefill of a 512-id prompt (seed 1), the reference's own CPU path
+on the host cores, `replica_batch` (64 sequences, prompt lengths uniform in
+[16, 512] with seed 5, 128 sampled tokens each, spread over the N replicas)
+and at N > 1 the tensor-parallel decode latency (prompt 64, seed 4, greedy
+256).
 
   python bench.py [--gpus N --steps K --warmup W]          # this engine
   python bench.py --impl reference [...]                   # reference CPU path
