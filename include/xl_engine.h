@@ -175,6 +175,30 @@ XL_API long long xl_kernel_launches(void);
  * from CUDA events.  Leaves the logits of the last step unchanged in value. */
 XL_API int xl_engine_profile_lm_head(xl_engine* e, int iters, float* avg_ms);
 
+/* ---- batched decode (no reference counterpart) -------------------------
+ * XL_BATCH sequences decode together on one GPU, sharing one pass over the
+ * weights of a loaded single-GPU engine (the reference decodes one sequence at
+ * a time).  Each sequence has its own KV cache, repetition set, Philox stream
+ * and position.  xl_batch_prefill runs the engine's own prefill (so the
+ * engine's single sequence is overwritten) and makes the result sequence seq;
+ * xl_batch_decode feeds tokens[b] to every sequence b and returns the next id
+ * of each, with the same sampling arguments for all.  The engine must outlive
+ * the batch decoder, and the two must not be used from different threads at
+ * once (they share the engine's stream). */
+#define XL_BATCH 8
+typedef struct xl_batch xl_batch;
+XL_API int xl_batch_create(xl_engine* e, xl_batch** out);
+XL_API void xl_batch_destroy(xl_batch* b);
+XL_API int xl_batch_seed(xl_batch* b, int seq, unsigned long long seed);
+XL_API int xl_batch_prefill(xl_batch* b, int seq, const int* ids, int n, float temperature, float top_p,
+                            float repetition_penalty, int* token_out);
+XL_API int xl_batch_decode(xl_batch* b, const int* tokens, float temperature, float top_p,
+                           float repetition_penalty, int* tokens_out);
+/* Penalised logits of sequence seq after the last decode step (n >= vocab). */
+XL_API int xl_batch_last_logits(xl_batch* b, int seq, float* out, int n);
+XL_API int xl_batch_ctx_len(const xl_batch* b, int seq);
+XL_API int xl_batch_last_device_ms(const xl_batch* b, float* ms);
+
 /* ---- op-level entry points (device pointers, caller's stream) ---------- */
 
 /* RMSNorm::forward (src/rmsnorm.cu:112-147) fused with

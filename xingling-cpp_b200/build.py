@@ -25,7 +25,7 @@ OBJ = os.path.join(HERE, "_build")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 CXX = os.environ.get("XL_CXX", "g++")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["decode.cu", "decode_persistent.cu", "prefill.cu", "gemm_tc.cu", "engine.cu", "c_api.cu"]
+CU_SOURCES = ["decode.cu", "decode_persistent.cu", "prefill.cu", "gemm_tc.cu", "engine.cu", "batch.cu", "c_api.cu"]
 LIB = os.path.join(HERE, "libxl_engine.so")
 EXT = os.path.join(HERE, "llm_cpp_engine" + sysconfig.get_config_var("EXT_SUFFIX"))
 

@@ -12,6 +12,9 @@ using xl::Engine;
 struct xl_engine {
     Engine* impl;
 };
+struct xl_batch {
+    xl::BatchDecoder* impl;
+};
 
 namespace {
 
@@ -71,6 +74,57 @@ int xl_engine_create(const xl_config* cfg, int device, int tp_size, int tp_rank,
     const int rc = Engine::create(*cfg, device, tp_size, tp_rank, nccl_id, &impl);
     if (rc != XL_OK) return rc;
     *out = new xl_engine{impl};
+    return XL_OK;
+}
+
+int xl_batch_create(xl_engine* e, xl_batch** out) {
+    xl::clear_error();
+    if (!e || !out) return bad("null argument");
+    static_assert(XL_BATCH == xl::kBatch, "batch size of the ABI");
+    xl::BatchDecoder* b = nullptr;
+    const int rc = xl::BatchDecoder::create(e->impl, &b);
+    if (rc != XL_OK) return rc;
+    *out = new xl_batch{b};
+    return XL_OK;
+}
+
+void xl_batch_destroy(xl_batch* b) {
+    if (!b) return;
+    delete b->impl;
+    delete b;
+}
+
+int xl_batch_seed(xl_batch* b, int seq, unsigned long long seed) {
+    xl::clear_error();
+    if (!b) return bad("null batch decoder");
+    return b->impl->seed(seq, seed);
+}
+
+int xl_batch_prefill(xl_batch* b, int seq, const int* ids, int n, float temperature, float top_p,
+                     float repetition_penalty, int* token_out) {
+    xl::clear_error();
+    if (!b || !token_out) return bad("null argument");
+    return b->impl->prefill(seq, ids, n, temperature, top_p, repetition_penalty, token_out);
+}
+
+int xl_batch_decode(xl_batch* b, const int* tokens, float temperature, float top_p, float repetition_penalty,
+                    int* tokens_out) {
+    xl::clear_error();
+    if (!b) return bad("null batch decoder");
+    return b->impl->decode(tokens, temperature, top_p, repetition_penalty, tokens_out);
+}
+
+int xl_batch_last_logits(xl_batch* b, int seq, float* out, int n) {
+    xl::clear_error();
+    if (!b) return bad("null batch decoder");
+    return b->impl->last_logits(seq, out, n);
+}
+
+int xl_batch_ctx_len(const xl_batch* b, int seq) { return b ? b->impl->ctx_len(seq) : -1; }
+
+int xl_batch_last_device_ms(const xl_batch* b, float* ms) {
+    if (!b || !ms) return bad("null argument");
+    *ms = b->impl->last_device_ms();
     return XL_OK;
 }
 

@@ -389,7 +389,7 @@ __device__ void draw_token(const unsigned long long* cand, int kc, float* prob, 
     }
 }
 
-__global__ void __launch_bounds__(kSampThreads) sample_kernel(const SampleParams p) {
+__device__ __forceinline__ void sample_block(const SampleParams& p) {
     __shared__ unsigned int hist[2048];
     __shared__ unsigned long long cand[kTopK];
     __shared__ float prob[kTopK];
@@ -423,9 +423,22 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const SampleParams
             __syncthreads();
             const int sh = shifts[pass];
             const uint32_t bm = (1u << bits[pass]) - 1u;
-            for (int i = tid; i < V; i += kSampThreads) {
-                const uint32_t k = float_key(p.logits[i]);
-                if ((k & pmask) == prefix) atomicAdd(&hist[(k >> sh) & bm], 1u);
+            // Warp-aggregated counts: logits crowd into few bins, so lanes that
+            // share a bin add once (their leader adds the group's size).
+            for (int base = warp * 32; base < V; base += kSampThreads) {
+                const int i = base + lane;
+                uint32_t bin = 0;
+                bool act = false;
+                if (i < V) {
+                    const uint32_t k = float_key(p.logits[i]);
+                    act = (k & pmask) == prefix;
+                    bin = (k >> sh) & bm;
+                }
+                const unsigned amask = __ballot_sync(0xffffffffu, act);
+                if (act) {
+                    const unsigned peers = __match_any_sync(amask, bin);
+                    if (lane == __ffs(peers) - 1) atomicAdd(&hist[bin], static_cast<unsigned>(__popc(peers)));
+                }
             }
             __syncthreads();
             // Thread t owns bins (2047 - 2t, 2046 - 2t); scan counts from the top.
@@ -526,6 +539,19 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const SampleParams
     }
 }
 
+__global__ void __launch_bounds__(kSampThreads) sample_kernel(const SampleParams p) { sample_block(p); }
+
+// kBatch independent sequences, one CTA each: sequence b's logits at
+// logits + b * stride, its flags at rep_flags + b * stride, its state st + b.
+__global__ void __launch_bounds__(kSampThreads) sample_batch_kernel(const SampleParams p, int stride) {
+    SampleParams q = p;
+    const int b = blockIdx.x;
+    q.logits = p.logits + static_cast<size_t>(b) * stride;
+    q.rep_flags = p.rep_flags + static_cast<size_t>(b) * stride;
+    q.st = p.st + b;
+    sample_block(q);
+}
+
 // Tensor-parallel merge of sample_cpu (src/inference.cu:58-114) over vocab
 // shards: every rank holds the same all-gathered candidate lists (each shard's
 // sorted top-1024, packed (key, ~global id)), sorts their union by value (ties:
@@ -620,6 +646,11 @@ cudaError_t launch_attn_decode(const AttnDecodeParams& p, bool pdl, cudaStream_t
 
 cudaError_t launch_sample(const SampleParams& p, bool pdl, cudaStream_t s) {
     return launch_ex(sample_kernel, dim3(1), dim3(kSampThreads), 0, pdl, s, p);
+}
+
+cudaError_t launch_sample_batch(const SampleParams& p, int batch, int stride, bool pdl, cudaStream_t s) {
+    if (batch <= 0) return cudaErrorInvalidValue;
+    return launch_ex(sample_batch_kernel, dim3(batch), dim3(kSampThreads), 0, pdl, s, p, stride);
 }
 
 cudaError_t launch_sample_merge(const SampleMergeParams& p, bool pdl, cudaStream_t s) {

@@ -36,7 +36,11 @@ struct LayerWeights {
     TcOperands tc_qkv, tc_wo, tc_w13, tc_w2;  // TMA maps of the prefill GEMM operands
 };
 
+class BatchDecoder;
+
 class Engine {
+    friend class BatchDecoder;
+
    public:
     static int create(const xl_config& cfg, int device, int tp_size, int tp_rank, const void* nccl_id, Engine** out);
     ~Engine();
@@ -151,6 +155,49 @@ class Engine {
     std::deque<float> uniforms_;
     uint64_t philox_seed_ = 0;
     uint64_t philox_ctr_ = 0;
+};
+
+// kBatch sequences decoding together on one GPU over a loaded Engine's
+// weights (batch.cu).  The Engine's own sequence serves as the prefill
+// scratch: prefill(seq) runs the Engine's prefill and copies the result into
+// sequence seq.
+class BatchDecoder {
+   public:
+    static int create(Engine* eng, BatchDecoder** out);
+    ~BatchDecoder();
+    int seed(int seq, uint64_t s);
+    int prefill(int seq, const int* ids, int n, float temperature, float top_p, float rp, int* token_out);
+    int decode(const int* tokens, float temperature, float top_p, float rp, int* tokens_out);
+    int last_logits(int seq, float* out, int n);
+    int ctx_len(int seq) const { return seq >= 0 && seq < kBatch ? n_[seq] : -1; }
+    float last_device_ms() const { return last_ms_; }
+
+   private:
+    BatchDecoder() = default;
+    int init();
+    int enqueue(cudaStream_t s);
+    int capture();
+    float next_uniform(int seq);
+    int cuda_fail(cudaError_t e, const char* what);
+
+    Engine* eng_ = nullptr;
+    char* arena_ = nullptr;
+    std::vector<float*> kc_, vc_;  // per layer [kBatch][heads][T][64]
+    float *x_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *ffh_ = nullptr, *logits_ = nullptr;
+    uint8_t* rep_ = nullptr;       // [kBatch][V]
+    DevState* st_ = nullptr;       // [kBatch]
+    StepIn* in_ = nullptr;         // [kBatch]
+    int* tokens_ = nullptr;        // [kBatch]
+    int* ticket_ = nullptr;
+    StepIn* h_in_ = nullptr;       // pinned
+    DevState* h_st_ = nullptr;     // pinned
+    cudaGraphExec_t exec_ = nullptr;
+    long long graph_kernels_ = 0;
+    cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
+    float last_ms_ = 0.0f;
+    uint64_t seed_[kBatch] = {};
+    uint64_t ctr_[kBatch] = {};
+    int n_[kBatch] = {};
 };
 
 // Tensor-parallel partition of one rank (see xl_tp_plan in xl_engine.h).

@@ -186,15 +186,89 @@ class InferenceEngine {
     int role_id_user = 872;
     int role_id_assistant = 77091;
 
+    xl_engine* handle() const { return e_; }
+
    private:
     xl_engine* e_ = nullptr;
     std::string device_;
+};
+
+// XL_BATCH sequences decoding together over an InferenceEngine's weights (no
+// reference counterpart; see xl_batch_* in xl_engine.h).
+class BatchDecoder {
+   public:
+    explicit BatchDecoder(InferenceEngine& eng) {
+        int rc;
+        {
+            py::gil_scoped_release nogil;
+            rc = xl_batch_create(eng.handle(), &b_);
+        }
+        check(rc);
+    }
+    ~BatchDecoder() { xl_batch_destroy(b_); }
+    BatchDecoder(const BatchDecoder&) = delete;
+    BatchDecoder& operator=(const BatchDecoder&) = delete;
+
+    void seed(int seq, unsigned long long s) { check(xl_batch_seed(b_, seq, s)); }
+
+    int prefill(int seq, const std::vector<int>& ids, float temperature, float top_p, float repetition_penalty) {
+        int tok = 0, rc;
+        {
+            py::gil_scoped_release nogil;
+            rc = xl_batch_prefill(b_, seq, ids.data(), static_cast<int>(ids.size()), temperature, top_p,
+                                  repetition_penalty, &tok);
+        }
+        check(rc);
+        return tok;
+    }
+
+    std::vector<int> step(const std::vector<int>& tokens, float temperature, float top_p, float repetition_penalty) {
+        if (tokens.size() != XL_BATCH) throw py::value_error("step: one token per sequence (" +
+                                                             std::to_string(XL_BATCH) + ")");
+        std::vector<int> out(XL_BATCH);
+        int rc;
+        {
+            py::gil_scoped_release nogil;
+            rc = xl_batch_decode(b_, tokens.data(), temperature, top_p, repetition_penalty, out.data());
+        }
+        check(rc);
+        return out;
+    }
+
+    py::bytes last_logits(int seq, int vocab) {
+        std::string buf(static_cast<size_t>(vocab) * sizeof(float), '\0');
+        check(xl_batch_last_logits(b_, seq, reinterpret_cast<float*>(&buf[0]), vocab));
+        return py::bytes(buf);
+    }
+
+    int ctx_len(int seq) const { return xl_batch_ctx_len(b_, seq); }
+
+    float last_device_ms() const {
+        float ms = 0.0f;
+        check(xl_batch_last_device_ms(b_, &ms));
+        return ms;
+    }
+
+   private:
+    xl_batch* b_ = nullptr;
 };
 
 }  // namespace
 
 PYBIND11_MODULE(llm_cpp_engine, m) {
     m.doc() = "XingLing-0.68B token loop on NVIDIA B200 (sm_100a), drop-in for the reference's llm_cpp_engine";
+
+    py::class_<BatchDecoder>(m, "BatchDecoder")
+        .def(py::init<InferenceEngine&>(), py::arg("engine"), py::keep_alive<1, 2>())
+        .def_property_readonly_static("size", [](py::object) { return XL_BATCH; })
+        .def("seed", &BatchDecoder::seed, py::arg("seq"), py::arg("seed"))
+        .def("prefill", &BatchDecoder::prefill, py::arg("seq"), py::arg("input_ids"), py::arg("temperature") = 0.7f,
+             py::arg("top_p") = 0.9f, py::arg("repetition_penalty") = 1.1f)
+        .def("step", &BatchDecoder::step, py::arg("tokens"), py::arg("temperature") = 0.7f, py::arg("top_p") = 0.9f,
+             py::arg("repetition_penalty") = 1.1f)
+        .def("last_logits", &BatchDecoder::last_logits, py::arg("seq"), py::arg("vocab"))
+        .def("ctx_len", &BatchDecoder::ctx_len, py::arg("seq"))
+        .def("last_device_ms", &BatchDecoder::last_device_ms);
 
     m.def("kernel_launches", []() { return xl_kernel_launches(); },
           "Kernels this library has run in this process (decode-graph kernels count at each replay).");

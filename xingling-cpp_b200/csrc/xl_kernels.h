@@ -9,6 +9,7 @@ namespace xl {
 
 constexpr int kHeadDim = 64;   // XingLing attention head width (src/inference.cu:19-28: 1536 / 24)
 constexpr int kHalfHead = 32;  // rotate-half RoPE pairs (j, j + 32), src/rope.cu:20-45
+constexpr int kBatch = 8;      // sequences of a batched decode step (batch.cu)
 constexpr int kTopK = 1024;    // sampler candidate count, src/inference.cu:66
 
 // Host-written inputs of one step (copied to the device before each call).
@@ -170,6 +171,9 @@ struct SampleParams {
     unsigned long long* cand_out;  // tensor parallel: write the shard's sorted top-1024 here, draw nothing
 };
 cudaError_t launch_sample(const SampleParams& p, bool pdl, cudaStream_t s);
+// `batch` sequences in one launch (a CTA each): sequence b samples logits +
+// b * stride with rep_flags + b * stride and state st + b.
+cudaError_t launch_sample_batch(const SampleParams& p, int batch, int stride, bool pdl, cudaStream_t s);
 
 // Tensor-parallel sampling merge: the all-gathered per-shard candidate lists
 // (packed (value key, ~global id), n = tp x 1024), sorted as one; draws as
