@@ -54,6 +54,7 @@ struct BatchGemvParams {
     const uint8_t* rep_flags;  // logits: [kBatch][M]
     DevState* st;              // logits: [kBatch]
     int* ticket;               // logits: CTAs finished (the last one resets it)
+    int wpg;                   // warps per row group (each a K slice; 1 = a warp owns its groups)
 };
 
 // Butterfly reduce-scatter of 32 values held by every lane: afterwards lane l
@@ -78,14 +79,18 @@ __global__ void __launch_bounds__(kBgThreads) batch_gemv_kernel(const BatchGemvP
     extern __shared__ float4 xs4[];  // [kBatch][K/4]
     __shared__ float red[kBatch][kBgWarps];
     __shared__ unsigned long long best_s[kBatch][kBgWarps];
+    __shared__ float part[kBgWarps][32];
     const int K4 = p.K >> 2;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nwarps = blockDim.x >> 5;  // 1 .. kBgWarps
-    const int gw = blockIdx.x * nwarps + warp, GW = gridDim.x * nwarps;
+    // Teams of wpg warps share a row group, each warp one K slice.
+    const int wpg = p.wpg, teams = nwarps / wpg, team = warp / wpg, ks = warp % wpg;
+    const int gw = blockIdx.x * teams + team, GW = gridDim.x * teams;
     const int G = (p.M + kBgRows - 1) / kBgRows;
+    const int k_lo = K4 * ks / wpg, k_hi = K4 * (ks + 1) / wpg;
     const size_t group_floats = static_cast<size_t>(kBgRows) * p.K;
 
-    if (lane == 0) {
+    if (lane == 0 && ks == 0 && warp < teams * wpg) {
         for (int d = 0; d < kBgPrefetch; ++d) {
             const int g = gw + d * GW;
             if (g < G) {
@@ -141,8 +146,12 @@ __global__ void __launch_bounds__(kBgThreads) batch_gemv_kernel(const BatchGemvP
     float best_v = -INFINITY;
     int best_i = -1;
     const float4* W4 = reinterpret_cast<const float4*>(p.W);
-    for (int g = gw; g < G; g += GW) {
-        if (lane == 0) {
+    const bool in_team = warp < teams * wpg;
+    const int iters = (G + GW - 1) / GW;  // the same trip count for every warp (block barriers inside)
+    for (int it = 0; it < iters; ++it) {
+        const int g = gw + it * GW;
+        const bool has = in_team && g < G;
+        if (has && lane == 0 && ks == 0) {
             const int gp = g + kBgPrefetch * GW;
             if (gp < G) {
                 const int rows = min(kBgRows, p.M - kBgRows * gp);
@@ -153,20 +162,20 @@ __global__ void __launch_bounds__(kBgThreads) batch_gemv_kernel(const BatchGemvP
         float acc[kBgRows * kBatch];
 #pragma unroll
         for (int i = 0; i < kBgRows * kBatch; ++i) acc[i] = 0.0f;
-        for (int base = 0; base < K4; base += 32 * kBgU) {
+        for (int base = has ? k_lo : k_hi; base < k_hi; base += 32 * kBgU) {
             float4 w[kBgRows][kBgU];
 #pragma unroll
             for (int r = 0; r < kBgRows; ++r)
 #pragma unroll
                 for (int u = 0; u < kBgU; ++u) {
                     const int i = base + u * 32 + lane;
-                    w[r][u] = (i < K4 && r0 + r < p.M) ? ld_stream(W4 + static_cast<size_t>(r0 + r) * K4 + i)
-                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+                    w[r][u] = (i < k_hi && r0 + r < p.M) ? ld_stream(W4 + static_cast<size_t>(r0 + r) * K4 + i)
+                                                         : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
             for (int u = 0; u < kBgU; ++u) {
                 const int i = base + u * 32 + lane;
-                if (i < K4) {
+                if (i < k_hi) {
 #pragma unroll
                     for (int b = 0; b < kBatch; ++b) {
                         const float4 xv = xs4[b * K4 + i];
@@ -176,7 +185,18 @@ __global__ void __launch_bounds__(kBgThreads) batch_gemv_kernel(const BatchGemvP
                 }
             }
         }
-        const float v = reduce_scatter32(acc);
+        float v = reduce_scatter32(acc);
+        if (wpg > 1) {
+            // the team's K slices, summed in slice order by the team's first warp
+            part[warp][lane] = v;
+            __syncthreads();
+            if (ks == 0) {
+                v = part[warp][lane];
+                for (int q = 1; q < wpg; ++q) v += part[warp + q][lane];
+            }
+            __syncthreads();
+        }
+        if (!has || ks != 0) continue;
         const int row = r0 + my_r;
         const bool ok = row < p.M;
         if (MODE == kGemvSwiGLU) {
@@ -373,30 +393,35 @@ cudaError_t launch_batch_gemv(int mode, const BatchGemvParams& p, int num_sms, c
     const int groups = (p.M + kBgRows - 1) / kBgRows;
     // Small matrices: fewer warps per CTA so that every SM streams part of the
     // weights; large ones (the LM head): full CTAs looping over the groups.
-    const int warps = std::max(1, std::min(kBgWarps, (groups + num_sms - 1) / num_sms));
-    const int grid = std::min((groups + warps - 1) / warps, num_sms);
-    const dim3 block(32 * warps);
+    // Row groups per CTA needed to cover the matrix with one CTA per SM; the
+    // spare warps split each group's K range (teams of wpg warps).
+    const int per_cta = (groups + num_sms - 1) / num_sms;
+    BatchGemvParams q = p;
+    q.wpg = std::max(1, kBgWarps / std::min(per_cta, kBgWarps));
+    const int teams = kBgWarps / q.wpg;
+    const int grid = std::min((groups + teams - 1) / teams, num_sms);
+    const dim3 block(kBgThreads);
     cudaError_t e;
     switch (mode) {
         case kGemvPlain:
             e = cudaFuncSetAttribute(batch_gemv_kernel<kGemvPlain>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem));
-            return e != cudaSuccess ? e : launch_pdl(batch_gemv_kernel<kGemvPlain>, dim3(grid), block, smem, s, p);
+            return e != cudaSuccess ? e : launch_pdl(batch_gemv_kernel<kGemvPlain>, dim3(grid), block, smem, s, q);
         case kGemvSwiGLU:
             e = cudaFuncSetAttribute(batch_gemv_kernel<kGemvSwiGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem));
             return e != cudaSuccess ? e
-                                    : launch_pdl(batch_gemv_kernel<kGemvSwiGLU>, dim3(grid), block, smem, s, p);
+                                    : launch_pdl(batch_gemv_kernel<kGemvSwiGLU>, dim3(grid), block, smem, s, q);
         case kGemvResidual:
             e = cudaFuncSetAttribute(batch_gemv_kernel<kGemvResidual>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem));
             return e != cudaSuccess ? e
-                                    : launch_pdl(batch_gemv_kernel<kGemvResidual>, dim3(grid), block, smem, s, p);
+                                    : launch_pdl(batch_gemv_kernel<kGemvResidual>, dim3(grid), block, smem, s, q);
         case kGemvLogits:
             e = cudaFuncSetAttribute(batch_gemv_kernel<kGemvLogits>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem));
             return e != cudaSuccess ? e
-                                    : launch_pdl(batch_gemv_kernel<kGemvLogits>, dim3(grid), block, smem, s, p);
+                                    : launch_pdl(batch_gemv_kernel<kGemvLogits>, dim3(grid), block, smem, s, q);
         default:
             return cudaErrorInvalidValue;
     }
