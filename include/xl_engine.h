@@ -257,8 +257,8 @@ XL_API int xl_op_lm_head(const float* x, const float* gamma, const float* table,
 /* sample_cpu (src/inference.cu:69-114) on the device with the uniform r
  * supplied: top-1024 by value, / (T + 0.001), softmax, top-p prefix, draw.
  * logits must already carry the repetition penalty.  workspace:
- * xl_op_sample_workspace_bytes(vocab) bytes; synchronous (the id is
- * returned in *token_out). */
+ * xl_op_sample_workspace_bytes(vocab) bytes (any contents; cleared on the
+ * stream by the call); synchronous (the id is returned in *token_out). */
 XL_API size_t xl_op_sample_workspace_bytes(int vocab);
 XL_API int xl_op_sample(const float* logits, int vocab, float temperature, float top_p, float r, int* token_out,
                         void* workspace, void* stream);

@@ -67,7 +67,7 @@ def test_batch_greedy_matches_oracle_per_sequence(eng_mod, shape_name, steps):
     for step in range(steps):
         n0 = eng_mod.kernel_launches()
         out = bd.step(teach, temperature=0.7, top_p=0.0, repetition_penalty=1.0)
-        assert eng_mod.kernel_launches() - n0 == 1 + 6 * sh.layers + 2  # inputs, layers, LM head, samplers
+        assert eng_mod.kernel_launches() - n0 == 1 + 6 * sh.layers + 2  # inputs, layers, LM head, greedy finish
         nxt = []
         for b in range(B):
             ref = ports[b].decode(teach[b])
@@ -101,7 +101,9 @@ def test_batch_sampled_draws_match_sample_cpu(eng_mod):
         hist.append([tok])
         toks.append(tok)
     for step in range(5):
+        n0 = eng_mod.kernel_launches()
         out = bd.step(toks, temperature=T, top_p=P, repetition_penalty=RP)
+        assert eng_mod.kernel_launches() - n0 == 1 + 6 * sh.layers + 1 + 4  # ..., LM head, sampler chain
         for b in range(B):
             got = logits_of(bd, b, sh.vocab)
             u = float(S.philox_uniforms(seeds[b], 1, step + 1)[0])

@@ -116,8 +116,10 @@ def test_tiny_kv_reset_rounds(eng_mod, tiny_weights, path):
 
 def test_tiny_kernel_events_and_launch_count(eng_mod, tiny_weights):
     """Event nodes around the persistent kernel time it alone (within the step),
-    change no token, and the library counts the decode graph's two kernels
-    (persistent step + sampler) at every replay."""
+    change no token, and the library counts the decode graph's kernels at every
+    replay: a greedy step is the persistent kernel alone (its last CTA writes the
+    argmax as the id), a sampled step adds the sampler chain (three histogram
+    passes and the gather)."""
     sh = S.TINY
     ids = [int(t) for t in np.random.default_rng(5).integers(0, sh.vocab, 9)]
     toks = {}
@@ -130,13 +132,16 @@ def test_tiny_kernel_events_and_launch_count(eng_mod, tiny_weights):
         for _ in range(4):
             n0 = eng_mod.kernel_launches()
             t = eng.next_token(t, top_p=0.0, repetition_penalty=1.0)
-            assert eng_mod.kernel_launches() - n0 == 2
+            assert eng_mod.kernel_launches() - n0 == 1
             seq.append(t)
             k = eng.last_kernel_ms()
             if ev:
                 assert 0.0 < k <= eng.last_device_ms()
             else:
                 assert k == -1.0
+        n0 = eng_mod.kernel_launches()
+        eng.next_token(t, temperature=0.7, top_p=0.9, repetition_penalty=1.1)
+        assert eng_mod.kernel_launches() - n0 == 5
         toks[ev] = seq
     assert toks[0] == toks[1]
 

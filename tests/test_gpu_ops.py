@@ -175,6 +175,49 @@ def test_sample(torch_cuda, temperature, top_p, r):
     assert tok.value == O.sample(logits, temperature, top_p, 1.0, [], r)
 
 
+def sample_logits(dist, g):
+    """Logit vectors that drive each branch of the sampler's candidate select."""
+    n = 151669
+    if dist == "ties_in_window":  # 0.1 steps: a few hundred ids tie at the 1024th value
+        return (np.round(g.standard_normal(n) * 1.2, 1)).astype(np.float32)
+    if dist == "wide_tie":  # integers: ~9000 ids tie at the threshold (ordered collection)
+        return np.round(g.standard_normal(n)).astype(np.float32)
+    if dist == "constant":  # every id ties: the 1024 lowest ids are the candidates
+        return np.full(n, 0.5, np.float32)
+    if dist in ("signed_zeros", "signed_zeros_wide"):  # +0.0 and -0.0 compare equal, lower id first
+        x = (np.float32(-1.0) - g.random(n).astype(np.float32)).astype(np.float32)
+        ids = g.permutation(n)
+        nz = 2000 if dist == "signed_zeros" else 20000
+        x[ids[:nz]] = np.where(g.random(nz) < 0.5, np.float32(0.0), np.float32(-0.0))
+        x[ids[nz:nz + 900]] = 5.0
+        return x
+    if dist == "narrow":  # one exponent bin: the first radix pass cannot narrow
+        return (np.float32(10.0) + g.standard_normal(n).astype(np.float32) * np.float32(1e-3)).astype(np.float32)
+    if dist == "small_vocab":  # fewer ids than candidates
+        return (g.standard_normal(700) * 2).astype(np.float32)
+    if dist == "mid_vocab":  # all ids gathered without a radix pass
+        return (g.standard_normal(3000) * 2).astype(np.float32)
+    raise ValueError(dist)
+
+
+@pytest.mark.parametrize("dist", ["ties_in_window", "wide_tie", "constant", "signed_zeros", "signed_zeros_wide",
+                                  "narrow", "small_vocab", "mid_vocab"])
+def test_sample_select_branches(torch_cuda, dist):
+    """The candidate select gathers ids at or above a radix prefix unordered and sorts
+    them, or (a tie wider than its buffer) collects them in id order; every branch must
+    give sample_cpu's candidate list, ties to the lower id."""
+    torch = torch_cuda
+    g = rng(41)
+    logits = sample_logits(dist, g)
+    n = logits.size
+    dl = dev(torch, logits)
+    ws = torch.zeros(X.lib().xl_op_sample_workspace_bytes(n), dtype=torch.uint8, device="cuda")
+    for temperature, top_p, r in [(0.7, 0.9, 0.3), (1.0, 1.0, 0.999), (0.5, 0.95, 0.61), (1.0, 1.0, 0.0)]:
+        tok = C.c_int(-1)
+        X.check(X.lib().xl_op_sample(X.ptr(dl), n, temperature, top_p, r, C.byref(tok), X.ptr(ws), X.stream()))
+        assert tok.value == O.sample(logits, temperature, top_p, 1.0, [], r), (dist, temperature, top_p, r)
+
+
 @pytest.mark.parametrize("tensor_cores", [True, False], ids=["tcgen05_3xtf32", "fp32_fma"])
 @pytest.mark.parametrize("mode,n,m,k", [(0, 37, H, H), (0, 512, 3 * H, H), (2, 37, H, F), (1, 77, 2 * F, H),
                                         (0, 5, 576, 192), (2, 130, 200, 64)])

@@ -434,6 +434,7 @@ BatchDecoder::~BatchDecoder() {
     if (!eng_) return;
     cudaSetDevice(eng_->device_);
     if (exec_) cudaGraphExecDestroy(exec_);
+    if (exec_s_) cudaGraphExecDestroy(exec_s_);
     if (arena_) cudaFree(arena_);
     if (h_in_) cudaFreeHost(h_in_);
     if (h_st_) cudaFreeHost(h_st_);
@@ -498,6 +499,9 @@ int BatchDecoder::init() {
     add(&in_, kBatch * sizeof(StepIn));
     add(&tokens_, kBatch * 4);
     add(&ticket_, 256);
+    samp_grid_ = sample_grid(E.V_, E.num_sms_, kBatch);
+    samp_stride_ = sample_work_bytes(E.V_, samp_grid_);
+    add(&samp_work_, kBatch * samp_stride_);
     size_t total = 0;
     for (auto& pr : plan) total += (pr.second + 255) / 256 * 256;
     XB_CUDA(cudaMalloc(reinterpret_cast<void**>(&arena_), total));
@@ -519,7 +523,7 @@ int BatchDecoder::init() {
     return capture();
 }
 
-int BatchDecoder::enqueue(cudaStream_t s) {
+int BatchDecoder::enqueue(cudaStream_t s, bool sampled) {
     Engine& E = *eng_;
     const int H = E.H_, Hl = E.Hl_, Fl = E.Fl_, T = E.T_, V = E.V_, heads = E.heads_l_;
     count_launch();
@@ -605,27 +609,36 @@ int BatchDecoder::enqueue(cudaStream_t s) {
     sp.st = st_;
     sp.rep_flags = rep_;
     sp.full = 0;
-    XB_CUDA(launch_sample_batch(sp, kBatch, V, true, s));
+    sp.work = samp_work_;
+    sp.work_stride = samp_stride_;
+    sp.stride = V;
+    sp.grid = samp_grid_;
+    if (sampled) XB_CUDA(launch_sample_chain(sp, kBatch, true, s));
+    else XB_CUDA(launch_sample_finish(sp, kBatch, true, s));
     return XL_OK;
 }
 
 int BatchDecoder::capture() {
     cudaStream_t s = eng_->stream_;
-    cudaGraph_t g = nullptr;
-    XB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-    const long long recorded0 = launch_count();
-    const int rc = enqueue(s);
-    graph_kernels_ = launch_count() - recorded0;
-    count_graph_kernels(-graph_kernels_);
-    const cudaError_t ce = cudaStreamEndCapture(s, &g);
-    if (rc != XL_OK) {
-        if (g) cudaGraphDestroy(g);
-        return rc;
+    for (int sampled = 0; sampled < 2; ++sampled) {
+        cudaGraphExec_t& exec = sampled ? exec_s_ : exec_;
+        long long& kernels = sampled ? graph_kernels_s_ : graph_kernels_;
+        cudaGraph_t g = nullptr;
+        XB_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        const long long recorded0 = launch_count();
+        const int rc = enqueue(s, sampled != 0);
+        kernels = launch_count() - recorded0;
+        count_graph_kernels(-kernels);
+        const cudaError_t ce = cudaStreamEndCapture(s, &g);
+        if (rc != XL_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+        const cudaError_t ie = cudaGraphInstantiate(&exec, g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) return cuda_fail(ie, "cudaGraphInstantiate");
     }
-    if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
-    const cudaError_t ie = cudaGraphInstantiate(&exec_, g, 0);
-    cudaGraphDestroy(g);
-    if (ie != cudaSuccess) return cuda_fail(ie, "cudaGraphInstantiate");
     return XL_OK;
 }
 
@@ -704,8 +717,9 @@ int BatchDecoder::decode(const int* tokens, float temperature, float top_p, floa
     cudaStream_t s = E.stream_;
     XB_CUDA(cudaMemcpyAsync(in_, h_in_, kBatch * sizeof(StepIn), cudaMemcpyHostToDevice, s));
     XB_CUDA(cudaEventRecord(ev0_, s));
-    XB_CUDA(cudaGraphLaunch(exec_, s));
-    count_graph_kernels(graph_kernels_);
+    const bool sampled = top_p > 0.0f;
+    XB_CUDA(cudaGraphLaunch(sampled ? exec_s_ : exec_, s));
+    count_graph_kernels(sampled ? graph_kernels_s_ : graph_kernels_);
     XB_CUDA(cudaEventRecord(ev1_, s));
     XB_CUDA(cudaMemcpyAsync(h_st_, st_, kBatch * sizeof(DevState), cudaMemcpyDeviceToHost, s));
     XB_CUDA(cudaStreamSynchronize(s));

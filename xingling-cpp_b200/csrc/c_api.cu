@@ -332,8 +332,16 @@ int xl_op_lm_head(const float* x, const float* gamma, const float* table, float*
     return XL_OK;
 }
 
+namespace {
+// The sampler chain of xl_op_sample runs on as many vocab slices as a B200 has SMs.
+constexpr int kOpSampleSms = 148;
+size_t op_flags_bytes(int vocab) { return (static_cast<size_t>(vocab) + 255) / 256 * 256; }
+}  // namespace
+
 size_t xl_op_sample_workspace_bytes(int vocab) {
-    return (sizeof(OpState) + 255) / 256 * 256 + static_cast<size_t>(vocab > 0 ? vocab : 0);
+    if (vocab <= 0) return 0;
+    return (sizeof(OpState) + 255) / 256 * 256 + op_flags_bytes(vocab) +
+           xl::sample_work_bytes(vocab, xl::sample_grid(vocab, kOpSampleSms, 1));
 }
 
 int xl_op_sample(const float* logits, int vocab, float temperature, float top_p, float r, int* token_out,
@@ -343,12 +351,17 @@ int xl_op_sample(const float* logits, int vocab, float temperature, float top_p,
     cudaStream_t s = as_stream(stream);
     xl::DevState* st = static_cast<xl::DevState*>(workspace);
     uint8_t* flags = static_cast<uint8_t*>(workspace) + (sizeof(OpState) + 255) / 256 * 256;
+    void* work = flags + op_flags_bytes(vocab);
+    const int grid = xl::sample_grid(vocab, kOpSampleSms, 1);
     xl::DevState hs{};
     hs.in.temperature = temperature;
     hs.in.top_p = top_p;
     hs.in.rp = 1.0f;
     hs.in.uniform = r;
     int rc = cuda_status(cudaMemcpyAsync(st, &hs, sizeof(hs), cudaMemcpyHostToDevice, s), "xl_op_sample copy");
+    if (rc != XL_OK) return rc;
+    // The chain leaves its work area zeroed; clearing it here also covers a workspace never used before.
+    rc = cuda_status(cudaMemsetAsync(work, 0, xl::sample_work_bytes(vocab, grid), s), "xl_op_sample clear");
     if (rc != XL_OK) return rc;
     xl::SampleParams sp{};
     sp.logits = logits;
@@ -357,12 +370,20 @@ int xl_op_sample(const float* logits, int vocab, float temperature, float top_p,
     sp.st = st;
     sp.rep_flags = flags;
     sp.full = 1;
-    rc = cuda_status(xl::launch_sample(sp, false, s), "xl_op_sample");
+    sp.work = work;
+    sp.work_stride = xl::sample_work_bytes(vocab, grid);
+    sp.stride = vocab;
+    sp.grid = grid;
+    rc = cuda_status(xl::launch_sample_chain(sp, 1, false, s), "xl_op_sample");
     if (rc != XL_OK) return rc;
     rc = cuda_status(cudaMemcpyAsync(&hs, st, sizeof(hs), cudaMemcpyDeviceToHost, s), "xl_op_sample copy");
     if (rc != XL_OK) return rc;
     rc = cuda_status(cudaStreamSynchronize(s), "xl_op_sample sync");
     if (rc != XL_OK) return rc;
+    if (hs.err != 0) {
+        xl::set_error("xl_op_sample: device error word " + std::to_string(hs.err));
+        return XL_ERR_DEVICE;
+    }
     *token_out = hs.token_out;
     return XL_OK;
 }

@@ -10,7 +10,7 @@
 //  attn_decode_kernel RoPE (src/rope.cu:20-45) + KV append + split-K
 //                     attention over the head-major cache, replacing
 //                     MultiHeadAttention::forward (src/attn.cu:372-447, 490-547).
-//  sample_kernel      repetition-penalised top-1024 / temperature / top-p
+//  sample_*_kernel    repetition-penalised top-1024 / temperature / top-p
 //                     sampling on the device, replacing sample_cpu
 //                     (src/inference.cu:58-114).
 #include <math.h>
@@ -320,9 +320,10 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnDecodeParams
 }
 
 // ---------------------------------------------------------------------------
-// Sampler: one CTA of 1024 threads.
-constexpr int kSampThreads = 1024;
+// Sampler: the histogram / gather chain declared with SampleWorkHdr.
 constexpr int kSampWarps = kSampThreads / 32;
+constexpr int kSampLoads = 4;      // keys per thread loaded before any is used
+constexpr int kErrSample = 8;      // DevState::err bit: the chain found inconsistent counts
 
 // Block-wide inclusive scan of one int per thread.
 __device__ int block_inclusive_scan(int v, int* warp_tot) {
@@ -351,9 +352,16 @@ __device__ int block_inclusive_scan(int v, int* warp_tot) {
 
 // Temperature, softmax over the kc sorted candidates (packed (key, ~global
 // id)), top-p and the draw with the step's uniform: the arithmetic of
-// src/inference.cu:87-111, sequential float sums in candidate order on one
-// thread.  All threads of the block call it; thread 0 writes *s_token.
+// src/inference.cu:87-111.  The two float sums (the softmax denominator and
+// the running probability) are sequential in candidate order on one thread,
+// as in the reference; the divides and the two "first index" searches of the
+// top-p cut and the draw run across the block on the stored prefix sums, which
+// gives the same index as the reference's early-exit loops because the prefix
+// sums never decrease.  All threads of the block call it; thread 0 writes
+// *s_token.
 __device__ void draw_token(const unsigned long long* cand, int kc, float* prob, const DevState* st, int* s_token) {
+    __shared__ float s_sum;
+    __shared__ int s_first, s_pick;
     const int tid = threadIdx.x;
     const float top_p = st->in.top_p;
     const float inv_t_den = st->in.temperature + 0.001f;
@@ -364,192 +372,386 @@ __device__ void draw_token(const unsigned long long* cand, int kc, float* prob, 
         e = expf(v - v0);
     }
     prob[tid] = e;
+    if (tid == 0) {
+        s_first = kc;
+        s_pick = kc - 1;
+    }
     __syncthreads();
     if (tid == 0) {
         float sum_exp = 1.0f;
+#pragma unroll 16
         for (int i = 1; i < kc; ++i) sum_exp += prob[i];
-        prob[0] = prob[0] / sum_exp;
-        for (int i = 1; i < kc; ++i) prob[i] = prob[i] / sum_exp;
-        float total = 0.0f;
-        for (int i = 0; i < kc; ++i) {
-            total += prob[i];
-            if (total >= top_p) break;
-        }
-        const float r = st->in.uniform;
+        s_sum = sum_exp;
+    }
+    __syncthreads();
+    if (tid < kc) prob[tid] = prob[tid] / s_sum;
+    __syncthreads();
+    if (tid == 0) {
         float acc = 0.0f;
-        int pick = kc - 1;
+#pragma unroll 16
         for (int i = 0; i < kc; ++i) {
             acc += prob[i];
-            if (acc > r * total) {
-                pick = i;
-                break;
-            }
+            prob[i] = acc;
         }
-        *s_token = static_cast<int>(0xffffffffu - static_cast<uint32_t>(cand[pick] & 0xffffffffull));
     }
+    __syncthreads();
+    // top-p: the first prefix reaching top_p, else the whole list
+    if (tid < kc && prob[tid] >= top_p) atomicMin(&s_first, tid);
+    __syncthreads();
+    const float total = prob[min(s_first, kc - 1)];
+    const float thr = st->in.uniform * total;
+    if (tid < kc && prob[tid] > thr) atomicMin(&s_pick, tid);
+    __syncthreads();
+    if (tid == 0) *s_token = static_cast<int>(0xffffffffu - static_cast<uint32_t>(cand[s_pick] & 0xffffffffull));
 }
 
-__device__ __forceinline__ void sample_block(const SampleParams& p) {
+// Device view of one sequence's work area (layout of sample_work_bytes).
+struct SampleWork {
+    SampleWorkHdr* h;
+    unsigned int* hist;        // [2048]
+    unsigned long long* cand;  // [kCandCap]
+    int* tie_cnt;              // [grid]
+    unsigned int* tie_ids;     // [grid][slice]
+};
+constexpr size_t kWorkHdrBytes = 256;
+constexpr size_t kWorkHistBytes = 2048 * sizeof(unsigned int);
+constexpr size_t kWorkCandBytes = static_cast<size_t>(kCandCap) * sizeof(unsigned long long);
+__host__ __device__ inline size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+__host__ __device__ inline int sample_slice(int V, int grid) { return (V + grid - 1) / grid; }
+
+__device__ __forceinline__ SampleWork work_of(const SampleParams& p, int b) {
+    char* base = static_cast<char*>(p.work) + static_cast<size_t>(b) * p.work_stride;
+    SampleWork w;
+    w.h = reinterpret_cast<SampleWorkHdr*>(base);
+    base += kWorkHdrBytes;
+    w.hist = reinterpret_cast<unsigned int*>(base);
+    base += kWorkHistBytes;
+    w.cand = reinterpret_cast<unsigned long long*>(base);
+    base += kWorkCandBytes;
+    w.tie_cnt = reinterpret_cast<int*>(base);
+    base += align256(static_cast<size_t>(p.grid) * sizeof(int));
+    w.tie_ids = reinterpret_cast<unsigned int*>(base);
+    return w;
+}
+
+__device__ __forceinline__ bool greedy_step(const SampleParams& p, const DevState* st) {
+    return !(st->in.top_p > 0.0f) && !p.full;
+}
+
+// The step's id: state, repetition flag, KV position (src/inference.cu:113 and
+// the caller's history update).
+__device__ __forceinline__ void finish_token(const SampleParams& p, int b, DevState* st, int tok) {
+    st->token_out = tok;
+    const int local = tok - p.v0;
+    if (local >= 0 && local < p.V) p.rep_flags[static_cast<size_t>(b) * p.stride + local] = 1;
+    if (st->in.decode_mode) st->pos += 1;
+}
+
+// One radix pass over this CTA's vocab slice (grid (p.grid, batch)):
+// pass 0 counts the top 11 key bits of every id (shared-memory histogram,
+// then one global add per non-empty bin); passes 1 and 2 count the next 11 /
+// 10 bits of the few ids inside the chosen prefix straight into the global
+// histogram.  The last CTA to finish picks the bin that holds the kc-th
+// largest key, extends the prefix, zeroes the histogram and decides whether
+// the ids at or above the prefix are few enough to gather.
+__global__ void __launch_bounds__(kSampThreads) sample_hist_kernel(const SampleParams p, int pass) {
     __shared__ unsigned int hist[2048];
-    __shared__ unsigned long long cand[kTopK];
-    __shared__ float prob[kTopK];
     __shared__ int warp_tot[32];
-    __shared__ int wcnt[2][kSampWarps];
-    __shared__ unsigned int sel_bin;
-    __shared__ int sel_need;
-    __shared__ int s_token;
+    __shared__ int s_last;
+    __shared__ unsigned int s_bin, s_cnt;
+    __shared__ int s_excl;
 
     pdl_launch_dependents();
     pdl_wait();
-
-    DevState* st = p.st;
+    const int b = blockIdx.y;
+    DevState* st = p.st + b;
+    if (greedy_step(p, st)) return;
+    const SampleWork w = work_of(p, b);
     const int tid = threadIdx.x;
-    const int lane = tid & 31, warp = tid >> 5;
-    const float top_p = st->in.top_p;
-    if (!(top_p > 0.0f) && !p.full) {
-        // top_p <= 0: the prefix loop of src/inference.cu:100-103 stops at the
-        // first (largest) candidate and any r in [0,1) returns it.
-        if (tid == 0) s_token = unpack_argmax_index(st->argmax_final);
-    } else {
-        const int V = p.V;
-        const int kc = V < kTopK ? V : kTopK;
-        // --- radix select of the kc-th largest key: 11 + 11 + 10 bits ---
-        uint32_t prefix = 0, pmask = 0;
-        int need = kc;
-        const int shifts[3] = {21, 10, 0};
-        const int bits[3] = {11, 11, 10};
-        for (int pass = 0; pass < 3; ++pass) {
-            for (int i = tid; i < 2048; i += kSampThreads) hist[i] = 0;
-            __syncthreads();
-            const int sh = shifts[pass];
-            const uint32_t bm = (1u << bits[pass]) - 1u;
-            // Warp-aggregated counts: logits crowd into few bins, so lanes that
-            // share a bin add once (their leader adds the group's size).
-            for (int base = warp * 32; base < V; base += kSampThreads) {
-                const int i = base + lane;
-                uint32_t bin = 0;
-                bool act = false;
-                if (i < V) {
-                    const uint32_t k = float_key(p.logits[i]);
-                    act = (k & pmask) == prefix;
-                    bin = (k >> sh) & bm;
-                }
-                const unsigned amask = __ballot_sync(0xffffffffu, act);
-                if (act) {
-                    const unsigned peers = __match_any_sync(amask, bin);
-                    if (lane == __ffs(peers) - 1) atomicAdd(&hist[bin], static_cast<unsigned>(__popc(peers)));
-                }
-            }
-            __syncthreads();
-            // Thread t owns bins (2047 - 2t, 2046 - 2t); scan counts from the top.
-            const int bhi = 2047 - 2 * tid, blo = 2046 - 2 * tid;
-            const int chi = static_cast<int>(hist[bhi]), clo = static_cast<int>(hist[blo]);
-            const int incl = block_inclusive_scan(chi + clo, warp_tot);
-            const int excl = incl - chi - clo;
-            if (excl < need && need <= excl + chi) {
-                sel_bin = static_cast<unsigned>(bhi);
-                sel_need = need - excl;
-            } else if (excl + chi < need && need <= incl) {
-                sel_bin = static_cast<unsigned>(blo);
-                sel_need = need - excl - chi;
-            }
-            __syncthreads();
-            prefix |= sel_bin << sh;
-            pmask |= bm << sh;
-            need = sel_need;
-            __syncthreads();
+    const int V = p.V;
+    const int kc = V < kTopK ? V : kTopK;
+    if (pass == 0 && V <= kCandCap) {  // every id is a candidate
+        if (blockIdx.x == 0 && tid == 0) {
+            w.h->n_ge = V;
+            w.h->done = 1;
         }
-        const uint32_t T = prefix;  // key of the kc-th largest value
-        const int need_eq = need;   // how many ids with key == T are taken (lowest ids first)
-        const int n_gt = kc - need_eq;
-        // --- ordered collection: warp w scans ids [w*per, (w+1)*per) ---
-        const int per = ((V + kSampWarps * 32 - 1) / (kSampWarps * 32)) * 32;
-        const int lo = warp * per, hi = min(V, lo + per);
-        int cgt = 0, ceq = 0;
-        for (int b = lo; b < hi; b += 32) {
-            const int i = b + lane;
-            const uint32_t k = i < hi ? float_key(p.logits[i]) : 0u;
-            cgt += __popc(__ballot_sync(0xffffffffu, i < hi && k > T));
-            ceq += __popc(__ballot_sync(0xffffffffu, i < hi && k == T));
-        }
-        if (lane == 0) {
-            wcnt[0][warp] = cgt;
-            wcnt[1][warp] = ceq;
-        }
+        return;
+    }
+    if (w.h->done) return;
+    const uint32_t prefix = w.h->prefix, pmask = w.h->pmask;
+    const int sh = pass == 0 ? 21 : pass == 1 ? 10 : 0;
+    const uint32_t bm = pass == 2 ? 0x3ffu : 0x7ffu;
+    const int S = sample_slice(V, p.grid);
+    const int lo = blockIdx.x * S, hi = min(V, lo + S);
+    const float* x = p.logits + static_cast<size_t>(b) * p.stride;
+    if (pass == 0) {
+        for (int i = tid; i < 2048; i += kSampThreads) hist[i] = 0;
         __syncthreads();
-        int off_gt = 0, off_eq = 0;
-        for (int w = 0; w < warp; ++w) {
-            off_gt += wcnt[0][w];
-            off_eq += wcnt[1][w];
+    }
+    for (int base = lo; base < hi; base += kSampThreads * kSampLoads) {
+        uint32_t k[kSampLoads];
+#pragma unroll
+        for (int j = 0; j < kSampLoads; ++j) {
+            const int i = base + j * kSampThreads + tid;
+            k[j] = i < hi ? float_key(__ldcg(x + i)) : 0u;
         }
-        const unsigned lt = (1u << lane) - 1u;
-        for (int b = lo; b < hi; b += 32) {
-            const int i = b + lane;
-            const uint32_t k = i < hi ? float_key(p.logits[i]) : 0u;
-            const bool gt = i < hi && k > T;
-            const bool eq = i < hi && k == T;
-            const unsigned bg = __ballot_sync(0xffffffffu, gt);
-            const unsigned be = __ballot_sync(0xffffffffu, eq);
-            const unsigned long long packed =
-                (static_cast<unsigned long long>(k) << 32) | (0xffffffffu - static_cast<uint32_t>(p.v0 + i));
-            if (gt) {
-                const int at = off_gt + __popc(bg & lt);
-                if (at < n_gt) cand[at] = packed;
+#pragma unroll
+        for (int j = 0; j < kSampLoads; ++j) {
+            const int i = base + j * kSampThreads + tid;
+            if (i >= hi) continue;
+            if (pass == 0) {
+                atomicAdd(&hist[k[j] >> 21], 1u);
+            } else if ((k[j] & pmask) == prefix) {
+                atomicAdd(&w.hist[(k[j] >> sh) & bm], 1u);
             }
-            if (eq) {
-                const int r = off_eq + __popc(be & lt);
-                if (r < need_eq && n_gt + r < kTopK) cand[n_gt + r] = packed;
-            }
-            off_gt += __popc(bg);
-            off_eq += __popc(be);
         }
-        for (int i = kc + tid; i < kTopK; i += kSampThreads) cand[i] = 0ull;
+    }
+    if (pass == 0) {
         __syncthreads();
-        // --- bitonic sort, descending by (value, then lower id) ---
-        for (int k = 2; k <= kTopK; k <<= 1) {
-            for (int j = k >> 1; j > 0; j >>= 1) {
-                const int i = tid;
-                const int ixj = i ^ j;
-                if (ixj > i) {
-                    const unsigned long long a = cand[i], b = cand[ixj];
-                    const bool desc = (i & k) == 0;
-                    if (desc ? (a < b) : (a > b)) {
-                        cand[i] = b;
-                        cand[ixj] = a;
-                    }
-                }
-                __syncthreads();
-            }
+        for (int i = tid; i < 2048; i += kSampThreads) {
+            const unsigned int c = hist[i];
+            if (c) atomicAdd(&w.hist[i], c);
         }
-        if (p.cand_out) {
-            // Tensor-parallel select: this shard's sorted top-kc, merged across ranks by sample_merge_kernel.
-            for (int i = tid; i < kTopK; i += kSampThreads) p.cand_out[i] = cand[i];
-            return;
-        }
-        // --- temperature, softmax over the candidates, top-p, draw ---
-        draw_token(cand, kc, prob, st, &s_token);
     }
     __syncthreads();
     if (tid == 0) {
-        const int tok = s_token;
-        st->token_out = tok;
-        const int local = tok - p.v0;
-        if (local >= 0 && local < p.V) p.rep_flags[local] = 1;
-        if (st->in.decode_mode) st->pos += 1;
+        __threadfence();
+        s_last = atomicAdd(&w.h->ticket, 1) == static_cast<int>(gridDim.x) - 1;
+        s_bin = 0;
+        s_cnt = 0;
+        s_excl = -1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int need = kc - w.h->n_above;
+    // Thread t owns bins (2047 - 2t, 2046 - 2t); scan counts from the top.
+    const int bhi = 2047 - 2 * tid, blo = 2046 - 2 * tid;
+    const int chi = static_cast<int>(__ldcg(w.hist + bhi)), clo = static_cast<int>(__ldcg(w.hist + blo));
+    const int incl = block_inclusive_scan(chi + clo, warp_tot);
+    const int excl = incl - chi - clo;
+    if (excl < need && need <= excl + chi) {
+        s_bin = static_cast<unsigned>(bhi);
+        s_cnt = static_cast<unsigned>(chi);
+        s_excl = excl;
+    } else if (excl + chi < need && need <= incl) {
+        s_bin = static_cast<unsigned>(blo);
+        s_cnt = static_cast<unsigned>(clo);
+        s_excl = excl + chi;
+    }
+    w.hist[bhi] = 0;
+    w.hist[blo] = 0;
+    __syncthreads();
+    if (tid == 0) {
+        if (s_excl < 0) {
+            atomicOr(&st->err, kErrSample);
+            w.h->done = 1;  // the gather reports the error and resets the work area
+            w.h->exact = 0;
+            w.h->n_ge = -1;
+        } else {
+            const int n_above = w.h->n_above + s_excl;
+            const int n_ge = n_above + static_cast<int>(s_cnt);
+            w.h->prefix = prefix | (s_bin << sh);
+            w.h->pmask = pmask | (bm << sh);
+            w.h->n_above = n_above;
+            w.h->n_ge = n_ge;
+            w.h->passes = pass + 1;
+            w.h->exact = n_ge > kCandCap;  // only after the last pass: the prefix is then the full key
+            w.h->done = n_ge <= kCandCap || pass == 2;
+        }
+        w.h->ticket = 0;
     }
 }
 
-__global__ void __launch_bounds__(kSampThreads) sample_kernel(const SampleParams p) { sample_block(p); }
+// Descending bitonic sort of M x 1024 packed candidates, element i at
+// a[i] (thread i % 1024 holds elements tid, 1024 + tid, ...): distances of
+// 1024 and more compare registers of one thread, 32 .. 512 go through shared
+// memory, below 32 through warp shuffles.
+template <int M>
+__device__ void bitonic_sort_desc(unsigned long long* a) {
+    constexpr int n = M * kSampThreads;
+    const int tid = threadIdx.x;
+    unsigned long long v[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) v[m] = a[m * kSampThreads + tid];
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j >= kSampThreads) {
+                const int mj = j / kSampThreads;
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+#pragma unroll
+                    for (int m2 = m + 1; m2 < M; ++m2) {
+                        if ((m ^ m2) != mj) continue;
+                        const int i = m * kSampThreads + tid;
+                        const bool desc = (i & k) == 0;
+                        const unsigned long long x = v[m], y = v[m2];
+                        if (desc ? (x < y) : (x > y)) {
+                            v[m] = y;
+                            v[m2] = x;
+                        }
+                    }
+                }
+            } else if (j >= 32) {
+                __syncthreads();
+#pragma unroll
+                for (int m = 0; m < M; ++m) a[m * kSampThreads + tid] = v[m];
+                __syncthreads();
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    const int i = m * kSampThreads + tid;
+                    const unsigned long long y = a[m * kSampThreads + (tid ^ j)];
+                    const bool keep_max = ((i & j) == 0) == ((i & k) == 0);
+                    v[m] = keep_max ? (v[m] > y ? v[m] : y) : (v[m] < y ? v[m] : y);
+                }
+            } else {
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    const int i = m * kSampThreads + tid;
+                    const unsigned long long y = __shfl_xor_sync(0xffffffffu, v[m], j);
+                    const bool keep_max = ((i & j) == 0) == ((i & k) == 0);
+                    v[m] = keep_max ? (v[m] > y ? v[m] : y) : (v[m] < y ? v[m] : y);
+                }
+            }
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < M; ++m) a[m * kSampThreads + tid] = v[m];
+    __syncthreads();
+}
 
-// kBatch independent sequences, one CTA each: sequence b's logits at
-// logits + b * stride, its flags at rep_flags + b * stride, its state st + b.
-__global__ void __launch_bounds__(kSampThreads) sample_batch_kernel(const SampleParams p, int stride) {
-    SampleParams q = p;
-    const int b = blockIdx.x;
-    q.logits = p.logits + static_cast<size_t>(b) * stride;
-    q.rep_flags = p.rep_flags + static_cast<size_t>(b) * stride;
-    q.st = p.st + b;
-    sample_block(q);
+// Gather and draw (grid (p.grid, batch)).  Each CTA adds the ids of its slice
+// whose key is at or above the chosen prefix (above it, when the prefix is an
+// exact threshold with a wide tie) to the candidate list, packed (key, ~global
+// id), and, for an exact threshold, lists its tied ids in id order.  The last
+// CTA loads the list, appends the lowest tied ids the count still needs,
+// sorts (value, then lower id) so that the first kc are sample_cpu's candidate
+// list, then draws (or, tensor parallel, writes the list out) and leaves the
+// work area zeroed.
+__global__ void __launch_bounds__(kSampThreads) sample_gather_kernel(const SampleParams p) {
+    __shared__ unsigned long long s_cand[kCandCap];
+    __shared__ float prob[kTopK];
+    __shared__ int tie_pre[kSampThreads + 1];
+    __shared__ int warp_tot[32];
+    __shared__ int s_last, s_token, s_run;
+
+    pdl_launch_dependents();
+    pdl_wait();
+    const int b = blockIdx.y;
+    DevState* st = p.st + b;
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (greedy_step(p, st)) {
+        if (blockIdx.x == 0 && tid == 0) finish_token(p, b, st, unpack_argmax_index(st->argmax_final));
+        return;
+    }
+    const SampleWork w = work_of(p, b);
+    const int V = p.V;
+    const int kc = V < kTopK ? V : kTopK;
+    const uint32_t prefix = w.h->prefix;
+    const int exact = w.h->exact;
+    const int n_ge = w.h->n_ge;
+    const bool ok = w.h->done && n_ge >= 0;
+    const int S = sample_slice(V, p.grid);
+    const int lo = blockIdx.x * S, hi = min(V, lo + S);
+    const float* x = p.logits + static_cast<size_t>(b) * p.stride;
+    const unsigned lt = (1u << lane) - 1u;
+    if (tid == 0) s_run = 0;
+    if (ok) {
+        for (int base = lo; base < hi; base += kSampThreads * kSampLoads) {
+            uint32_t k[kSampLoads];
+#pragma unroll
+            for (int j = 0; j < kSampLoads; ++j) {
+                const int i = base + j * kSampThreads + tid;
+                k[j] = i < hi ? float_key(__ldcg(x + i)) : 0u;
+            }
+#pragma unroll
+            for (int j = 0; j < kSampLoads; ++j) {
+                const int i = base + j * kSampThreads + tid;
+                const bool take = i < hi && (exact ? k[j] > prefix : k[j] >= prefix);
+                const unsigned bt = __ballot_sync(0xffffffffu, take);
+                if (bt) {
+                    const int leader = __ffs(bt) - 1;
+                    int slot = 0;
+                    if (lane == leader) slot = atomicAdd(&w.h->n_gt, __popc(bt));
+                    slot = __shfl_sync(0xffffffffu, slot, leader) + __popc(bt & lt);
+                    if (take && slot < kCandCap)
+                        w.cand[slot] = (static_cast<unsigned long long>(k[j]) << 32) |
+                                       (0xffffffffu - static_cast<uint32_t>(p.v0 + i));
+                }
+                if (exact) {  // block-uniform: list this slice's tied ids in id order
+                    const int tie = i < hi && k[j] == prefix;
+                    const int incl = block_inclusive_scan(tie, warp_tot);
+                    if (tie) w.tie_ids[static_cast<size_t>(blockIdx.x) * S + s_run + incl - 1] = static_cast<unsigned>(i);
+                    __syncthreads();
+                    if (tid == kSampThreads - 1) s_run += incl;
+                    __syncthreads();
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        if (exact) w.tie_cnt[blockIdx.x] = s_run;
+        __threadfence();
+        s_last = atomicAdd(&w.h->ticket, 1) == static_cast<int>(gridDim.x) - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // --- last CTA: candidate list, sort, draw ---
+    const int n_gt = exact ? w.h->n_above : n_ge;
+    const bool counts_ok = ok && __ldcg(&w.h->n_gt) == n_gt && n_gt <= kCandCap;
+    if (!counts_ok) {
+        if (tid == 0) {
+            atomicOr(&st->err, kErrSample);
+            finish_token(p, b, st, unpack_argmax_index(st->argmax_final));
+        }
+    } else {
+        int n_sort = kTopK;
+        while (n_sort < n_gt) n_sort <<= 1;
+        for (int i = tid; i < n_sort; i += kSampThreads) s_cand[i] = i < n_gt ? __ldcg(w.cand + i) : 0ull;
+        if (exact) {
+            // the need_eq lowest tied ids: slices in order, each slice's list in id order
+            const int need_eq = kc - n_gt;
+            const int c = tid < p.grid ? __ldcg(w.tie_cnt + tid) : 0;
+            const int incl = block_inclusive_scan(c, warp_tot);
+            tie_pre[tid + 1] = incl;
+            if (tid == 0) tie_pre[0] = 0;
+            __syncthreads();
+            for (int r = tid; r < need_eq; r += kSampThreads) {
+                int a = 0, z = p.grid - 1;  // the last slice whose first tie index is <= r
+                while (a < z) {
+                    const int mid = (a + z + 1) >> 1;
+                    if (tie_pre[mid] <= r) a = mid;
+                    else z = mid - 1;
+                }
+                const unsigned id = __ldcg(w.tie_ids + static_cast<size_t>(a) * S + (r - tie_pre[a]));
+                s_cand[n_gt + r] = (static_cast<unsigned long long>(prefix) << 32) | (0xffffffffu - (p.v0 + id));
+            }
+        }
+        __syncthreads();
+        if (n_sort == kTopK) bitonic_sort_desc<1>(s_cand);
+        else if (n_sort == 2 * kTopK) bitonic_sort_desc<2>(s_cand);
+        else bitonic_sort_desc<4>(s_cand);
+        if (p.cand_out) {
+            // Tensor-parallel select: this shard's sorted top-kc, merged across ranks by sample_merge_kernel.
+            p.cand_out[tid] = tid < kc ? s_cand[tid] : 0ull;
+        } else {
+            draw_token(s_cand, kc, prob, st, &s_token);
+            if (tid == 0) finish_token(p, b, st, s_token);
+        }
+    }
+    __syncthreads();
+    if (tid < static_cast<int>(sizeof(SampleWorkHdr) / sizeof(int))) reinterpret_cast<int*>(w.h)[tid] = 0;
+}
+
+// Greedy steps: the LM head's argmax is the step's id (grid (1, batch)).
+__global__ void __launch_bounds__(32) sample_finish_kernel(const SampleParams p) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int b = blockIdx.y;
+    if (threadIdx.x == 0) finish_token(p, b, p.st + b, unpack_argmax_index(p.st[b].argmax_final));
 }
 
 // Tensor-parallel merge of sample_cpu (src/inference.cu:58-114) over vocab
@@ -644,13 +846,37 @@ cudaError_t launch_attn_decode(const AttnDecodeParams& p, bool pdl, cudaStream_t
     return launch_ex(attn_decode_kernel, dim3(p.heads, attn_max_splits(p.max_ctx)), dim3(128), 0, pdl, s, p);
 }
 
-cudaError_t launch_sample(const SampleParams& p, bool pdl, cudaStream_t s) {
-    return launch_ex(sample_kernel, dim3(1), dim3(kSampThreads), 0, pdl, s, p);
+size_t sample_work_bytes(int V, int grid) {
+    if (V <= 0 || grid <= 0) return 0;
+    return kWorkHdrBytes + kWorkHistBytes + kWorkCandBytes + align256(static_cast<size_t>(grid) * sizeof(int)) +
+           align256(static_cast<size_t>(grid) * sample_slice(V, grid) * sizeof(unsigned int));
 }
 
-cudaError_t launch_sample_batch(const SampleParams& p, int batch, int stride, bool pdl, cudaStream_t s) {
-    if (batch <= 0) return cudaErrorInvalidValue;
-    return launch_ex(sample_batch_kernel, dim3(batch), dim3(kSampThreads), 0, pdl, s, p, stride);
+int sample_grid(int V, int num_sms, int batch) {
+    int g = num_sms / (batch > 0 ? batch : 1);
+    const int by_size = (V + 255) / 256;  // at least 256 ids per slice
+    if (g > by_size) g = by_size;
+    if (g > kSampThreads) g = kSampThreads;
+    return g > 0 ? g : 1;
+}
+
+cudaError_t launch_sample_chain(const SampleParams& p, int batch, bool pdl, cudaStream_t s) {
+    if (batch <= 0 || batch > 65535 || p.grid <= 0 || p.grid > kSampThreads || !p.work || p.V <= 0 ||
+        (batch > 1 && (p.stride < p.V || p.work_stride < sample_work_bytes(p.V, p.grid))) ||
+        (p.cand_out && batch != 1)) {
+        return cudaErrorInvalidValue;
+    }
+    const dim3 grid(p.grid, batch);
+    for (int pass = 0; pass < 3; ++pass) {
+        const cudaError_t e = launch_ex(sample_hist_kernel, grid, dim3(kSampThreads), 0, pass > 0 || pdl, s, p, pass);
+        if (e != cudaSuccess) return e;
+    }
+    return launch_ex(sample_gather_kernel, grid, dim3(kSampThreads), 0, true, s, p);
+}
+
+cudaError_t launch_sample_finish(const SampleParams& p, int batch, bool pdl, cudaStream_t s) {
+    if (batch <= 0 || batch > 65535 || (batch > 1 && p.stride < p.V)) return cudaErrorInvalidValue;
+    return launch_ex(sample_finish_kernel, dim3(1, batch), dim3(32), 0, pdl, s, p);
 }
 
 cudaError_t launch_sample_merge(const SampleMergeParams& p, bool pdl, cudaStream_t s) {

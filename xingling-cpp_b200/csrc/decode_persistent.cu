@@ -716,8 +716,15 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
         if (ticket == static_cast<int>(gridDim.x) - 1) {
             __threadfence();
             const unsigned long long fin = atomicExch(&st->argmax_key, 0ull);
+            const int tok = unpack_argmax_index(fin);
             st->argmax_final = fin;
-            st->greedy_token = unpack_argmax_index(fin);
+            st->greedy_token = tok;
+            if (p.finish_greedy) {
+                // Greedy step: the argmax is the step's id (no sampler launch follows).
+                st->token_out = tok;
+                if (tok >= 0 && tok < p.V) p.rep_flags[tok] = 1;
+                if (st->in.decode_mode) st->pos += 1;
+            }
         }
     }
 }

@@ -229,6 +229,8 @@ int Engine::alloc_all() {
     add(&done_, (5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_) * 4);
     add(&rep_flags_, vl);
     add(&st_, sizeof(DevState));
+    samp_grid_ = sample_grid(vl_, num_sms_, 1);
+    add(&samp_work_, sample_work_bytes(vl_, samp_grid_));
     add(&px_, T * H * 4);
     add(&pxn_, T * H * 4);
     add(&pqkv_, T * 3 * Hl * 4);
@@ -458,7 +460,7 @@ int Engine::prefill_linear(int mode, const TcOperands& o, const float* x, const 
 // norm2+W1/V+SwiGLU, W2+residual] -> final norm + LM head -> sampler.
 // Single-GPU decode step: zero the phase counters, one persistent kernel for
 // all 16 layers and the LM head, then the sampler.
-int Engine::enqueue_decode_persistent(cudaStream_t s) {
+int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     PersistentParams p{};
     if (cfg_.layers > kMaxLayers) {
         set_error("persistent decode supports at most 32 layers");
@@ -497,6 +499,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     p.Fl = Fl_;
     p.V = V_;
     p.T = T_;
+    p.finish_greedy = sampled ? 0 : 1;
     XL_CUDA(cudaMemsetAsync(
         done_, 0, (5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_) * sizeof(int),
         s));
@@ -506,6 +509,11 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     XL_CUDA(launch_decode_persistent(p, num_sms_, s));
     if (kernel_events_) XL_CUDA(cudaEventRecordWithFlags(kev1_, s, cudaEventRecordExternal));
     lm_x_ = xa_;
+    if (sampled) XL_CUDA(launch_sample_chain(sample_params(), 1, true, s));
+    return XL_OK;
+}
+
+SampleParams Engine::sample_params() const {
     SampleParams sp{};
     sp.logits = logits_;
     sp.V = vl_;
@@ -513,13 +521,16 @@ int Engine::enqueue_decode_persistent(cudaStream_t s) {
     sp.st = st_;
     sp.rep_flags = rep_flags_;
     sp.full = 0;
-    XL_CUDA(launch_sample(sp, true, s));
-    return XL_OK;
+    sp.work = samp_work_;
+    sp.work_stride = sample_work_bytes(vl_, samp_grid_);
+    sp.stride = vl_;
+    sp.grid = samp_grid_;
+    return sp;
 }
 
 int Engine::enqueue_decode(cudaStream_t s, bool sampled) {
     persistent_graph_ = tp_ == 1 && decode_path_ == 0 && persistent_fits();
-    if (persistent_graph_) return enqueue_decode_persistent(s);
+    if (persistent_graph_) return enqueue_decode_persistent(s, sampled);
     float* cur = xa_;
     float* other = xb_;
     bool pending = false;  // TP: part_ holds a reduced delta not yet added to cur
@@ -637,18 +648,16 @@ int Engine::run_lm_head_and_sample(const float* x_last, const float* delta, cuda
     const int rc = launch_lm_head(x_last, delta, true, s);
     if (rc != XL_OK) return rc;
     if (tp_ > 1) XL_NCCL(ncclAllReduce(&st_->argmax_final, &st_->argmax_final, 1, ncclUint64, ncclMax, comm_, s));
-    SampleParams sp{};
-    sp.logits = logits_;
-    sp.V = vl_;
-    sp.v0 = v0_;
-    sp.st = st_;
-    sp.rep_flags = rep_flags_;
-    sp.full = 0;
-    if (tp_ > 1 && sampled) {
+    SampleParams sp = sample_params();
+    if (!sampled) {
+        XL_CUDA(launch_sample_finish(sp, 1, true, s));
+        return XL_OK;
+    }
+    if (tp_ > 1) {
         // Sampling merge across vocab shards: local top-1024, all-gather, one draw on every rank.
         sp.full = 1;
         sp.cand_out = cand_local_;
-        XL_CUDA(launch_sample(sp, true, s));
+        XL_CUDA(launch_sample_chain(sp, 1, true, s));
         XL_NCCL(ncclAllGather(cand_local_, cand_all_, kTopK, ncclUint64, comm_, s));
         SampleMergeParams mp{};
         mp.cand = cand_all_;
@@ -663,7 +672,7 @@ int Engine::run_lm_head_and_sample(const float* x_last, const float* delta, cuda
         XL_CUDA(launch_sample_merge(mp, false, s));
         return XL_OK;
     }
-    XL_CUDA(launch_sample(sp, true, s));
+    XL_CUDA(launch_sample_chain(sp, 1, true, s));
     return XL_OK;
 }
 
@@ -675,7 +684,6 @@ int Engine::capture_decode_graph() {
             cudaGraphExecDestroy(exec);
             exec = nullptr;
         }
-        if (sampled && tp_ == 1) break;  // one graph serves both on a single GPU
         cudaGraph_t g = nullptr;
         XL_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
         const long long recorded0 = launch_count();
@@ -840,7 +848,7 @@ int Engine::decode(int token, float temperature, float top_p, float rp, int* tok
     in->decode_mode = 1;
     XL_CUDA(cudaMemcpyAsync(&st_->in, in, sizeof(StepIn), cudaMemcpyHostToDevice, stream_));
     XL_CUDA(cudaEventRecord(ev0_, stream_));
-    const bool use_sampled = tp_ > 1 && top_p > 0.0f;
+    const bool use_sampled = top_p > 0.0f;
     XL_CUDA(cudaGraphLaunch(use_sampled ? decode_exec_s_ : decode_exec_, stream_));
     count_graph_kernels(use_sampled ? decode_graph_kernels_s_ : decode_graph_kernels_);
     const int rc = finish_step(token_out);

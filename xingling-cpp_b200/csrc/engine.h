@@ -67,7 +67,8 @@ class Engine {
     int alloc_all();
     int capture_decode_graph();
     int enqueue_decode(cudaStream_t s, bool sampled);
-    int enqueue_decode_persistent(cudaStream_t s);
+    int enqueue_decode_persistent(cudaStream_t s, bool sampled);
+    SampleParams sample_params() const;  // this engine's sequence, single-step sampler chain
     // The persistent kernel streams K in 256-float tiles of at most 4096 floats,
     // runs at most one attention item per SM and lets at most
     // kPersistMaxContrib SMs share a row group of the residual projections.
@@ -116,6 +117,8 @@ class Engine {
     unsigned long long* trace_ = nullptr;  // optional phase timeline of the persistent kernel
     uint8_t* rep_flags_ = nullptr;  // [vl]
     DevState* st_ = nullptr;
+    void* samp_work_ = nullptr;     // sampler chain work area (sample_work_bytes)
+    int samp_grid_ = 1;             // CTAs of the sampler kernels
     // prefill buffers [T][...]
     float *px_ = nullptr, *pxn_ = nullptr, *pqkv_ = nullptr, *patt_ = nullptr, *pffh_ = nullptr;
     float *pxn_lo_ = nullptr, *patt_lo_ = nullptr, *pffh_lo_ = nullptr;
@@ -129,8 +132,8 @@ class Engine {
     int* h_ids_ = nullptr;     // pinned prompt staging
     cudaStream_t stream_ = nullptr;
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
-    cudaGraphExec_t decode_exec_ = nullptr;
-    cudaGraphExec_t decode_exec_s_ = nullptr;  // tensor parallel: the sampled step (candidate merge)
+    cudaGraphExec_t decode_exec_ = nullptr;    // greedy step (top_p <= 0)
+    cudaGraphExec_t decode_exec_s_ = nullptr;  // sampled step (the sampler chain; TP: candidate merge)
     long long decode_graph_kernels_s_ = 0;
     unsigned long long *cand_local_ = nullptr, *cand_all_ = nullptr;  // tensor-parallel sampling merge
     ncclComm_t comm_ = nullptr;
@@ -175,7 +178,7 @@ class BatchDecoder {
    private:
     BatchDecoder() = default;
     int init();
-    int enqueue(cudaStream_t s);
+    int enqueue(cudaStream_t s, bool sampled);
     int capture();
     float next_uniform(int seq);
     int cuda_fail(cudaError_t e, const char* what);
@@ -191,8 +194,12 @@ class BatchDecoder {
     int* ticket_ = nullptr;
     StepIn* h_in_ = nullptr;       // pinned
     DevState* h_st_ = nullptr;     // pinned
-    cudaGraphExec_t exec_ = nullptr;
-    long long graph_kernels_ = 0;
+    cudaGraphExec_t exec_ = nullptr;    // greedy step
+    cudaGraphExec_t exec_s_ = nullptr;  // sampled step (sampler chain)
+    long long graph_kernels_ = 0, graph_kernels_s_ = 0;
+    void* samp_work_ = nullptr;         // [kBatch] sampler work areas
+    size_t samp_stride_ = 0;
+    int samp_grid_ = 1;
     cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
     float last_ms_ = 0.0f;
     uint64_t seed_[kBatch] = {};

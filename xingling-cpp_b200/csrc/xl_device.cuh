@@ -49,8 +49,11 @@ __device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
 }
 
 // Order-preserving map of an fp32 value to uint32 (larger float -> larger key).
+// -0.0 maps to the key of +0.0: the reference compares floats, so the two
+// zeros tie and the lower id wins.
 __device__ __forceinline__ uint32_t float_key(float f) {
     uint32_t u = __float_as_uint(f);
+    if (u == 0x80000000u) u = 0u;
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 __device__ __forceinline__ float key_float(uint32_t k) {

@@ -146,12 +146,13 @@ struct PersistentParams {
     int* head_done;         // [layers][heads] CTA tickets of the cross-CTA attention merge
     float* ffh;             // [Fl] SwiGLU activations
     float* logits;          // [V]
-    const uint8_t* rep_flags;
+    uint8_t* rep_flags;     // [V] ids already generated (penalised; finish_greedy flags the step's id)
     DevState* st;
     int* done;              // [5*layers + 1] phase counters (then head_done), zeroed before each launch
     unsigned long long* trace;  // optional [grid][5*layers + 1][kTraceFields] timestamps (ns), or nullptr
     int inflight;               // weight boxes requested but not landed, per CTA (1 .. kPersistSlots)
     int H, Hl, heads, Fl, V, T;
+    int finish_greedy;          // 1: the LM head's last CTA writes the argmax as the step's id
 };
 constexpr int kTraceFields = 5;
 size_t persistent_smem_bytes();
@@ -161,6 +162,35 @@ size_t persistent_smem_bytes();
 cudaError_t make_stream_map(CUtensorMap* map, const float* base, int rows, int cols);
 cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cudaStream_t s);
 
+// ---- sampler: sample_cpu (src/inference.cu:58-114) over one vocab shard ----
+// A chain of grid-wide kernels per step: up to three radix-histogram passes
+// over the float keys (11 + 11 + 10 bits from the top), each over vocab
+// slices on all SMs, whose last CTA (an atomic ticket) picks the bin holding
+// the 1024th largest key; then one gather kernel whose slices collect the
+// selected ids and whose last CTA sorts them and draws.  No CTA waits on
+// another.  The selection stops as soon as the ids at or above the chosen
+// prefix fit kCandCap; a tie at the exact threshold key wider than that is
+// resolved in id order from per-slice lists.
+constexpr int kCandCap = 4096;   // candidates sorted by the last CTA
+constexpr int kSampThreads = 1024;
+struct SampleWorkHdr {
+    unsigned int prefix, pmask;  // radix prefix chosen so far and its mask
+    int n_above;                 // ids whose masked key is above prefix (all taken)
+    int n_ge;                    // ids whose key is at or above prefix
+    int passes;                  // histogram passes done this step
+    int done;                    // 1: selection finished (gather may run)
+    int exact;                   // 1: prefix is the exact threshold key and ties are wider than kCandCap
+    int ticket;                  // CTAs finished in the current kernel
+    int n_gt;                    // gather: candidate slots taken
+    int pad[7];
+};
+// Per-sequence work area (zeroed once; every step leaves it zeroed):
+// header, histogram [2048], candidates [kCandCap], per-slice tie counts
+// [grid] and tie ids [grid][slice].
+size_t sample_work_bytes(int V, int grid);
+// CTAs per sequence of the sampler kernels for `batch` sequences.
+int sample_grid(int V, int num_sms, int batch);
+
 struct SampleParams {
     const float* logits;   // [V] penalised logits of this vocab shard
     int V;                 // shard size
@@ -169,15 +199,21 @@ struct SampleParams {
     uint8_t* rep_flags;    // [V]
     int full;              // 1: always run the full top-k path (no argmax shortcut)
     unsigned long long* cand_out;  // tensor parallel: write the shard's sorted top-1024 here, draw nothing
+    void* work;            // sample_work_bytes(V, grid) per sequence
+    size_t work_stride;    // bytes between sequences' work areas
+    int stride;            // floats (and flag bytes) between sequences' logits
+    int grid;              // CTAs per sequence (sample_grid)
 };
-cudaError_t launch_sample(const SampleParams& p, bool pdl, cudaStream_t s);
-// `batch` sequences in one launch (a CTA each): sequence b samples logits +
-// b * stride with rep_flags + b * stride and state st + b.
-cudaError_t launch_sample_batch(const SampleParams& p, int batch, int stride, bool pdl, cudaStream_t s);
+// The sampling chain for `batch` sequences (sequence b: logits + b * stride,
+// rep_flags + b * stride, st + b, work + b * work_stride): three histogram
+// launches and the gather launch.
+cudaError_t launch_sample_chain(const SampleParams& p, int batch, bool pdl, cudaStream_t s);
+// Greedy steps (top_p <= 0): write the LM head's argmax as the step's id.
+cudaError_t launch_sample_finish(const SampleParams& p, int batch, bool pdl, cudaStream_t s);
 
 // Tensor-parallel sampling merge: the all-gathered per-shard candidate lists
 // (packed (value key, ~global id), n = tp x 1024), sorted as one; draws as
-// sample_kernel does.  n_pad: n rounded up to a power of two.
+// the single-GPU gather kernel does.  n_pad: n rounded up to a power of two.
 constexpr int kMaxMergeCandidates = 8 * kTopK;
 struct SampleMergeParams {
     const unsigned long long* cand;
