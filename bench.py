@@ -12,13 +12,14 @@ the step inputs from pinned memory and the device->host read of the result.
 `roofline` is the dominant kernel, the persistent decode kernel (one launch
 per token, >99% of a decode step's kernel time), timed by CUDA event nodes
 around it inside the decode graph in one more step right after the timed
-region (the nodes cost the sampler its early launch, so the timed steps run
-without them).  Also reported: the whole decode step against the same
-roofline, prefill of a 512-id prompt (seed 1), the reference's own CPU path
-on the host cores, `replica_batch` (64 sequences, prompt lengths uniform in
-[16, 512] with seed 5, 128 sampled tokens each, spread over the N replicas)
-and at N > 1 the tensor-parallel decode latency (prompt 64, seed 4, greedy
-256).
+region (the timed steps run without the nodes).  Also reported: the whole
+decode step against the same roofline, prefill of a 512-id prompt (seed 1),
+the reference's own CPU path on the host cores, `replica_batch` (64
+sequences, prompt lengths uniform in [16, 512] with seed 5, 128 sampled
+tokens each, spread over the N replicas, each replica decoding waves of 8
+sequences with one batched step per token, and the same sequences one at a
+time beside it) and at N > 1 the tensor-parallel decode latency (prompt 64,
+seed 4, greedy 256).
 
   python bench.py [--gpus N --steps K --warmup W]          # this engine
   python bench.py --impl reference [...]                   # reference CPU path
@@ -450,41 +451,71 @@ def tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks) -
 def replica_batch(eng, rank, world, max_over_ranks, barrier) -> dict:
     """64 independent sequences over the ranks' replicas: prompt lengths uniform
     in [16, 512] and ids uniform (seed 5), 128 sampled tokens each (T 0.7,
-    top_p 0.9, repetition penalty 1.1, Philox seed 5000 + sequence).  Reports
-    the box's aggregate decode tokens/s over prefill + decode time."""
+    top_p 0.9, repetition penalty 1.1, Philox seed 5000 + sequence).  Each
+    replica decodes its sequences in waves of BatchDecoder.size (one batched
+    step advances every sequence of the wave by one token, over one read of the
+    weights); the same sequences decoded one at a time on the engine are timed
+    beside it.  Reports the box's aggregate decode tokens/s over prefill +
+    decode time."""
     import numpy as np
+    import llm_cpp_engine
 
     rng = np.random.default_rng(5)
     lens = rng.integers(16, 513, size=64)
     seqs = [[int(t) for t in rng.integers(0, S.FULL.vocab, size=int(n))] for n in lens]
     mine = list(range(rank, 64, world))
+    samp = dict(temperature=0.7, top_p=0.9, repetition_penalty=1.1)
+    bd = llm_cpp_engine.BatchDecoder(eng)
+    B = llm_cpp_engine.BatchDecoder.size
     barrier()
     dev_ms, w0 = 0.0, time.perf_counter()
-    for j in mine:
-        eng.seed(5000 + j)
-        tok = eng.next_token(seqs[j], temperature=0.7, top_p=0.9, repetition_penalty=1.1)
-        dev_ms += eng.last_device_ms()
-        for _ in range(DECODE):
-            tok = eng.next_token(tok, temperature=0.7, top_p=0.9, repetition_penalty=1.1)
+    for w in range(0, len(mine), B):
+        wave = mine[w:w + B]
+        toks = []
+        for b, j in enumerate(wave):
+            bd.seed(b, 5000 + j)
+            toks.append(bd.prefill(b, seqs[j], **samp))
             dev_ms += eng.last_device_ms()
+        while len(toks) < B:  # a short last wave repeats its first sequence in the idle slots
+            b = len(toks)
+            bd.seed(b, 5000 + wave[0])
+            toks.append(bd.prefill(b, seqs[wave[0]], **samp))
+            dev_ms += eng.last_device_ms()
+        for _ in range(DECODE):
+            toks = bd.step(toks, **samp)
+            dev_ms += bd.last_device_ms()
     wall = time.perf_counter() - w0
     dev_s = max_over_ranks(dev_ms / 1e3)
     wall = max_over_ranks(wall)
+    # the same sequences one at a time on the engine
+    barrier()
+    seq_ms = 0.0
+    for j in mine:
+        eng.seed(5000 + j)
+        tok = eng.next_token(seqs[j], **samp)
+        seq_ms += eng.last_device_ms()
+        for _ in range(DECODE):
+            tok = eng.next_token(tok, **samp)
+            seq_ms += eng.last_device_ms()
+    seq_s = max_over_ranks(seq_ms / 1e3)
     tokens = 64 * DECODE
     return {"sequences": 64, "prompt_len": "uniform [16, 512], seed 5", "decode_tokens_each": DECODE,
-            "sampling": "T 0.7, top_p 0.9, rp 1.1", "replicas": world, "tokens_per_s": tokens / dev_s,
-            "e2e_tokens_per_s": tokens / wall, "timing": "device time of every prefill and decode step; max over ranks"}
+            "sampling": "T 0.7, top_p 0.9, rp 1.1", "replicas": world, "batch_per_replica": B,
+            "tokens_per_s": tokens / dev_s, "e2e_tokens_per_s": tokens / wall,
+            "sequential_tokens_per_s": tokens / seq_s,
+            "timing": "device time of every prefill and decode step; max over ranks"}
 
 
 def ncu_case(args) -> None:
     """Short fixed workloads for Nsight Compute captures (no timing output):
     decode-full: XingLing-0.68B, prefill 32 + 4 decode steps;
+    decode-sampled: XingLing-0.68B, prefill 32 + 4 decode steps sampled (T 0.7, top_p 0.9, rp 1.1);
     decode-wide: 2 full-width layers, vocab 8192 (weights 276 MB > L2), prefill 32 + 3 decode steps;
     prefill-512: XingLing-0.68B, one prefill of 512 ids.
     --decode-path selects the persistent (0) or per-op (1) decode kernels."""
     import llm_cpp_engine
 
-    shape = S.FULL if args.ncu_case in ("decode-full", "prefill-512") else S.WIDE2
+    shape = S.FULL if args.ncu_case in ("decode-full", "decode-sampled", "prefill-512") else S.WIDE2
     wdir = WEIGHT_DIR if shape is S.FULL else WEIGHT_DIR + "_wide2"
     S.write_weight_tree(wdir, shape)
     eng = llm_cpp_engine.InferenceEngine("cuda:0", **shape.engine_kwargs())
@@ -493,9 +524,12 @@ def ncu_case(args) -> None:
     if args.ncu_case == "prefill-512":
         eng.next_token(S.prompt_ids(1, PREFILL_N, shape.vocab), top_p=0.0, repetition_penalty=1.0)
         return
-    tok = eng.next_token(S.prompt_ids(0, PROMPT, shape.vocab), top_p=0.0, repetition_penalty=1.0)
-    for _ in range(4 if args.ncu_case == "decode-full" else 3):
-        tok = eng.next_token(tok, top_p=0.0, repetition_penalty=1.0)
+    samp = dict(temperature=0.7, top_p=0.9, repetition_penalty=1.1) if args.ncu_case == "decode-sampled" else \
+        dict(top_p=0.0, repetition_penalty=1.0)
+    eng.seed(3)
+    tok = eng.next_token(S.prompt_ids(0, PROMPT, shape.vocab), **samp)
+    for _ in range(3 if args.ncu_case == "decode-wide" else 4):
+        tok = eng.next_token(tok, **samp)
     print("ncu case done", args.ncu_case, tok)
 
 
@@ -506,7 +540,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["xl", "reference"], default="xl")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--ncu-case", choices=["decode-full", "decode-wide", "prefill-512"], default=None)
+    ap.add_argument("--ncu-case", choices=["decode-full", "decode-sampled", "decode-wide", "prefill-512"],
+                    default=None)
     ap.add_argument("--decode-path", type=int, default=0, choices=[0, 1])
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--budget", type=float, default=15.0, help=argparse.SUPPRESS)

@@ -353,16 +353,16 @@ __device__ int block_inclusive_scan(int v, int* warp_tot) {
 // Temperature, softmax over the kc sorted candidates (packed (key, ~global
 // id)), top-p and the draw with the step's uniform: the arithmetic of
 // src/inference.cu:87-111.  The two float sums (the softmax denominator and
-// the running probability) are sequential in candidate order on one thread,
-// as in the reference; the divides and the two "first index" searches of the
-// top-p cut and the draw run across the block on the stored prefix sums, which
-// gives the same index as the reference's early-exit loops because the prefix
-// sums never decrease.  All threads of the block call it; thread 0 writes
-// *s_token.
+// the running probability, which stops at the top-p cut) are sequential in
+// candidate order on one thread, as in the reference; the exponentials, the
+// divides and the search for the drawn index run across the block, which
+// gives the reference's index because the running sums never decrease and
+// r * total < total.  prob: 1024 floats, 16-byte aligned.  All threads of
+// the block call it; thread 0 writes *s_token.
 __device__ void draw_token(const unsigned long long* cand, int kc, float* prob, const DevState* st, int* s_token) {
     __shared__ float s_sum;
-    __shared__ int s_first, s_pick;
-    const int tid = threadIdx.x;
+    __shared__ int s_cut, s_pick, s_done;
+    const int tid = threadIdx.x, lane = tid & 31;
     const float top_p = st->in.top_p;
     const float inv_t_den = st->in.temperature + 0.001f;
     const float v0 = key_float(static_cast<uint32_t>(cand[0] >> 32)) / inv_t_den;
@@ -373,34 +373,78 @@ __device__ void draw_token(const unsigned long long* cand, int kc, float* prob, 
     }
     prob[tid] = e;
     if (tid == 0) {
-        s_first = kc;
+        s_cut = kc - 1;
         s_pick = kc - 1;
     }
     __syncthreads();
+    float4* p4 = reinterpret_cast<float4*>(prob);
+    constexpr int nq = kTopK / 4;
     if (tid == 0) {
-        float sum_exp = 1.0f;
-#pragma unroll 16
-        for (int i = 1; i < kc; ++i) sum_exp += prob[i];
-        s_sum = sum_exp;
+        // 1 + e_1 + ... (prob[0] = exp(0) = 1; entries past kc are 0 and add nothing)
+        float4 q = p4[0];
+        float sum = 1.0f;
+        sum += q.y;
+        sum += q.z;
+        sum += q.w;
+#pragma unroll 8
+        for (int i = 1; i < nq; ++i) {
+            q = p4[i];
+            sum += q.x;
+            sum += q.y;
+            sum += q.z;
+            sum += q.w;
+        }
+        s_sum = sum;
     }
     __syncthreads();
     if (tid < kc) prob[tid] = prob[tid] / s_sum;
     __syncthreads();
     if (tid == 0) {
+        // running sums, in place, up to the group of 16 where one reaches top_p
+        // (the next group's loads are issued before this group's adds)
         float acc = 0.0f;
-#pragma unroll 16
-        for (int i = 0; i < kc; ++i) {
-            acc += prob[i];
-            prob[i] = acc;
+        int q = 0;
+        float4 c[4], n[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) c[u] = p4[u];
+        for (; q < nq; q += 4) {
+            if (q + 4 < nq) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) n[u] = p4[q + 4 + u];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                float4 x = c[u];
+                acc += x.x;
+                x.x = acc;
+                acc += x.y;
+                x.y = acc;
+                acc += x.z;
+                x.z = acc;
+                acc += x.w;
+                x.w = acc;
+                p4[q + u] = x;
+            }
+            if (acc >= top_p) {
+                q += 4;
+                break;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) c[u] = n[u];
         }
+        s_done = 4 * q;
     }
     __syncthreads();
-    // top-p: the first prefix reaching top_p, else the whole list
-    if (tid < kc && prob[tid] >= top_p) atomicMin(&s_first, tid);
+    // top-p cut: the first running sum reaching top_p, else the last candidate
+    const int lim = min(s_done, kc);
+    const unsigned hc = __ballot_sync(0xffffffffu, tid < lim && prob[tid] >= top_p);
+    if (lane == 0 && hc) atomicMin(&s_cut, (tid & ~31) + __ffs(hc) - 1);
     __syncthreads();
-    const float total = prob[min(s_first, kc - 1)];
-    const float thr = st->in.uniform * total;
-    if (tid < kc && prob[tid] > thr) atomicMin(&s_pick, tid);
+    // the draw: the first running sum above r * total (total = the sum at the cut)
+    const int cut = s_cut;
+    const float thr = st->in.uniform * prob[cut];
+    const unsigned hit = __ballot_sync(0xffffffffu, tid <= cut && prob[tid] > thr);
+    if (lane == 0 && hit) atomicMin(&s_pick, (tid & ~31) + __ffs(hit) - 1);
     __syncthreads();
     if (tid == 0) *s_token = static_cast<int>(0xffffffffu - static_cast<uint32_t>(cand[s_pick] & 0xffffffffull));
 }
@@ -452,8 +496,8 @@ __device__ __forceinline__ void finish_token(const SampleParams& p, int b, DevSt
 // then one global add per non-empty bin); passes 1 and 2 count the next 11 /
 // 10 bits of the few ids inside the chosen prefix straight into the global
 // histogram.  The last CTA to finish picks the bin that holds the kc-th
-// largest key, extends the prefix, zeroes the histogram and decides whether
-// the ids at or above the prefix are few enough to gather.
+// largest key, extends the prefix and zeroes the histogram; the selection is
+// done when exactly kc ids are at or above the prefix, or after pass 2.
 __global__ void __launch_bounds__(kSampThreads) sample_hist_kernel(const SampleParams p, int pass) {
     __shared__ unsigned int hist[2048];
     __shared__ int warp_tot[32];
@@ -556,17 +600,30 @@ __global__ void __launch_bounds__(kSampThreads) sample_hist_kernel(const SampleP
             w.h->n_above = n_above;
             w.h->n_ge = n_ge;
             w.h->passes = pass + 1;
-            w.h->exact = n_ge > kCandCap;  // only after the last pass: the prefix is then the full key
-            w.h->done = n_ge <= kCandCap || pass == 2;
+            // Stop once exactly kc ids are at or above the prefix; after the last
+            // pass the prefix is the full threshold key and a wider count is a tie
+            // there, resolved by id order.
+            w.h->exact = pass == 2 && n_ge > kc;
+            w.h->done = n_ge == kc || pass == 2;
         }
         w.h->ticket = 0;
     }
 }
 
-// Descending bitonic sort of M x 1024 packed candidates, element i at
-// a[i] (thread i % 1024 holds elements tid, 1024 + tid, ...): distances of
-// 1024 and more compare registers of one thread, 32 .. 512 go through shared
-// memory, below 32 through warp shuffles.
+// One compare-exchange of a descending bitonic stage of size k at distance
+// j: element i keeps the larger value when it is the lower index of a
+// descending pair or the upper index of an ascending one.
+__device__ __forceinline__ unsigned long long bitonic_pick(unsigned long long v, unsigned long long y, int i, int j,
+                                                           int k) {
+    const bool keep_max = ((i & j) == 0) == ((i & k) == 0);
+    return (v < y) == keep_max ? y : v;
+}
+
+// Descending bitonic sort of M x 1024 packed candidates, element i at a[i]
+// (thread t holds elements t, 1024 + t, ...), unrolled: distances of 1024 and
+// more compare registers of one thread, 32 .. 512 go through shared memory
+// (for M = 1 alternating between a[0, 1024) and a[1024, 2048), one barrier a
+// stage), below 32 through warp shuffles.
 template <int M>
 __device__ void bitonic_sort_desc(unsigned long long* a) {
     constexpr int n = M * kSampThreads;
@@ -574,18 +631,20 @@ __device__ void bitonic_sort_desc(unsigned long long* a) {
     unsigned long long v[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) v[m] = a[m * kSampThreads + tid];
+    __syncthreads();
+    int half = 0;
+#pragma unroll
     for (int k = 2; k <= n; k <<= 1) {
+#pragma unroll
         for (int j = k >> 1; j > 0; j >>= 1) {
             if (j >= kSampThreads) {
-                const int mj = j / kSampThreads;
 #pragma unroll
                 for (int m = 0; m < M; ++m) {
 #pragma unroll
                     for (int m2 = m + 1; m2 < M; ++m2) {
-                        if ((m ^ m2) != mj) continue;
-                        const int i = m * kSampThreads + tid;
-                        const bool desc = (i & k) == 0;
+                        if ((m ^ m2) * kSampThreads != j) continue;
                         const unsigned long long x = v[m], y = v[m2];
+                        const bool desc = ((m * kSampThreads + tid) & k) == 0;
                         if (desc ? (x < y) : (x > y)) {
                             v[m] = y;
                             v[m2] = x;
@@ -593,25 +652,25 @@ __device__ void bitonic_sort_desc(unsigned long long* a) {
                     }
                 }
             } else if (j >= 32) {
-                __syncthreads();
+                if (M == 1) {
+                    unsigned long long* t = a + half * kSampThreads;
+                    t[tid] = v[0];
+                    __syncthreads();
+                    v[0] = bitonic_pick(v[0], t[tid ^ j], tid, j, k);
+                    half ^= 1;
+                } else {
+                    __syncthreads();
 #pragma unroll
-                for (int m = 0; m < M; ++m) a[m * kSampThreads + tid] = v[m];
-                __syncthreads();
+                    for (int m = 0; m < M; ++m) a[m * kSampThreads + tid] = v[m];
+                    __syncthreads();
 #pragma unroll
-                for (int m = 0; m < M; ++m) {
-                    const int i = m * kSampThreads + tid;
-                    const unsigned long long y = a[m * kSampThreads + (tid ^ j)];
-                    const bool keep_max = ((i & j) == 0) == ((i & k) == 0);
-                    v[m] = keep_max ? (v[m] > y ? v[m] : y) : (v[m] < y ? v[m] : y);
+                    for (int m = 0; m < M; ++m)
+                        v[m] = bitonic_pick(v[m], a[m * kSampThreads + (tid ^ j)], m * kSampThreads + tid, j, k);
                 }
             } else {
 #pragma unroll
-                for (int m = 0; m < M; ++m) {
-                    const int i = m * kSampThreads + tid;
-                    const unsigned long long y = __shfl_xor_sync(0xffffffffu, v[m], j);
-                    const bool keep_max = ((i & j) == 0) == ((i & k) == 0);
-                    v[m] = keep_max ? (v[m] > y ? v[m] : y) : (v[m] < y ? v[m] : y);
-                }
+                for (int m = 0; m < M; ++m)
+                    v[m] = bitonic_pick(v[m], __shfl_xor_sync(0xffffffffu, v[m], j), m * kSampThreads + tid, j, k);
             }
         }
     }
@@ -630,8 +689,8 @@ __device__ void bitonic_sort_desc(unsigned long long* a) {
 // list, then draws (or, tensor parallel, writes the list out) and leaves the
 // work area zeroed.
 __global__ void __launch_bounds__(kSampThreads) sample_gather_kernel(const SampleParams p) {
-    __shared__ unsigned long long s_cand[kCandCap];
-    __shared__ float prob[kTopK];
+    __shared__ unsigned long long s_cand[kCandCap];  // M = 1 sorts use [1024, 2048) as the second buffer
+    __shared__ __align__(16) float prob[kTopK];
     __shared__ int tie_pre[kSampThreads + 1];
     __shared__ int warp_tot[32];
     __shared__ int s_last, s_token, s_run;
@@ -762,7 +821,7 @@ __global__ void __launch_bounds__(32) sample_finish_kernel(const SampleParams p)
 // agree on the id.  Greedy steps take the all-reduced argmax instead.
 __global__ void __launch_bounds__(kSampThreads) sample_merge_kernel(const SampleMergeParams p) {
     extern __shared__ unsigned long long all[];  // n_pad packed candidates
-    __shared__ float prob[kTopK];
+    __shared__ __align__(16) float prob[kTopK];
     __shared__ int s_token;
     pdl_launch_dependents();
     pdl_wait();

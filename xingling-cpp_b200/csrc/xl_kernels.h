@@ -168,9 +168,9 @@ cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cud
 // slices on all SMs, whose last CTA (an atomic ticket) picks the bin holding
 // the 1024th largest key; then one gather kernel whose slices collect the
 // selected ids and whose last CTA sorts them and draws.  No CTA waits on
-// another.  The selection stops as soon as the ids at or above the chosen
-// prefix fit kCandCap; a tie at the exact threshold key wider than that is
-// resolved in id order from per-slice lists.
+// another.  The selection stops as soon as exactly 1024 ids are at or above
+// the chosen prefix; a tie at the full threshold key is resolved in id order
+// from per-slice lists.  A vocab of at most kCandCap ids is taken whole.
 constexpr int kCandCap = 4096;   // candidates sorted by the last CTA
 constexpr int kSampThreads = 1024;
 struct SampleWorkHdr {
@@ -179,7 +179,7 @@ struct SampleWorkHdr {
     int n_ge;                    // ids whose key is at or above prefix
     int passes;                  // histogram passes done this step
     int done;                    // 1: selection finished (gather may run)
-    int exact;                   // 1: prefix is the exact threshold key and ties are wider than kCandCap
+    int exact;                   // 1: prefix is the full threshold key and more than kc ids reach it
     int ticket;                  // CTAs finished in the current kernel
     int n_gt;                    // gather: candidate slots taken
     int pad[7];
