@@ -510,12 +510,13 @@ def ncu_case(args) -> None:
     """Short fixed workloads for Nsight Compute captures (no timing output):
     decode-full: XingLing-0.68B, prefill 32 + 4 decode steps;
     decode-sampled: XingLing-0.68B, prefill 32 + 4 decode steps sampled (T 0.7, top_p 0.9, rp 1.1);
+    batch-sampled: XingLing-0.68B, 8 sequences (prompts of 32 ids) + 3 batched decode steps, sampled;
     decode-wide: 2 full-width layers, vocab 8192 (weights 276 MB > L2), prefill 32 + 3 decode steps;
     prefill-512: XingLing-0.68B, one prefill of 512 ids.
     --decode-path selects the persistent (0) or per-op (1) decode kernels."""
     import llm_cpp_engine
 
-    shape = S.FULL if args.ncu_case in ("decode-full", "decode-sampled", "prefill-512") else S.WIDE2
+    shape = S.WIDE2 if args.ncu_case == "decode-wide" else S.FULL
     wdir = WEIGHT_DIR if shape is S.FULL else WEIGHT_DIR + "_wide2"
     S.write_weight_tree(wdir, shape)
     eng = llm_cpp_engine.InferenceEngine("cuda:0", **shape.engine_kwargs())
@@ -524,8 +525,15 @@ def ncu_case(args) -> None:
     if args.ncu_case == "prefill-512":
         eng.next_token(S.prompt_ids(1, PREFILL_N, shape.vocab), top_p=0.0, repetition_penalty=1.0)
         return
-    samp = dict(temperature=0.7, top_p=0.9, repetition_penalty=1.1) if args.ncu_case == "decode-sampled" else \
+    samp = dict(temperature=0.7, top_p=0.9, repetition_penalty=1.1) if "sampled" in args.ncu_case else \
         dict(top_p=0.0, repetition_penalty=1.0)
+    if args.ncu_case == "batch-sampled":
+        bd = llm_cpp_engine.BatchDecoder(eng)
+        toks = [bd.prefill(b, S.prompt_ids(10 + b, PROMPT, shape.vocab), **samp) for b in range(bd.size)]
+        for _ in range(3):
+            toks = bd.step(toks, **samp)
+        print("ncu case done", args.ncu_case, toks)
+        return
     eng.seed(3)
     tok = eng.next_token(S.prompt_ids(0, PROMPT, shape.vocab), **samp)
     for _ in range(3 if args.ncu_case == "decode-wide" else 4):
@@ -540,7 +548,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["xl", "reference"], default="xl")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--ncu-case", choices=["decode-full", "decode-sampled", "decode-wide", "prefill-512"],
+    ap.add_argument("--ncu-case", choices=["decode-full", "decode-sampled", "batch-sampled", "decode-wide", "prefill-512"],
                     default=None)
     ap.add_argument("--decode-path", type=int, default=0, choices=[0, 1])
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)

@@ -137,12 +137,15 @@ XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, fl
  *                    input staged, phase done, producer first and last issue;
  *                    read with xl_engine_phase_trace (a profiling aid);
  *   "tma_inflight" n  weight boxes (32 KB) each SM of the persistent kernel
- *                    keeps requested but not landed, in [1, 6] (default 2):
+ *                    keeps requested but not landed, in [1, 6] (default 3):
  *                    enough to keep HBM busy, few enough that other memory
  *                    accesses do not queue behind the stream;
+ *   "tma_evict_first" 1  the persistent kernel loads weight boxes with an L2
+ *                    evict-first policy (default), keeping activations and
+ *                    cached K/V in L2; 0  the default L2 policy;
  *   "kernel_events" 1  event-record nodes around the persistent kernel in the
  *                    decode graph, so xl_engine_last_kernel_ms reports its
- *                    own duration (costs the sampler its early launch);
+ *                    own duration;
  *   "prefill_gemm" 0  prefill projections on tcgen05 with the 3xTF32 split
  *                     (default); 1  fp32 FMA tiles.
  *   "prefill_attn" 0  prefill attention on tcgen05 with the 3xTF32 split:

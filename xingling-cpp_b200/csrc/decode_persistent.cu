@@ -8,7 +8,10 @@
 // with 16 KB boxes and ~90 GB/s with 32 KB ones), gated by free ring slots and
 // by a cap on boxes in flight (requested, not landed), so HBM keeps streaming
 // across phase boundaries without queueing more requests than it needs to
-// stay busy.  Warps 1..8 consume: per phase they wait for the previous phase
+// stay busy.  The boxes are loaded with an L2 evict-first policy: a weight
+// line is dead once read, and the 113 MB a layer streams would otherwise push
+// the activations, partial sums and cached K/V rows that the stagings and the
+// attention wait on out of L2.  Warps 1..8 consume: per phase they wait for the previous phase
 // of every CTA (a global counter), stage the phase's input vector in shared
 // memory, take ring boxes (two rows per warp) and reduce with warp shuffles.
 //
@@ -104,6 +107,20 @@ __device__ __forceinline__ void tma_box(void* dst, const CUtensorMap* map, int k
         "[%5];" ::"r"(smem_u32(dst)),
         "l"(map), "r"(0), "r"(kt), "r"(row), "r"(smem_u32(bar))
         : "memory");
+}
+// The same load with an L2 cache policy (evict-first: a weight line is dead once read).
+__device__ __forceinline__ void tma_box_hint(void* dst, const CUtensorMap* map, int kt, int row, uint64_t* bar,
+                                             uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(0), "r"(kt), "r"(row), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
 }
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerThreads) : "memory"); }
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -230,6 +247,7 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
     int issued = 0;
     bool ok = true;
     const int inflight = p.inflight;
+    const uint64_t policy = evict_first_policy();
     Cursor c;
     for (cursor_first(p, 0, c); c.valid;) {
         if (!wait_parity(&empty[slot], par ^ 1u, st)) {
@@ -250,7 +268,11 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
         // Rows past M and k-tiles past K of the box are zero-filled by TMA and
         // still counted in the transaction bytes.
         mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(kPersistTileRows * kPersistTileK * 4 * c.kd));
-        tma_box(ring + static_cast<size_t>(slot) * kSlotBytes, c.map, bi * c.kd, g * kPersistTileRows, &full[slot]);
+        if (p.tma_evict_first)
+            tma_box_hint(ring + static_cast<size_t>(slot) * kSlotBytes, c.map, bi * c.kd, g * kPersistTileRows,
+                         &full[slot], policy);
+        else
+            tma_box(ring + static_cast<size_t>(slot) * kSlotBytes, c.map, bi * c.kd, g * kPersistTileRows, &full[slot]);
         ++issued;
         if (++slot == kSlots) {
             slot = 0;

@@ -500,6 +500,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     p.V = V_;
     p.T = T_;
     p.finish_greedy = sampled ? 0 : 1;
+    p.tma_evict_first = tma_evict_first_;
     XL_CUDA(cudaMemsetAsync(
         done_, 0, (5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_) * sizeof(int),
         s));
@@ -917,6 +918,14 @@ int Engine::set_option(const char* key, int value) {
             return XL_ERR_ARG;
         }
         inflight_ = value;
+        return loaded_ ? capture_decode_graph() : XL_OK;
+    }
+    if (k == "tma_evict_first") {
+        if (value != 0 && value != 1) {
+            set_error("tma_evict_first must be 0 or 1");
+            return XL_ERR_ARG;
+        }
+        tma_evict_first_ = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
     if (k == "kernel_events") {

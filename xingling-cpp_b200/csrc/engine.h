@@ -146,7 +146,8 @@ class Engine {
     float *ap_ = nullptr, *ap_lo_ = nullptr;
     TcOperands tc_attn_s_{}, tc_attn_pv_{};
     long long decode_graph_kernels_ = 0;  // kernels recorded in the decode graph
-    int inflight_ = 2;  // persistent decode: weight boxes requested but not landed, per SM
+    int inflight_ = 3;  // persistent decode: weight boxes requested but not landed, per SM
+    int tma_evict_first_ = 1;  // persistent decode: weight boxes loaded with an L2 evict-first policy
     bool loaded_ = false;
     bool has_seq_ = false;
     int n_ = 0;

@@ -153,6 +153,7 @@ struct PersistentParams {
     int inflight;               // weight boxes requested but not landed, per CTA (1 .. kPersistSlots)
     int H, Hl, heads, Fl, V, T;
     int finish_greedy;          // 1: the LM head's last CTA writes the argmax as the step's id
+    int tma_evict_first;        // 1: weight boxes are loaded with an L2 evict-first policy
 };
 constexpr int kTraceFields = 5;
 size_t persistent_smem_bytes();
