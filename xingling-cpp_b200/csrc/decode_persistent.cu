@@ -24,12 +24,12 @@
 // residual stream ping-pongs between xa (entering a layer) and xb (after the
 // out-projection); each CTA stores one slice of it.
 //
-// Attention.  Head h runs on one CTA (three at most, at 768 positions); its
-// warps take one 32-position chunk each.  Each warp prefetches its chunk's
-// cached K/V rows into L2 (two bulk prefetches) before the wait for the QKV
-// phase, so their HBM latency overlaps the grid barrier; the chunks merge in
-// shared memory, and only a head split over several CTAs merges through
-// global memory (ticket).
+// Attention.  Head h runs on one CTA (six at most, at 768 positions); its
+// warps take one 16-position chunk each and load the chunk's cached K/V rows
+// into registers before the wait for the QKV phase, so only the new
+// position's q / k / v is read after it; the chunks merge in shared memory,
+// and only a head split over several CTAs merges through global memory
+// (ticket).
 //
 // Replaces, for one decode token, the reference's Transformer::forward(int)
 // (src/transformer.cu:180-186) with TransformerBlock::forward
@@ -63,14 +63,16 @@ constexpr uint32_t kFlagSpinLimit = 1u << 24;
 constexpr int kErrMbar = 1, kErrFlag = 2;
 // Attention scratch inside the staging buffer xs (free between the QKV and
 // out-projection stagings): per warp the rotated q (64 floats), then per warp
-// (max, sum, o[64]) partials.
+// (max, sum, o[64]) partials, then per warp the rotated k of the new position.
 constexpr int kAttnWarpScratch = kHeadDim;
 constexpr int kAttnPartStride = kHeadDim + 4;
 constexpr int kStageQuads = kMaxK / 4 / kConsumerThreads;  // float4 of a staged vector per consumer thread
+constexpr int kStageBatch = 2;  // quads of an RMSNorm staging whose loads are issued together
 constexpr int kPreGroups = 4;  // row groups per CTA whose biases are loaded before the phase wait
 
 static_assert(kPersistTileRows == 2 * kConsumerWarps, "each consumer warp owns two rows of a box");
-static_assert(kConsumerWarps * (kAttnWarpScratch + kAttnPartStride) <= kMaxK, "attention scratch fits in xs");
+static_assert(kConsumerWarps * (kAttnWarpScratch + kAttnPartStride + kHeadDim) <= kMaxK, "attention scratch fits in xs");
+static_assert(kPersistChunk == 16, "attention lanes: two per position of a 16-position chunk");
 
 enum PhaseKind : int { kQKV = 0, kAttn = 1, kWo = 2, kW13 = 3, kW2 = 4, kLM = 5 };
 
@@ -373,7 +375,9 @@ __device__ __forceinline__ float4 residual_quad(const float* x_old, const float*
 
 // xs = rmsnorm(x) * gamma, where x is the embedding row (cres == nullptr) or
 // the residual after a split projection of nb boxes per group; this CTA stores
-// its slice of x to x_out.  float4 accesses; gamma is loaded with x.
+// its slice of x to x_out.  float4 accesses; every load of a batch of quads
+// (x, partial sums, bias, gamma) is issued before the first store, so a
+// staging costs one L2 round trip per batch (one in all at K <= 2048).
 __device__ __noinline__ void stage_norm(const PersistentParams& p, const float* x_old, const float* bias, const float* cres,
                            int nb, const float* gamma, float* xs, float* red, float* x_out) {
     const int t = threadIdx.x - 32;
@@ -386,18 +390,29 @@ __device__ __noinline__ void stage_norm(const PersistentParams& p, const float* 
     float4 gk[kStageQuads];
     float ss = 0.0f;
 #pragma unroll
-    for (int k = 0; k < kStageQuads; ++k) {
-        const int q = t + k * kConsumerThreads;
-        if (q < (K >> 2)) {
-            gk[k] = g4[q];
-            const float4 v =
-                cres ? residual_quad(x_old, bias, cres, q, nb, T) : __ldcg(reinterpret_cast<const float4*>(x_old) + q);
-            x4[q] = v;
-            const float e[4] = {v.x, v.y, v.z, v.w};
+    for (int k0 = 0; k0 < kStageQuads; k0 += kStageBatch) {
+        if (k0 * kConsumerThreads >= (K >> 2)) break;
+        float4 v[kStageBatch];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                if (4 * q + u >= s0 && 4 * q + u < s1) x_out[4 * q + u] = e[u];
-            ss = dot4(v, v, ss);
+        for (int u = 0; u < kStageBatch; ++u) {
+            const int q = t + (k0 + u) * kConsumerThreads;
+            if (q < (K >> 2)) {
+                gk[k0 + u] = g4[q];
+                v[u] = cres ? residual_quad(x_old, bias, cres, q, nb, T)
+                            : __ldcg(reinterpret_cast<const float4*>(x_old) + q);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kStageBatch; ++u) {
+            const int q = t + (k0 + u) * kConsumerThreads;
+            if (q < (K >> 2)) {
+                x4[q] = v[u];
+                const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (4 * q + c >= s0 && 4 * q + c < s1) x_out[4 * q + c] = e[c];
+                ss = dot4(v[u], v[u], ss);
+            }
         }
     }
     const float tot = consumer_sum(ss, red);
@@ -417,10 +432,20 @@ __device__ __noinline__ void stage_norm(const PersistentParams& p, const float* 
     }
 }
 
+// xs = src[0, K): all of a thread's loads before its shared-memory stores.
 __device__ void stage_copy(const float* src, int K, float* xs) {
     const int t = threadIdx.x - 32;
-    for (int i = t; i < (K >> 2); i += kConsumerThreads)
-        reinterpret_cast<float4*>(xs)[i] = __ldcg(reinterpret_cast<const float4*>(src) + i);
+    float4 v[kStageQuads];
+#pragma unroll
+    for (int k = 0; k < kStageQuads; ++k) {
+        const int q = t + k * kConsumerThreads;
+        if (q < (K >> 2)) v[k] = __ldcg(reinterpret_cast<const float4*>(src) + q);
+    }
+#pragma unroll
+    for (int k = 0; k < kStageQuads; ++k) {
+        const int q = t + k * kConsumerThreads;
+        if (q < (K >> 2)) reinterpret_cast<float4*>(xs)[q] = v[k];
+    }
 }
 
 // This CTA's attention item of the token: head h, CTA j of the head's nct;
@@ -450,64 +475,81 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
     const int s = j * kConsumerWarps + warp;
     const bool active = has && s < nsplit;
     const int t0 = s * kPersistChunk;
-    const int pos = t0 + lane;
-    const bool mine = active && pos <= n;
     float* kc = y.kc + static_cast<size_t>(h) * p.T * kHeadDim;
     float* vc = y.vc + static_cast<size_t>(h) * p.T * kHeadDim;
-    // Cached rows t0 .. min(t0 + 32, n) - 1 of this chunk (rows are 256 B, contiguous per head).
+    // The chunk's cached rows (positions t0 .. min(t0 + 16, n) - 1) do not depend
+    // on this token's QKV phase: load them before its wait, so the only L2 round
+    // trip after it is q / k / v of the new position.  Scores: lane pair
+    // (2 kp, 2 kp + 1) owns position t0 + kp, half kh of its 64 dims (8 float4
+    // of K).  P.V: lane owns output dims (2 lane, 2 lane + 1) of every row.
+    const int kp = lane >> 1, kh = lane & 1;
+    const int posk = t0 + kp;
     const int cached = active ? min(kPersistChunk, n - t0) : 0;
-    if (lane == 0 && cached > 0) {
-        prefetch_l2_bulk(kc + static_cast<size_t>(t0) * kHeadDim, static_cast<uint32_t>(cached) * kHeadDim * 4);
-        prefetch_l2_bulk(vc + static_cast<size_t>(t0) * kHeadDim, static_cast<uint32_t>(cached) * kHeadDim * 4);
-    }
+    float4 kv[8];
+    float2 vrow[kPersistChunk];
+    const float4* kr = reinterpret_cast<const float4*>(kc + static_cast<size_t>(kp < cached ? posk : 0) * kHeadDim) +
+                       8 * kh;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) kv[i] = kp < cached ? __ldcg(kr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float2* vr = reinterpret_cast<const float2*>(vc + static_cast<size_t>(t0) * kHeadDim) + lane;
+#pragma unroll
+    for (int jp = 0; jp < kPersistChunk; ++jp)
+        vrow[jp] = jp < cached ? __ldcg(vr + jp * (kHeadDim / 2)) : make_float2(0.0f, 0.0f);
+    const float2 cs = active ? p.rope[n * kHalfHead + lane] : make_float2(0.0f, 0.0f);
     if (!wait_phase(p, ph - 1, s_ok)) return false;
     if (t == 0) trace_at(p, ph, kTrConsStart);
     if (!has) return true;
     float* qsh = xs + warp * kAttnWarpScratch;
     float* apart = xs + kConsumerWarps * kAttnWarpScratch;  // [8][68]
+    float* knew = xs + kConsumerWarps * (kAttnWarpScratch + kAttnPartStride) + warp * kHeadDim;  // rotated k of row n
     if (active) {
-        const float2 cs = p.rope[n * kHalfHead + lane];
+        const bool has_n = n >= t0 && n < t0 + kPersistChunk;
         const float* q = p.qkv + h * kHeadDim;
+        const float* kn = p.qkv + p.Hl + h * kHeadDim;
+        const float* vn = p.qkv + 2 * p.Hl + h * kHeadDim;
         const float qa = __ldcg(q + lane), qb = __ldcg(q + lane + kHalfHead);
+        float ka = 0.0f, kb = 0.0f;
+        float2 vnew = make_float2(0.0f, 0.0f);
+        if (has_n) {
+            ka = __ldcg(kn + lane);
+            kb = __ldcg(kn + lane + kHalfHead);
+            vnew = __ldcg(reinterpret_cast<const float2*>(vn) + lane);
+        }
         qsh[lane] = (qa * cs.x + qb * cs.y) * 0.125f;  // 1/sqrt(64) is exact
         qsh[lane + kHalfHead] = (-qa * cs.y + qb * cs.x) * 0.125f;
-        if (n >= t0 && n < t0 + kPersistChunk) {
-            const float* kn = p.qkv + p.Hl + h * kHeadDim;
-            const float* vn = p.qkv + 2 * p.Hl + h * kHeadDim;
-            const float ka = __ldcg(kn + lane), kb = __ldcg(kn + lane + kHalfHead);
-            const float va = __ldcg(vn + lane), vb = __ldcg(vn + lane + kHalfHead);
-            kc[n * kHeadDim + lane] = ka * cs.x + kb * cs.y;
-            kc[n * kHeadDim + lane + kHalfHead] = -ka * cs.y + kb * cs.x;
-            vc[n * kHeadDim + lane] = va;
-            vc[n * kHeadDim + lane + kHalfHead] = vb;
+        if (has_n) {
+            // RoPE of k at position n and the KV append (read back from the cache by later tokens).
+            const float k0 = ka * cs.x + kb * cs.y, k1 = -ka * cs.y + kb * cs.x;
+            knew[lane] = k0;
+            knew[lane + kHalfHead] = k1;
+            kc[n * kHeadDim + lane] = k0;
+            kc[n * kHeadDim + lane + kHalfHead] = k1;
+            reinterpret_cast<float2*>(vc + n * kHeadDim)[lane] = vnew;
         }
-        __syncwarp();  // orders the row-n stores before the lane that owns position n reads them
-        const float4* kr = reinterpret_cast<const float4*>(kc + static_cast<size_t>(mine ? pos : t0) * kHeadDim);
-        float4 kv[16];
+        __syncwarp();
+        const float4* q4 = reinterpret_cast<const float4*>(qsh) + 8 * kh;
+        if (posk == n) {
+            const float4* k4 = reinterpret_cast<const float4*>(knew) + 8 * kh;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) kv[i] = __ldcg(kr + i);
-        const float4* q4 = reinterpret_cast<const float4*>(qsh);
+            for (int i = 0; i < 8; ++i) kv[i] = k4[i];
+        }
         float d = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) d = dot4(kv[i], q4[i], d);
+        for (int i = 0; i < 8; ++i) d = dot4(kv[i], q4[i], d);
+        d += __shfl_xor_sync(0xffffffffu, d, 1);
+        const bool mine = posk <= n;
         const float sc = mine ? d : -INFINITY;
         const float m = warp_max(sc);
         const float e = mine ? expf(sc - m) : 0.0f;
-        const float l = warp_sum(e);
-        // P.V with lane = output dims (2 lane, 2 lane + 1): every row of the chunk
-        // is read as 32 coalesced float2 (lanes past the chunk's end weigh 0).
-        const int cnt = min(kPersistChunk, n + 1 - t0);
-        const float2* vr = reinterpret_cast<const float2*>(vc + static_cast<size_t>(t0) * kHeadDim) + lane;
-        float2 vrow[kPersistChunk];
-#pragma unroll
-        for (int jpos = 0; jpos < kPersistChunk; ++jpos)
-            vrow[jpos] = jpos < cnt ? __ldcg(vr + jpos * (kHeadDim / 2)) : make_float2(0.0f, 0.0f);
+        const float l = warp_sum(kh == 0 ? e : 0.0f);  // each position counted once
+        // P.V over the chunk's rows; row n comes from this token's v.
         float2 o = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int jpos = 0; jpos < kPersistChunk; ++jpos) {
-            const float ej = __shfl_sync(0xffffffffu, e, jpos);
-            o.x = fmaf(ej, vrow[jpos].x, o.x);
-            o.y = fmaf(ej, vrow[jpos].y, o.y);
+        for (int jp = 0; jp < kPersistChunk; ++jp) {
+            const float ej = __shfl_sync(0xffffffffu, e, 2 * jp);
+            const float2 v = t0 + jp == n ? vnew : vrow[jp];
+            o.x = fmaf(ej, v.x, o.x);
+            o.y = fmaf(ej, v.y, o.y);
         }
         float* ap = apart + warp * kAttnPartStride;
         reinterpret_cast<float2*>(ap + 4)[lane] = o;

@@ -87,7 +87,7 @@ long long launch_count();
 
 // Persistent decode step (decode_persistent.cu): one cooperative launch per token.
 constexpr int kMaxLayers = 32;
-constexpr int kPersistChunk = 32;     // attention positions per warp
+constexpr int kPersistChunk = 16;     // attention positions per warp
 constexpr int kPersistTileRows = 16;  // weight box streamed per TMA load: 16 rows x 2 k-tiles x 256 floats
 constexpr int kPersistTileK = 256;
 constexpr int kPersistBoxTiles = 2;
