@@ -11,7 +11,10 @@
 // stay busy.  The boxes are loaded with an L2 evict-first policy: a weight
 // line is dead once read, and the 113 MB a layer streams would otherwise push
 // the activations, partial sums and cached K/V rows that the stagings and the
-// attention wait on out of L2.  Warps 1..8 consume: per phase they wait for the previous phase
+// attention wait on out of L2.  Between the landing of a phase's last box and
+// the staging of the next phase's input the producer pauses: the phase's
+// release signal, the grid-counter polls and the staging loads would
+// otherwise wait behind the SM's in-flight weight data.  Warps 1..8 consume: per phase they wait for the previous phase
 // of every CTA (a global counter), stage the phase's input vector in shared
 // memory, take ring boxes (two rows per warp) and reduce with warp shuffles.
 //
@@ -58,8 +61,12 @@ constexpr int kSlotBytes = kPersistTileRows * kBoxK * 4;         // 32 KB
 constexpr int kSlots = kPersistSlots;                            // 192 KB ring
 constexpr int kMaxK = 4096;
 constexpr size_t kSmemBytes = static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 + 2 * kSlots * 8 + 512;
+// Every wait is bounded twice: by polls and by wall-clock time (an mbarrier
+// try_wait may suspend the thread for a while, so a poll count alone can last
+// far longer than intended).  A decode step takes under a millisecond.
 constexpr uint32_t kMbarSpinLimit = 1u << 24;
 constexpr uint32_t kFlagSpinLimit = 1u << 24;
+constexpr unsigned long long kWaitLimitNs = 200ull * 1000 * 1000;
 constexpr int kErrMbar = 1, kErrFlag = 2;
 // Attention scratch inside the staging buffer xs (free between the QKV and
 // out-projection stagings): per warp the rotated q (64 floats), then per warp
@@ -146,10 +153,16 @@ __device__ __forceinline__ void trace_at(const PersistentParams& p, int ph, int 
 // Bounded wait on an mbarrier phase; false (and the error bit) on timeout or abort.
 __device__ bool wait_parity(uint64_t* bar, uint32_t parity, DevState* st) {
     uint32_t it = 0;
+    unsigned long long t0 = 0;
     while (!mbar_try_wait(bar, parity)) {
-        if (++it >= kMbarSpinLimit || ((it & 1023u) == 0 && aborted(st))) {
-            atomicOr(&st->err, kErrMbar);
-            return false;
+        ++it;
+        if ((it & 63u) == 0) {
+            const unsigned long long now = globaltimer();
+            if (t0 == 0) t0 = now;
+            if (it >= kMbarSpinLimit || now - t0 > kWaitLimitNs || aborted(st)) {
+                atomicOr(&st->err, kErrMbar);
+                return false;
+            }
         }
     }
     return true;
@@ -242,7 +255,8 @@ __device__ void cursor_first(const PersistentParams& p, int ph, Cursor& c) {
     c.valid = false;
 }
 
-__device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, uint64_t* empty) {
+__device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, uint64_t* empty,
+                         const volatile int* quiet) {
     DevState* st = p.st;
     int slot = 0;
     uint32_t par = 0;
@@ -255,6 +269,18 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
         if (!wait_parity(&empty[slot], par ^ 1u, st)) {
             ok = false;
             break;
+        }
+        // Quiet window (set by the consumers from the moment the last box of a
+        // phase has landed until the next phase's input is staged): issue
+        // nothing, so that the result stores' acknowledgements the phase
+        // signal waits for, the grid-counter polls and the staging loads do not
+        // queue behind this SM's weight stream.
+        if (*quiet) {
+            uint32_t it = 0;
+            const unsigned long long t0 = globaltimer();
+            while (*quiet) {
+                if ((++it & 63u) == 0 && (globaltimer() - t0 > kWaitLimitNs || aborted(st))) break;
+            }
         }
         // At most `inflight` boxes requested but not landed: a deeper queue only
         // adds latency to every other memory access once HBM is saturated.
@@ -293,7 +319,13 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
             const int s = k % kSlots;
             const uint32_t pp = static_cast<uint32_t>((k / kSlots) & 1);
             uint32_t it = 0;
+            unsigned long long t0 = 0;
             while (!mbar_try_wait(&full[s], pp) && ++it < kMbarSpinLimit) {
+                if ((it & 63u) == 0) {
+                    const unsigned long long now = globaltimer();
+                    if (t0 == 0) t0 = now;
+                    if (now - t0 > kWaitLimitNs) break;
+                }
             }
         }
     }
@@ -308,12 +340,18 @@ __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
     if (threadIdx.x == 32) {
         const int* c = p.done + ph;
         uint32_t it = 0;
+        unsigned long long t0 = 0;
         int ok = 1;
         while (ld_acquire(c) < static_cast<int>(gridDim.x) * kConsumerWarps) {
-            if (++it >= kFlagSpinLimit || ((it & 255u) == 0 && aborted(p.st))) {
-                atomicOr(&p.st->err, kErrFlag);
-                ok = 0;
-                break;
+            ++it;
+            if ((it & 255u) == 0) {
+                const unsigned long long now = globaltimer();
+                if (t0 == 0) t0 = now;
+                if (it >= kFlagSpinLimit || now - t0 > kWaitLimitNs || aborted(p.st)) {
+                    atomicOr(&p.st->err, kErrFlag);
+                    ok = 0;
+                    break;
+                }
             }
         }
         *s_ok = ok;
@@ -614,7 +652,7 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
 }
 
 __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint64_t* full, uint64_t* empty,
-                          float* red, unsigned long long* best_s, int* s_ok) {
+                          float* red, unsigned long long* best_s, int* s_ok, volatile int* quiet) {
     DevState* st = p.st;
     const int t = threadIdx.x - 32;
     const int warp = t >> 5, lane = t & 31;
@@ -631,6 +669,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
         const int kind = phase_kind(ph, p.layers);
         if (kind == kAttn) {
             if (!attention_phase(p, ph / 5, ph, n, xs, s_ok)) return;
+            if (t == 0) *quiet = 0;
             if (t == 0) trace_at(p, ph, kTrConsStaged);
             signal_phase(p, ph);
             if (t == 0) trace_at(p, ph, kTrConsEnd);
@@ -674,6 +713,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
             stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, p.gnorm, xs, red, p.xa);
         }
         consumer_sync();
+        if (t == 0) *quiet = 0;
         if (t == 0) trace_at(p, ph, kTrConsStaged);
         const int rs4 = r.kd * (kPersistTileK / 4);  // float4 per row of a box
         const float4* x4 = reinterpret_cast<const float4*>(xs);
@@ -704,6 +744,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 // After a failed wait this warp only walks the schedule so that it
                 // meets the other consumer warps at every named barrier.
                 if (ok && !wait_parity(&full[slot], par, st)) ok = false;
+                // Every box of this phase has landed: quiet window until the next staging.
+                if (t == 0 && kind != kLM && tau + (bi - bi0) == r.t1 - 1) *quiet = 1;
                 if (ok) {
                     const int k0 = bi * r.kd * kPersistTileK;
                     const int kc4 = min(r.kd * kPersistTileK, d.K - k0) >> 2;
@@ -802,6 +844,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     float* red = reinterpret_cast<float*>(empty + kSlots);                  // 16 floats
     unsigned long long* best_s = reinterpret_cast<unsigned long long*>(red + 16);  // 8
     int* s_ok = reinterpret_cast<int*>(best_s + kConsumerWarps);            // 1 (+pad)
+    volatile int* quiet = s_ok + 8;                                           // producer pause flag
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
@@ -809,14 +852,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
             mbar_init(&empty[s], kConsumerWarps);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        *quiet = 0;
     }
     __syncthreads();
     pdl_launch_dependents();
     pdl_wait();
     if (threadIdx.x < 32) {
-        if (threadIdx.x == 0) producer(p, ring, full, empty);
+        if (threadIdx.x == 0) producer(p, ring, full, empty, quiet);
     } else {
-        consumers(p, ring, xs, full, empty, red, best_s, s_ok);
+        consumers(p, ring, xs, full, empty, red, best_s, s_ok, quiet);
     }
 }
 

@@ -41,6 +41,7 @@ constexpr int kStageBytes = 4 * kTileBytes;  // W, W_lo, X, X_lo
 constexpr int kGemmThreads = 192;
 constexpr size_t kGemmSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
 constexpr uint32_t kSpinLimit = 1u << 26;
+constexpr unsigned long long kWaitLimitNs = 200ull * 1000 * 1000;  // a tile's operands land in microseconds
 constexpr int kGemmPartial = 4;  // epilogue: raw slice accumulator into the split-K workspace
 constexpr int kGemmScores = 5;   // attention: S[z][n][m] = q_n . k_m per head z (tiles above the diagonal skipped)
 constexpr int kGemmPV = 6;       // attention: O[n][z*64 + f] (+ lo) = P[z][n][:] . V[:][f], keys up to the tile's last query
@@ -66,12 +67,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded by polls and by wall-clock time (a try_wait may suspend the thread).
 __device__ bool wait_bar(uint64_t* bar, uint32_t parity, int* err) {
     uint32_t it = 0;
+    unsigned long long t0 = 0;
     while (!mbar_try_wait(bar, parity)) {
-        if (++it >= kSpinLimit) {
-            if (err) atomicOr(err, 4);
-            return false;
+        ++it;
+        if ((it & 63u) == 0) {
+            const unsigned long long now = globaltimer_ns();
+            if (t0 == 0) t0 = now;
+            if (it >= kSpinLimit || now - t0 > kWaitLimitNs) {
+                if (err) atomicOr(err, 4);
+                return false;
+            }
         }
     }
     return true;
