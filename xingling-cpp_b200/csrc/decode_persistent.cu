@@ -334,15 +334,17 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
 // ---------------------------------------------------------------------------
 // Consumer helpers (256 threads, named barrier 1).
 
-// Wait until every consumer warp of every CTA finished phase ph (counter ==
-// 8 x gridDim.x).
+// Wait until phase ph is complete (its counter reaches its target).
 __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
+    // An attention phase is signalled once per head (by the warp that writes
+    // the head's output); every other phase by every consumer warp of every CTA.
+    const int target = phase_kind(ph, p.layers) == kAttn ? p.heads : static_cast<int>(gridDim.x) * kConsumerWarps;
     if (threadIdx.x == 32) {
         const int* c = p.done + ph;
         uint32_t it = 0;
         unsigned long long t0 = 0;
         int ok = 1;
-        while (ld_acquire(c) < static_cast<int>(gridDim.x) * kConsumerWarps) {
+        while (ld_acquire(c) < target) {
             ++it;
             if ((it & 255u) == 0) {
                 const unsigned long long now = globaltimer();
@@ -534,9 +536,11 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
     for (int jp = 0; jp < kPersistChunk; ++jp)
         vrow[jp] = jp < cached ? __ldcg(vr + jp * (kHeadDim / 2)) : make_float2(0.0f, 0.0f);
     const float2 cs = active ? p.rope[n * kHalfHead + lane] : make_float2(0.0f, 0.0f);
+    // A CTA without an attention item neither waits nor signals: the next
+    // phase waits for the heads' outputs, which imply the QKV phase.
+    if (!has) return true;
     if (!wait_phase(p, ph - 1, s_ok)) return false;
     if (t == 0) trace_at(p, ph, kTrConsStart);
-    if (!has) return true;
     float* qsh = xs + warp * kAttnWarpScratch;
     float* apart = xs + kConsumerWarps * kAttnWarpScratch;  // [8][68]
     float* knew = xs + kConsumerWarps * (kAttnWarpScratch + kAttnPartStride) + warp * kHeadDim;  // rotated k of row n
@@ -616,6 +620,7 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
     float2* out = reinterpret_cast<float2*>(p.att + h * kHeadDim);
     if (nct == 1) {
         out[lane] = make_float2(acc.x / L, acc.y / L);
+        signal_phase(p, ph);
         return true;
     }
     // A head split over nct CTAs: the last CTA to finish merges their partials.
@@ -648,6 +653,7 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
         acc2.y = fmaf(wt, ok.y, acc2.y);
     }
     out[lane] = make_float2(acc2.x / L2, acc2.y / L2);
+    signal_phase(p, ph);
     return true;
 }
 
@@ -668,10 +674,10 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
     for (int ph = 0; ph <= last; ++ph) {
         const int kind = phase_kind(ph, p.layers);
         if (kind == kAttn) {
+            // Head outputs are signalled inside; the pause that began with the
+            // QKV phase's last box lasts through this CTA's attention.
             if (!attention_phase(p, ph / 5, ph, n, xs, s_ok)) return;
             if (t == 0) *quiet = 0;
-            if (t == 0) trace_at(p, ph, kTrConsStaged);
-            signal_phase(p, ph);
             if (t == 0) trace_at(p, ph, kTrConsEnd);
             continue;
         }
