@@ -95,6 +95,20 @@ XL_API int xl_engine_prefill(xl_engine* e, const int* ids, int n, float temperat
 XL_API int xl_engine_decode(xl_engine* e, int token, float temperature, float top_p, float repetition_penalty,
                             int* token_out);
 
+/* Device-side multi-token loop (no reference counterpart; replaces the
+ * per-token host loop of the reference's main.py:26-27 and
+ * test_speed.py:52-57): up to n decode steps, step 0 fed `token`, each later
+ * step the previous step's id, all without a host round trip between steps
+ * (one CUDA graph launch per step, one synchronisation at the end).  Stops
+ * after producing stop_id (when >= 0; it is returned) or when the cache is
+ * full.  tokens_out receives the ids (capacity n), *n_out their count.  The
+ * ids, the uniforms consumed (one per step taken) and the engine state equal
+ * those of *n_out successive xl_engine_decode calls.  On a single GPU with the
+ * persistent decode kernel the loop runs on the device; otherwise it is that
+ * host loop. */
+XL_API int xl_engine_generate(xl_engine* e, int token, int n, float temperature, float top_p,
+                              float repetition_penalty, int stop_id, int* tokens_out, int* n_out);
+
 /* Sampling-uniform control (no reference counterpart: the reference seeds a
  * std::mt19937 from std::random_device, src/inference.cu:37-38).  Each
  * next-token call consumes one uniform in [0, 1): first the queued values

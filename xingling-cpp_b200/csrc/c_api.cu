@@ -154,6 +154,13 @@ int xl_engine_decode(xl_engine* e, int token, float temperature, float top_p, fl
     return e->impl->decode(token, temperature, top_p, repetition_penalty, token_out);
 }
 
+int xl_engine_generate(xl_engine* e, int token, int n, float temperature, float top_p, float repetition_penalty,
+                       int stop_id, int* tokens_out, int* n_out) {
+    xl::clear_error();
+    if (!e || !n_out) return bad("null argument");
+    return e->impl->generate(token, n, temperature, top_p, repetition_penalty, stop_id, tokens_out, n_out);
+}
+
 int xl_engine_set_uniforms(xl_engine* e, const float* u, int n) {
     xl::clear_error();
     if (!e) return bad("null engine");

@@ -481,6 +481,7 @@ __device__ __forceinline__ SampleWork work_of(const SampleParams& p, int b) {
 __device__ __forceinline__ bool greedy_step(const SampleParams& p, const DevState* st) {
     return !(st->in.top_p > 0.0f) && !p.full;
 }
+__device__ __forceinline__ bool skipped(const DevState* st) { return st->in.skip != 0; }
 
 // The step's id: state, repetition flag, KV position (src/inference.cu:113 and
 // the caller's history update).
@@ -509,7 +510,7 @@ __global__ void __launch_bounds__(kSampThreads) sample_hist_kernel(const SampleP
     pdl_wait();
     const int b = blockIdx.y;
     DevState* st = p.st + b;
-    if (greedy_step(p, st)) return;
+    if (greedy_step(p, st) || skipped(st)) return;
     const SampleWork w = work_of(p, b);
     const int tid = threadIdx.x;
     const int V = p.V;
@@ -700,6 +701,7 @@ __global__ void __launch_bounds__(kSampThreads) sample_gather_kernel(const Sampl
     const int b = blockIdx.y;
     DevState* st = p.st + b;
     const int tid = threadIdx.x, lane = tid & 31;
+    if (skipped(st)) return;
     if (greedy_step(p, st)) {
         if (blockIdx.x == 0 && tid == 0) finish_token(p, b, st, unpack_argmax_index(st->argmax_final));
         return;
@@ -810,7 +812,40 @@ __global__ void __launch_bounds__(32) sample_finish_kernel(const SampleParams p)
     pdl_launch_dependents();
     pdl_wait();
     const int b = blockIdx.y;
-    if (threadIdx.x == 0) finish_token(p, b, p.st + b, unpack_argmax_index(p.st[b].argmax_final));
+    if (threadIdx.x == 0 && !skipped(p.st + b)) finish_token(p, b, p.st + b, unpack_argmax_index(p.st[b].argmax_final));
+}
+
+// Step input of a device-side generation: the previous step's id (or the
+// first id), the sampling arguments and the step's uniform; a run that has
+// produced its stop id, done its steps or filled the cache skips the step.
+__global__ void __launch_bounds__(32) gen_feed_kernel(const GenParams p) {
+    if (threadIdx.x != 0) return;
+    GenCtl* c = p.ctl;
+    DevState* st = p.st;
+    const int i = c->step;
+    if (c->stopped || i >= c->n || st->pos >= c->max_ctx) {
+        st->in.skip = 1;
+        return;
+    }
+    st->in.skip = 0;
+    st->in.token_in = i == 0 ? c->first : st->token_out;
+    st->in.temperature = c->temperature;
+    st->in.top_p = c->top_p;
+    st->in.rp = c->rp;
+    st->in.uniform = p.uniforms[i];
+    st->in.decode_mode = 1;
+}
+
+// Records the step's id; the stop id ends the run (it is returned).
+__global__ void __launch_bounds__(32) gen_collect_kernel(const GenParams p) {
+    if (threadIdx.x != 0) return;
+    GenCtl* c = p.ctl;
+    DevState* st = p.st;
+    if (st->in.skip) return;
+    const int tok = st->token_out;
+    p.out[c->step] = tok;
+    c->step += 1;
+    if (tok == c->stop_id) c->stopped = 1;
 }
 
 // Tensor-parallel merge of sample_cpu (src/inference.cu:58-114) over vocab
@@ -931,6 +966,14 @@ cudaError_t launch_sample_chain(const SampleParams& p, int batch, bool pdl, cuda
         if (e != cudaSuccess) return e;
     }
     return launch_ex(sample_gather_kernel, grid, dim3(kSampThreads), 0, true, s, p);
+}
+
+cudaError_t launch_gen_feed(const GenParams& p, cudaStream_t s) {
+    return launch_ex(gen_feed_kernel, dim3(1), dim3(32), 0, false, s, p);
+}
+
+cudaError_t launch_gen_collect(const GenParams& p, cudaStream_t s) {
+    return launch_ex(gen_collect_kernel, dim3(1), dim3(32), 0, false, s, p);
 }
 
 cudaError_t launch_sample_finish(const SampleParams& p, int batch, bool pdl, cudaStream_t s) {

@@ -863,6 +863,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     __syncthreads();
     pdl_launch_dependents();
     pdl_wait();
+    // A stopped device-side generation: nothing to do this step (every CTA reads the same flag).
+    if (p.st->in.skip) return;
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) producer(p, ring, full, empty, quiet);
     } else {

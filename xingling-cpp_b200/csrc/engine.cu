@@ -5,6 +5,7 @@
 // instead of exit(1).
 #include <sys/stat.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -166,6 +167,8 @@ int Engine::init(const xl_config& cfg, int device, int tp_size, int tp_rank, con
     XL_CUDA(cudaEventCreate(&kev1_));
     XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_in_), sizeof(DevState), cudaHostAllocDefault));
     XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_out_), sizeof(DevState), cudaHostAllocDefault));
+    XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_gen_), sizeof(GenCtl) + 2 * static_cast<size_t>(T_) * 4,
+                          cudaHostAllocDefault));
     XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_ids_), sizeof(int) * (T_ + 1), cudaHostAllocDefault));
     std::random_device rd;
     philox_seed_ = (static_cast<uint64_t>(rd()) << 32) ^ rd();
@@ -221,6 +224,9 @@ int Engine::alloc_all() {
     add(&ffh_, Fl * 4);
     add(&part_, H * 4);
     add(&cand_local_, kTopK * 8);
+    add(&gen_ctl_, sizeof(GenCtl));
+    add(&gen_u_, T * 4);
+    add(&gen_out_, T * 4);
     add(&cand_all_, static_cast<size_t>(tp_) * kTopK * 8);
     add(&cres_, H / kPersistTileRows * kPersistMaxContrib * kPersistTileRows * 4);
     add(&logits_, vl * 4);
@@ -272,10 +278,13 @@ Engine::~Engine() {
     if (stream_) cudaStreamSynchronize(stream_);
     if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
     if (decode_exec_s_) cudaGraphExecDestroy(decode_exec_s_);
+    if (gen_exec_) cudaGraphExecDestroy(gen_exec_);
+    if (gen_exec_s_) cudaGraphExecDestroy(gen_exec_s_);
     if (comm_) ncclCommDestroy(comm_);
     if (arena_) cudaFree(arena_);
     if (h_in_) cudaFreeHost(h_in_);
     if (h_out_) cudaFreeHost(h_out_);
+    if (h_gen_) cudaFreeHost(h_gen_);
     if (h_ids_) cudaFreeHost(h_ids_);
     if (trace_) cudaFree(trace_);
     if (ev0_) cudaEventDestroy(ev0_);
@@ -701,6 +710,47 @@ int Engine::capture_decode_graph() {
         cudaGraphDestroy(g);
         if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
     }
+    return capture_gen_graphs();
+}
+
+// Device-side generation graphs: gen_feed, the persistent decode step and
+// gen_collect (single GPU, persistent path only: its kernels skip a step
+// once the run has stopped).
+int Engine::capture_gen_graphs() {
+    for (int sampled = 0; sampled < 2; ++sampled) {
+        cudaGraphExec_t& exec = sampled ? gen_exec_s_ : gen_exec_;
+        if (exec) {
+            cudaGraphExecDestroy(exec);
+            exec = nullptr;
+        }
+    }
+    if (!persistent_graph_) return XL_OK;
+    GenParams gp{};
+    gp.ctl = gen_ctl_;
+    gp.uniforms = gen_u_;
+    gp.out = gen_out_;
+    gp.st = st_;
+    for (int sampled = 0; sampled < 2; ++sampled) {
+        cudaGraphExec_t& exec = sampled ? gen_exec_s_ : gen_exec_;
+        long long& kernels = sampled ? gen_graph_kernels_s_ : gen_graph_kernels_;
+        cudaGraph_t g = nullptr;
+        XL_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+        const long long recorded0 = launch_count();
+        cudaError_t le = launch_gen_feed(gp, stream_);
+        int rc = le == cudaSuccess ? enqueue_decode(stream_, sampled != 0) : XL_OK;
+        if (le == cudaSuccess && rc == XL_OK) le = launch_gen_collect(gp, stream_);
+        kernels = launch_count() - recorded0;
+        count_graph_kernels(-kernels);
+        cudaError_t ce = cudaStreamEndCapture(stream_, &g);
+        if (rc != XL_OK || le != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return rc != XL_OK ? rc : cuda_fail(le, "generation graph capture");
+        }
+        if (ce != cudaSuccess) return cuda_fail(ce, "cudaStreamEndCapture");
+        ce = cudaGraphInstantiate(&exec, g, 0);
+        cudaGraphDestroy(g);
+        if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate");
+    }
     return XL_OK;
 }
 
@@ -857,6 +907,94 @@ int Engine::decode(int token, float temperature, float top_p, float rp, int* tok
     last_kernel_ms_ = -1.0f;
     if (kernel_events_ && persistent_graph_) XL_CUDA(cudaEventElapsedTime(&last_kernel_ms_, kev0_, kev1_));
     n_ += 1;
+    return XL_OK;
+}
+
+int Engine::generate(int token, int n, float temperature, float top_p, float rp, int stop_id, int* tokens_out,
+                     int* n_out) {
+    XL_CUDA(cudaSetDevice(device_));
+    *n_out = 0;
+    if (n < 0 || (n > 0 && tokens_out == nullptr)) {
+        set_error("generate: n must be >= 0 and tokens_out non-null");
+        return XL_ERR_ARG;
+    }
+    if (n == 0) return XL_OK;
+    if (!loaded_) {
+        set_error("decode before load");
+        return XL_ERR_STATE;
+    }
+    if (!has_seq_) {
+        set_error("decode before any prefill: the KV cache is empty");
+        return XL_ERR_STATE;
+    }
+    if (token < 0 || token >= V_) {
+        set_error("Embedding : Invalid token: " + std::to_string(token));
+        return XL_ERR_TOKEN;
+    }
+    if (n_ >= T_) {
+        set_error("KV cache full: position " + std::to_string(n_) + " of max_seq_len " + std::to_string(T_));
+        return XL_ERR_CTX;
+    }
+    if (!gen_exec_) {
+        // Per-op or tensor-parallel engines: the same loop on the host.
+        int tok = token;
+        for (int i = 0; i < n && n_ < T_; ++i) {
+            const int rc = decode(tok, temperature, top_p, rp, &tok);
+            if (rc != XL_OK) return rc;
+            tokens_out[(*n_out)++] = tok;
+            if (tok == stop_id) break;
+        }
+        return XL_OK;
+    }
+    const int steps = std::min(n, T_ - n_);
+    // The draws of successive next_token calls; those of steps that never run are handed back below.
+    const size_t queued = uniforms_.size();
+    const uint64_t ctr0 = philox_ctr_;
+    std::deque<float> queue0 = uniforms_;
+    GenCtl* c = reinterpret_cast<GenCtl*>(h_gen_);
+    float* hu = reinterpret_cast<float*>(h_gen_ + sizeof(GenCtl));
+    int* ho = reinterpret_cast<int*>(hu + T_);
+    std::memset(c, 0, sizeof(GenCtl));
+    c->n = steps;
+    c->first = token;
+    c->stop_id = stop_id;
+    c->max_ctx = T_;
+    c->temperature = temperature;
+    c->top_p = top_p;
+    c->rp = rp;
+    for (int i = 0; i < steps; ++i) hu[i] = next_uniform();
+    XL_CUDA(cudaMemcpyAsync(gen_ctl_, c, sizeof(GenCtl), cudaMemcpyHostToDevice, stream_));
+    XL_CUDA(cudaMemcpyAsync(gen_u_, hu, static_cast<size_t>(steps) * 4, cudaMemcpyHostToDevice, stream_));
+    XL_CUDA(cudaEventRecord(ev0_, stream_));
+    const bool sampled = top_p > 0.0f;
+    cudaGraphExec_t exec = sampled ? gen_exec_s_ : gen_exec_;
+    for (int i = 0; i < steps; ++i) {
+        XL_CUDA(cudaGraphLaunch(exec, stream_));
+        count_graph_kernels(sampled ? gen_graph_kernels_s_ : gen_graph_kernels_);
+    }
+    XL_CUDA(cudaEventRecord(ev1_, stream_));
+    XL_CUDA(cudaMemcpyAsync(c, gen_ctl_, sizeof(GenCtl), cudaMemcpyDeviceToHost, stream_));
+    XL_CUDA(cudaMemcpyAsync(ho, gen_out_, static_cast<size_t>(steps) * 4, cudaMemcpyDeviceToHost, stream_));
+    XL_CUDA(cudaMemcpyAsync(h_out_, st_, sizeof(DevState), cudaMemcpyDeviceToHost, stream_));
+    XL_CUDA(cudaStreamSynchronize(stream_));
+    XL_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
+    const DevState* hs = reinterpret_cast<const DevState*>(h_out_);
+    if (hs->err != 0) {
+        set_error("device error word " + std::to_string(hs->err));
+        return XL_ERR_DEVICE;
+    }
+    const int done = c->step;
+    if (done < steps) {
+        // Return the unused draws: queued values go back in order, the Philox counter rewinds.
+        uniforms_ = queue0;
+        const size_t from_queue = std::min(static_cast<size_t>(done), queued);
+        for (size_t i = 0; i < from_queue; ++i) uniforms_.pop_front();
+        philox_ctr_ = ctr0 + (static_cast<size_t>(done) > queued ? static_cast<size_t>(done) - queued : 0);
+    }
+    for (int i = 0; i < done; ++i) tokens_out[i] = ho[i];
+    *n_out = done;
+    n_ += done;
+    last_kernel_ms_ = -1.0f;
     return XL_OK;
 }
 

@@ -48,6 +48,11 @@ class Engine {
     int load(const char* dir);
     int prefill(const int* ids, int n, float temperature, float top_p, float rp, int* token_out);
     int decode(int token, float temperature, float top_p, float rp, int* token_out);
+    // Up to n decode steps fed on the device (each step's input is the previous
+    // step's id), stopping after stop_id (>= 0) or a full cache; the ids go to
+    // tokens_out, their count to *n_out.  Same ids, draws and state as that many
+    // decode calls.
+    int generate(int token, int n, float temperature, float top_p, float rp, int stop_id, int* tokens_out, int* n_out);
     int set_uniforms(const float* u, int n);
     int seed(uint64_t s);
     int last_logits(float* out, int n);
@@ -66,6 +71,7 @@ class Engine {
     int init(const xl_config& cfg, int device, int tp_size, int tp_rank, const void* nccl_id);
     int alloc_all();
     int capture_decode_graph();
+    int capture_gen_graphs();
     int enqueue_decode(cudaStream_t s, bool sampled);
     int enqueue_decode_persistent(cudaStream_t s, bool sampled);
     SampleParams sample_params() const;  // this engine's sequence, single-step sampler chain
@@ -136,6 +142,12 @@ class Engine {
     cudaGraphExec_t decode_exec_s_ = nullptr;  // sampled step (the sampler chain; TP: candidate merge)
     long long decode_graph_kernels_s_ = 0;
     unsigned long long *cand_local_ = nullptr, *cand_all_ = nullptr;  // tensor-parallel sampling merge
+    GenCtl* gen_ctl_ = nullptr;    // device-side generation: control block
+    float* gen_u_ = nullptr;       // [T] its draws
+    int* gen_out_ = nullptr;       // [T] its ids
+    char* h_gen_ = nullptr;        // pinned: GenCtl, draws [T], ids [T]
+    cudaGraphExec_t gen_exec_ = nullptr, gen_exec_s_ = nullptr;  // gen_feed + decode step + gen_collect
+    long long gen_graph_kernels_ = 0, gen_graph_kernels_s_ = 0;
     ncclComm_t comm_ = nullptr;
 
     int decode_path_ = 0;      // 0: persistent kernel (single GPU), 1: per-op kernels

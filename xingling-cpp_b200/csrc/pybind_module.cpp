@@ -115,6 +115,19 @@ class InferenceEngine {
         return tok;
     }
 
+    std::vector<int> generate(int token, int n, float temperature, float top_p, float rp, int stop_id) {
+        if (n < 0) throw py::value_error("generate: n must be >= 0");
+        std::vector<int> out(static_cast<size_t>(n));
+        int got = 0, rc;
+        {
+            py::gil_scoped_release nogil;
+            rc = xl_engine_generate(e_, token, n, temperature, top_p, rp, stop_id, out.data(), &got);
+        }
+        check(rc);
+        out.resize(static_cast<size_t>(got));
+        return out;
+    }
+
     void set_uniforms(const std::vector<float>& u) { check(xl_engine_set_uniforms(e_, u.data(), static_cast<int>(u.size()))); }
     void seed(unsigned long long s) { check(xl_engine_seed(e_, s)); }
 
@@ -290,6 +303,9 @@ PYBIND11_MODULE(llm_cpp_engine, m) {
              py::arg("top_p") = 0.9f, py::arg("repetition_penalty") = 1.1f)
         .def("next_token", &InferenceEngine::next_token_decode, py::arg("token"), py::arg("temperature") = 0.7f,
              py::arg("top_p") = 0.9f, py::arg("repetition_penalty") = 1.1f)
+        .def("generate", &InferenceEngine::generate, py::arg("token"), py::arg("n"), py::arg("temperature") = 0.7f,
+             py::arg("top_p") = 0.9f, py::arg("repetition_penalty") = 1.1f, py::arg("stop_id") = -1,
+             "up to n decode steps fed on the device; stops after stop_id (returned) or a full cache")
         .def("set_uniforms", &InferenceEngine::set_uniforms, py::arg("uniforms"))
         .def("seed", &InferenceEngine::seed, py::arg("seed"))
         .def("vocab_shard", &InferenceEngine::vocab_shard)

@@ -20,7 +20,8 @@ struct StepIn {
     float rp;
     float uniform;      // the draw r in [0, 1), src/inference.cu:105
     int decode_mode;    // 1: the sampler also advances pos (decode), 0: prefill
-    int pad[2];
+    int skip;           // 1: a device-side generation has stopped; every kernel of the step returns at once
+    int pad;
 };
 
 // Device-resident state of one engine (one sequence per GPU).
@@ -211,6 +212,28 @@ struct SampleParams {
 cudaError_t launch_sample_chain(const SampleParams& p, int batch, bool pdl, cudaStream_t s);
 // Greedy steps (top_p <= 0): write the LM head's argmax as the step's id.
 cudaError_t launch_sample_finish(const SampleParams& p, int batch, bool pdl, cudaStream_t s);
+
+// Device-side generation (InferenceEngine.generate): each step of a decode
+// graph is bracketed by gen_feed (step input from the previous step's id and
+// the step's uniform) and gen_collect (record the id; a stop id ends the run).
+struct GenCtl {
+    int step;      // steps done
+    int n;         // steps requested
+    int first;     // input id of step 0
+    int stop_id;   // -1: none
+    int stopped;   // 1 after the stop id was produced
+    int max_ctx;
+    float temperature, top_p, rp;
+    int pad[7];
+};
+struct GenParams {
+    GenCtl* ctl;
+    const float* uniforms;  // [n] the draws of the steps, in order
+    int* out;               // [n] the ids produced
+    DevState* st;
+};
+cudaError_t launch_gen_feed(const GenParams& p, cudaStream_t s);
+cudaError_t launch_gen_collect(const GenParams& p, cudaStream_t s);
 
 // Tensor-parallel sampling merge: the all-gathered per-shard candidate lists
 // (packed (value key, ~global id), n = tp x 1024), sorted as one; draws as
