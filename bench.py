@@ -10,10 +10,12 @@ weights 2.75 GB per token, far above the 126 MB L2, so no flush is needed);
 next_token(int)), wall clock, including the per-token host->device copy of
 the step inputs from pinned memory and the device->host read of the result.
 `roofline` is the dominant kernel, the persistent decode kernel (one launch
-per token, >99% of a decode step's kernel time), timed by CUDA event nodes
-around it inside the decode graph in one more step right after the timed
-region (the timed steps run without the nodes).  Also reported: the whole
-decode step against the same roofline, prefill of a 512-id prompt (seed 1),
+per token, all of a greedy decode step's kernel time), timed by CUDA event
+nodes around it inside the decode graph in one more step right after the
+timed region (the timed steps run without the nodes).  Also reported: the
+whole decode step against the same roofline, the same 128 ids through the
+device-side loop (`generate`, one call per prefill), prefill of a 512-id
+prompt (seed 1),
 the reference's own CPU path on the host cores, `replica_batch` (64
 sequences, prompt lengths uniform in [16, 512] with seed 5, 128 sampled
 tokens each, spread over the N replicas, each replica decoding waves of 8
@@ -349,8 +351,7 @@ def xl_arm(args) -> None:
 
     # the dominant kernel: the persistent decode kernel, one launch per token at
     # context PROMPT + i, timed by event nodes around it in the decode graph
-    # (a separate pass: the nodes cost the sampler its early launch, so the
-    # headline steps above run without them)
+    # (a separate pass, so that the headline steps above run without them)
     eng.set_option("kernel_events", 1)
     kres = [step() for _ in range(2)][1:]
     eng.set_option("kernel_events", 0)
@@ -360,6 +361,25 @@ def xl_arm(args) -> None:
     kern_bytes = [decode_bytes_per_token(shape, PROMPT + i) for _ in kres for i in range(DECODE)]
     kern_avg_ms = sum(kern_ms) / len(kern_ms)
     kern_gbs = sum(kern_bytes) / (sum(kern_ms) / 1e3) / 1e9
+
+    # the same decode workload through the device-side loop: one generate call
+    # for the 128 ids after each prefill (wall clock around the call, and the
+    # device time from the call's own CUDA events)
+    gen_wall, gen_dev = [], []
+    for i in range(max(3, args.steps) + 1):
+        tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
+        w0 = time.perf_counter()
+        out = eng.generate(tok, DECODE, top_p=0.0, repetition_penalty=1.0)
+        if i > 0:
+            gen_wall.append(time.perf_counter() - w0)
+            gen_dev.append(eng.last_device_ms())
+        if len(out) != DECODE:
+            raise RuntimeError("generate returned fewer ids than asked")
+    gen_info = {"api": "llm_cpp_engine.InferenceEngine.generate", "tokens_per_call": DECODE,
+                "e2e_tokens_per_s": DECODE / statistics.median(gen_wall),
+                "device_tokens_per_s": DECODE / (statistics.median(gen_dev) / 1e3),
+                "h2d_bytes_per_call": 64 + 4 * DECODE, "d2h_bytes_per_call": 64 + 4 * DECODE + 80,
+                "timing": "median over calls; wall clock around the call / CUDA events inside it"}
 
     # prefill of the 512-id prompt (seed 1)
     pids = S.prompt_ids(1, PREFILL_N, shape.vocab)
@@ -413,6 +433,7 @@ def xl_arm(args) -> None:
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    line["generate"] = gen_info
     line["replica_batch"] = batch_info
     if tp_info is not None:
         line["tp"] = tp_info
