@@ -157,6 +157,9 @@ XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, fl
  *   "tma_evict_first" 1  the persistent kernel loads weight boxes with an L2
  *                    evict-first policy (default), keeping activations and
  *                    cached K/V in L2; 0  the default L2 policy;
+ *   "load_threads" n  worker threads of xl_engine_load, in [1, 64] (default
+ *                    4): each preads chunks of the weight files into its own
+ *                    pinned buffers and copies them on its own stream;
  *   "kernel_events" 1  event-record nodes around the persistent kernel in the
  *                    decode graph, so xl_engine_last_kernel_ms reports its
  *                    own duration;
@@ -180,6 +183,10 @@ XL_API int xl_engine_last_device_ms(const xl_engine* e, float* ms);
  * (CUDA events in the decode graph; needs option "kernel_events" = 1 and the
  * persistent path), else -1.  No reference counterpart: a profiling aid. */
 XL_API int xl_engine_last_kernel_ms(const xl_engine* e, float* ms);
+
+/* Wall time in seconds of the last xl_engine_load's file reads and
+ * host-to-device copies (option "load_threads" workers, default 4). */
+XL_API int xl_engine_last_load_s(const xl_engine* e, float* s);
 
 /* Kernels this library has run in this process, every engine and op entry
  * point included (a decode graph's kernels count at each replay).  No

@@ -206,6 +206,12 @@ int xl_engine_last_kernel_ms(const xl_engine* e, float* ms) {
     return XL_OK;
 }
 
+int xl_engine_last_load_s(const xl_engine* e, float* s) {
+    if (!e || !s) return bad("null argument");
+    *s = e->impl->last_load_s();
+    return XL_OK;
+}
+
 long long xl_kernel_launches(void) { return xl::launch_count(); }
 
 int xl_engine_set_option(xl_engine* e, const char* key, int value) {

@@ -3,15 +3,22 @@
 // tensor parallelism.  Mirrors the reference's InferenceEngine / Transformer
 // (src/inference.cu:18-151, src/transformer.cu:107-186) with status codes
 // instead of exit(1).
+#include <fcntl.h>
 #include <sys/stat.h>
+#include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <random>
 #include <string>
+#include <mutex>
+#include <thread>
 #include <utility>
+#include <vector>
 
 #include "engine.h"
 
@@ -20,16 +27,9 @@ namespace xl {
 namespace {
 thread_local std::string g_err;
 constexpr double kEps = 1e-6;  // RMSNorm eps, src/rmsnorm.cu:72,100
-constexpr size_t kStagingBytes = 64u << 20;
+constexpr size_t kLoadChunkBytes = 8u << 20;  // weight-file bytes per staging chunk of the loader
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
-
-struct PinnedBuf {
-    void* p = nullptr;
-    ~PinnedBuf() {
-        if (p) cudaFreeHost(p);
-    }
-};
 }  // namespace
 
 void set_error(const std::string& msg) { g_err = msg; }
@@ -299,60 +299,144 @@ Engine::~Engine() {
 // fails on a short file.  Rows [r0, r1) x columns [c0, c1) of a [rows][cols]
 // file go to dst with a destination pitch, through pinned staging.
 namespace {
+// The raw-fp32 weight tree (scripts/export_weights.py:13-25, one file per
+// tensor, [rows][cols] row-major) to device memory.  Each job copies rows
+// [r0, r1) and columns [c0, c1) of one file (a tensor-parallel shard is read
+// straight from its rows / columns) to dst with a row pitch, or, with
+// elem_pitch > 0, single elements of one row with that pitch (bias
+// interleave).  Jobs are cut into chunks of whole rows; worker threads each
+// pread chunks into two pinned staging buffers of their own and copy them to
+// the device on their own stream, so file reads, host-to-device copies and
+// the other workers overlap.
+struct LoadJob {
+    std::string rel;
+    size_t rows, cols, r0, r1, c0, c1;
+    void* dst;
+    size_t dpitch, elem_pitch;
+};
+
 struct Loader {
     std::string dir;
-    char* staging = nullptr;
-    cudaStream_t stream = nullptr;
+    std::vector<LoadJob> jobs;
     std::string err;
 
-    int copy(const std::string& rel, size_t rows, size_t cols, size_t r0, size_t r1, size_t c0, size_t c1, void* dst,
-             size_t dpitch_bytes, size_t elem_pitch_bytes = 0) {
-        const std::string path = dir + "/" + rel;
-        struct stat sb;
-        if (stat(path.c_str(), &sb) != 0) {
-            err = "cannot open weight file " + path;
-            return XL_ERR_IO;
-        }
-        if (static_cast<size_t>(sb.st_size) < rows * cols * 4) {
-            err = "weight file too short: " + path + " (" + std::to_string(sb.st_size) + " bytes, need " +
-                  std::to_string(rows * cols * 4) + ")";
-            return XL_ERR_IO;
-        }
-        FILE* f = std::fopen(path.c_str(), "rb");
-        if (!f) {
-            err = "cannot open weight file " + path;
-            return XL_ERR_IO;
-        }
-        const size_t row_bytes = cols * 4;
-        const size_t chunk_rows = std::max<size_t>(1, kStagingBytes / row_bytes);
-        int rc = XL_OK;
-        for (size_t r = r0; r < r1 && rc == XL_OK; r += chunk_rows) {
-            const size_t nr = std::min(chunk_rows, r1 - r);
-            if (std::fseek(f, static_cast<long>(r * row_bytes), SEEK_SET) != 0 ||
-                std::fread(staging, row_bytes, nr, f) != nr) {
-                err = "read failed: " + path;
-                rc = XL_ERR_IO;
-                break;
+    void copy(const std::string& rel, size_t rows, size_t cols, size_t r0, size_t r1, size_t c0, size_t c1, void* dst,
+              size_t dpitch_bytes, size_t elem_pitch_bytes = 0) {
+        jobs.push_back({rel, rows, cols, r0, r1, c0, c1, dst, dpitch_bytes, elem_pitch_bytes});
+    }
+
+    int run(int threads, int device) {
+        for (const LoadJob& j : jobs) {  // existence and size first, in job order
+            const std::string path = dir + "/" + j.rel;
+            struct stat sb;
+            if (stat(path.c_str(), &sb) != 0) {
+                err = "cannot open weight file " + path;
+                return XL_ERR_IO;
             }
-            char* d = static_cast<char*>(dst) + (r - r0) * dpitch_bytes;
-            const size_t width = elem_pitch_bytes ? 4 : (c1 - c0) * 4;
-            cudaError_t ce;
-            if (elem_pitch_bytes) {
-                // scatter single elements with a pitch (bias interleave); rows == 1
-                ce = cudaMemcpy2DAsync(d, elem_pitch_bytes, staging + c0 * 4, 4, width, c1 - c0,
-                                       cudaMemcpyHostToDevice, stream);
-            } else {
-                ce = cudaMemcpy2DAsync(d, dpitch_bytes, staging + c0 * 4, row_bytes, width, nr, cudaMemcpyHostToDevice,
-                                       stream);
-            }
-            if (ce == cudaSuccess) ce = cudaStreamSynchronize(stream);
-            if (ce != cudaSuccess) {
-                err = std::string("H2D copy failed for ") + path + ": " + cudaGetErrorString(ce);
-                rc = XL_ERR_CUDA;
+            if (static_cast<size_t>(sb.st_size) < j.rows * j.cols * 4) {
+                err = "weight file too short: " + path + " (" + std::to_string(sb.st_size) + " bytes, need " +
+                      std::to_string(j.rows * j.cols * 4) + ")";
+                return XL_ERR_IO;
             }
         }
-        std::fclose(f);
-        return rc;
+        struct Chunk {
+            int job;
+            size_t r, nr;
+        };
+        std::vector<Chunk> chunks;
+        for (size_t i = 0; i < jobs.size(); ++i) {
+            const size_t row_bytes = jobs[i].cols * 4;
+            const size_t per = std::max<size_t>(1, kLoadChunkBytes / row_bytes);
+            for (size_t r = jobs[i].r0; r < jobs[i].r1; r += per)
+                chunks.push_back({static_cast<int>(i), r, std::min(per, jobs[i].r1 - r)});
+        }
+        size_t max_chunk = 0;
+        for (const Chunk& c : chunks) max_chunk = std::max(max_chunk, c.nr * jobs[c.job].cols * 4);
+        std::atomic<size_t> next{0};
+        std::atomic<int> rc{XL_OK};
+        std::mutex mu;
+        auto fail = [&](int code, const std::string& msg) {
+            std::lock_guard<std::mutex> g(mu);
+            if (rc.load() == XL_OK) {
+                err = msg;
+                rc = code;
+            }
+        };
+        auto worker = [&]() {
+            if (cudaSetDevice(device) != cudaSuccess) return fail(XL_ERR_CUDA, "load: cudaSetDevice failed");
+            cudaStream_t s = nullptr;
+            cudaEvent_t ev[2] = {nullptr, nullptr};
+            void* buf[2] = {nullptr, nullptr};
+            std::vector<std::pair<int, int>> fds;  // (job's file index, fd), small per-thread cache
+            cudaError_t ce = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+            for (int b = 0; b < 2 && ce == cudaSuccess; ++b) {
+                ce = cudaHostAlloc(&buf[b], max_chunk, cudaHostAllocDefault);
+                if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&ev[b], cudaEventDisableTiming);
+            }
+            if (ce != cudaSuccess) fail(XL_ERR_CUDA, std::string("load: ") + cudaGetErrorString(ce));
+            int use = 0;
+            while (rc.load() == XL_OK) {
+                const size_t i = next.fetch_add(1);
+                if (i >= chunks.size()) break;
+                const Chunk& c = chunks[i];
+                const LoadJob& j = jobs[c.job];
+                const std::string path = dir + "/" + j.rel;
+                int fd = -1;
+                for (auto& kv : fds)
+                    if (kv.first == c.job) fd = kv.second;
+                if (fd < 0) {
+                    fd = open(path.c_str(), O_RDONLY);
+                    if (fd < 0) {
+                        fail(XL_ERR_IO, "cannot open weight file " + path);
+                        break;
+                    }
+                    fds.emplace_back(c.job, fd);
+                }
+                const int b = use++ & 1;
+                ce = cudaEventSynchronize(ev[b]);  // the copy that last used this buffer has finished
+                const size_t row_bytes = j.cols * 4, want = c.nr * row_bytes;
+                size_t got = 0;
+                while (ce == cudaSuccess && got < want) {
+                    const ssize_t k = pread(fd, static_cast<char*>(buf[b]) + got, want - got,
+                                            static_cast<off_t>(c.r * row_bytes + got));
+                    if (k <= 0) break;
+                    got += static_cast<size_t>(k);
+                }
+                if (ce == cudaSuccess && got != want) {
+                    fail(XL_ERR_IO, "read failed: " + path);
+                    break;
+                }
+                char* d = static_cast<char*>(j.dst) + (c.r - j.r0) * j.dpitch;
+                const char* src = static_cast<const char*>(buf[b]) + j.c0 * 4;
+                if (ce == cudaSuccess) {
+                    ce = j.elem_pitch ? cudaMemcpy2DAsync(d, j.elem_pitch, src, 4, 4, j.c1 - j.c0,
+                                                          cudaMemcpyHostToDevice, s)
+                                      : cudaMemcpy2DAsync(d, j.dpitch, src, row_bytes, (j.c1 - j.c0) * 4, c.nr,
+                                                          cudaMemcpyHostToDevice, s);
+                }
+                if (ce == cudaSuccess) ce = cudaEventRecord(ev[b], s);
+                if (ce != cudaSuccess) {
+                    fail(XL_ERR_CUDA, std::string("H2D copy failed for ") + path + ": " + cudaGetErrorString(ce));
+                    break;
+                }
+            }
+            if (s) {
+                ce = cudaStreamSynchronize(s);
+                if (ce != cudaSuccess) fail(XL_ERR_CUDA, std::string("load: ") + cudaGetErrorString(ce));
+                cudaStreamDestroy(s);
+            }
+            for (int b = 0; b < 2; ++b) {
+                if (ev[b]) cudaEventDestroy(ev[b]);
+                if (buf[b]) cudaFreeHost(buf[b]);
+            }
+            for (auto& kv : fds) close(kv.second);
+        };
+        const int n = std::max(1, std::min(threads, static_cast<int>(chunks.size())));
+        std::vector<std::thread> pool;
+        for (int t = 1; t < n; ++t) pool.emplace_back(worker);
+        worker();
+        for (auto& th : pool) th.join();
+        return rc.load();
     }
 };
 }  // namespace
@@ -363,41 +447,38 @@ int Engine::load(const char* dir) {
         set_error("load: null path");
         return XL_ERR_ARG;
     }
-    PinnedBuf pin;
-    XL_CUDA(cudaHostAlloc(&pin.p, kStagingBytes, cudaHostAllocDefault));
     Loader ld;
     ld.dir = dir;
-    ld.staging = static_cast<char*>(pin.p);
-    ld.stream = stream_;
     const size_t H = H_, Hl = Hl_, Fl = Fl_, F = F_;
     const size_t hq0 = static_cast<size_t>(rank_) * Hl, hq1 = hq0 + Hl;
     const size_t f0 = static_cast<size_t>(rank_) * Fl, f1 = f0 + Fl;
-    int rc = XL_OK;
-    auto chk = [&](int r) {
-        if (rc == XL_OK && r != XL_OK) rc = r;
-    };
     // Embedding (full table: the decode gather may need any row) and final norm.
-    chk(ld.copy("embedding/weight.bin", V_, H, 0, V_, 0, H, emb_, H * 4));
-    chk(ld.copy("norm/weight.bin", 1, H, 0, 1, 0, H, gnorm_, H * 4));
-    for (int l = 0; l < cfg_.layers && rc == XL_OK; ++l) {
+    ld.copy("embedding/weight.bin", V_, H, 0, V_, 0, H, emb_, H * 4);
+    ld.copy("norm/weight.bin", 1, H, 0, 1, 0, H, gnorm_, H * 4);
+    for (int l = 0; l < cfg_.layers; ++l) {
         const std::string b = "blocks/" + std::to_string(l) + "/";
         LayerWeights& L = layers_[l];
         const char* qkv_names[3] = {"attn/Q", "attn/K", "attn/V"};
         for (int i = 0; i < 3; ++i) {
-            chk(ld.copy(b + qkv_names[i] + "/weight.bin", H, H, hq0, hq1, 0, H, L.wqkv + i * Hl * H, H * 4));
-            chk(ld.copy(b + qkv_names[i] + "/bias.bin", 1, H, 0, 1, hq0, hq1, L.bqkv + i * Hl, Hl * 4));
+            ld.copy(b + qkv_names[i] + "/weight.bin", H, H, hq0, hq1, 0, H, L.wqkv + i * Hl * H, H * 4);
+            ld.copy(b + qkv_names[i] + "/bias.bin", 1, H, 0, 1, hq0, hq1, L.bqkv + i * Hl, Hl * 4);
         }
-        chk(ld.copy(b + "attn/W/weight.bin", H, H, 0, H, hq0, hq1, L.wo, Hl * 4));
-        if (rank_ == 0) chk(ld.copy(b + "attn/W/bias.bin", 1, H, 0, 1, 0, H, L.bo, H * 4));
-        chk(ld.copy(b + "ffn/W1/weight.bin", F, H, f0, f1, 0, H, L.w13, 2 * H * 4));
-        chk(ld.copy(b + "ffn/V/weight.bin", F, H, f0, f1, 0, H, L.w13 + H, 2 * H * 4));
-        chk(ld.copy(b + "ffn/W1/bias.bin", 1, F, 0, 1, f0, f1, L.b13, 0, 8));
-        chk(ld.copy(b + "ffn/V/bias.bin", 1, F, 0, 1, f0, f1, L.b13 + 1, 0, 8));
-        chk(ld.copy(b + "ffn/W2/weight.bin", H, F, 0, H, f0, f1, L.w2, Fl * 4));
-        if (rank_ == 0) chk(ld.copy(b + "ffn/W2/bias.bin", 1, H, 0, 1, 0, H, L.b2, H * 4));
-        chk(ld.copy(b + "norm1/weight.bin", 1, H, 0, 1, 0, H, L.g1, H * 4));
-        chk(ld.copy(b + "norm2/weight.bin", 1, H, 0, 1, 0, H, L.g2, H * 4));
+        ld.copy(b + "attn/W/weight.bin", H, H, 0, H, hq0, hq1, L.wo, Hl * 4);
+        if (rank_ == 0) ld.copy(b + "attn/W/bias.bin", 1, H, 0, 1, 0, H, L.bo, H * 4);
+        ld.copy(b + "ffn/W1/weight.bin", F, H, f0, f1, 0, H, L.w13, 2 * H * 4);
+        ld.copy(b + "ffn/V/weight.bin", F, H, f0, f1, 0, H, L.w13 + H, 2 * H * 4);
+        ld.copy(b + "ffn/W1/bias.bin", 1, F, 0, 1, f0, f1, L.b13, 0, 8);
+        ld.copy(b + "ffn/V/bias.bin", 1, F, 0, 1, f0, f1, L.b13 + 1, 0, 8);
+        ld.copy(b + "ffn/W2/weight.bin", H, F, 0, H, f0, f1, L.w2, Fl * 4);
+        if (rank_ == 0) ld.copy(b + "ffn/W2/bias.bin", 1, H, 0, 1, 0, H, L.b2, H * 4);
+        ld.copy(b + "norm1/weight.bin", 1, H, 0, 1, 0, H, L.g1, H * 4);
+        ld.copy(b + "norm2/weight.bin", 1, H, 0, 1, 0, H, L.g2, H * 4);
     }
+    // The device is idle while loading: nothing else may use the destination buffers.
+    XL_CUDA(cudaStreamSynchronize(stream_));
+    const auto t0 = std::chrono::steady_clock::now();
+    int rc = ld.run(load_threads_, device_);
+    last_load_s_ = std::chrono::duration<float>(std::chrono::steady_clock::now() - t0).count();
     if (rc != XL_OK) {
         set_error(ld.err);
         return rc;
@@ -1057,6 +1138,14 @@ int Engine::set_option(const char* key, int value) {
         }
         inflight_ = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
+    }
+    if (k == "load_threads") {
+        if (value < 1 || value > 64) {
+            set_error("load_threads must be in [1, 64]");
+            return XL_ERR_ARG;
+        }
+        load_threads_ = value;
+        return XL_OK;
     }
     if (k == "tma_evict_first") {
         if (value != 0 && value != 1) {

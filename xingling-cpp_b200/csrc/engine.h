@@ -63,6 +63,7 @@ class Engine {
     int ctx_len() const { return n_; }
     float last_device_ms() const { return last_ms_; }
     float last_kernel_ms() const { return last_kernel_ms_; }
+    float last_load_s() const { return last_load_s_; }
     int vocab_begin() const { return v0_; }
     int vocab_count() const { return vl_; }
 
@@ -158,6 +159,8 @@ class Engine {
     float *ap_ = nullptr, *ap_lo_ = nullptr;
     TcOperands tc_attn_s_{}, tc_attn_pv_{};
     long long decode_graph_kernels_ = 0;  // kernels recorded in the decode graph
+    int load_threads_ = 4;      // weight loader worker threads
+    float last_load_s_ = 0.0f;  // wall time of the last load's file reads and copies
     int inflight_ = 3;  // persistent decode: weight boxes requested but not landed, per SM
     int tma_evict_first_ = 1;  // persistent decode: weight boxes loaded with an L2 evict-first policy
     bool loaded_ = false;

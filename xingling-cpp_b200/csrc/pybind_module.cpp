@@ -25,9 +25,7 @@ namespace {
         case XL_ERR_ARG:
         case XL_ERR_TOKEN:
             throw py::value_error(msg);
-        case XL_ERR_IO:
-            throw std::ios_base::failure(msg);
-        default:
+        default:  // XL_ERR_IO too: the reference's Tensor::load throws std::runtime_error (src/tensor.cu:116,121)
             throw std::runtime_error(msg.empty() ? ("xl status " + std::to_string(rc)) : msg);
     }
 }
@@ -164,6 +162,12 @@ class InferenceEngine {
         float ms = 0.0f;
         check(xl_engine_last_kernel_ms(e_, &ms));
         return ms;
+    }
+
+    float last_load_s() const {
+        float sec = 0.0f;
+        check(xl_engine_last_load_s(e_, &sec));
+        return sec;
     }
 
     void set_option(const std::string& key, int value) {
@@ -314,6 +318,7 @@ PYBIND11_MODULE(llm_cpp_engine, m) {
         .def("ctx_len", &InferenceEngine::ctx_len)
         .def("last_device_ms", &InferenceEngine::last_device_ms)
         .def("last_kernel_ms", &InferenceEngine::last_kernel_ms)
+        .def("last_load_s", &InferenceEngine::last_load_s)
         .def("set_option", &InferenceEngine::set_option, py::arg("key"), py::arg("value"))
         .def("phase_trace", &InferenceEngine::phase_trace, py::arg("n"))
         .def("profile_lm_head", &InferenceEngine::profile_lm_head, py::arg("iters") = 20)
