@@ -90,6 +90,15 @@ XL_API int xl_engine_load(xl_engine* e, const char* dir);
 XL_API int xl_engine_prefill(xl_engine* e, const int* ids, int n, float temperature, float top_p,
                              float repetition_penalty, int* token_out);
 
+/* Prefill continuation (no reference counterpart: the reference restarts the
+ * cache on every prompt, src/attn.cu:350,360): the n ids extend the cached
+ * sequence at positions ctx_len .. ctx_len + n - 1, attending to every cached
+ * position; the repetition set is kept.  Samples the next id like
+ * xl_engine_prefill.  XL_ERR_STATE before any prefill, XL_ERR_CTX past the
+ * context. */
+XL_API int xl_engine_extend(xl_engine* e, const int* ids, int n, float temperature, float top_p,
+                            float repetition_penalty, int* token_out);
+
 /* InferenceEngine::next_token(int) (src/inference.cu:138-151): one decode
  * step at position ctx_len (XL_ERR_CTX when the cache is full). */
 XL_API int xl_engine_decode(xl_engine* e, int token, float temperature, float top_p, float repetition_penalty,

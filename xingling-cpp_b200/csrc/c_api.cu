@@ -154,6 +154,13 @@ int xl_engine_decode(xl_engine* e, int token, float temperature, float top_p, fl
     return e->impl->decode(token, temperature, top_p, repetition_penalty, token_out);
 }
 
+int xl_engine_extend(xl_engine* e, const int* ids, int n, float temperature, float top_p, float repetition_penalty,
+                     int* token_out) {
+    xl::clear_error();
+    if (!e || !token_out) return bad("null argument");
+    return e->impl->prefill(ids, n, temperature, top_p, repetition_penalty, token_out, true);
+}
+
 int xl_engine_generate(xl_engine* e, int token, int n, float temperature, float top_p, float repetition_penalty,
                        int stop_id, int* tokens_out, int* n_out) {
     xl::clear_error();

@@ -859,7 +859,7 @@ int Engine::finish_step(int* token_out) {
 }
 
 // InferenceEngine::next_token(vector), src/inference.cu:116-136.
-int Engine::prefill(const int* ids, int n, float temperature, float top_p, float rp, int* token_out) {
+int Engine::prefill(const int* ids, int n, float temperature, float top_p, float rp, int* token_out, bool append) {
     XL_CUDA(cudaSetDevice(device_));
     if (!loaded_) {
         set_error("prefill before load");
@@ -869,8 +869,14 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
         set_error("prefill: empty prompt");
         return XL_ERR_ARG;
     }
-    if (n > T_) {
-        set_error("Input sequence length exceeds max_seq_len (" + std::to_string(n) + " > " + std::to_string(T_) + ")");
+    if (append && !has_seq_) {
+        set_error("extend before any prefill: the KV cache is empty");
+        return XL_ERR_STATE;
+    }
+    const int p0 = append ? n_ : 0;  // position of the first new id
+    if (p0 + n > T_) {
+        set_error("Input sequence length exceeds max_seq_len (" + std::to_string(p0 + n) + " > " + std::to_string(T_) +
+                  ")");
         return XL_ERR_CTX;
     }
     for (int i = 0; i < n; ++i) {
@@ -891,12 +897,13 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
     DevState* hs = reinterpret_cast<DevState*>(h_in_);
     std::memset(hs, 0, sizeof(DevState));
     hs->in = in;
-    hs->pos = n;
+    hs->pos = p0 + n;
     cudaStream_t s = stream_;
     XL_CUDA(cudaMemcpyAsync(pids_, h_ids_, sizeof(int) * n, cudaMemcpyHostToDevice, s));
-    // in + pos: the first 36 bytes of DevState
+    // in + pos: the first bytes of DevState
     XL_CUDA(cudaMemcpyAsync(st_, hs, offsetof(DevState, pos) + sizeof(int), cudaMemcpyHostToDevice, s));
-    XL_CUDA(cudaMemsetAsync(rep_flags_, 0, vl_, s));
+    // A new prompt clears the repetition set (src/inference.cu:116-136); an appended one keeps it.
+    if (!append) XL_CUDA(cudaMemsetAsync(rep_flags_, 0, vl_, s));
     XL_CUDA(cudaEventRecord(ev0_, s));
 
     const size_t H = H_;
@@ -907,15 +914,15 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
         XL_CUDA(launch_rmsnorm_rows(px_, L.g1, pxn_, pxn_lo_, n, H_, s));
         rc = prefill_linear(kGemvPlain, L.tc_qkv, pxn_, L.wqkv, L.bqkv, pqkv_, nullptr, n, 3 * Hl_, H_, s);
         if (rc != XL_OK) break;
-        XL_CUDA(launch_rope_kv_prefill(pqkv_, rope_, L.kc, L.vc, n, heads_l_, T_, s));
-        if (prefill_attn_ == 0 && T_ % 32 == 0) {
+        XL_CUDA(launch_rope_kv_prefill(pqkv_, rope_, L.kc, L.vc, n, heads_l_, T_, s, p0));
+        if (prefill_attn_ == 0 && T_ % 32 == 0 && p0 == 0) {
             XL_CUDA(launch_attn_operands(pqkv_, L.kc, L.vc, aq_, aq_lo_, ak_, ak_lo_, avt_, avt_lo_, n, heads_l_, T_,
                                          s));
             XL_CUDA(launch_attn_scores_tc(tc_attn_s_, ap_, n, heads_l_, T_, &st_->err, s));
             XL_CUDA(launch_attn_softmax(ap_, ap_lo_, n, heads_l_, T_, s));
             XL_CUDA(launch_attn_pv_tc(tc_attn_pv_, patt_, patt_lo_, n, heads_l_, T_, &st_->err, s));
         } else {
-            XL_CUDA(launch_attn_prefill(pqkv_, L.kc, L.vc, patt_, patt_lo_, n, heads_l_, T_, s));
+            XL_CUDA(launch_attn_prefill(pqkv_, L.kc, L.vc, patt_, patt_lo_, n, heads_l_, T_, s, p0));
         }
         if (tp_ == 1) {
             rc = prefill_linear(kGemvResidual, L.tc_wo, patt_, L.wo, L.bo, px_, nullptr, n, H_, Hl_, s);
@@ -946,7 +953,7 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
     if (rc != XL_OK) return rc;
     rc = finish_step(token_out);
     if (rc != XL_OK) return rc;
-    n_ = n;
+    n_ = p0 + n;
     has_seq_ = true;
     return XL_OK;
 }

@@ -46,7 +46,9 @@ class Engine {
     ~Engine();
 
     int load(const char* dir);
-    int prefill(const int* ids, int n, float temperature, float top_p, float rp, int* token_out);
+    // append: the ids continue the cached sequence (positions ctx_len ..), and
+    // the repetition set is kept; otherwise the cache and the set restart.
+    int prefill(const int* ids, int n, float temperature, float top_p, float rp, int* token_out, bool append = false);
     int decode(int token, float temperature, float top_p, float rp, int* token_out);
     // Up to n decode steps fed on the device (each step's input is the previous
     // step's id), stopping after stop_id (>= 0) or a full cache; the ids go to

@@ -164,14 +164,17 @@ __global__ void __launch_bounds__(256) sgemm_tn_kernel(const float* __restrict__
     }
 }
 
-// One (row, head): rotate q in place and k, copy k / v into the head-major cache.
+// One (row, head): rotate q in place and k, copy k / v into the head-major
+// cache.  Row t of qkv is position p0 + t (p0 > 0: a prompt appended to a
+// cached sequence).
 __global__ void __launch_bounds__(32) rope_kv_prefill_kernel(float* __restrict__ qkv, const float2* __restrict__ rope,
                                                              float* __restrict__ kc, float* __restrict__ vc, int heads,
-                                                             int max_ctx) {
+                                                             int max_ctx, int p0) {
     const int t = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
     const int HL = heads * kHeadDim;
     float* row = qkv + static_cast<size_t>(t) * 3 * HL;
-    const float2 cs = rope[t * kHalfHead + j];
+    const int pos = p0 + t;
+    const float2 cs = rope[pos * kHalfHead + j];
     float* q = row + h * kHeadDim;
     const float qa = q[j], qb = q[j + kHalfHead];
     q[j] = qa * cs.x + qb * cs.y;
@@ -179,8 +182,8 @@ __global__ void __launch_bounds__(32) rope_kv_prefill_kernel(float* __restrict__
     const float* k = row + HL + h * kHeadDim;
     const float* v = row + 2 * HL + h * kHeadDim;
     const float ka = k[j], kb = k[j + kHalfHead];
-    float* kd = kc + (static_cast<size_t>(h) * max_ctx + t) * kHeadDim;
-    float* vd = vc + (static_cast<size_t>(h) * max_ctx + t) * kHeadDim;
+    float* kd = kc + (static_cast<size_t>(h) * max_ctx + pos) * kHeadDim;
+    float* vd = vc + (static_cast<size_t>(h) * max_ctx + pos) * kHeadDim;
     kd[j] = ka * cs.x + kb * cs.y;
     kd[j + kHalfHead] = -ka * cs.y + kb * cs.x;
     vd[j] = v[j];
@@ -236,13 +239,16 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(float* __restrict__ S
 }
 
 // Causal attention for one (64-query tile, head); 256 threads as 16 x 16,
-// each owning a 4 x 4 block of the score tile and of the output tile.
+// each owning a 4 x 4 block of the score tile and of the output tile.  Query
+// row r is position p0 + r and attends to the cached positions 0 .. p0 + r
+// (p0 > 0: a prompt appended to a cached sequence).
 constexpr int kAT = 64;
 constexpr int kAP = kAT + 4;
 
 __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
                                                            const float* __restrict__ vc, float* __restrict__ out,
-                                                           float* __restrict__ out_lo, int N, int heads, int max_ctx) {
+                                                           float* __restrict__ out_lo, int N, int heads, int max_ctx,
+                                                           int p0) {
     extern __shared__ __align__(16) float smem[];
     float* Qt = smem;              // [64 dims][kAP] (q scaled by 1/8, transposed)
     float* Kt = Qt + kAT * kAP;    // [64 dims][kAP] (transposed)
@@ -269,14 +275,15 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
 #pragma unroll
         for (int j = 0; j < 4; ++j) o[i][j] = 0.0f;
     }
-    const int last_kt = qt;  // causal: key tiles 0..qt
+    const int nk = p0 + N;  // keys: cached positions 0 .. p0 + N - 1
+    const int last_kt = (p0 + min(q0 + kAT, N) - 1) / kAT;  // causal: through the tile's last query position
     for (int kt = 0; kt <= last_kt; ++kt) {
         const int k0 = kt * kAT;
         __syncthreads();
         for (int e = tid; e < kAT * kHeadDim / 4; e += 256) {
             const int r = e >> 4, d4 = (e & 15) * 4;
             const int t = k0 + r;
-            const bool ok = t < N;
+            const bool ok = t < nk;
             const float4 kv = ok ? *reinterpret_cast<const float4*>(kh + static_cast<size_t>(t) * kHeadDim + d4)
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
             const float4 vv = ok ? *reinterpret_cast<const float4*>(vh + static_cast<size_t>(t) * kHeadDim + d4)
@@ -307,12 +314,12 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float* __restri
         // causal / length mask, online softmax per query row
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const int qi = q0 + ty * 4 + i;
+            const int qi = p0 + q0 + ty * 4 + i;  // query position
             float mx = -INFINITY;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int kj = k0 + tx * 4 + j;
-                if (kj > qi || kj >= N) s[i][j] = -INFINITY;
+                if (kj > qi || kj >= nk) s[i][j] = -INFINITY;
                 mx = fmaxf(mx, s[i][j]);
             }
 #pragma unroll
@@ -418,22 +425,22 @@ cudaError_t launch_add_rows(float* x, const float* d, int n, cudaStream_t s) {
 }
 
 cudaError_t launch_rope_kv_prefill(float* qkv, const float2* rope, float* kc, float* vc, int n, int heads,
-                                   int max_ctx, cudaStream_t s) {
-    if (n <= 0 || n > max_ctx) return cudaErrorInvalidValue;
+                                   int max_ctx, cudaStream_t s, int p0) {
+    if (n <= 0 || p0 < 0 || p0 + n > max_ctx) return cudaErrorInvalidValue;
     count_launch();
-    rope_kv_prefill_kernel<<<dim3(n, heads), 32, 0, s>>>(qkv, rope, kc, vc, heads, max_ctx);
+    rope_kv_prefill_kernel<<<dim3(n, heads), 32, 0, s>>>(qkv, rope, kc, vc, heads, max_ctx, p0);
     return cudaGetLastError();
 }
 
 cudaError_t launch_attn_prefill(const float* qkv, const float* kc, const float* vc, float* out, float* out_lo, int n,
-                                int heads, int max_ctx, cudaStream_t s) {
-    if (n <= 0 || n > max_ctx) return cudaErrorInvalidValue;
+                                int heads, int max_ctx, cudaStream_t s, int p0) {
+    if (n <= 0 || p0 < 0 || p0 + n > max_ctx) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kAttnPrefillSmem));
     if (e != cudaSuccess) return e;
     count_launch();
     attn_prefill_kernel<<<dim3((n + kAT - 1) / kAT, heads), 256, kAttnPrefillSmem, s>>>(qkv, kc, vc, out, out_lo, n,
-                                                                                        heads, max_ctx);
+                                                                                        heads, max_ctx, p0);
     return cudaGetLastError();
 }
 

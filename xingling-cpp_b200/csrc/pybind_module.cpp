@@ -103,6 +103,16 @@ class InferenceEngine {
         return tok;
     }
 
+    int extend(const std::vector<int>& ids, float temperature, float top_p, float rp) {
+        int tok = -1, rc;
+        {
+            py::gil_scoped_release nogil;
+            rc = xl_engine_extend(e_, ids.data(), static_cast<int>(ids.size()), temperature, top_p, rp, &tok);
+        }
+        check(rc);
+        return tok;
+    }
+
     int next_token_decode(int token, float temperature, float top_p, float rp) {
         int tok = -1, rc;
         {
@@ -307,6 +317,9 @@ PYBIND11_MODULE(llm_cpp_engine, m) {
              py::arg("top_p") = 0.9f, py::arg("repetition_penalty") = 1.1f)
         .def("next_token", &InferenceEngine::next_token_decode, py::arg("token"), py::arg("temperature") = 0.7f,
              py::arg("top_p") = 0.9f, py::arg("repetition_penalty") = 1.1f)
+        .def("extend", &InferenceEngine::extend, py::arg("input_ids"), py::arg("temperature") = 0.7f,
+             py::arg("top_p") = 0.9f, py::arg("repetition_penalty") = 1.1f,
+             "prefill continuation: the ids extend the cached sequence (the repetition set is kept)")
         .def("generate", &InferenceEngine::generate, py::arg("token"), py::arg("n"), py::arg("temperature") = 0.7f,
              py::arg("top_p") = 0.9f, py::arg("repetition_penalty") = 1.1f, py::arg("stop_id") = -1,
              "up to n decode steps fed on the device; stops after stop_id (returned) or a full cache")

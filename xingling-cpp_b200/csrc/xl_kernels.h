@@ -297,11 +297,12 @@ cudaError_t launch_rmsnorm_rows(const float* x, const float* gamma, float* out, 
 // Y[N][M] (+)= X[N][K] . W[M][K]^T + b; mode as GemvMode (Plain / SwiGLU / Residual).
 cudaError_t launch_linear_prefill(int mode, const float* X, const float* W, const float* b, float* Y, int n,
                                   int m, int k, cudaStream_t s);
+// Rows t < n of qkv are positions p0 + t (p0 > 0: a prompt appended to a cached sequence).
 cudaError_t launch_rope_kv_prefill(float* qkv, const float2* rope, float* kc, float* vc, int n, int heads,
-                                   int max_ctx, cudaStream_t s);
+                                   int max_ctx, cudaStream_t s, int p0 = 0);
 // x[i] += d[i] for i < n (tensor-parallel residual add after an all-reduce).
 cudaError_t launch_add_rows(float* x, const float* d, int n, cudaStream_t s);
 cudaError_t launch_attn_prefill(const float* qkv, const float* kc, const float* vc, float* out, float* out_lo, int n,
-                                int heads, int max_ctx, cudaStream_t s);
+                                int heads, int max_ctx, cudaStream_t s, int p0 = 0);
 
 }  // namespace xl
