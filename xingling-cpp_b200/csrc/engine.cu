@@ -914,14 +914,14 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
         XL_CUDA(launch_rmsnorm_rows(px_, L.g1, pxn_, pxn_lo_, n, H_, s));
         rc = prefill_linear(kGemvPlain, L.tc_qkv, pxn_, L.wqkv, L.bqkv, pqkv_, nullptr, n, 3 * Hl_, H_, s);
         if (rc != XL_OK) break;
-        XL_CUDA(launch_rope_kv_prefill(pqkv_, rope_, L.kc, L.vc, n, heads_l_, T_, s, p0));
         if (prefill_attn_ == 0 && T_ % 32 == 0 && p0 == 0) {
-            XL_CUDA(launch_attn_operands(pqkv_, L.kc, L.vc, aq_, aq_lo_, ak_, ak_lo_, avt_, avt_lo_, n, heads_l_, T_,
-                                         s));
+            XL_CUDA(launch_attn_prep(pqkv_, rope_, L.kc, L.vc, aq_, aq_lo_, ak_, ak_lo_, avt_, avt_lo_, n, heads_l_, T_,
+                                     s));
             XL_CUDA(launch_attn_scores_tc(tc_attn_s_, ap_, n, heads_l_, T_, &st_->err, s));
             XL_CUDA(launch_attn_softmax(ap_, ap_lo_, n, heads_l_, T_, s));
             XL_CUDA(launch_attn_pv_tc(tc_attn_pv_, patt_, patt_lo_, n, heads_l_, T_, &st_->err, s));
         } else {
+            XL_CUDA(launch_rope_kv_prefill(pqkv_, rope_, L.kc, L.vc, n, heads_l_, T_, s, p0));
             XL_CUDA(launch_attn_prefill(pqkv_, L.kc, L.vc, patt_, patt_lo_, n, heads_l_, T_, s, p0));
         }
         if (tp_ == 1) {

@@ -278,31 +278,64 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
 }
 
-// Sum of the split-K slices in slice order, then the mode's epilogue.
+// Sum of the split-K slices in slice order, then the mode's epilogue.  Plain
+// and residual rows of a multiple of 4 go 4 at a time (float4), indices in 32
+// bits (the launcher checks the sizes).
 template <int MODE>
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, int slices,
                                                             const float* __restrict__ bias, float* __restrict__ C,
                                                             float* __restrict__ C_lo, int N, int M) {
-    const size_t total = static_cast<size_t>(N) * (MODE == kGemvSwiGLU ? M / 2 : M);
-    const size_t plane = static_cast<size_t>(N) * M;
-    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        if (MODE == kGemvSwiGLU) {
-            const size_t n = i / (M / 2), j = i % (M / 2);
-            const size_t ia = n * M + 2 * j;
+    const int plane = N * M;
+    const int stride = gridDim.x * blockDim.x;
+    if (MODE == kGemvSwiGLU) {
+        const int half = M / 2, total = N * half;
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+            const int n = i / half, j = i - n * half;
+            const int ia = n * M + 2 * j;
             float a = 0.0f, c = 0.0f;
             for (int z = 0; z < slices; ++z) {
-                a += ws[z * plane + ia];
-                c += ws[z * plane + ia + 1];
+                const float2 v = *reinterpret_cast<const float2*>(ws + z * plane + ia);
+                a += v.x;
+                c += v.y;
             }
             const float h = silu(a + bias[2 * j]) * (c + bias[2 * j + 1]);
             C[i] = h;
             C_lo[i] = tf32_lo(h);
-        } else {
-            const int m = static_cast<int>(i % M);
+        }
+    } else if ((M & 3) == 0) {
+        const int total4 = plane >> 2, M4 = M >> 2;
+        const float4* w4 = reinterpret_cast<const float4*>(ws);
+        float4* c4 = reinterpret_cast<float4*>(C);
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += stride) {
+            float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int z = 0; z < slices; ++z) {
+                const float4 v = w4[z * total4 + i];
+                a.x += v.x;
+                a.y += v.y;
+                a.z += v.z;
+                a.w += v.w;
+            }
+            if (bias) {
+                const float4 b = reinterpret_cast<const float4*>(bias)[i % M4];
+                a.x += b.x;
+                a.y += b.y;
+                a.z += b.z;
+                a.w += b.w;
+            }
+            if (MODE == kGemvResidual) {
+                const float4 y = c4[i];
+                a.x += y.x;
+                a.y += y.y;
+                a.z += y.z;
+                a.w += y.w;
+            }
+            c4[i] = a;
+        }
+    } else {
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < plane; i += stride) {
             float a = 0.0f;
             for (int z = 0; z < slices; ++z) a += ws[z * plane + i];
-            const float v = a + (bias ? bias[m] : 0.0f);
+            const float v = a + (bias ? bias[i % M] : 0.0f);
             if (MODE == kGemvResidual) C[i] += v;
             else C[i] = v;
         }
@@ -394,6 +427,8 @@ cudaError_t launch_gemm_tc(int mode, const TcOperands& o, const float* bias, flo
     }
     dim3 grid((m + kBM - 1) / kBM, (n + kBN - 1) / kBN, slices);
     cudaError_t e;
+    if (slices > 1 && static_cast<size_t>(slices) * n * m >= (size_t{1} << 31)) slices = 1;  // 32-bit reduce indices
+    grid.z = slices;
     if (slices > 1) {
         e = launch_tc<kGemmPartial>(grid, o, nullptr, ws, nullptr, m, n, k, err, s);
         if (e != cudaSuccess) return e;

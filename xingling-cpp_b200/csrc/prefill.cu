@@ -190,28 +190,62 @@ __global__ void __launch_bounds__(32) rope_kv_prefill_kernel(float* __restrict__
     vd[j + kHalfHead] = v[j + kHalfHead];
 }
 
-// Operands of the tensor-core attention for one (row t, head h), after
-// rope_kv_prefill: q/8 (the exact 1/sqrt(64) scale) into q8[t][h*64 + d], the
-// rotated k into kq[h][t][d] and v transposed into vt[h*64 + d][t], each with
-// its tf32 lo half for the 3xTF32 products.
-__global__ void __launch_bounds__(64) attn_operands_kernel(const float* __restrict__ qkv, const float* __restrict__ kc,
-                                                           const float* __restrict__ vc, float* __restrict__ q8,
-                                                           float* __restrict__ q8_lo, float* __restrict__ kq,
-                                                           float* __restrict__ kq_lo, float* __restrict__ vt,
-                                                           float* __restrict__ vt_lo, int heads, int max_ctx) {
-    const int t = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+// RoPE, KV append and the operands of the tensor-core attention for a tile of
+// 32 rows of one head (prompts that start at position 0): rotates q and k with
+// the angle table as rope_kv_prefill does, writes k and v into the
+// head-major cache, q/8 (the exact 1/sqrt(64) scale) into q8[t][h*64 + d],
+// the rotated k into kq[h][t][d] and v transposed into vt[h*64 + d][t]
+// (through shared memory, so that every store is a contiguous row), each
+// operand with its tf32 lo half for the 3xTF32 products.
+constexpr int kPrepRows = 32;
+__global__ void __launch_bounds__(256) attn_prep_kernel(const float* __restrict__ qkv, const float2* __restrict__ rope,
+                                                        float* __restrict__ kc, float* __restrict__ vc,
+                                                        float* __restrict__ q8, float* __restrict__ q8_lo,
+                                                        float* __restrict__ kq, float* __restrict__ kq_lo,
+                                                        float* __restrict__ vt, float* __restrict__ vt_lo, int n,
+                                                        int heads, int max_ctx) {
+    __shared__ float vs[kHeadDim][kPrepRows + 1];
+    const int t0 = blockIdx.x * kPrepRows, h = blockIdx.y;
     const int HL = heads * kHeadDim;
-    const float q = qkv[static_cast<size_t>(t) * 3 * HL + h * kHeadDim + d] * 0.125f;
-    const size_t qi = static_cast<size_t>(t) * HL + h * kHeadDim + d;
-    q8[qi] = q;
-    q8_lo[qi] = lo19(q);
-    const size_t ci = (static_cast<size_t>(h) * max_ctx + t) * kHeadDim + d;
-    const float k = kc[ci], v = vc[ci];
-    kq[ci] = k;
-    kq_lo[ci] = lo19(k);
-    const size_t vi = (static_cast<size_t>(h) * kHeadDim + d) * max_ctx + t;
-    vt[vi] = v;
-    vt_lo[vi] = lo19(v);
+    for (int e = threadIdx.x; e < kPrepRows * kHalfHead; e += blockDim.x) {
+        const int r = e >> 5, j = e & 31;  // a warp covers the 32 pairs (j, j + 32) of one row
+        const int t = t0 + r;
+        if (t >= n) continue;
+        const float* row = qkv + static_cast<size_t>(t) * 3 * HL + h * kHeadDim;
+        const float2 cs = rope[t * kHalfHead + j];
+        const float qa = row[j], qb = row[j + kHalfHead];
+        const float ka = row[HL + j], kb = row[HL + j + kHalfHead];
+        const float va = row[2 * HL + j], vb = row[2 * HL + j + kHalfHead];
+        const float qr0 = qa * cs.x + qb * cs.y, qr1 = -qa * cs.y + qb * cs.x;
+        const float q0 = qr0 * 0.125f, q1 = qr1 * 0.125f;
+        const float k0 = ka * cs.x + kb * cs.y, k1 = -ka * cs.y + kb * cs.x;
+        const size_t qi = static_cast<size_t>(t) * HL + h * kHeadDim + j;
+        q8[qi] = q0;
+        q8[qi + kHalfHead] = q1;
+        q8_lo[qi] = lo19(q0);
+        q8_lo[qi + kHalfHead] = lo19(q1);
+        const size_t ci = (static_cast<size_t>(h) * max_ctx + t) * kHeadDim + j;
+        kc[ci] = k0;
+        kc[ci + kHalfHead] = k1;
+        vc[ci] = va;
+        vc[ci + kHalfHead] = vb;
+        kq[ci] = k0;
+        kq[ci + kHalfHead] = k1;
+        kq_lo[ci] = lo19(k0);
+        kq_lo[ci + kHalfHead] = lo19(k1);
+        vs[j][r] = va;
+        vs[j + kHalfHead][r] = vb;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < kHeadDim * kPrepRows; e += blockDim.x) {
+        const int d = e >> 5, r = e & 31;  // a warp stores 32 consecutive positions of one dim
+        const int t = t0 + r;
+        if (t >= n) continue;
+        const float v = vs[d][r];
+        const size_t vi = (static_cast<size_t>(h) * kHeadDim + d) * max_ctx + t;
+        vt[vi] = v;
+        vt_lo[vi] = lo19(v);
+    }
 }
 
 // Causal softmax of one score row per warp: P[h][q][k] = exp(s - max) / sum for
@@ -444,13 +478,13 @@ cudaError_t launch_attn_prefill(const float* qkv, const float* kc, const float* 
     return cudaGetLastError();
 }
 
-cudaError_t launch_attn_operands(const float* qkv, const float* kc, const float* vc, float* q8, float* q8_lo,
-                                 float* kq, float* kq_lo, float* vt, float* vt_lo, int n, int heads, int max_ctx,
-                                 cudaStream_t s) {
+cudaError_t launch_attn_prep(const float* qkv, const float2* rope, float* kc, float* vc, float* q8, float* q8_lo,
+                             float* kq, float* kq_lo, float* vt, float* vt_lo, int n, int heads, int max_ctx,
+                             cudaStream_t s) {
     if (n <= 0 || n > max_ctx) return cudaErrorInvalidValue;
     count_launch();
-    attn_operands_kernel<<<dim3(n, heads), kHeadDim, 0, s>>>(qkv, kc, vc, q8, q8_lo, kq, kq_lo, vt, vt_lo, heads,
-                                                             max_ctx);
+    attn_prep_kernel<<<dim3((n + kPrepRows - 1) / kPrepRows, heads), 256, 0, s>>>(qkv, rope, kc, vc, q8, q8_lo, kq,
+                                                                                  kq_lo, vt, vt_lo, n, heads, max_ctx);
     return cudaGetLastError();
 }
 

@@ -260,11 +260,12 @@ cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int col
 // C[N][M] (+)= X[N][K] . W[M][K]^T + b with the 3xTF32 split; SwiGLU writes C and C_lo as [N][M/2].
 // With a workspace (ws, ws_floats) and fewer output tiles than SMs, K is split
 // into slices whose partial sums are added in slice order by a second kernel.
-// Tensor-core prefill attention, around the two GEMMs below: the operands
-// (after launch_rope_kv_prefill) and the causal row softmax of S in place.
-cudaError_t launch_attn_operands(const float* qkv, const float* kc, const float* vc, float* q8, float* q8_lo,
-                                 float* kq, float* kq_lo, float* vt, float* vt_lo, int n, int heads, int max_ctx,
-                                 cudaStream_t s);
+// Tensor-core prefill attention, around the two GEMMs below: RoPE + KV append
+// + the operands (a prompt starting at position 0), and the causal row softmax
+// of S in place.
+cudaError_t launch_attn_prep(const float* qkv, const float2* rope, float* kc, float* vc, float* q8, float* q8_lo,
+                             float* kq, float* kq_lo, float* vt, float* vt_lo, int n, int heads, int max_ctx,
+                             cudaStream_t s);
 cudaError_t launch_attn_softmax(float* S, float* P_lo, int n, int heads, int max_ctx, cudaStream_t s);
 // Prefill attention on tcgen05 (3xTF32), per head z as the grid's third
 // dimension: operand tile coordinates advance by (w_x, w_y) and (x_x, x_y) per
