@@ -298,6 +298,15 @@ def xl_arm(args) -> None:
     if local == 0:
         S.write_weight_tree(WEIGHT_DIR, shape)
     barrier()
+    if args.tp_only:
+        if world < 2:
+            raise SystemExit("--tp-only needs two or more ranks")
+        tp_info = tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks)
+        if rank == 0:
+            print(json.dumps({"metric": "tensor-parallel decode latency", "tp": tp_info}))
+            sys.stdout.flush()
+        dist.destroy_process_group()
+        return
     eng = llm_cpp_engine.InferenceEngine(f"cuda:{local}")
     eng.load(WEIGHT_DIR)
     eng.load(WEIGHT_DIR)  # the second load reads the tree from the page cache
@@ -447,10 +456,23 @@ def xl_arm(args) -> None:
 
 
 def tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks) -> dict:
-    """Tensor-parallel decode across all ranks: prompt 64 (seed 4), greedy 256."""
+    """Tensor-parallel decode across all ranks: prompt 64 (seed 4), greedy 256,
+    on the persistent path (the split projections' partial sums exchanged over
+    NVLink inside the kernel) and on the per-op path (NCCL all-reduces) for
+    comparison."""
+    out = tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, 0)
+    per_op = tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, 1)
+    out["per_op_ms_per_token"] = per_op["ms_per_token"]
+    out["per_op_first_tokens"] = per_op["first_tokens"]
+    out["per_op_gpu_launches"] = per_op["gpu_launches"]
+    return out
+
+
+def tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, path) -> dict:
     id_holder = [llm_cpp_engine.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(id_holder, src=0)
     eng = llm_cpp_engine.InferenceEngine(f"cuda:{local}", tp=world, rank=rank, nccl_id=id_holder[0])
+    eng.set_option("decode_path", path)
     eng.load(WEIGHT_DIR)
     ids = S.prompt_ids(4, 64, S.FULL.vocab)
     n_dec = 256
@@ -467,11 +489,14 @@ def tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks) -
 
     run()
     dist.barrier()
+    n0 = llm_cpp_engine.kernel_launches()
     dev, toks = run()
+    launches = llm_cpp_engine.kernel_launches() - n0
     dev = max_over_ranks(dev)
     del eng
     return {"tp": world, "prompt": 64, "decode_tokens": n_dec, "ms_per_token": dev / n_dec,
-            "tokens_per_s": n_dec / (dev / 1e3), "first_tokens": toks[:8]}
+            "tokens_per_s": n_dec / (dev / 1e3), "first_tokens": toks[:8], "decode_path": path,
+            "gpu_launches": launches}
 
 
 def replica_batch(eng, rank, world, max_over_ranks, barrier) -> dict:
@@ -577,6 +602,7 @@ def main() -> None:
     ap.add_argument("--ncu-case", choices=["decode-full", "decode-sampled", "batch-sampled", "decode-wide", "prefill-512"],
                     default=None)
     ap.add_argument("--decode-path", type=int, default=0, choices=[0, 1])
+    ap.add_argument("--tp-only", action="store_true", help="only the tensor-parallel decode latency (torchrun, N>1)")
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--budget", type=float, default=15.0, help=argparse.SUPPRESS)
     ap.add_argument("--weights", default=WEIGHT_DIR, help=argparse.SUPPRESS)

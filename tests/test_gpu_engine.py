@@ -114,6 +114,33 @@ def test_tiny_kv_reset_rounds(eng_mod, tiny_weights, path):
         assert eng.ctx_len() == n + 2
 
 
+ODD = S.ModelShape(layers=2, hidden=384, heads=6, ffn=1088, vocab=3001, max_ctx=768)
+
+
+@PATHS
+def test_odd_widths_greedy(eng_mod, path):
+    """Widths that are multiples of 64 but not of 256 (the shard widths of
+    tensor-parallel ranks): the persistent kernel streams hidden 384 as k-tiles
+    of 128 (one 384-float box per group), ffn 1088 as k-tiles of 64 (boxes of
+    512, 512 and 64 floats, the last one's tiles past K zero-filled), and a
+    vocab of 3001 rows (the last group partly past M)."""
+    sh = ODD
+    wdir = S.write_weight_tree("/tmp/xl_weights/odd", sh)
+    eng = make_engine(eng_mod, path, **sh.engine_kwargs())
+    eng.load(wdir)
+    port = O.Port(sh)
+    port.load(wdir)
+    ids = S.prompt_ids(6, 45, sh.vocab)
+    toks = run_greedy(eng, port, ids, 3)
+    n0 = eng_mod.kernel_launches()
+    tok = eng.next_token(toks[-1], top_p=0.0, repetition_penalty=1.0)
+    if path == 0:
+        assert eng_mod.kernel_launches() - n0 == 1  # the persistent kernel took the step
+    ref = port.decode(toks[-1])
+    assert_logits_close(logits_of(eng), ref)
+    check_token(tok, int(np.argmax(ref)), ref)
+
+
 def test_tiny_kernel_events_and_launch_count(eng_mod, tiny_weights):
     """Event nodes around the persistent kernel time it alone (within the step),
     change no token, and the library counts the decode graph's kernels at every

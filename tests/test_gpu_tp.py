@@ -3,6 +3,12 @@ each one shard of the engine on its own GPU with the engine's own NCCL
 communicator (rank 0's id handed over through a queue), against the oracle
 port on the same weight tree.
 
+Both decode paths: the persistent kernel (the out-projection and W2 partial
+sums of every CTA go to every rank's exchange buffer over NVLink and each
+rank sums them in the same order; one kernel + the greedy finish per step;
+TINY's shards stream as k-tiles of 128 floats) and the per-op path (NCCL
+all-reduces).
+
 * Greedy, teacher-forced on the oracle's ids: the ranks' vocab shards,
   concatenated, match the oracle's logits within 1e-3 of their range, and
   every rank returns the same id (the greedy merge of per-shard maxima).
@@ -37,7 +43,7 @@ def _gpus() -> int:
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _rank(rank, world, wdir, shape_kw, ids, teach, q_id, q_out, sampled=None):
+def _rank(rank, world, wdir, shape_kw, ids, teach, q_id, q_out, sampled=None, path=0):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     sys.path[:0] = [os.path.join(ROOT, "xingling-cpp_b200")]
     try:
@@ -50,14 +56,18 @@ def _rank(rank, world, wdir, shape_kw, ids, teach, q_id, q_out, sampled=None):
         else:
             ident = q_id.get(timeout=120)
         eng = m.InferenceEngine(f"cuda:{rank}", tp=world, rank=rank, nccl_id=ident, **shape_kw)
+        eng.set_option("decode_path", path)
         eng.load(wdir)
         toks, logits = [], []
+        step_launches = 0
         if sampled is None:
             tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
             toks.append(tok)
             logits.append(np.frombuffer(eng.last_logits(), np.float32).copy())
             for t in teach:
+                n0 = m.kernel_launches()
                 tok = eng.next_token(int(t), top_p=0.0, repetition_penalty=1.0)
+                step_launches = m.kernel_launches() - n0
                 toks.append(tok)
                 logits.append(np.frombuffer(eng.last_logits(), np.float32).copy())
         else:
@@ -70,17 +80,18 @@ def _rank(rank, world, wdir, shape_kw, ids, teach, q_id, q_out, sampled=None):
                 tok = eng.next_token(tok, temperature=T, top_p=P, repetition_penalty=RP)
                 toks.append(tok)
                 logits.append(np.frombuffer(eng.last_logits(), np.float32).copy())
-        q_out.put((rank, "ok", toks, logits, eng.vocab_shard()))
+        q_out.put((rank, "ok", toks, logits, eng.vocab_shard(), step_launches))
     except Exception as e:  # noqa: BLE001
-        q_out.put((rank, "error", repr(e)[:400], None, None))
+        q_out.put((rank, "error", repr(e)[:400], None, None, None))
 
 
-def _run_tp(wdir, shape, ids, teach, sampled=None):
+def _run_tp(wdir, shape, ids, teach, sampled=None, path=0):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q_id, q_out = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, WORLD, wdir, shape.engine_kwargs(), ids, teach, q_id, q_out, sampled))
+    procs = [ctx.Process(target=_rank, args=(r, WORLD, wdir, shape.engine_kwargs(), ids, teach, q_id, q_out, sampled,
+                                                        path))
              for r in range(WORLD)]
     for p in procs:
         p.start()
@@ -98,8 +109,9 @@ def _run_tp(wdir, shape, ids, teach, sampled=None):
     return out
 
 
-@pytest.mark.parametrize("shape_name", ["TINY", "WIDE2"])
-def test_tp2_greedy_matches_oracle(built, shape_name):
+@pytest.mark.parametrize("shape_name,path", [("TINY", 0), ("TINY", 1), ("WIDE2", 0), ("WIDE2", 1)],
+                         ids=["tiny-persistent", "tiny-per_op", "wide2-persistent", "wide2-per_op"])
+def test_tp2_greedy_matches_oracle(built, shape_name, path):
     if _gpus() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     shape = getattr(S, shape_name)
@@ -114,10 +126,13 @@ def test_tp2_greedy_matches_oracle(built, shape_name):
         teach.append(int(np.argmax(refs[-1])))
         refs.append(port.decode(teach[-1]))
 
-    out = _run_tp(wdir, shape, ids, teach)
+    out = _run_tp(wdir, shape, ids, teach, path=path)
     assert sorted(out) == list(range(WORLD)), f"ranks missing: {out}"
     for r in range(WORLD):
         assert out[r][1] == "ok", out[r][2]
+    if path == 0:
+        # the persistent kernel (NVLink exchange of the split projections) + the greedy finish
+        assert all(out[r][5] == 2 for r in range(WORLD)), [out[r][5] for r in range(WORLD)]
     shards = [out[r][4] for r in range(WORLD)]
     assert shards[0][0] == 0 and shards[-1][0] + shards[-1][1] == shape.vocab
     for r in range(1, WORLD):
@@ -145,8 +160,9 @@ def _check_ranks(out, shape):
         assert shards[r][0] == shards[r - 1][0] + shards[r - 1][1]
 
 
-@pytest.mark.parametrize("shape_name", ["TINY", "WIDE2"])
-def test_tp2_sampled_merge_matches_sample_cpu(built, shape_name):
+@pytest.mark.parametrize("shape_name,path", [("TINY", 0), ("WIDE2", 0), ("WIDE2", 1)],
+                         ids=["tiny-persistent", "wide2-persistent", "wide2-per_op"])
+def test_tp2_sampled_merge_matches_sample_cpu(built, shape_name, path):
     if _gpus() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     shape = getattr(S, shape_name)
@@ -154,7 +170,7 @@ def test_tp2_sampled_merge_matches_sample_cpu(built, shape_name):
     T, P, RP = 0.7, 0.9, 1.1
     uniforms = S.philox_uniforms(3, 12)
     ids = S.prompt_ids(2, 41, shape.vocab)
-    out = _run_tp(wdir, shape, ids, [], sampled=(T, P, RP, uniforms))
+    out = _run_tp(wdir, shape, ids, [], sampled=(T, P, RP, uniforms), path=path)
     _check_ranks(out, shape)
     port = O.Port(shape)
     port.load(wdir)

@@ -41,6 +41,15 @@
 // 490-547), SwishGLU::forward_vec (src/ffn.cu:126-139), Linear::forward_vec
 // (src/linear.cu:260-282) and Embedding::inverse (src/embedding.cu:130-205).
 //
+// Tensor parallel (one kernel per rank, each on its own GPU, same grid): each
+// rank runs its heads, FFN columns and vocab shard; the out-projection and W2
+// partial row sums of every CTA are stored straight into every rank's
+// exchange buffer (peer memory, NVLink) and counted on every rank's counter
+// for that layer with a system-scope release, so the next staging on each
+// rank sums all ranks' partials, in the same (rank, CTA) order everywhere,
+// without a collective launch.  The counters only grow, by tp * grid * 8 per
+// layer and step, so nothing resets them between steps.
+//
 // Every wait is bounded: a timed-out wait sets a bit in DevState::err, makes
 // the other CTAs leave at their next wait, and the producer drains its
 // in-flight copies before returning.
@@ -56,7 +65,7 @@ namespace {
 constexpr int kConsumerWarps = kPersistWarps;
 constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kBoxK = kPersistBoxTiles * kPersistTileK;        // 512 floats of K per box
+constexpr int kBoxK = kPersistBoxK;                             // 512 floats of K per box at most
 constexpr int kSlotBytes = kPersistTileRows * kBoxK * 4;         // 32 KB
 constexpr int kSlots = kPersistSlots;                            // 192 KB ring
 constexpr int kMaxK = 4096;
@@ -107,9 +116,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// 3D TMA load (no multicast) of one [16 rows][kd k-tiles][256 floats] box whose
+// 3D TMA load (no multicast) of one [16 rows][kd k-tiles][tw floats] box whose
 // first k-tile is kt and first row is row; the map views W[rows][K] as
-// [rows][K/256][256].
+// [rows][K/tw][tw].
 __device__ __forceinline__ void tma_box(void* dst, const CUtensorMap* map, int kt, int row, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
@@ -213,11 +222,12 @@ __device__ __forceinline__ Gemv gemv_of(const PersistentParams& p, int ph) {
 // QKV, W1/V and the LM head; an even split of the boxes for the residual
 // projections.
 struct Boxes {
-    int t0, t1, nb, kd, T;
+    int t0, t1, nb, kd, bw, T;  // kd k-tiles, bw floats of K per box
 };
 __device__ __forceinline__ Boxes boxes_of(const Gemv& d) {
     Boxes r;
     r.kd = persist_box_tiles(d.K);
+    r.bw = persist_box_width(d.K);
     r.nb = persist_boxes_per_group(d.K);
     const int groups = (d.M + kPersistTileRows - 1) / kPersistTileRows;
     r.T = groups * r.nb;
@@ -231,11 +241,26 @@ __device__ __forceinline__ Boxes boxes_of(const Gemv& d) {
     return r;
 }
 
+// Tensor parallel: rank r's exchange slot for the partial row sums that rank
+// src's CTA c computed for 16-row group g of a split projection (w2 = 0: the
+// out-projection, 1: W2).
+__device__ __forceinline__ float* xc_part(const PersistentParams& p, int r, int w2, int src, int g, int c) {
+    const int groups = p.H / kPersistTileRows;
+    return p.xc[r] +
+           ((static_cast<size_t>(w2 * p.tp + src) * groups + g) * kPersistMaxContrib + c) * kPersistTileRows;
+}
+// Phases whose results every rank needs: the out-projection and W2 of every
+// layer (in the tensor-parallel instantiation of the kernel).
+template <bool TP>
+__device__ __forceinline__ bool cross_rank(int kind) {
+    return TP && (kind == kWo || kind == kW2);
+}
+
 // ---------------------------------------------------------------------------
 // Producer: walks this CTA's boxes of every GEMV phase in order.
 struct Cursor {
     const CUtensorMap* map;
-    int ph, tau, t1, t0, nb, kd;
+    int ph, tau, t1, t0, nb, kd, bw;
     bool valid;
 };
 
@@ -247,7 +272,7 @@ __device__ void cursor_first(const PersistentParams& p, int ph, Cursor& c) {
         const Boxes r = boxes_of(d);
         if (r.t0 < r.t1) {
             c.map = d.map;
-            c.ph = ph, c.tau = r.t0, c.t0 = r.t0, c.t1 = r.t1, c.nb = r.nb, c.kd = r.kd;
+            c.ph = ph, c.tau = r.t0, c.t0 = r.t0, c.t1 = r.t1, c.nb = r.nb, c.kd = r.kd, c.bw = r.bw;
             c.valid = true;
             return;
         }
@@ -295,7 +320,7 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
         const int g = c.tau / c.nb, bi = c.tau % c.nb;
         // Rows past M and k-tiles past K of the box are zero-filled by TMA and
         // still counted in the transaction bytes.
-        mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(kPersistTileRows * kPersistTileK * 4 * c.kd));
+        mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(kPersistTileRows * c.bw * 4));
         if (p.tma_evict_first)
             tma_box_hint(ring + static_cast<size_t>(slot) * kSlotBytes, c.map, bi * c.kd, g * kPersistTileRows,
                          &full[slot], policy);
@@ -335,10 +360,41 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
 // Consumer helpers (256 threads, named barrier 1).
 
 // Wait until phase ph is complete (its counter reaches its target).
+template <bool TP>
 __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
+    const int kind = phase_kind(ph, p.layers);
+    if (cross_rank<TP>(kind)) {
+        // Every consumer warp of every CTA of every rank, counted up across steps.
+        if (threadIdx.x == 32) {
+            const unsigned long long target =
+                static_cast<unsigned long long>(p.st->epoch + 1) * p.tp * gridDim.x * kConsumerWarps;
+            const unsigned long long* c = p.xdone[p.rank] + (ph / 5) * 2 + (kind == kW2);
+            uint32_t it = 0;
+            unsigned long long t0 = 0;
+            int ok = 1;
+            for (;;) {
+                unsigned long long v;
+                asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(c) : "memory");
+                if (v >= target) break;
+                ++it;
+                if ((it & 255u) == 0) {
+                    const unsigned long long now = globaltimer();
+                    if (t0 == 0) t0 = now;
+                    if (it >= kFlagSpinLimit || now - t0 > kWaitLimitNs || aborted(p.st)) {
+                        atomicOr(&p.st->err, kErrFlag);
+                        ok = 0;
+                        break;
+                    }
+                }
+            }
+            *s_ok = ok;
+        }
+        consumer_sync();
+        return *s_ok != 0;
+    }
     // An attention phase is signalled once per head (by the warp that writes
     // the head's output); every other phase by every consumer warp of every CTA.
-    const int target = phase_kind(ph, p.layers) == kAttn ? p.heads : static_cast<int>(gridDim.x) * kConsumerWarps;
+    const int target = kind == kAttn ? p.heads : static_cast<int>(gridDim.x) * kConsumerWarps;
     if (threadIdx.x == 32) {
         const int* c = p.done + ph;
         uint32_t it = 0;
@@ -365,9 +421,19 @@ __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
 // Each warp publishes its own stores of phase ph as soon as it has issued
 // them: lane 0 releases (cumulative over the warp's lanes, ordered by the
 // __syncwarp) and adds 1 to the counter, so no warp waits for its CTA.
+template <bool TP>
 __device__ void signal_phase(const PersistentParams& p, int ph) {
     __syncwarp();
-    if ((threadIdx.x & 31) == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.done + ph) : "memory");
+    if ((threadIdx.x & 31) != 0) return;
+    const int kind = phase_kind(ph, p.layers);
+    if (cross_rank<TP>(kind)) {
+        // The partial sums went to every rank: release at system scope, then count on every rank.
+        const int slot = (ph / 5) * 2 + (kind == kW2);
+        for (int r = 0; r < p.tp; ++r)
+            asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(p.xdone[r] + slot) : "memory");
+    } else {
+        asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.done + ph) : "memory");
+    }
 }
 
 // Block-wide (consumers) sum of one float per thread.
@@ -472,6 +538,85 @@ __device__ __noinline__ void stage_norm(const PersistentParams& p, const float* 
     }
 }
 
+// Tensor parallel: as residual_quad, with the partial row sums of every rank
+// (already in this rank's exchange buffer) added in (rank, CTA) order, so that
+// every rank computes the same residual.
+__device__ __forceinline__ float4 residual_quad_tp(const PersistentParams& p, const float* x_old, const float* bias,
+                                                   int w2, int q, int nb, int T) {
+    const int g = (4 * q) / kPersistTileRows;
+    const int G = gridDim.x;
+    const int c0 = ((g * nb + 1) * G - 1) / T;
+    const int nc = ((g * nb + nb) * G - 1) / T - c0 + 1;
+    const int qq = q % (kPersistTileRows / 4);
+    float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int src = 0; src < p.tp; ++src) {
+        const float4* part = reinterpret_cast<const float4*>(xc_part(p, p.rank, w2, src, g, 0)) + qq;
+        float4 v[kPersistMaxContrib];
+#pragma unroll
+        for (int c = 0; c < kPersistMaxContrib; ++c)
+            v[c] = c < nc ? __ldcg(part + c * (kPersistTileRows / 4)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int c = 0; c < kPersistMaxContrib; ++c) {
+            if (c < nc) {
+                if (src == 0 && c == 0) {
+                    s = v[0];
+                } else {
+                    s.x += v[c].x;
+                    s.y += v[c].y;
+                    s.z += v[c].z;
+                    s.w += v[c].w;
+                }
+            }
+        }
+    }
+    const float4 xo = __ldcg(reinterpret_cast<const float4*>(x_old) + q);
+    const float4 b = reinterpret_cast<const float4*>(bias)[q];
+    return make_float4(xo.x + (s.x + b.x), xo.y + (s.y + b.y), xo.z + (s.z + b.z), xo.w + (s.w + b.w));
+}
+
+// stage_norm for tensor parallel: the residual after a split projection whose
+// partial sums all ranks exchanged (w2: which projection).
+__device__ __noinline__ void stage_norm_tp(const PersistentParams& p, const float* x_old, const float* bias, int w2,
+                                           int nb, const float* gamma, float* xs, float* red, float* x_out) {
+    const int t = threadIdx.x - 32;
+    const int K = p.H;
+    const int T = (K / kPersistTileRows) * nb;
+    const int s0 = static_cast<int>(blockIdx.x) * K / static_cast<int>(gridDim.x);
+    const int s1 = static_cast<int>(blockIdx.x + 1) * K / static_cast<int>(gridDim.x);
+    float4* x4 = reinterpret_cast<float4*>(xs);
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+    float4 gk[kStageQuads];
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kStageQuads; ++k) {
+        const int q = t + k * kConsumerThreads;
+        if (q < (K >> 2)) {
+            gk[k] = g4[q];
+            const float4 v = residual_quad_tp(p, x_old, bias, w2, q, nb, T);
+            x4[q] = v;
+            const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (4 * q + u >= s0 && 4 * q + u < s1) x_out[4 * q + u] = e[u];
+            ss = dot4(v, v, ss);
+        }
+    }
+    const float tot = consumer_sum(ss, red);
+    const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(tot / static_cast<float>(K)) + 1e-6));
+#pragma unroll
+    for (int k = 0; k < kStageQuads; ++k) {
+        const int q = t + k * kConsumerThreads;
+        if (q < (K >> 2)) {
+            float4 v = x4[q];
+            v.x = v.x * inv * gk[k].x;
+            v.y = v.y * inv * gk[k].y;
+            v.z = v.z * inv * gk[k].z;
+            v.w = v.w * inv * gk[k].w;
+            x4[q] = v;
+        }
+    }
+}
+
 // xs = src[0, K): all of a thread's loads before its shared-memory stores.
 __device__ void stage_copy(const float* src, int K, float* xs) {
     const int t = threadIdx.x - 32;
@@ -539,7 +684,7 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
     // A CTA without an attention item neither waits nor signals: the next
     // phase waits for the heads' outputs, which imply the QKV phase.
     if (!has) return true;
-    if (!wait_phase(p, ph - 1, s_ok)) return false;
+    if (!wait_phase<false>(p, ph - 1, s_ok)) return false;
     if (t == 0) trace_at(p, ph, kTrConsStart);
     float* qsh = xs + warp * kAttnWarpScratch;
     float* apart = xs + kConsumerWarps * kAttnWarpScratch;  // [8][68]
@@ -620,7 +765,7 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
     float2* out = reinterpret_cast<float2*>(p.att + h * kHeadDim);
     if (nct == 1) {
         out[lane] = make_float2(acc.x / L, acc.y / L);
-        signal_phase(p, ph);
+        signal_phase<false>(p, ph);
         return true;
     }
     // A head split over nct CTAs: the last CTA to finish merges their partials.
@@ -653,10 +798,11 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
         acc2.y = fmaf(wt, ok.y, acc2.y);
     }
     out[lane] = make_float2(acc2.x / L2, acc2.y / L2);
-    signal_phase(p, ph);
+    signal_phase<false>(p, ph);
     return true;
 }
 
+template <bool TP>
 __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint64_t* full, uint64_t* empty,
                           float* red, unsigned long long* best_s, int* s_ok, volatile int* quiet) {
     DevState* st = p.st;
@@ -700,28 +846,36 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 }
             }
         }
-        if (ph > 0 && !wait_phase(p, ph - 1, s_ok)) return;
+        if (ph > 0 && !wait_phase<TP>(p, ph - 1, s_ok)) return;
         if (t == 0) trace_at(p, ph, kTrConsStart);
         // Stage this phase's input vector.
         if (kind == kQKV) {
             if (l == 0)
                 stage_norm(p, p.emb + static_cast<size_t>(st->in.token_in) * p.H, nullptr, nullptr, 0, y->g1, xs, red,
                            p.xa);
+            else if (TP)
+                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, nb_w2, y->g1, xs, red, p.xa);
             else
                 stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, y->g1, xs, red, p.xa);
         } else if (kind == kWo) {
             stage_copy(p.att, p.Hl, xs);
         } else if (kind == kW13) {
-            stage_norm(p, p.xa, y->bo, p.cres, nb_wo, y->g2, xs, red, p.xb);
+            if (TP)
+                stage_norm_tp(p, p.xa, y->bo, 0, nb_wo, y->g2, xs, red, p.xb);
+            else
+                stage_norm(p, p.xa, y->bo, p.cres, nb_wo, y->g2, xs, red, p.xb);
         } else if (kind == kW2) {
             stage_copy(p.ffh, p.Fl, xs);
         } else {  // kLM
-            stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, p.gnorm, xs, red, p.xa);
+            if (TP)
+                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, nb_w2, p.gnorm, xs, red, p.xa);
+            else
+                stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, p.gnorm, xs, red, p.xa);
         }
         consumer_sync();
         if (t == 0) *quiet = 0;
         if (t == 0) trace_at(p, ph, kTrConsStaged);
-        const int rs4 = r.kd * (kPersistTileK / 4);  // float4 per row of a box
+        const int rs4 = r.bw / 4;  // float4 per row of a box
         const float4* x4 = reinterpret_cast<const float4*>(xs);
         const bool split = kind == kWo || kind == kW2;
         for (int tau = r.t0; tau < r.t1;) {
@@ -753,8 +907,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 // Every box of this phase has landed: quiet window until the next staging.
                 if (t == 0 && kind != kLM && tau + (bi - bi0) == r.t1 - 1) *quiet = 1;
                 if (ok) {
-                    const int k0 = bi * r.kd * kPersistTileK;
-                    const int kc4 = min(r.kd * kPersistTileK, d.K - k0) >> 2;
+                    const int k0 = bi * r.bw;
+                    const int kc4 = min(r.bw, d.K - k0) >> 2;
                     const float4* tile =
                         reinterpret_cast<const float4*>(ring + static_cast<size_t>(slot) * kSlotBytes);
                     const float4* wa = tile + ra * rs4;
@@ -788,9 +942,17 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 case kWo:
                 case kW2: {  // partial row sums of this CTA's boxes of group g (c: this CTA's rank among its owners)
                     const int c = blockIdx.x - ((g * r.nb + 1) * static_cast<int>(gridDim.x) - 1) / r.T;
-                    float* q = p.cres + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows;
-                    if (lane == 0) q[ra] = acc_a;
-                    if (lane == 1) q[rb] = acc_b;
+                    if (!TP) {
+                        float* q = p.cres + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows;
+                        if (lane == 0) q[ra] = acc_a;
+                        if (lane == 1) q[rb] = acc_b;
+                    } else {
+                        for (int rr = 0; rr < p.tp; ++rr) {  // this rank's slot on every rank (NVLink stores)
+                            float* q = xc_part(p, rr, kind == kW2, p.rank, g, c);
+                            if (lane == 0) q[ra] = acc_a;
+                            if (lane == 1) q[rb] = acc_b;
+                        }
+                    }
                     break;
                 }
                 case kW13:
@@ -812,11 +974,11 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 }
             }
         }
-        if (kind != kLM) signal_phase(p, ph);
+        if (kind != kLM) signal_phase<TP>(p, ph);
         if (t == 0) trace_at(p, ph, kTrConsEnd);
     }
     // LM head: CTA argmax -> global max; the last CTA publishes the winner.
-    if (lane == 0) best_s[warp] = best_i >= 0 ? pack_argmax(best_v, best_i) : 0ull;
+    if (lane == 0) best_s[warp] = best_i >= 0 ? pack_argmax(best_v, p.v0 + best_i) : 0ull;
     consumer_sync();
     if (t == 0) {
         unsigned long long k = 0;
@@ -831,6 +993,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
             const int tok = unpack_argmax_index(fin);
             st->argmax_final = fin;
             st->greedy_token = tok;
+            st->epoch += 1;  // every CTA has read it for this step's cross-rank targets
             if (p.finish_greedy) {
                 // Greedy step: the argmax is the step's id (no sampler launch follows).
                 st->token_out = tok;
@@ -841,6 +1004,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
     }
 }
 
+template <bool TP>
 __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __grid_constant__ PersistentParams p) {
     extern __shared__ __align__(128) char smem[];
     char* ring = smem;
@@ -868,7 +1032,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) producer(p, ring, full, empty, quiet);
     } else {
-        consumers(p, ring, xs, full, empty, red, best_s, s_ok, quiet);
+        consumers<TP>(p, ring, xs, full, empty, red, best_s, s_ok, quiet);
     }
 }
 
@@ -877,18 +1041,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
 size_t persistent_smem_bytes() { return kSmemBytes; }
 
 cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cudaStream_t s) {
-    if (p.H > kMaxK || p.Hl > kMaxK || p.Fl > kMaxK || p.H % kPersistTileK || p.Hl % kPersistTileK ||
-        p.Fl % kPersistTileK)
+    if (p.H <= 0 || p.Hl <= 0 || p.Fl <= 0 || p.H > kMaxK || p.Hl > kMaxK || p.Fl > kMaxK ||
+        p.H % kPersistKAlign || p.Hl % kPersistKAlign || p.Fl % kPersistKAlign)
         return cudaErrorInvalidValue;
     // Attention: at most one item per CTA, at most 32 CTAs per head (one lane each in the merge).
     const int nct = persist_attn_ctas_per_head(p.T);
     if (p.heads * nct > num_sms || nct > 32) return cudaErrorInvalidValue;
     if (p.inflight < 1 || p.inflight > kSlots) return cudaErrorInvalidValue;
+    if (p.tp < 1 || p.tp > kMaxTp || p.rank < 0 || p.rank >= p.tp || (p.tp > 1 && p.finish_greedy))
+        return cudaErrorInvalidValue;
+    for (int r = 0; r < p.tp && p.tp > 1; ++r)
+        if (!p.xc[r] || !p.xdone[r]) return cudaErrorInvalidValue;
     if (persist_max_contrib(p.H, p.Hl, num_sms) > kPersistMaxContrib ||
         persist_max_contrib(p.H, p.Fl, num_sms) > kPersistMaxContrib)
         return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemBytes));
+    auto kern = p.tp > 1 ? decode_persistent_kernel<true> : decode_persistent_kernel<false>;
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
@@ -901,7 +1070,7 @@ cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cud
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     count_launch();
-    return cudaLaunchKernelEx(&cfg, decode_persistent_kernel, p);
+    return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 }  // namespace xl

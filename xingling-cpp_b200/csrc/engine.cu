@@ -186,7 +186,43 @@ int Engine::init(const xl_config& cfg, int device, int tp_size, int tp_rank, con
         for (size_t i = 0; i < sizeof(id); ++i) h = (h ^ static_cast<unsigned char>(id.internal[i])) * 1099511628211ull;
         philox_seed_ = h;
         XL_NCCL(ncclCommInitRank(&comm_, tp_, id, rank_));
+        if (xbuf_) {
+            rc = setup_peers();
+            if (rc != XL_OK) return rc;
+        }
     }
+    return XL_OK;
+}
+
+// Every rank exports its exchange buffer (CUDA IPC) and maps every other
+// rank's; the handles are all-gathered over the engine's NCCL communicator.
+int Engine::setup_peers() {
+    cudaIpcMemHandle_t mine;
+    XL_CUDA(cudaIpcGetMemHandle(&mine, xbuf_));
+    constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
+    char* dev = nullptr;
+    XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&dev), kH * tp_));
+    std::vector<char> all(kH * tp_);
+    cudaError_t ce = cudaMemcpy(dev + kH * rank_, &mine, kH, cudaMemcpyHostToDevice);
+    ncclResult_t nr = ncclSuccess;
+    if (ce == cudaSuccess) nr = ncclAllGather(dev + kH * rank_, dev, kH, ncclUint8, comm_, stream_);
+    if (ce == cudaSuccess && nr == ncclSuccess) ce = cudaStreamSynchronize(stream_);
+    if (ce == cudaSuccess && nr == ncclSuccess) ce = cudaMemcpy(all.data(), dev, kH * tp_, cudaMemcpyDeviceToHost);
+    cudaFree(dev);
+    if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather (exchange buffer handles)");
+    if (ce != cudaSuccess) return cuda_fail(ce, "exchange buffer handles");
+    for (int r = 0; r < tp_; ++r) {
+        if (r == rank_) {
+            xpeer_[r] = xbuf_;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, all.data() + kH * r, kH);
+        void* ptr = nullptr;
+        XL_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        xpeer_[r] = static_cast<char*>(ptr);
+    }
+    peers_ = true;
     return XL_OK;
 }
 
@@ -216,6 +252,8 @@ int Engine::alloc_all() {
         add(&L.wo_lo, H * Hl * 4);
         add(&L.w13_lo, 2 * Fl * H * 4);
         add(&L.w2_lo, H * Fl * 4);
+        add(&L.bo_full, tp_ > 1 ? H * 4 : 0);
+        add(&L.b2_full, tp_ > 1 ? H * 4 : 0);
     }
     add(&xa_, H * 4);
     add(&xb_, H * 4);
@@ -262,6 +300,13 @@ int Engine::alloc_all() {
     XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&arena_), total));
     arena_bytes_ = total;
     XL_CUDA(cudaMemset(arena_, 0, total));
+    if (tp_ > 1 && tp_ <= kMaxTp) {
+        // Its own allocation, so that the peers can map it (an IPC handle covers a whole allocation).
+        const size_t xc = 2 * static_cast<size_t>(tp_) * (H / kPersistTileRows) * kPersistMaxContrib *
+                          kPersistTileRows * 4;
+        XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&xbuf_), xdone_bytes() + xc));
+        XL_CUDA(cudaMemset(xbuf_, 0, xdone_bytes() + xc));
+    }
     size_t off = 0;
     for (auto& pr : plan) {
         *pr.first = arena_ + off;
@@ -280,7 +325,10 @@ Engine::~Engine() {
     if (decode_exec_s_) cudaGraphExecDestroy(decode_exec_s_);
     if (gen_exec_) cudaGraphExecDestroy(gen_exec_);
     if (gen_exec_s_) cudaGraphExecDestroy(gen_exec_s_);
+    for (int r = 0; r < kMaxTp; ++r)
+        if (xpeer_[r] && xpeer_[r] != xbuf_) cudaIpcCloseMemHandle(xpeer_[r]);
     if (comm_) ncclCommDestroy(comm_);
+    if (xbuf_) cudaFree(xbuf_);
     if (arena_) cudaFree(arena_);
     if (h_in_) cudaFreeHost(h_in_);
     if (h_out_) cudaFreeHost(h_out_);
@@ -465,12 +513,14 @@ int Engine::load(const char* dir) {
         }
         ld.copy(b + "attn/W/weight.bin", H, H, 0, H, hq0, hq1, L.wo, Hl * 4);
         if (rank_ == 0) ld.copy(b + "attn/W/bias.bin", 1, H, 0, 1, 0, H, L.bo, H * 4);
+        if (tp_ > 1) ld.copy(b + "attn/W/bias.bin", 1, H, 0, 1, 0, H, L.bo_full, H * 4);
         ld.copy(b + "ffn/W1/weight.bin", F, H, f0, f1, 0, H, L.w13, 2 * H * 4);
         ld.copy(b + "ffn/V/weight.bin", F, H, f0, f1, 0, H, L.w13 + H, 2 * H * 4);
         ld.copy(b + "ffn/W1/bias.bin", 1, F, 0, 1, f0, f1, L.b13, 0, 8);
         ld.copy(b + "ffn/V/bias.bin", 1, F, 0, 1, f0, f1, L.b13 + 1, 0, 8);
         ld.copy(b + "ffn/W2/weight.bin", H, F, 0, H, f0, f1, L.w2, Fl * 4);
         if (rank_ == 0) ld.copy(b + "ffn/W2/bias.bin", 1, H, 0, 1, 0, H, L.b2, H * 4);
+        if (tp_ > 1) ld.copy(b + "ffn/W2/bias.bin", 1, H, 0, 1, 0, H, L.b2_full, H * 4);
         ld.copy(b + "norm1/weight.bin", 1, H, 0, 1, 0, H, L.g1, H * 4);
         ld.copy(b + "norm2/weight.bin", 1, H, 0, 1, 0, H, L.g2, H * 4);
     }
@@ -552,19 +602,22 @@ int Engine::prefill_linear(int mode, const TcOperands& o, const float* x, const 
 // all 16 layers and the LM head, then the sampler.
 int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     PersistentParams p{};
+    const bool tpk = tp_ > 1;
     if (cfg_.layers > kMaxLayers) {
         set_error("persistent decode supports at most 32 layers");
         return XL_ERR_ARG;
     }
     for (int l = 0; l < cfg_.layers; ++l) {
         const LayerWeights& L = layers_[l];
-        p.layer[l] = LayerPtrs{L.wqkv, L.bqkv, L.wo, L.bo, L.w13, L.b13, L.w2, L.b2, L.g1, L.g2, L.kc, L.vc};
+        // Tensor parallel: the stagings add the whole biases once (the exchanged partial sums carry none).
+        p.layer[l] = LayerPtrs{L.wqkv, L.bqkv, L.wo, tpk ? L.bo_full : L.bo, L.w13, L.b13, L.w2,
+                               tpk ? L.b2_full : L.b2, L.g1, L.g2, L.kc, L.vc};
         XL_CUDA(make_stream_map(&p.maps[4 * l + 0], L.wqkv, 3 * Hl_, H_));
         XL_CUDA(make_stream_map(&p.maps[4 * l + 1], L.wo, H_, Hl_));
         XL_CUDA(make_stream_map(&p.maps[4 * l + 2], L.w13, 2 * Fl_, H_));
         XL_CUDA(make_stream_map(&p.maps[4 * l + 3], L.w2, H_, Fl_));
     }
-    XL_CUDA(make_stream_map(&p.maps[kPersistMaps - 1], emb_, V_, H_));
+    XL_CUDA(make_stream_map(&p.maps[kPersistMaps - 1], emb_ + static_cast<size_t>(v0_) * H_, vl_, H_));
     p.layers = cfg_.layers;
     p.emb = emb_;
     p.gnorm = gnorm_;
@@ -587,10 +640,23 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     p.Hl = Hl_;
     p.heads = heads_l_;
     p.Fl = Fl_;
-    p.V = V_;
+    p.V = vl_;
+    p.v0 = v0_;
     p.T = T_;
-    p.finish_greedy = sampled ? 0 : 1;
+    p.finish_greedy = sampled || tpk ? 0 : 1;
     p.tma_evict_first = tma_evict_first_;
+    p.tp = tp_;
+    p.rank = rank_;
+    if (tpk) {
+        for (int r = 0; r < tp_; ++r) {
+            p.xdone[r] = reinterpret_cast<unsigned long long*>(xpeer_[r]);
+            p.xc[r] = reinterpret_cast<float*>(xpeer_[r] + xdone_bytes());
+        }
+        // The ranks' kernels wait on one another (with a time limit), so they
+        // start together, after a one-word NCCL barrier: the hosts may launch
+        // a step at very different times.
+        XL_NCCL(ncclAllReduce(&st_->tp_sync, &st_->tp_sync, 1, ncclInt32, ncclMax, comm_, s));
+    }
     XL_CUDA(cudaMemsetAsync(
         done_, 0, (5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_) * sizeof(int),
         s));
@@ -600,6 +666,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     XL_CUDA(launch_decode_persistent(p, num_sms_, s));
     if (kernel_events_) XL_CUDA(cudaEventRecordWithFlags(kev1_, s, cudaEventRecordExternal));
     lm_x_ = xa_;
+    if (tpk) return lm_tail(s, sampled);
     if (sampled) XL_CUDA(launch_sample_chain(sample_params(), 1, true, s));
     return XL_OK;
 }
@@ -620,7 +687,7 @@ SampleParams Engine::sample_params() const {
 }
 
 int Engine::enqueue_decode(cudaStream_t s, bool sampled) {
-    persistent_graph_ = tp_ == 1 && decode_path_ == 0 && persistent_fits();
+    persistent_graph_ = decode_path_ == 0 && persistent_fits();
     if (persistent_graph_) return enqueue_decode_persistent(s, sampled);
     float* cur = xa_;
     float* other = xb_;
@@ -738,6 +805,12 @@ int Engine::launch_lm_head(const float* x_last, const float* delta, bool pdl, cu
 int Engine::run_lm_head_and_sample(const float* x_last, const float* delta, cudaStream_t s, bool sampled) {
     const int rc = launch_lm_head(x_last, delta, true, s);
     if (rc != XL_OK) return rc;
+    return lm_tail(s, sampled);
+}
+
+// After the LM head: the argmax merge across vocab shards (tensor parallel),
+// then the greedy id or the sampler.
+int Engine::lm_tail(cudaStream_t s, bool sampled) {
     if (tp_ > 1) XL_NCCL(ncclAllReduce(&st_->argmax_final, &st_->argmax_final, 1, ncclUint64, ncclMax, comm_, s));
     SampleParams sp = sample_params();
     if (!sampled) {
@@ -805,7 +878,7 @@ int Engine::capture_gen_graphs() {
             exec = nullptr;
         }
     }
-    if (!persistent_graph_) return XL_OK;
+    if (!persistent_graph_ || tp_ > 1) return XL_OK;
     GenParams gp{};
     gp.ctl = gen_ctl_;
     gp.uniforms = gen_u_;

@@ -29,6 +29,7 @@ struct LayerWeights {
     float* b2;    // [H] (zero on ranks > 0)
     float* g1;    // [H]
     float* g2;    // [H]
+    float *bo_full, *b2_full;  // [H] the whole biases (tensor parallel only: the persistent kernel's stagings)
     float* kc;    // [heads_l][max_ctx][64]
     float* vc;    // [heads_l][max_ctx][64]
     // TF32 residuals (w - trunc19(w)) of the four projections, for the 3xTF32 prefill GEMMs
@@ -78,12 +79,13 @@ class Engine {
     int enqueue_decode(cudaStream_t s, bool sampled);
     int enqueue_decode_persistent(cudaStream_t s, bool sampled);
     SampleParams sample_params() const;  // this engine's sequence, single-step sampler chain
-    // The persistent kernel streams K in 256-float tiles of at most 4096 floats,
-    // runs at most one attention item per SM and lets at most
-    // kPersistMaxContrib SMs share a row group of the residual projections.
+    // The persistent kernel streams K in tiles of 64 floats or more, at most
+    // 4096 floats, runs at most one attention item per SM and lets at most
+    // kPersistMaxContrib SMs share a row group of the residual projections;
+    // tensor-parallel ranks need every peer's exchange buffer mapped.
     bool persistent_fits() const {
-        return cfg_.layers <= kMaxLayers && H_ % kPersistTileK == 0 && Hl_ % kPersistTileK == 0 &&
-               Fl_ % kPersistTileK == 0 && H_ <= 4096 && Hl_ <= 4096 && Fl_ <= 4096 &&
+        return cfg_.layers <= kMaxLayers && (tp_ == 1 || (tp_ <= kMaxTp && peers_)) && H_ % kPersistKAlign == 0 &&
+               Hl_ % kPersistKAlign == 0 && Fl_ % kPersistKAlign == 0 && H_ <= 4096 && Hl_ <= 4096 && Fl_ <= 4096 &&
                heads_l_ * persist_attn_ctas_per_head(T_) <= num_sms_ &&
                persist_max_contrib(H_, Hl_, num_sms_) <= kPersistMaxContrib &&
                persist_max_contrib(H_, Fl_, num_sms_) <= kPersistMaxContrib;
@@ -92,6 +94,8 @@ class Engine {
     int prefill_linear(int mode, const TcOperands& o, const float* x, const float* w, const float* b, float* y,
                        float* y_lo, int n, int m, int k, cudaStream_t s);
     int run_lm_head_and_sample(const float* x_last, const float* delta, cudaStream_t s, bool sampled);
+    int lm_tail(cudaStream_t s, bool sampled);  // after the LM head: argmax merge across ranks, id or sampler
+    int setup_peers();                          // tensor parallel: map every rank's exchange buffer
     int launch_lm_head(const float* x_last, const float* delta, bool pdl, cudaStream_t s);
     const float* lm_x_ = nullptr;  // residual stream the decode graph's LM head reads
     int finish_step(int* token_out);
@@ -152,8 +156,16 @@ class Engine {
     cudaGraphExec_t gen_exec_ = nullptr, gen_exec_s_ = nullptr;  // gen_feed + decode step + gen_collect
     long long gen_graph_kernels_ = 0, gen_graph_kernels_s_ = 0;
     ncclComm_t comm_ = nullptr;
+    // Tensor parallel, persistent decode: this rank's exchange buffer (its own
+    // allocation, exported over CUDA IPC): counters [layers][2] (u64), then
+    // the partial sums [2][tp][H/16][kPersistMaxContrib][16]; and every
+    // rank's buffer mapped here (xpeer_[rank_] == xbuf_).
+    char* xbuf_ = nullptr;
+    char* xpeer_[kMaxTp] = {};
+    bool peers_ = false;
+    size_t xdone_bytes() const { return (static_cast<size_t>(cfg_.layers) * 2 * 8 + 255) / 256 * 256; }
 
-    int decode_path_ = 0;      // 0: persistent kernel (single GPU), 1: per-op kernels
+    int decode_path_ = 0;      // 0: persistent kernel (where it fits), 1: per-op kernels
     int prefill_gemm_ = 0;     // 0: tcgen05 3xTF32, 1: fp32 SIMT tiles
     int prefill_attn_ = 0;     // 0: tcgen05 3xTF32 (S GEMM, softmax, PV GEMM), 1: fp32 FMA flash tiles
     // tensor-core prefill attention: q/8 [T][Hl], k [heads][T][64], v^T [heads*64][T], S/P [heads][T][T]

@@ -386,12 +386,13 @@ cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int col
 cudaError_t make_stream_map(CUtensorMap* map, const float* base, int rows, int cols) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
-    if (reinterpret_cast<uintptr_t>(base) % 16 || cols % kPersistTileK) return cudaErrorInvalidValue;
-    const int nkt = cols / kPersistTileK;
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kPersistTileK), static_cast<cuuint64_t>(nkt),
+    if (reinterpret_cast<uintptr_t>(base) % 16 || cols <= 0 || cols % kPersistKAlign) return cudaErrorInvalidValue;
+    const int tw = persist_tile_w(cols);
+    const int nkt = cols / tw;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(tw), static_cast<cuuint64_t>(nkt),
                                 static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kPersistTileK) * 4, static_cast<cuuint64_t>(cols) * 4};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kPersistTileK),
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(tw) * 4, static_cast<cuuint64_t>(cols) * 4};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(tw),
                                static_cast<cuuint32_t>(persist_box_tiles(cols)),
                                static_cast<cuuint32_t>(kPersistTileRows)};
     const cuuint32_t elem[3] = {1, 1, 1};

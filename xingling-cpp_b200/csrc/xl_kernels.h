@@ -34,7 +34,9 @@ struct DevState {
     unsigned long long argmax_key;    // scratch for the LM-head argmax (zero between steps)
     unsigned long long argmax_final;  // packed (value, id) of the winning logit
     int err;                          // device-side error bits (0 = ok)
-    int pad[3];
+    int epoch;                        // persistent decode steps run (tensor parallel: cross-rank counter targets)
+    int tp_sync;                      // tensor parallel: the word of the step-start NCCL barrier
+    int pad;
 };
 
 enum GemvMode : int {
@@ -89,23 +91,31 @@ long long launch_count();
 // Persistent decode step (decode_persistent.cu): one cooperative launch per token.
 constexpr int kMaxLayers = 32;
 constexpr int kPersistChunk = 16;     // attention positions per warp
-constexpr int kPersistTileRows = 16;  // weight box streamed per TMA load: 16 rows x 2 k-tiles x 256 floats
-constexpr int kPersistTileK = 256;
-constexpr int kPersistBoxTiles = 2;
+constexpr int kPersistTileRows = 16;  // weight box streamed per TMA load: 16 rows x up to 512 floats of K
+constexpr int kPersistBoxK = 512;     // floats of K per box at most (k-tiles of 256, 128 or 64)
+constexpr int kPersistKAlign = 64;    // every streamed K is a multiple of this
 constexpr int kPersistSlots = 6;      // 32 KB ring slots per CTA
 constexpr int kPersistWarps = 8;      // consumer warps per CTA (attention: one chunk each)
 constexpr int kPersistMaxContrib = 4; // CTAs that may share one 16-row group of a residual projection
 constexpr int kPersistMaps = 4 * kMaxLayers + 1;  // QKV, Wo, W1/V, W2 per layer, then the LM head
+constexpr int kMaxTp = 8;  // tensor-parallel ranks of the persistent decode kernel
 __host__ __device__ inline int persistent_max_splits(int max_ctx) {
     return (max_ctx + kPersistChunk - 1) / kPersistChunk;
 }
-// k-tiles per box and boxes per 16-row group of a K-column weight (K % 256 == 0).
+// Geometry of a K-column weight (K % 64 == 0) streamed as 16-row boxes: a
+// 3D tensor map of k-tiles of persist_tile_w(K) floats (the widest of 256,
+// 128, 64 dividing K; a box dimension holds at most 256 elements), boxes of
+// persist_box_tiles(K) tiles (at most 512 floats), persist_boxes_per_group(K)
+// boxes per 16-row group (k-tiles past K in the last box are zero-filled).
+__host__ __device__ inline int persist_tile_w(int K) { return K % 256 == 0 ? 256 : K % 128 == 0 ? 128 : 64; }
 __host__ __device__ inline int persist_box_tiles(int K) {
-    return K / kPersistTileK < kPersistBoxTiles ? K / kPersistTileK : kPersistBoxTiles;
+    const int n = K / persist_tile_w(K), m = kPersistBoxK / persist_tile_w(K);
+    return n < m ? n : m;
 }
+__host__ __device__ inline int persist_box_width(int K) { return persist_tile_w(K) * persist_box_tiles(K); }
 __host__ __device__ inline int persist_boxes_per_group(int K) {
     const int kd = persist_box_tiles(K);
-    return (K / kPersistTileK + kd - 1) / kd;
+    return (K / persist_tile_w(K) + kd - 1) / kd;
 }
 // The residual projections (out-proj, W2) are split evenly by boxes: CTA b of
 // G takes boxes [b*T/G, (b+1)*T/G) of T = (M/16) * nb; box tau belongs to
@@ -152,15 +162,24 @@ struct PersistentParams {
     int* done;              // [5*layers + 1] phase counters (then head_done), zeroed before each launch
     unsigned long long* trace;  // optional [grid][5*layers + 1][kTraceFields] timestamps (ns), or nullptr
     int inflight;               // weight boxes requested but not landed, per CTA (1 .. kPersistSlots)
-    int H, Hl, heads, Fl, V, T;
+    int H, Hl, heads, Fl, V, T;  // V: rows of this rank's vocab shard
     int finish_greedy;          // 1: the LM head's last CTA writes the argmax as the step's id
     int tma_evict_first;        // 1: weight boxes are loaded with an L2 evict-first policy
+    // Tensor parallel (tp > 1): every CTA writes its out-projection / W2 partial
+    // row sums into every rank's exchange buffer xc[r] (peer memory over NVLink),
+    // laid out [2 (out-proj, W2)][tp][H/16][kPersistMaxContrib][16], and counts
+    // them on every rank's xdone[r][layer * 2 + (W2)], counters that only grow
+    // (target (epoch + 1) * tp * grid * 8 in a step).
+    int tp, rank;
+    int v0;                     // global id of this rank's vocab row 0 (argmax keys carry global ids)
+    float* xc[kMaxTp];
+    unsigned long long* xdone[kMaxTp];
 };
 constexpr int kTraceFields = 5;
 size_t persistent_smem_bytes();
 // The TMA map (no swizzle) of a row-major [rows][cols] weight viewed as
-// [rows][cols/256][256], box [16 rows][min(2, cols/256) k-tiles][256 floats];
-// cols must be a multiple of 256.
+// [rows][cols/tw][tw] (tw = persist_tile_w(cols)), box [16 rows]
+// [persist_box_tiles(cols) k-tiles][tw floats]; cols must be a multiple of 64.
 cudaError_t make_stream_map(CUtensorMap* map, const float* base, int rows, int cols);
 cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cudaStream_t s);
 
