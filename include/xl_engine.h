@@ -150,11 +150,13 @@ XL_API int xl_engine_ctx_len(const xl_engine* e);
 XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, float* v_out);
 
 /* Engine options (no reference counterpart):
- *   "decode_path" 0  one persistent kernel per decode token (default; single
- *                    GPU): a TMA weight stream through shared memory across
- *                    all layers and the LM head, phases gated by grid-wide
- *                    counters;
- *                 1  one kernel per fused op (the tensor-parallel path).
+ *   "decode_path" 0  one persistent kernel per decode token (default): a TMA
+ *                    weight stream through shared memory across all layers
+ *                    and the LM head, phases gated by grid-wide counters;
+ *                    tensor-parallel ranks exchange the out-projection and
+ *                    W2 partial sums inside it over NVLink peer memory;
+ *                 1  one kernel per fused op (NCCL all-reduces under tensor
+ *                    parallelism).
  *   "phase_trace" 1  the persistent kernel stamps %globaltimer (ns) per CTA
  *                    and phase: consumer start (after the grid-wide wait),
  *                    input staged, phase done, producer first and last issue;

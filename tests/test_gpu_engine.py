@@ -114,16 +114,16 @@ def test_tiny_kv_reset_rounds(eng_mod, tiny_weights, path):
         assert eng.ctx_len() == n + 2
 
 
-ODD = S.ModelShape(layers=2, hidden=384, heads=6, ffn=1088, vocab=3001, max_ctx=768)
+ODD = S.ModelShape(layers=2, hidden=640, heads=10, ffn=1088, vocab=3001, max_ctx=768)
 
 
 @PATHS
 def test_odd_widths_greedy(eng_mod, path):
     """Widths that are multiples of 64 but not of 256 (the shard widths of
-    tensor-parallel ranks): the persistent kernel streams hidden 384 as k-tiles
-    of 128 (one 384-float box per group), ffn 1088 as k-tiles of 64 (boxes of
-    512, 512 and 64 floats, the last one's tiles past K zero-filled), and a
-    vocab of 3001 rows (the last group partly past M)."""
+    tensor-parallel ranks): the persistent kernel streams hidden 640 as k-tiles
+    of 128 (boxes of 512 and 128 floats of K: the last box's k-tiles past K
+    are zero-filled), ffn 1088 as k-tiles of 64 (boxes of 512, 512 and 64
+    floats), and a vocab of 3001 rows (the last group partly past M)."""
     sh = ODD
     wdir = S.write_weight_tree("/tmp/xl_weights/odd", sh)
     eng = make_engine(eng_mod, path, **sh.engine_kwargs())
