@@ -456,8 +456,7 @@ __device__ __forceinline__ float4 residual_quad(const float* x_old, const float*
                                                 int T) {
     const int g = (4 * q) / kPersistTileRows;
     const int G = gridDim.x;
-    const int c0 = ((g * nb + 1) * G - 1) / T;            // persist_owner_cta of the group's first box
-    const int nc = ((g * nb + nb) * G - 1) / T - c0 + 1;  // ... through its last box
+    const int nc = persist_group_contrib(g, nb, T, G);
     const float4* part = reinterpret_cast<const float4*>(cres + g * (kPersistMaxContrib * kPersistTileRows)) +
                          (q % (kPersistTileRows / 4));
     float4 v[kPersistMaxContrib];
@@ -545,8 +544,7 @@ __device__ __forceinline__ float4 residual_quad_tp(const PersistentParams& p, co
                                                    int w2, int q, int nb, int T) {
     const int g = (4 * q) / kPersistTileRows;
     const int G = gridDim.x;
-    const int c0 = ((g * nb + 1) * G - 1) / T;
-    const int nc = ((g * nb + nb) * G - 1) / T - c0 + 1;
+    const int nc = persist_group_contrib(g, nb, T, G);
     const int qq = q % (kPersistTileRows / 4);
     float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (int src = 0; src < p.tp; ++src) {
@@ -941,7 +939,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                     break;
                 case kWo:
                 case kW2: {  // partial row sums of this CTA's boxes of group g (c: this CTA's rank among its owners)
-                    const int c = blockIdx.x - ((g * r.nb + 1) * static_cast<int>(gridDim.x) - 1) / r.T;
+                    const int c = persist_contrib_slot(blockIdx.x, g, bi0, r.nb, r.T, gridDim.x);
                     if (!TP) {
                         float* q = p.cres + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows;
                         if (lane == 0) q[ra] = acc_a;

@@ -120,15 +120,29 @@ __host__ __device__ inline int persist_boxes_per_group(int K) {
 // The residual projections (out-proj, W2) are split evenly by boxes: CTA b of
 // G takes boxes [b*T/G, (b+1)*T/G) of T = (M/16) * nb; box tau belongs to
 // persist_owner_cta(tau).  A group's partial row sums come from the CTAs that
-// own its first to last box.
+// own its boxes, each writing one slot, summed in CTA order: with T >= G every
+// CTA owns a box, so they are the CTAs owner(first box) .. owner(last box);
+// with T < G a CTA owns at most one box and CTAs without a box lie between,
+// so the slot is the box's index within the group.
 __host__ __device__ inline int persist_owner_cta(long long tau, long long T, int G) {
     return static_cast<int>(((tau + 1) * G - 1) / T);
 }
+// Slots (contributing CTAs) of group g.  32-bit arithmetic: the split
+// projections have at most 256 groups of 8 boxes, and G is the SM count.
+__host__ __device__ inline int persist_group_contrib(int g, int nb, int T, int G) {
+    if (T < G) return nb;
+    return ((g * nb + nb) * G - 1) / T - ((g * nb + 1) * G - 1) / T + 1;
+}
+// Slot of CTA b among the contributors of group g, whose first box of the group is bi0.
+__host__ __device__ inline int persist_contrib_slot(int b, int g, int bi0, int nb, int T, int G) {
+    if (T < G) return bi0;
+    return b - ((g * nb + 1) * G - 1) / T;
+}
 inline int persist_max_contrib(int M, int K, int G) {
-    const long long nb = persist_boxes_per_group(K), T = static_cast<long long>(M / kPersistTileRows) * nb;
+    const int nb = persist_boxes_per_group(K), T = (M / kPersistTileRows) * nb;
     int c = 0;
-    for (long long g = 0; g < M / kPersistTileRows; ++g) {
-        const int n = persist_owner_cta(g * nb + nb - 1, T, G) - persist_owner_cta(g * nb, T, G) + 1;
+    for (int g = 0; g < M / kPersistTileRows; ++g) {
+        const int n = persist_group_contrib(g, nb, T, G);
         c = n > c ? n : c;
     }
     return c;
