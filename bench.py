@@ -404,7 +404,9 @@ def xl_arm(args) -> None:
         pre_dev.append(eng.last_device_ms())
     pre_ms = statistics.median(pre_dev)
     flops = prefill_flops(shape, PREFILL_N)
-    tf32_peak = float(pk.get("bf16_tflops", 1590.0)) / 2.0
+    tf32_peak, tf32_kind = measure_tf32_peak(torch), "measured: cuBLAS fp32 GEMM on TF32 tensor cores, 8192^3, best of 10"
+    if tf32_peak is None:
+        tf32_peak, tf32_kind = float(pk.get("bf16_tflops", 1590.0)) / 2.0, "half of the measured dense bf16 peak"
 
     batch_info = replica_batch(eng, rank, world, max_over_ranks, barrier)
     tp_info = None
@@ -435,7 +437,7 @@ def xl_arm(args) -> None:
                           "ms_per_token": 1e3 * (sum(r[1] for r in res) / 1e3) / (args.steps * DECODE)},
         "prefill": {"prompt": PREFILL_N, "device_ms": pre_ms, "ttft_ms": 1e3 * statistics.median(pre_wall),
                     "tokens_per_s": PREFILL_N / (pre_ms / 1e3), "tflops": flops / (pre_ms / 1e3) / 1e12,
-                    "tf32_peak_tflops": tf32_peak, "tf32_peak_kind": "half of the measured dense bf16 peak",
+                    "tf32_peak_tflops": tf32_peak, "tf32_peak_kind": tf32_kind,
                     "frac_of_tf32": flops / (pre_ms / 1e3) / 1e12 / tf32_peak,
                     "hbm_floor_ms": 1e3 * decode_bytes_per_token(shape, 0) / (hbm * 1e9)},
         "cpu_baseline": cpu,
@@ -453,6 +455,35 @@ def xl_arm(args) -> None:
         line["tp"] = tp_info
     print(json.dumps(line))
     sys.stdout.flush()
+
+
+def measure_tf32_peak(torch) -> float | None:
+    """Dense TF32 tensor-core throughput of this GPU (TFLOP/s): a cuBLAS fp32
+    GEMM with TF32 allowed, 8192^3, best of 10 by CUDA events.  The prefill's
+    roofline denominator (its 3xTF32 GEMMs run on the same tensor-core kind)."""
+    try:
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = True
+        n = 8192
+        a = torch.randn(n, n, device="cuda")
+        b = torch.randn(n, n, device="cuda")
+        c = torch.empty(n, n, device="cuda")
+        for _ in range(3):
+            torch.matmul(a, b, out=c)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b, out=c)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        torch.backends.cuda.matmul.allow_tf32 = prev
+        del a, b, c
+        torch.cuda.empty_cache()
+        return 2.0 * n ** 3 / (best / 1e3) / 1e12
+    except Exception:  # noqa: BLE001
+        return None
 
 
 def tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks) -> dict:

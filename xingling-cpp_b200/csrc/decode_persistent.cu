@@ -249,6 +249,11 @@ __device__ __forceinline__ float* xc_part(const PersistentParams& p, int r, int 
     return p.xc[r] +
            ((static_cast<size_t>(w2 * p.tp + src) * groups + g) * kPersistMaxContrib + c) * kPersistTileRows;
 }
+// This rank's partial sum of row `row` of group g (slot c) into its slot on
+// every rank (stores to peer memory over NVLink).
+__device__ __noinline__ void store_partials_tp(const PersistentParams& p, int w2, int g, int c, int row, float v) {
+    for (int r = 0; r < p.tp; ++r) xc_part(p, r, w2, p.rank, g, c)[row] = v;
+}
 // Phases whose results every rank needs: the out-projection and W2 of every
 // layer (in the tensor-parallel instantiation of the kernel).
 template <bool TP>
@@ -944,12 +949,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                         float* q = p.cres + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows;
                         if (lane == 0) q[ra] = acc_a;
                         if (lane == 1) q[rb] = acc_b;
-                    } else {
-                        for (int rr = 0; rr < p.tp; ++rr) {  // this rank's slot on every rank (NVLink stores)
-                            float* q = xc_part(p, rr, kind == kW2, p.rank, g, c);
-                            if (lane == 0) q[ra] = acc_a;
-                            if (lane == 1) q[rb] = acc_b;
-                        }
+                    } else if (lane < 2) {
+                        store_partials_tp(p, kind == kW2, g, c, lane == 0 ? ra : rb, lane == 0 ? acc_a : acc_b);
                     }
                     break;
                 }
