@@ -504,30 +504,33 @@ def tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, pa
     dist.broadcast_object_list(id_holder, src=0)
     eng = llm_cpp_engine.InferenceEngine(f"cuda:{local}", tp=world, rank=rank, nccl_id=id_holder[0])
     eng.set_option("decode_path", path)
+    eng.set_option("kernel_events", 1)  # the persistent kernel's own time, apart from the NCCL steps
     eng.load(WEIGHT_DIR)
     ids = S.prompt_ids(4, 64, S.FULL.vocab)
     n_dec = 256
 
     def run():
         tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
-        dev = 0.0
+        dev = kern = 0.0
         toks = [tok]
         for _ in range(n_dec):
             tok = eng.next_token(tok, top_p=0.0, repetition_penalty=1.0)
             dev += eng.last_device_ms()
+            kern += max(0.0, eng.last_kernel_ms())
             toks.append(tok)
-        return dev, toks
+        return dev, kern, toks
 
     run()
     dist.barrier()
     n0 = llm_cpp_engine.kernel_launches()
-    dev, toks = run()
+    dev, kern, toks = run()
     launches = llm_cpp_engine.kernel_launches() - n0
     dev = max_over_ranks(dev)
+    kern = max_over_ranks(kern)
     del eng
     return {"tp": world, "prompt": 64, "decode_tokens": n_dec, "ms_per_token": dev / n_dec,
             "tokens_per_s": n_dec / (dev / 1e3), "first_tokens": toks[:8], "decode_path": path,
-            "gpu_launches": launches}
+            "persistent_kernel_ms_per_token": kern / n_dec if path == 0 else None, "gpu_launches": launches}
 
 
 def replica_batch(eng, rank, world, max_over_ranks, barrier) -> dict:

@@ -45,10 +45,10 @@
 // rank runs its heads, FFN columns and vocab shard; the out-projection and W2
 // partial row sums of every CTA are stored straight into every rank's
 // exchange buffer (peer memory, NVLink) and counted on every rank's counter
-// for that layer with a system-scope release, so the next staging on each
-// rank sums all ranks' partials, in the same (rank, CTA) order everywhere,
-// without a collective launch.  The counters only grow, by tp * grid * 8 per
-// layer and step, so nothing resets them between steps.
+// for that layer after one system-scope fence per CTA, so the next staging on
+// each rank sums all ranks' partials, in the same (rank, CTA) order
+// everywhere, without a collective launch.  The counters only grow, by
+// tp * grid per layer and step, so nothing resets them between steps.
 //
 // Every wait is bounded: a timed-out wait sets a bit in DevState::err, makes
 // the other CTAs leave at their next wait, and the producer drains its
@@ -369,10 +369,9 @@ template <bool TP>
 __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
     const int kind = phase_kind(ph, p.layers);
     if (cross_rank<TP>(kind)) {
-        // Every consumer warp of every CTA of every rank, counted up across steps.
+        // Every CTA of every rank, counted up across steps.
         if (threadIdx.x == 32) {
-            const unsigned long long target =
-                static_cast<unsigned long long>(p.st->epoch + 1) * p.tp * gridDim.x * kConsumerWarps;
+            const unsigned long long target = static_cast<unsigned long long>(p.st->epoch + 1) * p.tp * gridDim.x;
             const unsigned long long* c = p.xdone[p.rank] + (ph / 5) * 2 + (kind == kW2);
             uint32_t it = 0;
             unsigned long long t0 = 0;
@@ -426,19 +425,25 @@ __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
 // Each warp publishes its own stores of phase ph as soon as it has issued
 // them: lane 0 releases (cumulative over the warp's lanes, ordered by the
 // __syncwarp) and adds 1 to the counter, so no warp waits for its CTA.
+// Tensor parallel, the split projections: the partial sums went to every
+// rank, so the release is at system scope, and one per CTA (once all its
+// consumer warps have stored theirs: the barrier orders their stores before
+// the fence), then one count on every rank.
 template <bool TP>
 __device__ void signal_phase(const PersistentParams& p, int ph) {
-    __syncwarp();
-    if ((threadIdx.x & 31) != 0) return;
     const int kind = phase_kind(ph, p.layers);
     if (cross_rank<TP>(kind)) {
-        // The partial sums went to every rank: release at system scope, then count on every rank.
-        const int slot = (ph / 5) * 2 + (kind == kW2);
-        for (int r = 0; r < p.tp; ++r)
-            asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(p.xdone[r] + slot) : "memory");
-    } else {
-        asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.done + ph) : "memory");
+        consumer_sync();
+        if (threadIdx.x == 32) {
+            const int slot = (ph / 5) * 2 + (kind == kW2);
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
+            for (int r = 0; r < p.tp; ++r)
+                asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(p.xdone[r] + slot) : "memory");
+        }
+        return;
     }
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.done + ph) : "memory");
 }
 
 // Block-wide (consumers) sum of one float per thread.

@@ -182,8 +182,8 @@ struct PersistentParams {
     // Tensor parallel (tp > 1): every CTA writes its out-projection / W2 partial
     // row sums into every rank's exchange buffer xc[r] (peer memory over NVLink),
     // laid out [2 (out-proj, W2)][tp][H/16][kPersistMaxContrib][16], and counts
-    // them on every rank's xdone[r][layer * 2 + (W2)], counters that only grow
-    // (target (epoch + 1) * tp * grid * 8 in a step).
+    // them on every rank's xdone[r][layer * 2 + (W2)], one count per CTA,
+    // counters that only grow (target (epoch + 1) * tp * grid in a step).
     int tp, rank;
     int v0;                     // global id of this rank's vocab row 0 (argmax keys carry global ids)
     float* xc[kMaxTp];
