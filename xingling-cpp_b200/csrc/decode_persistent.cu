@@ -43,12 +43,13 @@
 //
 // Tensor parallel (one kernel per rank, each on its own GPU, same grid): each
 // rank runs its heads, FFN columns and vocab shard; the out-projection and W2
-// partial row sums of every CTA are stored straight into every rank's
-// exchange buffer (peer memory, NVLink) and counted on every rank's counter
-// for that layer after one system-scope fence per CTA, so the next staging on
-// each rank sums all ranks' partials, in the same (rank, CTA) order
-// everywhere, without a collective launch.  The counters only grow, by
-// tp * grid per layer and step, so nothing resets them between steps.
+// partial row sums of every CTA are stored, each as one 64-bit word of value
+// and tag (step, layer, projection), into this rank's exchange buffer before
+// the phase signal and into every peer's (NVLink) after it, so the next
+// staging on each rank waits for its own CTAs on the usual counter and for
+// the peers' words by their tags, and sums all ranks' partials in the same
+// (rank, CTA) order everywhere: no collective launch and no system-scope
+// fence.
 //
 // Every wait is bounded: a timed-out wait sets a bit in DevState::err, makes
 // the other CTAs leave at their next wait, and the producer drains its
@@ -243,24 +244,45 @@ __device__ __forceinline__ Boxes boxes_of(const Gemv& d) {
 
 // Tensor parallel: rank r's exchange slot for the partial row sums that rank
 // src's CTA c computed for 16-row group g of a split projection (w2 = 0: the
-// out-projection, 1: W2).
-__device__ __forceinline__ float* xc_part(const PersistentParams& p, int r, int w2, int src, int g, int c) {
+// out-projection, 1: W2).  A slot holds one word per row: the float's bits
+// in the low half, the tag of the step, layer and projection in the high half,
+// stored and loaded as one 64-bit access, so a reader that sees the tag it
+// expects holds that word's value (no fence on either side).
+__device__ __forceinline__ unsigned long long* xc_part(const PersistentParams& p, int r, int w2, int src, int g,
+                                                       int c) {
     const int groups = p.H / kPersistTileRows;
     return p.xc[r] +
            ((static_cast<size_t>(w2 * p.tp + src) * groups + g) * kPersistMaxContrib + c) * kPersistTileRows;
 }
-// This rank's partial sum of row `row` of group g (slot c) into its slot on
-// every rank (stores to peer memory over NVLink).
-__device__ __noinline__ void store_partials_tp(const PersistentParams& p, int w2, int g, int c, int row, float v) {
-    for (int r = 0; r < p.tp; ++r) xc_part(p, r, w2, p.rank, g, c)[row] = v;
+// Tag of layer l's split projection w2 in this step: grows with every use, and
+// the buffers start zeroed, so a stale word never carries it.
+__device__ __forceinline__ unsigned xtag(const PersistentParams& p, int l, int w2) {
+    return static_cast<unsigned>(p.st->epoch) * (2u * static_cast<unsigned>(p.layers)) + 2u * l + w2 + 1u;
 }
-// Phases whose results every rank needs: the out-projection and W2 of every
-// layer (in the tensor-parallel instantiation of the kernel).
-template <bool TP>
-__device__ __forceinline__ bool cross_rank(int kind) {
-    return TP && (kind == kWo || kind == kW2);
+__device__ __forceinline__ unsigned long long xword(float v, unsigned tag) {
+    return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
 }
-
+// This rank's partial sum of row `row` of group g (slot c) of layer l's split
+// projection w2, tagged, into its own exchange buffer.
+__device__ __noinline__ void store_own_tp(const PersistentParams& p, int l, int w2, int g, int c, int row, float v) {
+    xc_part(p, p.rank, w2, p.rank, g, c)[row] = xword(v, xtag(p, l, w2));
+}
+// After this warp's phase signal: its partial sums of the phase (row `row` of
+// each group of boxes [r.t0, r.t1), already in this rank's own slots) go to
+// the same slots on every other rank (stores to peer memory over NVLink).
+__device__ __noinline__ void forward_partials_tp(const PersistentParams& p, int t0, int t1, int nb, int T, int w2,
+                                                 int row) {
+    for (int tau = t0; tau < t1;) {
+        const int g = tau / nb, bi0 = tau % nb, bi1 = min(nb, bi0 + (t1 - tau));
+        const int c = persist_contrib_slot(blockIdx.x, g, bi0, nb, T, gridDim.x);
+        const unsigned long long w = xc_part(p, p.rank, w2, p.rank, g, c)[row];  // this thread's own store
+        for (int r = 0; r < p.tp; ++r)
+            if (r != p.rank)
+                asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(xc_part(p, r, w2, p.rank, g, c) + row), "l"(w)
+                             : "memory");
+        tau += bi1 - bi0;
+    }
+}
 // ---------------------------------------------------------------------------
 // Producer: walks this CTA's boxes of every GEMV phase in order.
 struct Cursor {
@@ -365,37 +387,8 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
 // Consumer helpers (256 threads, named barrier 1).
 
 // Wait until phase ph is complete (its counter reaches its target).
-template <bool TP>
 __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
     const int kind = phase_kind(ph, p.layers);
-    if (cross_rank<TP>(kind)) {
-        // Every CTA of every rank, counted up across steps.
-        if (threadIdx.x == 32) {
-            const unsigned long long target = static_cast<unsigned long long>(p.st->epoch + 1) * p.tp * gridDim.x;
-            const unsigned long long* c = p.xdone[p.rank] + (ph / 5) * 2 + (kind == kW2);
-            uint32_t it = 0;
-            unsigned long long t0 = 0;
-            int ok = 1;
-            for (;;) {
-                unsigned long long v;
-                asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(c) : "memory");
-                if (v >= target) break;
-                ++it;
-                if ((it & 255u) == 0) {
-                    const unsigned long long now = globaltimer();
-                    if (t0 == 0) t0 = now;
-                    if (it >= kFlagSpinLimit || now - t0 > kWaitLimitNs || aborted(p.st)) {
-                        atomicOr(&p.st->err, kErrFlag);
-                        ok = 0;
-                        break;
-                    }
-                }
-            }
-            *s_ok = ok;
-        }
-        consumer_sync();
-        return *s_ok != 0;
-    }
     // An attention phase is signalled once per head (by the warp that writes
     // the head's output); every other phase by every consumer warp of every CTA.
     const int target = kind == kAttn ? p.heads : static_cast<int>(gridDim.x) * kConsumerWarps;
@@ -425,23 +418,7 @@ __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
 // Each warp publishes its own stores of phase ph as soon as it has issued
 // them: lane 0 releases (cumulative over the warp's lanes, ordered by the
 // __syncwarp) and adds 1 to the counter, so no warp waits for its CTA.
-// Tensor parallel, the split projections: the partial sums went to every
-// rank, so the release is at system scope, and one per CTA (once all its
-// consumer warps have stored theirs: the barrier orders their stores before
-// the fence), then one count on every rank.
-template <bool TP>
 __device__ void signal_phase(const PersistentParams& p, int ph) {
-    const int kind = phase_kind(ph, p.layers);
-    if (cross_rank<TP>(kind)) {
-        consumer_sync();
-        if (threadIdx.x == 32) {
-            const int slot = (ph / 5) * 2 + (kind == kW2);
-            asm volatile("fence.acq_rel.sys;" ::: "memory");
-            for (int r = 0; r < p.tp; ++r)
-                asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(p.xdone[r] + slot) : "memory");
-        }
-        return;
-    }
     __syncwarp();
     if ((threadIdx.x & 31) == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.done + ph) : "memory");
 }
@@ -550,29 +527,61 @@ __device__ __noinline__ void stage_norm(const PersistentParams& p, const float* 
 // Tensor parallel: as residual_quad, with the partial row sums of every rank
 // (already in this rank's exchange buffer) added in (rank, CTA) order, so that
 // every rank computes the same residual.
+__device__ __forceinline__ void ld_words(const unsigned long long* a, unsigned long long& x, unsigned long long& y) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(a) : "memory");
+}
 __device__ __forceinline__ float4 residual_quad_tp(const PersistentParams& p, const float* x_old, const float* bias,
-                                                   int w2, int q, int nb, int T) {
+                                                   int w2, int q, int nb, int T, unsigned tag) {
     const int g = (4 * q) / kPersistTileRows;
     const int G = gridDim.x;
     const int nc = persist_group_contrib(g, nb, T, G);
     const int qq = q % (kPersistTileRows / 4);
     float4 s = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (int src = 0; src < p.tp; ++src) {
-        const float4* part = reinterpret_cast<const float4*>(xc_part(p, p.rank, w2, src, g, 0)) + qq;
-        float4 v[kPersistMaxContrib];
+        const unsigned long long* part = xc_part(p, p.rank, w2, src, g, 0) + 4 * qq;
+        unsigned long long w[kPersistMaxContrib][4];
+        // Spin until every word carries this use's tag (bounded like every wait).
+        uint32_t it = 0;
+        unsigned long long t0 = 0;
+        for (;;) {
 #pragma unroll
-        for (int c = 0; c < kPersistMaxContrib; ++c)
-            v[c] = c < nc ? __ldcg(part + c * (kPersistTileRows / 4)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int c = 0; c < kPersistMaxContrib; ++c) {
+                if (c < nc) {
+                    ld_words(part + c * kPersistTileRows, w[c][0], w[c][1]);
+                    ld_words(part + c * kPersistTileRows + 2, w[c][2], w[c][3]);
+                }
+            }
+            bool ok = true;
+#pragma unroll
+            for (int c = 0; c < kPersistMaxContrib; ++c)
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (c < nc && static_cast<unsigned>(w[c][k] >> 32) != tag) ok = false;
+            if (ok) break;
+            ++it;
+            if ((it & 15u) == 0) {
+                const unsigned long long now = globaltimer();
+                if (t0 == 0) t0 = now;
+                if (it >= kFlagSpinLimit || now - t0 > kWaitLimitNs || aborted(p.st)) {
+                    atomicOr(&p.st->err, kErrFlag);
+                    break;
+                }
+            }
+        }
 #pragma unroll
         for (int c = 0; c < kPersistMaxContrib; ++c) {
             if (c < nc) {
+                const float4 v = make_float4(__uint_as_float(static_cast<unsigned>(w[c][0])),
+                                             __uint_as_float(static_cast<unsigned>(w[c][1])),
+                                             __uint_as_float(static_cast<unsigned>(w[c][2])),
+                                             __uint_as_float(static_cast<unsigned>(w[c][3])));
                 if (src == 0 && c == 0) {
-                    s = v[0];
+                    s = v;
                 } else {
-                    s.x += v[c].x;
-                    s.y += v[c].y;
-                    s.z += v[c].z;
-                    s.w += v[c].w;
+                    s.x += v.x;
+                    s.y += v.y;
+                    s.z += v.z;
+                    s.w += v.w;
                 }
             }
         }
@@ -583,9 +592,10 @@ __device__ __forceinline__ float4 residual_quad_tp(const PersistentParams& p, co
 }
 
 // stage_norm for tensor parallel: the residual after a split projection whose
-// partial sums all ranks exchanged (w2: which projection).
+// partial sums all ranks exchanged (w2: which projection; tag: its use).
 __device__ __noinline__ void stage_norm_tp(const PersistentParams& p, const float* x_old, const float* bias, int w2,
-                                           int nb, const float* gamma, float* xs, float* red, float* x_out) {
+                                           unsigned tag, int nb, const float* gamma, float* xs, float* red,
+                                           float* x_out) {
     const int t = threadIdx.x - 32;
     const int K = p.H;
     const int T = (K / kPersistTileRows) * nb;
@@ -600,7 +610,7 @@ __device__ __noinline__ void stage_norm_tp(const PersistentParams& p, const floa
         const int q = t + k * kConsumerThreads;
         if (q < (K >> 2)) {
             gk[k] = g4[q];
-            const float4 v = residual_quad_tp(p, x_old, bias, w2, q, nb, T);
+            const float4 v = residual_quad_tp(p, x_old, bias, w2, q, nb, T, tag);
             x4[q] = v;
             const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -692,7 +702,7 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
     // A CTA without an attention item neither waits nor signals: the next
     // phase waits for the heads' outputs, which imply the QKV phase.
     if (!has) return true;
-    if (!wait_phase<false>(p, ph - 1, s_ok)) return false;
+    if (!wait_phase(p, ph - 1, s_ok)) return false;
     if (t == 0) trace_at(p, ph, kTrConsStart);
     float* qsh = xs + warp * kAttnWarpScratch;
     float* apart = xs + kConsumerWarps * kAttnWarpScratch;  // [8][68]
@@ -773,7 +783,7 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
     float2* out = reinterpret_cast<float2*>(p.att + h * kHeadDim);
     if (nct == 1) {
         out[lane] = make_float2(acc.x / L, acc.y / L);
-        signal_phase<false>(p, ph);
+        signal_phase(p, ph);
         return true;
     }
     // A head split over nct CTAs: the last CTA to finish merges their partials.
@@ -806,7 +816,7 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
         acc2.y = fmaf(wt, ok.y, acc2.y);
     }
     out[lane] = make_float2(acc2.x / L2, acc2.y / L2);
-    signal_phase<false>(p, ph);
+    signal_phase(p, ph);
     return true;
 }
 
@@ -854,7 +864,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 }
             }
         }
-        if (ph > 0 && !wait_phase<TP>(p, ph - 1, s_ok)) return;
+        if (ph > 0 && !wait_phase(p, ph - 1, s_ok)) return;
         if (t == 0) trace_at(p, ph, kTrConsStart);
         // Stage this phase's input vector.
         if (kind == kQKV) {
@@ -862,21 +872,21 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 stage_norm(p, p.emb + static_cast<size_t>(st->in.token_in) * p.H, nullptr, nullptr, 0, y->g1, xs, red,
                            p.xa);
             else if (TP)
-                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, nb_w2, y->g1, xs, red, p.xa);
+                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, xtag(p, l - 1, 1), nb_w2, y->g1, xs, red, p.xa);
             else
                 stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, y->g1, xs, red, p.xa);
         } else if (kind == kWo) {
             stage_copy(p.att, p.Hl, xs);
         } else if (kind == kW13) {
             if (TP)
-                stage_norm_tp(p, p.xa, y->bo, 0, nb_wo, y->g2, xs, red, p.xb);
+                stage_norm_tp(p, p.xa, y->bo, 0, xtag(p, l, 0), nb_wo, y->g2, xs, red, p.xb);
             else
                 stage_norm(p, p.xa, y->bo, p.cres, nb_wo, y->g2, xs, red, p.xb);
         } else if (kind == kW2) {
             stage_copy(p.ffh, p.Fl, xs);
         } else {  // kLM
             if (TP)
-                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, nb_w2, p.gnorm, xs, red, p.xa);
+                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, xtag(p, l - 1, 1), nb_w2, p.gnorm, xs, red, p.xa);
             else
                 stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, p.gnorm, xs, red, p.xa);
         }
@@ -954,8 +964,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                         float* q = p.cres + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows;
                         if (lane == 0) q[ra] = acc_a;
                         if (lane == 1) q[rb] = acc_b;
-                    } else if (lane < 2) {
-                        store_partials_tp(p, kind == kW2, g, c, lane == 0 ? ra : rb, lane == 0 ? acc_a : acc_b);
+                    } else if (lane < 2) {  // this rank's own slot; forwarded to the peers after the signal
+                        store_own_tp(p, l, kind == kW2, g, c, lane == 0 ? ra : rb, lane == 0 ? acc_a : acc_b);
                     }
                     break;
                 }
@@ -978,7 +988,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 }
             }
         }
-        if (kind != kLM) signal_phase<TP>(p, ph);
+        if (kind != kLM) signal_phase(p, ph);
+        if (TP && split && lane < 2) forward_partials_tp(p, r.t0, r.t1, r.nb, r.T, kind == kW2, lane == 0 ? ra : rb);
         if (t == 0) trace_at(p, ph, kTrConsEnd);
     }
     // LM head: CTA argmax -> global max; the last CTA publishes the winner.
@@ -1055,7 +1066,7 @@ cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cud
     if (p.tp < 1 || p.tp > kMaxTp || p.rank < 0 || p.rank >= p.tp || (p.tp > 1 && p.finish_greedy))
         return cudaErrorInvalidValue;
     for (int r = 0; r < p.tp && p.tp > 1; ++r)
-        if (!p.xc[r] || !p.xdone[r]) return cudaErrorInvalidValue;
+        if (!p.xc[r]) return cudaErrorInvalidValue;
     if (persist_max_contrib(p.H, p.Hl, num_sms) > kPersistMaxContrib ||
         persist_max_contrib(p.H, p.Fl, num_sms) > kPersistMaxContrib)
         return cudaErrorInvalidValue;

@@ -303,9 +303,9 @@ int Engine::alloc_all() {
     if (tp_ > 1 && tp_ <= kMaxTp) {
         // Its own allocation, so that the peers can map it (an IPC handle covers a whole allocation).
         const size_t xc = 2 * static_cast<size_t>(tp_) * (H / kPersistTileRows) * kPersistMaxContrib *
-                          kPersistTileRows * 4;
-        XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&xbuf_), xdone_bytes() + xc));
-        XL_CUDA(cudaMemset(xbuf_, 0, xdone_bytes() + xc));
+                          kPersistTileRows * 8;
+        XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&xbuf_), xc));
+        XL_CUDA(cudaMemset(xbuf_, 0, xc));  // tag 0: no use has written a word yet
     }
     size_t off = 0;
     for (auto& pr : plan) {
@@ -648,10 +648,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     p.tp = tp_;
     p.rank = rank_;
     if (tpk) {
-        for (int r = 0; r < tp_; ++r) {
-            p.xdone[r] = reinterpret_cast<unsigned long long*>(xpeer_[r]);
-            p.xc[r] = reinterpret_cast<float*>(xpeer_[r] + xdone_bytes());
-        }
+        for (int r = 0; r < tp_; ++r) p.xc[r] = reinterpret_cast<unsigned long long*>(xpeer_[r]);
         // The ranks' kernels wait on one another (with a time limit), so they
         // start together, after a one-word NCCL barrier: the hosts may launch
         // a step at very different times.

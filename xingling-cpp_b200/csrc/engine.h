@@ -157,13 +157,12 @@ class Engine {
     long long gen_graph_kernels_ = 0, gen_graph_kernels_s_ = 0;
     ncclComm_t comm_ = nullptr;
     // Tensor parallel, persistent decode: this rank's exchange buffer (its own
-    // allocation, exported over CUDA IPC): counters [layers][2] (u64), then
-    // the partial sums [2][tp][H/16][kPersistMaxContrib][16]; and every
-    // rank's buffer mapped here (xpeer_[rank_] == xbuf_).
+    // allocation, exported over CUDA IPC): the tagged partial sums
+    // [2][tp][H/16][kPersistMaxContrib][16] (u64); and every rank's buffer
+    // mapped here (xpeer_[rank_] == xbuf_).
     char* xbuf_ = nullptr;
     char* xpeer_[kMaxTp] = {};
     bool peers_ = false;
-    size_t xdone_bytes() const { return (static_cast<size_t>(cfg_.layers) * 2 * 8 + 255) / 256 * 256; }
 
     int decode_path_ = 0;      // 0: persistent kernel (where it fits), 1: per-op kernels
     int prefill_gemm_ = 0;     // 0: tcgen05 3xTF32, 1: fp32 SIMT tiles

@@ -181,13 +181,12 @@ struct PersistentParams {
     int tma_evict_first;        // 1: weight boxes are loaded with an L2 evict-first policy
     // Tensor parallel (tp > 1): every CTA writes its out-projection / W2 partial
     // row sums into every rank's exchange buffer xc[r] (peer memory over NVLink),
-    // laid out [2 (out-proj, W2)][tp][H/16][kPersistMaxContrib][16], and counts
-    // them on every rank's xdone[r][layer * 2 + (W2)], one count per CTA,
-    // counters that only grow (target (epoch + 1) * tp * grid in a step).
+    // laid out [2 (out-proj, W2)][tp][H/16][kPersistMaxContrib][16] words of
+    // (tag << 32 | float bits); the tag of layer l's projection w2 in step e is
+    // e * 2 * layers + 2 l + w2 + 1 (e = DevState::epoch).
     int tp, rank;
     int v0;                     // global id of this rank's vocab row 0 (argmax keys carry global ids)
-    float* xc[kMaxTp];
-    unsigned long long* xdone[kMaxTp];
+    unsigned long long* xc[kMaxTp];
 };
 constexpr int kTraceFields = 5;
 size_t persistent_smem_bytes();
