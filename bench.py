@@ -411,7 +411,10 @@ def xl_arm(args) -> None:
     batch_info = replica_batch(eng, rank, world, max_over_ranks, barrier)
     tp_info = None
     if world > 1:
-        tp_info = tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks)
+        try:  # a sub-measurement: a failure here is reported in the line, not lost with it
+            tp_info = tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks)
+        except Exception as e:  # noqa: BLE001
+            tp_info = {"tp": world, "error": repr(e)[:300]}
 
     if rank != 0:
         return
