@@ -494,7 +494,7 @@ def tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks) -
     on the persistent path (the split projections' partial sums exchanged over
     NVLink inside the kernel) and on the per-op path (NCCL all-reduces) for
     comparison."""
-    out = tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, 0)
+    out = tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, 0, trace=args.tp_only)
     per_op = tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, 1)
     out["per_op_ms_per_token"] = per_op["ms_per_token"]
     out["per_op_first_tokens"] = per_op["first_tokens"]
@@ -502,7 +502,43 @@ def tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks) -
     return out
 
 
-def tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, path) -> dict:
+PHASE_KINDS = ["QKV", "attention", "out-projection", "W1/V", "W2"]
+
+
+def phase_summary(raw: bytes, sms: int, layers: int) -> dict:
+    """Per-phase times (us) of one persistent decode step from its phase_trace
+    stamps ([CTA][phase][start, staged, end, producer first, producer last],
+    %globaltimer ns): per phase kind, the mean over layers of the median CTA's
+    staging (start -> staged) and consume (staged -> end) times, and of the
+    phase total (median CTA end of the phase minus that of the phase before)."""
+    import numpy as np
+
+    a = np.frombuffer(raw, dtype=np.uint64).reshape(sms, 5 * layers + 1, 5).astype(np.float64)
+
+    def med(col):
+        v = col[col > 0]
+        return float(np.median(v)) if v.size else float("nan")
+
+    ends = [med(a[:, ph, 2]) for ph in range(5 * layers + 1)]
+    out = {}
+    for k, name in enumerate(PHASE_KINDS + ["LM head"]):
+        phs = [5 * layers] if k == 5 else [5 * l + k for l in range(layers)]
+        stg, con, tot = [], [], []
+        for ph in phs:
+            ok = (a[:, ph, 0] > 0) & (a[:, ph, 1] > 0) & (a[:, ph, 2] > 0)
+            if ok.any():
+                stg.append(float(np.median(a[ok, ph, 1] - a[ok, ph, 0])) / 1e3)
+                con.append(float(np.median(a[ok, ph, 2] - a[ok, ph, 1])) / 1e3)
+            if ph > 0:
+                tot.append((ends[ph] - ends[ph - 1]) / 1e3)
+        out[name] = {"staging_us": float(np.mean(stg)) if stg else None,
+                     "consume_us": float(np.mean(con)) if con else None,
+                     "phase_us": float(np.mean(tot)) if tot else None}
+    out["step_us"] = (ends[-1] - med(a[:, 0, 0])) / 1e3
+    return out
+
+
+def tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, path, trace=False) -> dict:
     id_holder = [llm_cpp_engine.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(id_holder, src=0)
     eng = llm_cpp_engine.InferenceEngine(f"cuda:{local}", tp=world, rank=rank, nccl_id=id_holder[0])
@@ -530,10 +566,26 @@ def tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, pa
     launches = llm_cpp_engine.kernel_launches() - n0
     dev = max_over_ranks(dev)
     kern = max_over_ranks(kern)
+    phases = None
+    if trace and path == 0:
+        # Phase timeline of one more step (the kernel stamps %globaltimer itself), rank 0's.
+        import torch
+
+        eng.set_option("phase_trace", 1)
+        tok = toks[-1]
+        for _ in range(4):
+            tok = eng.next_token(tok, top_p=0.0, repetition_penalty=1.0)
+        sms = torch.cuda.get_device_properties(local).multi_processor_count
+        raw = eng.phase_trace(sms * (5 * S.FULL.layers + 1) * 5)
+        phases = phase_summary(raw, sms, S.FULL.layers)
+        phases["context"] = 64 + n_dec + 4
     del eng
-    return {"tp": world, "prompt": 64, "decode_tokens": n_dec, "ms_per_token": dev / n_dec,
-            "tokens_per_s": n_dec / (dev / 1e3), "first_tokens": toks[:8], "decode_path": path,
-            "persistent_kernel_ms_per_token": kern / n_dec if path == 0 else None, "gpu_launches": launches}
+    out = {"tp": world, "prompt": 64, "decode_tokens": n_dec, "ms_per_token": dev / n_dec,
+           "tokens_per_s": n_dec / (dev / 1e3), "first_tokens": toks[:8], "decode_path": path,
+           "persistent_kernel_ms_per_token": kern / n_dec if path == 0 else None, "gpu_launches": launches}
+    if phases is not None:
+        out["phase_timeline_rank0"] = phases
+    return out
 
 
 def replica_batch(eng, rank, world, max_over_ranks, barrier) -> dict:
