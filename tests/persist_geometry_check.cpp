@@ -7,7 +7,8 @@
 //    contributing CTAs must be distinct, below persist_group_contrib, cover
 //    every slot the staging sums (no slot left unwritten, which would be read
 //    stale) and rise with the CTA index (the summation order);
-//  * persist_max_contrib is the largest per-group count.
+//  * persist_max_contrib is the largest per-group count;
+//  * the full model fits the kernel at every tensor-parallel width.
 // Prints "ok" and exits 0, or prints the first failure and exits 1.
 #include <cstdio>
 #include <vector>
@@ -66,8 +67,24 @@ static int check_slots(int M, int K, int G) {
     return 0;
 }
 
+// XingLing-0.68B (hidden 1536, 24 heads, ffn 4096, context 768) on 148 SMs
+// takes the persistent kernel at TP 1, 2, 4 and 8: shard widths are multiples
+// of 64, each row group of the split projections has at most
+// kPersistMaxContrib contributors, and the attention items fit the grid.
+static int check_model_fits() {
+    const int H = 1536, heads = 24, F = 4096, ctx = 768, G = 148;
+    for (int tp : {1, 2, 4, 8}) {
+        const int Hl = H / tp, Fl = F / tp, hl = heads / tp;
+        if (Hl % kPersistKAlign || Fl % kPersistKAlign) return fail("shard width", H, Hl, tp, -1);
+        if (persist_max_contrib(H, Hl, G) > kPersistMaxContrib) return fail("out-proj contributors", H, Hl, tp, -1);
+        if (persist_max_contrib(H, Fl, G) > kPersistMaxContrib) return fail("W2 contributors", H, Fl, tp, -1);
+        if (hl * persist_attn_ctas_per_head(ctx) > G) return fail("attention items", H, hl, tp, -1);
+    }
+    return 0;
+}
+
 int main() {
-    int rc = 0;
+    int rc = check_model_fits();
     for (int K = kPersistKAlign; K <= 4096 && !rc; K += kPersistKAlign) rc = check_boxes(K);
     const int Ms[] = {256, 384, 640, 1024, 1536, 2048, 4096};
     const int Gs[] = {148, 132, 80, 8};
