@@ -68,7 +68,10 @@ XL_API void xl_config_default(xl_config* cfg);
  * buffers once.  tp_size / tp_rank / nccl_id select tensor-parallel decode:
  * tp_size 1 ignores the other two; otherwise nccl_id points to the
  * XL_NCCL_ID_BYTES bytes from xl_nccl_unique_id() on rank 0, shared by all
- * ranks, and every rank must create its engine concurrently. */
+ * ranks, and every rank must create its engine concurrently, one process per
+ * GPU of one node: creation also maps every rank's exchange buffer over CUDA
+ * IPC (the persistent decode kernel writes its partial sums there) and fails
+ * with XL_ERR_CUDA if a mapping cannot be made. */
 #define XL_NCCL_ID_BYTES 128
 XL_API int xl_engine_create(const xl_config* cfg, int device, int tp_size, int tp_rank, const void* nccl_id,
                             xl_engine** out);
