@@ -256,7 +256,10 @@ XL_API int xl_rope_table(float base, int max_ctx, float* out);
 
 /* RoPE::forward_vec (src/rope.cu:130-165) + KV append +
  * MultiHeadAttention::forward (src/attn.cu:490-547) for one token at
- * position pos (device int).  qkv = [q | k | v] of `heads` heads (pre-RoPE);
+ * position pos (device int, 0 <= pos < max_ctx: a position outside that
+ * range leaves the caches untouched and writes NaN to every output, since the
+ * value is on the device and the call does not synchronize to check it).
+ * qkv = [q | k | v] of `heads` heads (pre-RoPE);
  * kc / vc are head-major [heads][max_ctx][64].  workspace: at least
  * xl_op_attn_decode_workspace_bytes(heads, max_ctx) bytes, zero-filled
  * before first use (the kernel leaves it zeroed). */
@@ -277,7 +280,9 @@ XL_API int xl_op_attn_decode(const float* qkv, const float* rope, float* kc, flo
  * the array's device address with that device current; make that first call
  * before any stream capture.  All calls share the one array: calls that
  * overlap on the GPU (other streams, other threads) race on it, so order them
- * on one stream.  Same arguments and results as xl_op_attn_decode. */
+ * on one stream.  Same arguments, results and position precondition
+ * (0 <= pos < max_ctx, else NaN outputs and untouched caches) as
+ * xl_op_attn_decode. */
 XL_API int xl_op_attn_decode_noalloc(const float* qkv, const float* rope, float* kc, float* vc, float* out,
                                      const int* pos, int heads, int max_ctx, void* stream);
 

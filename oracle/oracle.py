@@ -24,7 +24,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "_build", "libxloracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libxlref.so")
-REFERENCE_SRC = os.environ.get("XL_REFERENCE_SRC", "/root/reference")
+# The reference checkout: XL_REFERENCE_SRC, else the directory `reference`
+# beside this repository's root.
+REFERENCE_SRC = os.environ.get("XL_REFERENCE_SRC",
+                               os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 _f = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _i = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")

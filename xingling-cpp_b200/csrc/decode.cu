@@ -222,6 +222,13 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnDecodeParams
     pdl_wait();
 
     const int n = *p.pos;
+    // A position outside [0, max_ctx) would write the caches, read the RoPE
+    // table and index the split partials out of range: nothing is touched,
+    // and the head's output is NaN so that the caller sees the error.
+    if (n < 0 || n >= p.max_ctx) {
+        if (s == 0 && tid < kHeadDim) p.out[h * kHeadDim + tid] = __int_as_float(0x7fc00000);
+        return;
+    }
     const int total = n + 1;
     const int nsplit = (total + kAttnChunk - 1) / kAttnChunk;
     if (s >= nsplit) return;

@@ -78,6 +78,9 @@ constexpr uint32_t kMbarSpinLimit = 1u << 24;
 constexpr uint32_t kFlagSpinLimit = 1u << 24;
 constexpr unsigned long long kWaitLimitNs = 200ull * 1000 * 1000;
 constexpr int kErrMbar = 1, kErrFlag = 2;
+// Tensor parallel: the step-start liveness sum (every rank adds 1) did not
+// reach tp, so a peer never joined this step (its all-reduce was aborted).
+constexpr int kErrPeer = 16;
 // Attention scratch inside the staging buffer xs (free between the QKV and
 // out-projection stagings): per warp the rotated q (64 floats), then per warp
 // (max, sum, o[64]) partials, then per warp the rotated k of the new position.
@@ -1044,6 +1047,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     pdl_wait();
     // A stopped device-side generation: nothing to do this step (every CTA reads the same flag).
     if (p.st->in.skip) return;
+    // Tensor parallel: every rank adds 1 to tp_sync in the step-start
+    // all-reduce.  A smaller sum means a peer did not join (the host aborted
+    // the communicator after its step timeout): leave before any load or any
+    // store to peer memory.  Every CTA reads the same word.
+    if (TP && *reinterpret_cast<const volatile int*>(&p.st->tp_sync) != p.tp) {
+        if (threadIdx.x == 0) atomicOr(&p.st->err, kErrPeer);
+        return;
+    }
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) producer(p, ring, full, empty, quiet);
     } else {

@@ -165,6 +165,7 @@ int Engine::init(const xl_config& cfg, int device, int tp_size, int tp_rank, con
     XL_CUDA(cudaEventCreate(&ev1_));
     XL_CUDA(cudaEventCreate(&kev0_));
     XL_CUDA(cudaEventCreate(&kev1_));
+    XL_CUDA(cudaEventCreateWithFlags(&ev_sync_, cudaEventDisableTiming));
     XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_in_), sizeof(DevState), cudaHostAllocDefault));
     XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_out_), sizeof(DevState), cudaHostAllocDefault));
     XL_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&h_gen_), sizeof(GenCtl) + 2 * static_cast<size_t>(T_) * 4,
@@ -174,6 +175,8 @@ int Engine::init(const xl_config& cfg, int device, int tp_size, int tp_rank, con
     philox_seed_ = (static_cast<uint64_t>(rd()) << 32) ^ rd();
     int rc = alloc_all();
     if (rc != XL_OK) return rc;
+    const int one = 1;  // this rank's share of the step-start liveness sum
+    XL_CUDA(cudaMemcpy(&st_->tp_one, &one, sizeof(int), cudaMemcpyHostToDevice));
     if (tp_ > 1) {
         if (nccl_id == nullptr) {
             set_error("tensor parallel: nccl_id is required when tp_size > 1");
@@ -195,14 +198,34 @@ int Engine::init(const xl_config& cfg, int device, int tp_size, int tp_rank, con
 }
 
 // Every rank exports its exchange buffer (CUDA IPC) and maps every other
-// rank's; the handles are all-gathered over the engine's NCCL communicator.
+// rank's; the handles are all-gathered over the engine's NCCL communicator
+// together with each rank's kernel geometry.  The persistent kernel's
+// exchange slots are laid out by the grid (one CTA per SM) and the shard
+// widths, and a reader sums the slots its own grid implies: ranks whose SM
+// counts or shapes differ would silently drop or misread contributions, so
+// creation fails instead.
+namespace {
+struct PeerInfo {
+    cudaIpcMemHandle_t handle;
+    int sms, hidden, hidden_local, ffn_local, layers, max_ctx, tp, rank;
+};
+}  // namespace
+
 int Engine::setup_peers() {
-    cudaIpcMemHandle_t mine;
-    XL_CUDA(cudaIpcGetMemHandle(&mine, xbuf_));
-    constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
+    PeerInfo mine{};
+    XL_CUDA(cudaIpcGetMemHandle(&mine.handle, xbuf_));
+    mine.sms = num_sms_;
+    mine.hidden = H_;
+    mine.hidden_local = Hl_;
+    mine.ffn_local = Fl_;
+    mine.layers = cfg_.layers;
+    mine.max_ctx = T_;
+    mine.tp = tp_;
+    mine.rank = rank_;
+    constexpr size_t kH = sizeof(PeerInfo);
     char* dev = nullptr;
     XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&dev), kH * tp_));
-    std::vector<char> all(kH * tp_);
+    std::vector<PeerInfo> all(tp_);
     cudaError_t ce = cudaMemcpy(dev + kH * rank_, &mine, kH, cudaMemcpyHostToDevice);
     ncclResult_t nr = ncclSuccess;
     if (ce == cudaSuccess) nr = ncclAllGather(dev + kH * rank_, dev, kH, ncclUint8, comm_, stream_);
@@ -212,14 +235,28 @@ int Engine::setup_peers() {
     if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather (exchange buffer handles)");
     if (ce != cudaSuccess) return cuda_fail(ce, "exchange buffer handles");
     for (int r = 0; r < tp_; ++r) {
+        const PeerInfo& q = all[r];
+        if (q.sms != mine.sms || q.hidden != mine.hidden || q.hidden_local != mine.hidden_local ||
+            q.ffn_local != mine.ffn_local || q.layers != mine.layers || q.max_ctx != mine.max_ctx ||
+            q.tp != mine.tp || q.rank != r) {
+            set_error("tensor parallel: rank " + std::to_string(r) + " has " + std::to_string(q.sms) + " SMs, hidden " +
+                      std::to_string(q.hidden) + "/" + std::to_string(q.hidden_local) + ", ffn shard " +
+                      std::to_string(q.ffn_local) + ", " + std::to_string(q.layers) + " layers, context " +
+                      std::to_string(q.max_ctx) + " (rank " + std::to_string(q.rank) + " of " + std::to_string(q.tp) +
+                      "); rank " + std::to_string(rank_) + " has " + std::to_string(mine.sms) + " SMs, hidden " +
+                      std::to_string(mine.hidden) + "/" + std::to_string(mine.hidden_local) + ", ffn shard " +
+                      std::to_string(mine.ffn_local) + ", " + std::to_string(mine.layers) + " layers, context " +
+                      std::to_string(mine.max_ctx) + ": every rank needs the same GPU model and the same shape");
+            return XL_ERR_ARG;
+        }
+    }
+    for (int r = 0; r < tp_; ++r) {
         if (r == rank_) {
             xpeer_[r] = xbuf_;
             continue;
         }
-        cudaIpcMemHandle_t h;
-        std::memcpy(&h, all.data() + kH * r, kH);
         void* ptr = nullptr;
-        XL_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        XL_CUDA(cudaIpcOpenMemHandle(&ptr, all[r].handle, cudaIpcMemLazyEnablePeerAccess));
         xpeer_[r] = static_cast<char*>(ptr);
     }
     peers_ = true;
@@ -320,6 +357,20 @@ int Engine::alloc_all() {
 
 Engine::~Engine() {
     cudaSetDevice(device_);
+    // A tensor-parallel stream may still wait on a peer that never joined:
+    // wait a bounded time, abort the communicator if it is still busy, and
+    // leak the device memory rather than block in cudaFree if it never drains.
+    if (stream_ && tp_ > 1 && stream_idle_ && !drain_stream(failed_ ? 10000 : 60000)) {
+        if (comm_)
+            abort_tp("engine destroyed while a step was still running");  // drains again, sets stream_idle_
+        else
+            stream_idle_ = false;
+    }
+    if (!stream_idle_) {
+        for (int r = 0; r < kMaxTp; ++r)
+            if (xpeer_[r] && xpeer_[r] != xbuf_) cudaIpcCloseMemHandle(xpeer_[r]);
+        return;
+    }
     if (stream_) cudaStreamSynchronize(stream_);
     if (decode_exec_) cudaGraphExecDestroy(decode_exec_);
     if (decode_exec_s_) cudaGraphExecDestroy(decode_exec_s_);
@@ -328,6 +379,7 @@ Engine::~Engine() {
     for (int r = 0; r < kMaxTp; ++r)
         if (xpeer_[r] && xpeer_[r] != xbuf_) cudaIpcCloseMemHandle(xpeer_[r]);
     if (comm_) ncclCommDestroy(comm_);
+    if (ev_sync_) cudaEventDestroy(ev_sync_);
     if (xbuf_) cudaFree(xbuf_);
     if (arena_) cudaFree(arena_);
     if (h_in_) cudaFreeHost(h_in_);
@@ -651,8 +703,13 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
         for (int r = 0; r < tp_; ++r) p.xc[r] = reinterpret_cast<unsigned long long*>(xpeer_[r]);
         // The ranks' kernels wait on one another (with a time limit), so they
         // start together, after a one-word NCCL barrier: the hosts may launch
-        // a step at very different times.
-        XL_NCCL(ncclAllReduce(&st_->tp_sync, &st_->tp_sync, 1, ncclInt32, ncclMax, comm_, s));
+        // a step at very different times.  The barrier is a liveness sum:
+        // every rank adds 1, and the kernel runs only if the sum is tp.  When a
+        // peer never joins, the host aborts the communicator after its step
+        // timeout; the aborted all-reduce leaves the sum short, and the kernel
+        // leaves before touching any peer's memory.
+        XL_CUDA(cudaMemsetAsync(&st_->tp_sync, 0, sizeof(int), s));
+        XL_NCCL(ncclAllReduce(&st_->tp_one, &st_->tp_sync, 1, ncclInt32, ncclSum, comm_, s));
     }
     XL_CUDA(cudaMemsetAsync(
         done_, 0, (5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_) * sizeof(int),
@@ -917,20 +974,109 @@ float Engine::next_uniform() {
 int Engine::finish_step(int* token_out) {
     XL_CUDA(cudaEventRecord(ev1_, stream_));
     XL_CUDA(cudaMemcpyAsync(h_out_, st_, sizeof(DevState), cudaMemcpyDeviceToHost, stream_));
-    XL_CUDA(cudaStreamSynchronize(stream_));
+    int rc = wait_stream("step");
+    if (rc != XL_OK) return rc;
     XL_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     const DevState* hs = reinterpret_cast<const DevState*>(h_out_);
-    if (hs->err != 0) {
-        set_error("device error word " + std::to_string(hs->err));
-        return XL_ERR_DEVICE;
-    }
+    if (hs->err != 0) return device_error(hs->err);
     *token_out = hs->token_out;
     return XL_OK;
+}
+
+// A kernel reported an error through DevState::err (a bounded wait ran out).
+// One GPU: the word is cleared and the sequence dropped, so the next prompt
+// starts clean.  Tensor parallel: the ranks' step counters (the exchange tags)
+// may now disagree, so the engine refuses every further step.
+int Engine::device_error(int bits) {
+    std::string msg = "device error word " + std::to_string(bits);
+    has_seq_ = false;
+    n_ = 0;
+    if (tp_ > 1) {
+        failed_ = true;
+        fail_msg_ = "tensor parallel: a step failed on the device (error word " + std::to_string(bits) +
+                    "); this engine is unusable: create a new one on every rank";
+        msg = fail_msg_;
+    } else {
+        XL_CUDA(cudaMemsetAsync(&st_->err, 0, sizeof(int), stream_));
+        XL_CUDA(cudaStreamSynchronize(stream_));
+        msg += "; the sequence was dropped: prefill a new prompt";
+    }
+    set_error(msg);
+    return XL_ERR_DEVICE;
+}
+
+// Waits for the engine stream.  A tensor-parallel step can wait on a peer
+// rank that never joins (its host stopped or died between steps): the wait is
+// then bounded by the step timeout (option step_timeout_ms) and by NCCL's
+// asynchronous error, after which the communicator is aborted.
+int Engine::wait_stream(const char* what) {
+    if (tp_ == 1) {
+        XL_CUDA(cudaStreamSynchronize(stream_));
+        return XL_OK;
+    }
+    XL_CUDA(cudaEventRecord(ev_sync_, stream_));
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint32_t it = 0;; ++it) {
+        const cudaError_t q = cudaEventQuery(ev_sync_);
+        if (q == cudaSuccess) return XL_OK;
+        if (q != cudaErrorNotReady) return cuda_fail(q, what);
+        if ((it & 255u) != 0) continue;
+        ncclResult_t ar = ncclSuccess;
+        if (comm_ && ncclCommGetAsyncError(comm_, &ar) != ncclSuccess) ar = ncclInternalError;
+        if (ar != ncclSuccess && ar != ncclInProgress)
+            return abort_tp(std::string(what) + ": NCCL reported " + ncclGetErrorString(ar));
+        const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        if (ms > step_timeout_ms_)
+            return abort_tp(std::string(what) + " did not finish within " + std::to_string(step_timeout_ms_) +
+                            " ms (a peer rank stopped or died?)");
+    }
+}
+
+// Polls the engine stream until it is idle or timeout_ms has passed.
+bool Engine::drain_stream(int timeout_ms) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(stream_);
+        if (q != cudaErrorNotReady) return q == cudaSuccess;
+        const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        if (ms > timeout_ms) return false;
+        std::this_thread::yield();
+    }
+}
+
+// Tensor parallel: gives up on the communicator.  The executable graphs that
+// hold its collectives go first (one still in flight is released when it
+// completes), then ncclCommAbort makes the collectives that wait for the
+// missing rank return; the persistent kernel of that step finds the liveness
+// sum short and leaves.  The engine refuses every later call.
+int Engine::abort_tp(const std::string& why) {
+    for (cudaGraphExec_t* e : {&decode_exec_, &decode_exec_s_, &gen_exec_, &gen_exec_s_}) {
+        if (*e) cudaGraphExecDestroy(*e);
+        *e = nullptr;
+    }
+    if (comm_) ncclCommAbort(comm_);
+    comm_ = nullptr;
+    failed_ = true;
+    fail_msg_ = "tensor parallel: " + why + "; the communicator was aborted and this engine is unusable: create a new "
+                "one on every rank";
+    const bool idle = drain_stream(10000);
+    if (!idle) fail_msg_ += " (its stream did not drain within 10 s)";
+    stream_idle_ = idle;
+    has_seq_ = false;
+    set_error(fail_msg_);
+    return XL_ERR_NCCL;
+}
+
+int Engine::check_usable() const {
+    if (!failed_) return XL_OK;
+    set_error(fail_msg_);
+    return XL_ERR_STATE;
 }
 
 // InferenceEngine::next_token(vector), src/inference.cu:116-136.
 int Engine::prefill(const int* ids, int n, float temperature, float top_p, float rp, int* token_out, bool append) {
     XL_CUDA(cudaSetDevice(device_));
+    if (const int u = check_usable()) return u;
     if (!loaded_) {
         set_error("prefill before load");
         return XL_ERR_STATE;
@@ -1031,6 +1177,7 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
 // InferenceEngine::next_token(int), src/inference.cu:138-151.
 int Engine::decode(int token, float temperature, float top_p, float rp, int* token_out) {
     XL_CUDA(cudaSetDevice(device_));
+    if (const int u = check_usable()) return u;
     if (!loaded_) {
         set_error("decode before load");
         return XL_ERR_STATE;
@@ -1072,6 +1219,7 @@ int Engine::generate(int token, int n, float temperature, float top_p, float rp,
                      int* n_out) {
     XL_CUDA(cudaSetDevice(device_));
     *n_out = 0;
+    if (const int u = check_usable()) return u;
     if (n < 0 || (n > 0 && tokens_out == nullptr)) {
         set_error("generate: n must be >= 0 and tokens_out non-null");
         return XL_ERR_ARG;
@@ -1137,10 +1285,7 @@ int Engine::generate(int token, int n, float temperature, float top_p, float rp,
     XL_CUDA(cudaStreamSynchronize(stream_));
     XL_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     const DevState* hs = reinterpret_cast<const DevState*>(h_out_);
-    if (hs->err != 0) {
-        set_error("device error word " + std::to_string(hs->err));
-        return XL_ERR_DEVICE;
-    }
+    if (hs->err != 0) return device_error(hs->err);
     const int done = c->step;
     if (done < steps) {
         // Return the unused draws: queued values go back in order, the Philox counter rewinds.
@@ -1215,6 +1360,14 @@ int Engine::set_option(const char* key, int value) {
         }
         inflight_ = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
+    }
+    if (k == "step_timeout_ms") {
+        if (value < 1) {
+            set_error("step_timeout_ms must be >= 1");
+            return XL_ERR_ARG;
+        }
+        step_timeout_ms_ = value;
+        return XL_OK;
     }
     if (k == "load_threads") {
         if (value < 1 || value > 64) {

@@ -99,6 +99,11 @@ class Engine {
     int launch_lm_head(const float* x_last, const float* delta, bool pdl, cudaStream_t s);
     const float* lm_x_ = nullptr;  // residual stream the decode graph's LM head reads
     int finish_step(int* token_out);
+    int wait_stream(const char* what);       // bounded under tensor parallelism (step_timeout_ms)
+    bool drain_stream(int timeout_ms);
+    int abort_tp(const std::string& why);    // graphs released, ncclCommAbort, engine unusable
+    int device_error(int bits);
+    int check_usable() const;
     float next_uniform();
     int cuda_fail(cudaError_t e, const char* what);
     int nccl_fail(ncclResult_t r, const char* what);
@@ -177,6 +182,11 @@ class Engine {
     int inflight_ = 3;  // persistent decode: weight boxes requested but not landed, per SM
     int tma_evict_first_ = 1;  // persistent decode: weight boxes loaded with an L2 evict-first policy
     bool loaded_ = false;
+    bool failed_ = false;          // tensor parallel: aborted or a device error; every later step is refused
+    std::string fail_msg_;
+    bool stream_idle_ = true;      // false: an aborted step never drained (device memory is leaked, not freed)
+    int step_timeout_ms_ = 30000;  // tensor parallel: longest host wait for one call's work
+    cudaEvent_t ev_sync_ = nullptr;
     bool has_seq_ = false;
     int n_ = 0;
     float last_ms_ = 0.0f;

@@ -35,8 +35,8 @@ struct DevState {
     unsigned long long argmax_final;  // packed (value, id) of the winning logit
     int err;                          // device-side error bits (0 = ok)
     int epoch;                        // persistent decode steps run (tensor parallel: cross-rank counter targets)
-    int tp_sync;                      // tensor parallel: the word of the step-start NCCL barrier
-    int pad;
+    int tp_sync;                      // tensor parallel: step-start liveness sum (tp when every rank joined)
+    int tp_one;                       // tensor parallel: the constant 1 each rank adds into tp_sync
 };
 
 enum GemvMode : int {
