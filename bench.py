@@ -48,7 +48,7 @@ for _p in (PKG, ORACLE):
 import xl_synth as S  # noqa: E402
 
 PROMPT, DECODE, PREFILL_N = 32, 128, 512
-REF_DECODE_SAMPLE = 32
+REF_DECODE_SAMPLE = 128  # the reference arm times the whole decode workload each step
 WEIGHT_DIR = os.environ.get("XL_BENCH_WEIGHTS", os.path.join(tempfile.gettempdir(), "xl_weights", "full"))
 METRIC = "decode tokens/s, XingLing-0.68B fp32, batch 1"
 
@@ -212,6 +212,24 @@ def run_cpu_baseline(budget: float) -> dict | None:
     return None
 
 
+def library_record(path: str) -> dict:
+    """The library the reference arm timed: its resolved path, size and hash,
+    and whether this process has it mapped (from /proc/self/maps)."""
+    import hashlib
+
+    real = os.path.realpath(path)
+    rec = {"path": os.path.relpath(real, ROOT), "bytes": os.path.getsize(real),
+           "sha256_16": hashlib.sha256(open(real, "rb").read()).hexdigest()[:16],
+           "what": "the reference's src/*.cu compiled from its sources by oracle/Makefile, behind oracle/ref_harness.cpp"
+           if real.endswith("libxlref.so") else "the oracle's C restatement (oracle/xl_oracle.c)"}
+    try:
+        with open("/proc/self/maps") as f:
+            rec["mapped"] = any(line.rstrip().endswith(real) for line in f)
+    except OSError:
+        rec["mapped"] = None
+    return rec
+
+
 # ---------------------------------------------------------------------------
 def reference_arm(args) -> None:
     """The reference's own CPU implementation (oracle/_ref, else the oracle port),
@@ -253,6 +271,7 @@ def reference_arm(args) -> None:
     wall = time.perf_counter() - t0
     value = args.steps * REF_DECODE_SAMPLE / dec
     cores = int(os.environ["OMP_NUM_THREADS"])
+    lib = oracle.REF_SO if kind == "reference" else oracle.PORT_SO
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * wall / args.steps, "higher_is_better": True,
@@ -263,6 +282,7 @@ def reference_arm(args) -> None:
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind,
                          "sample": f"per step: prefill {PROMPT} + {REF_DECODE_SAMPLE} of the {DECODE} decode tokens"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "library": library_record(lib),
     }
     print(json.dumps(line))
     sys.stdout.flush()

@@ -69,7 +69,7 @@ def build(verbose_ptxas: bool = False) -> None:
     with cf.ThreadPoolExecutor(max_workers=len(CU_SOURCES)) as ex:
         objs = list(ex.map(lambda s: _nvcc_obj(s, verbose_ptxas), CU_SOURCES))
     if _stale(LIB, objs):
-        _run([NVCC, "-shared", *ARCH, "-o", LIB, *objs, "-lnccl", "-Xlinker", "--no-undefined"])
+        _run([NVCC, "-shared", *ARCH, "-o", LIB, *objs, "-lnccl", "-ldl", "-Xlinker", "--no-undefined"])
     import pybind11
 
     mod_src = os.path.join(CSRC, "pybind_module.cpp")

@@ -20,6 +20,8 @@
 #include <utility>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "engine.h"
 
 namespace xl {
@@ -30,6 +32,31 @@ constexpr double kEps = 1e-6;  // RMSNorm eps, src/rmsnorm.cu:72,100
 constexpr size_t kLoadChunkBytes = 8u << 20;  // weight-file bytes per staging chunk of the loader
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// NVTX ranges (domain "xingling") around every public call, so that an
+// nsys / ncu timeline lines up with the engine's steps: "load", "prefill",
+// "extend", "decode", "generate"; the payload is the call's first position
+// (prefill: the prompt length).  Without an attached tool each push / pop is
+// a branch on a null function pointer.
+nvtxDomainHandle_t nvtx_domain() {
+    static nvtxDomainHandle_t d = nvtxDomainCreateA("xingling");
+    return d;
+}
+struct NvtxRange {
+    NvtxRange(const char* name, long long payload) {
+        nvtxEventAttributes_t a{};
+        a.version = NVTX_VERSION;
+        a.size = NVTX_EVENT_ATTRIB_STRUCT_SIZE;
+        a.messageType = NVTX_MESSAGE_TYPE_ASCII;
+        a.message.ascii = name;
+        a.payloadType = NVTX_PAYLOAD_TYPE_INT64;
+        a.payload.llValue = payload;
+        nvtxDomainRangePushEx(nvtx_domain(), &a);
+    }
+    ~NvtxRange() { nvtxDomainRangePop(nvtx_domain()); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 }  // namespace
 
 void set_error(const std::string& msg) { g_err = msg; }
@@ -542,6 +569,7 @@ struct Loader {
 }  // namespace
 
 int Engine::load(const char* dir) {
+    NvtxRange range("load", 0);
     XL_CUDA(cudaSetDevice(device_));
     if (dir == nullptr) {
         set_error("load: null path");
@@ -1075,6 +1103,7 @@ int Engine::check_usable() const {
 
 // InferenceEngine::next_token(vector), src/inference.cu:116-136.
 int Engine::prefill(const int* ids, int n, float temperature, float top_p, float rp, int* token_out, bool append) {
+    NvtxRange range(append ? "extend" : "prefill", n);
     XL_CUDA(cudaSetDevice(device_));
     if (const int u = check_usable()) return u;
     if (!loaded_) {
@@ -1176,6 +1205,7 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
 
 // InferenceEngine::next_token(int), src/inference.cu:138-151.
 int Engine::decode(int token, float temperature, float top_p, float rp, int* token_out) {
+    NvtxRange range("decode", n_);
     XL_CUDA(cudaSetDevice(device_));
     if (const int u = check_usable()) return u;
     if (!loaded_) {
@@ -1217,6 +1247,7 @@ int Engine::decode(int token, float temperature, float top_p, float rp, int* tok
 
 int Engine::generate(int token, int n, float temperature, float top_p, float rp, int stop_id, int* tokens_out,
                      int* n_out) {
+    NvtxRange range("generate", n_);
     XL_CUDA(cudaSetDevice(device_));
     *n_out = 0;
     if (const int u = check_usable()) return u;
