@@ -339,7 +339,7 @@ def test_full_prefill_512(eng_mod, full_weights):
         v = np.frombuffer(vb, np.float32).reshape(-1, sh.heads, 64)
         kr, vr = port.kv(layer, 512)
         # relative to the largest cached value: the 3xTF32 products' rounding
-        # grows through the layers (1.8e-4 absolute at layer 15, values up to ~4)
+        # grows through the layers (1.8e-4 absolute at layer 15)
         ek = float(np.abs(k - kr).max() / np.abs(kr).max())
         ev = float(np.abs(v - vr).max() / np.abs(vr).max())
         assert ek < 1e-4 and ev < 1e-4, f"layer {layer}: KV max err {ek:.2e} / {ev:.2e} of the largest value"

@@ -254,6 +254,10 @@ def _rank_stops(rank, world, wdir, shape_kw, ids, q_id, q_out, q_ctl, path, time
     host is stuck; nothing of it is in flight) until the test releases it;
     rank 0 takes one more step, which must end in RuntimeError within its step
     timeout, then a refused step, then destroys its engine."""
+    import faulthandler
+
+    faulthandler.dump_traceback_later(150, exit=False)  # a stuck call shows up in the log
+    os.environ["XL_TRACE_ABORT"] = "1"
     try:
         m, eng = _engine(rank, world, shape_kw, q_id, path)
         eng.load(wdir)
@@ -262,9 +266,10 @@ def _rank_stops(rank, world, wdir, shape_kw, ids, q_id, q_out, q_ctl, path, time
             tok = eng.next_token(tok, top_p=0.0, repetition_penalty=1.0)
         if rank != 0:
             q_out.put((rank, "stopped", tok, None, None, None))
-            q_ctl.get(timeout=600)  # released once rank 0 has reported
+            q_ctl.get(timeout=300)  # released once rank 0 has reported
             os._exit(0)  # leaves without a collective: the communicator's peer is gone
         eng.set_option("step_timeout_ms", timeout_ms)
+        print("[rank 0] stepping without the peer", file=sys.stderr, flush=True)
         t0 = time.monotonic()
         try:
             eng.next_token(tok, top_p=0.0, repetition_penalty=1.0)
@@ -277,8 +282,10 @@ def _rank_stops(rank, world, wdir, shape_kw, ids, q_id, q_out, q_ctl, path, time
             second = ("no error", time.monotonic() - t1)
         except RuntimeError as e:
             second = (str(e)[:300], time.monotonic() - t1)
+        print(f"[rank 0] first {first}, second {second}", file=sys.stderr, flush=True)
         t2 = time.monotonic()
         del eng
+        print("[rank 0] engine destroyed", file=sys.stderr, flush=True)
         q_out.put((rank, "ok", first, second, time.monotonic() - t2, None))
     except Exception as e:  # noqa: BLE001
         q_out.put((rank, "error", repr(e)[:400], None, None, None))
@@ -301,7 +308,7 @@ def test_tp_peer_stops_survivor_raises_within_timeout(built, tiny_weights, path)
     out = {}
     try:
         for _ in procs:
-            r = q_out.get(timeout=600)
+            r = q_out.get(timeout=240)
             out[r[0]] = r
     except queue.Empty:
         pass

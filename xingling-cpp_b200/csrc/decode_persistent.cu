@@ -71,6 +71,7 @@ constexpr int kSlotBytes = kPersistTileRows * kBoxK * 4;         // 32 KB
 constexpr int kSlots = kPersistSlots;                            // 192 KB ring
 constexpr int kMaxK = 4096;
 constexpr size_t kSmemBytes = static_cast<size_t>(kSlots) * kSlotBytes + kMaxK * 4 + 2 * kSlots * 8 + 512;
+constexpr size_t kMaxSmemPerBlock = 232448;  // sm_100: 227 KB of dynamic shared memory per block
 // Every wait is bounded twice: by polls and by wall-clock time (an mbarrier
 // try_wait may suspend the thread for a while, so a poll count alone can last
 // far longer than intended).  A decode step takes under a millisecond.
@@ -265,10 +266,80 @@ __device__ __forceinline__ unsigned xtag(const PersistentParams& p, int l, int w
 __device__ __forceinline__ unsigned long long xword(float v, unsigned tag) {
     return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
 }
+// tag_qkv: the QKV phase's outputs are tagged words (value, step and layer),
+// so an attention CTA waits for its own head's q / k / v, not for the grid.
+__device__ __forceinline__ unsigned qtag(const PersistentParams& p, int l) {
+    return static_cast<unsigned>(p.st->epoch) * static_cast<unsigned>(p.layers) + static_cast<unsigned>(l) + 1u;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* a) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* a, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+__device__ __forceinline__ bool tag_is(unsigned long long w, unsigned tag) { return static_cast<unsigned>(w >> 32) == tag; }
+__device__ __forceinline__ float word_val(unsigned long long w) { return __uint_as_float(static_cast<unsigned>(w)); }
+// One warp of head h's attention: q (and, for the chunk holding position n,
+// k and v) of layer l, spinning (bounded) until every word carries this
+// step's tag.  On a timeout the error bit is set and zeros come back.
+struct QkvWords {
+    float qa, qb, ka, kb, vx, vy;
+};
+__device__ __noinline__ QkvWords load_qkv_tagged(const PersistentParams& p, int l, int h, bool has_n) {
+    const int lane = threadIdx.x & 31;
+    const unsigned tag = qtag(p, l);
+    const unsigned long long* q = p.qkvw + h * kHeadDim;
+    const unsigned long long* k = p.qkvw + p.Hl + h * kHeadDim;
+    const unsigned long long* v = p.qkvw + 2 * p.Hl + h * kHeadDim;
+    uint32_t it = 0;
+    unsigned long long t0 = 0;
+    for (;;) {
+        const unsigned long long a = ld_relaxed_u64(q + lane), b = ld_relaxed_u64(q + lane + kHalfHead);
+        unsigned long long c = 0, d = 0, e = 0, f = 0;
+        bool ok = tag_is(a, tag) && tag_is(b, tag);
+        if (has_n) {
+            c = ld_relaxed_u64(k + lane);
+            d = ld_relaxed_u64(k + lane + kHalfHead);
+            e = ld_relaxed_u64(v + 2 * lane);
+            f = ld_relaxed_u64(v + 2 * lane + 1);
+            ok = ok && tag_is(c, tag) && tag_is(d, tag) && tag_is(e, tag) && tag_is(f, tag);
+        }
+        if (__all_sync(0xffffffffu, ok))
+            return QkvWords{word_val(a), word_val(b), word_val(c), word_val(d), word_val(e), word_val(f)};
+        ++it;
+        if ((it & 15u) == 0) {
+            const unsigned long long now = globaltimer();
+            if (t0 == 0) t0 = now;
+            if (it >= kFlagSpinLimit || now - t0 > kWaitLimitNs || aborted(p.st)) {
+                if (lane == 0) atomicOr(&p.st->err, kErrFlag);
+                return QkvWords{0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+            }
+        }
+    }
+}
+
 // This rank's partial sum of row `row` of group g (slot c) of layer l's split
 // projection w2, tagged, into its own exchange buffer.
 __device__ __noinline__ void store_own_tp(const PersistentParams& p, int l, int w2, int g, int c, int row, float v) {
     xc_part(p, p.rank, w2, p.rank, g, c)[row] = xword(v, xtag(p, l, w2));
+}
+// tag_split: this CTA's partial sum of row `row` of group g (slot c) of layer
+// l's split projection w2 goes, tagged, straight to every rank's exchange
+// buffer (this rank's own included): the next staging waits for the tags
+// alone, so the phase needs neither a release fence nor a grid counter.  The
+// stores are relaxed and single-copy atomic (one aligned 64-bit word each):
+// a reader that sees the expected tag holds the value stored with it.
+__device__ __noinline__ void store_all_tp(const PersistentParams& p, int l, int w2, int g, int c, int row, float v) {
+    const unsigned long long w = xword(v, xtag(p, l, w2));
+    for (int r = 0; r < p.tp; ++r) {
+        unsigned long long* a = xc_part(p, r, w2, p.rank, g, c) + row;
+        if (r == p.rank)
+            asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+        else
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+    }
 }
 // After this warp's phase signal: its partial sums of the phase (row `row` of
 // each group of boxes [r.t0, r.t1), already in this rank's own slots) go to
@@ -394,7 +465,7 @@ __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
     const int kind = phase_kind(ph, p.layers);
     // An attention phase is signalled once per head (by the warp that writes
     // the head's output); every other phase by every consumer warp of every CTA.
-    const int target = kind == kAttn ? p.heads : static_cast<int>(gridDim.x) * kConsumerWarps;
+    const int target = kind == kAttn ? p.heads : static_cast<int>(gridDim.x) * (p.sig_cta ? 1 : kConsumerWarps);
     if (threadIdx.x == 32) {
         const int* c = p.done + ph;
         uint32_t it = 0;
@@ -418,12 +489,25 @@ __device__ bool wait_phase(const PersistentParams& p, int ph, int* s_ok) {
     return *s_ok != 0;
 }
 
-// Each warp publishes its own stores of phase ph as soon as it has issued
+// One warp publishes its own stores of phase ph as soon as it has issued
 // them: lane 0 releases (cumulative over the warp's lanes, ordered by the
-// __syncwarp) and adds 1 to the counter, so no warp waits for its CTA.
-__device__ void signal_phase(const PersistentParams& p, int ph) {
+// __syncwarp) and adds 1 to the counter.
+__device__ void signal_warp(const PersistentParams& p, int ph) {
     __syncwarp();
     if ((threadIdx.x & 31) == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.done + ph) : "memory");
+}
+// A GEMV phase's signal, from every consumer warp: per warp (no warp waits
+// for its CTA), or with sig_cta one release per CTA after a consumer barrier
+// (the barrier orders the other warps' stores before the first consumer
+// thread's release, which is cumulative over them): 8x fewer reductions on
+// the phase counter's line.
+__device__ void signal_phase(const PersistentParams& p, int ph) {
+    if (!p.sig_cta) {
+        signal_warp(p, ph);
+        return;
+    }
+    consumer_sync();
+    if (threadIdx.x == 32) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.done + ph) : "memory");
 }
 
 // Block-wide (consumers) sum of one float per thread.
@@ -442,7 +526,7 @@ __device__ float consumer_sum(float v, float* red) {
 // Residual rows 4q .. 4q+3 (within one 16-row group) after a split
 // projection: x_old + (the partial row sums of the CTAs that own the group's
 // boxes, in CTA order, + bias).
-__device__ __forceinline__ float4 residual_quad(const float* x_old, const float* bias, const float* cres, int q, int nb,
+__device__ __forceinline__ float4 residual_quad(float4 xo, const float* bias, const float* cres, int q, int nb,
                                                 int T) {
     const int g = (4 * q) / kPersistTileRows;
     const int G = gridDim.x;
@@ -453,7 +537,6 @@ __device__ __forceinline__ float4 residual_quad(const float* x_old, const float*
 #pragma unroll
     for (int c = 0; c < kPersistMaxContrib; ++c)
         v[c] = c < nc ? __ldcg(part + c * (kPersistTileRows / 4)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    const float4 xo = __ldcg(reinterpret_cast<const float4*>(x_old) + q);
     const float4 b = reinterpret_cast<const float4*>(bias)[q];
     float4 s = v[0];
 #pragma unroll
@@ -473,8 +556,12 @@ __device__ __forceinline__ float4 residual_quad(const float* x_old, const float*
 // its slice of x to x_out.  float4 accesses; every load of a batch of quads
 // (x, partial sums, bias, gamma) is issued before the first store, so a
 // staging costs one L2 round trip per batch (one in all at K <= 2048).
+// With xr (resid_smem), the residual before the projection is this CTA's own
+// copy in shared memory (every CTA computes the same x in the same order) and
+// x is written back there; x_out then gets its slice only when out_too is set
+// (the LM head's input, read back by the host's LM-head profile).
 __device__ __noinline__ void stage_norm(const PersistentParams& p, const float* x_old, const float* bias, const float* cres,
-                           int nb, const float* gamma, float* xs, float* red, float* x_out) {
+                           int nb, const float* gamma, float* xs, float* red, float* x_out, float* xr, bool out_too) {
     const int t = threadIdx.x - 32;
     const int K = p.H;
     const int T = (K / kPersistTileRows) * nb;
@@ -493,8 +580,11 @@ __device__ __noinline__ void stage_norm(const PersistentParams& p, const float* 
             const int q = t + (k0 + u) * kConsumerThreads;
             if (q < (K >> 2)) {
                 gk[k0 + u] = g4[q];
-                v[u] = cres ? residual_quad(x_old, bias, cres, q, nb, T)
-                            : __ldcg(reinterpret_cast<const float4*>(x_old) + q);
+                // the residual before the projection: this CTA's copy in shared
+                // memory, or global memory written by other CTAs (L2, not L1)
+                const float4 xo = xr && cres ? reinterpret_cast<const float4*>(xr)[q]
+                                             : __ldcg(reinterpret_cast<const float4*>(x_old) + q);
+                v[u] = cres ? residual_quad(xo, bias, cres, q, nb, T) : xo;
             }
         }
 #pragma unroll
@@ -502,10 +592,13 @@ __device__ __noinline__ void stage_norm(const PersistentParams& p, const float* 
             const int q = t + (k0 + u) * kConsumerThreads;
             if (q < (K >> 2)) {
                 x4[q] = v[u];
-                const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                if (xr) reinterpret_cast<float4*>(xr)[q] = v[u];
+                if (!xr || out_too) {
+                    const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    if (4 * q + c >= s0 && 4 * q + c < s1) x_out[4 * q + c] = e[c];
+                    for (int c = 0; c < 4; ++c)
+                        if (4 * q + c >= s0 && 4 * q + c < s1) x_out[4 * q + c] = e[c];
+                }
                 ss = dot4(v[u], v[u], ss);
             }
         }
@@ -533,7 +626,7 @@ __device__ __noinline__ void stage_norm(const PersistentParams& p, const float* 
 __device__ __forceinline__ void ld_words(const unsigned long long* a, unsigned long long& x, unsigned long long& y) {
     asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(a) : "memory");
 }
-__device__ __forceinline__ float4 residual_quad_tp(const PersistentParams& p, const float* x_old, const float* bias,
+__device__ __forceinline__ float4 residual_quad_tp(const PersistentParams& p, float4 xo, const float* bias,
                                                    int w2, int q, int nb, int T, unsigned tag) {
     const int g = (4 * q) / kPersistTileRows;
     const int G = gridDim.x;
@@ -589,7 +682,6 @@ __device__ __forceinline__ float4 residual_quad_tp(const PersistentParams& p, co
             }
         }
     }
-    const float4 xo = __ldcg(reinterpret_cast<const float4*>(x_old) + q);
     const float4 b = reinterpret_cast<const float4*>(bias)[q];
     return make_float4(xo.x + (s.x + b.x), xo.y + (s.y + b.y), xo.z + (s.z + b.z), xo.w + (s.w + b.w));
 }
@@ -598,7 +690,7 @@ __device__ __forceinline__ float4 residual_quad_tp(const PersistentParams& p, co
 // partial sums all ranks exchanged (w2: which projection; tag: its use).
 __device__ __noinline__ void stage_norm_tp(const PersistentParams& p, const float* x_old, const float* bias, int w2,
                                            unsigned tag, int nb, const float* gamma, float* xs, float* red,
-                                           float* x_out) {
+                                           float* x_out, float* xr, bool out_too) {
     const int t = threadIdx.x - 32;
     const int K = p.H;
     const int T = (K / kPersistTileRows) * nb;
@@ -613,12 +705,17 @@ __device__ __noinline__ void stage_norm_tp(const PersistentParams& p, const floa
         const int q = t + k * kConsumerThreads;
         if (q < (K >> 2)) {
             gk[k] = g4[q];
-            const float4 v = residual_quad_tp(p, x_old, bias, w2, q, nb, T, tag);
+            const float4 xo = xr ? reinterpret_cast<const float4*>(xr)[q]
+                                 : __ldcg(reinterpret_cast<const float4*>(x_old) + q);
+            const float4 v = residual_quad_tp(p, xo, bias, w2, q, nb, T, tag);
             x4[q] = v;
-            const float e[4] = {v.x, v.y, v.z, v.w};
+            if (xr) reinterpret_cast<float4*>(xr)[q] = v;
+            if (!xr || out_too) {
+                const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                if (4 * q + u >= s0 && 4 * q + u < s1) x_out[4 * q + u] = e[u];
+                for (int u = 0; u < 4; ++u)
+                    if (4 * q + u >= s0 && 4 * q + u < s1) x_out[4 * q + u] = e[u];
+            }
             ss = dot4(v, v, ss);
         }
     }
@@ -705,7 +802,7 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
     // A CTA without an attention item neither waits nor signals: the next
     // phase waits for the heads' outputs, which imply the QKV phase.
     if (!has) return true;
-    if (!wait_phase(p, ph - 1, s_ok)) return false;
+    if (!p.tag_qkv && !wait_phase(p, ph - 1, s_ok)) return false;  // tag_qkv: each warp waits for its head's words
     if (t == 0) trace_at(p, ph, kTrConsStart);
     float* qsh = xs + warp * kAttnWarpScratch;
     float* apart = xs + kConsumerWarps * kAttnWarpScratch;  // [8][68]
@@ -715,13 +812,20 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
         const float* q = p.qkv + h * kHeadDim;
         const float* kn = p.qkv + p.Hl + h * kHeadDim;
         const float* vn = p.qkv + 2 * p.Hl + h * kHeadDim;
-        const float qa = __ldcg(q + lane), qb = __ldcg(q + lane + kHalfHead);
-        float ka = 0.0f, kb = 0.0f;
+        float qa, qb, ka = 0.0f, kb = 0.0f;
         float2 vnew = make_float2(0.0f, 0.0f);
-        if (has_n) {
-            ka = __ldcg(kn + lane);
-            kb = __ldcg(kn + lane + kHalfHead);
-            vnew = __ldcg(reinterpret_cast<const float2*>(vn) + lane);
+        if (p.tag_qkv) {
+            const QkvWords w = load_qkv_tagged(p, layer, h, has_n);
+            qa = w.qa, qb = w.qb, ka = w.ka, kb = w.kb;
+            vnew = make_float2(w.vx, w.vy);
+        } else {
+            qa = __ldcg(q + lane);
+            qb = __ldcg(q + lane + kHalfHead);
+            if (has_n) {
+                ka = __ldcg(kn + lane);
+                kb = __ldcg(kn + lane + kHalfHead);
+                vnew = __ldcg(reinterpret_cast<const float2*>(vn) + lane);
+            }
         }
         qsh[lane] = (qa * cs.x + qb * cs.y) * 0.125f;  // 1/sqrt(64) is exact
         qsh[lane + kHalfHead] = (-qa * cs.y + qb * cs.x) * 0.125f;
@@ -786,7 +890,7 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
     float2* out = reinterpret_cast<float2*>(p.att + h * kHeadDim);
     if (nct == 1) {
         out[lane] = make_float2(acc.x / L, acc.y / L);
-        signal_phase(p, ph);
+        signal_warp(p, ph);
         return true;
     }
     // A head split over nct CTAs: the last CTA to finish merges their partials.
@@ -819,13 +923,13 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
         acc2.y = fmaf(wt, ok.y, acc2.y);
     }
     out[lane] = make_float2(acc2.x / L2, acc2.y / L2);
-    signal_phase(p, ph);
+    signal_warp(p, ph);
     return true;
 }
 
 template <bool TP>
 __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint64_t* full, uint64_t* empty,
-                          float* red, unsigned long long* best_s, int* s_ok, volatile int* quiet) {
+                          float* red, unsigned long long* best_s, int* s_ok, volatile int* quiet, float* xr) {
     DevState* st = p.st;
     const int t = threadIdx.x - 32;
     const int warp = t >> 5, lane = t & 31;
@@ -867,31 +971,38 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 }
             }
         }
-        if (ph > 0 && !wait_phase(p, ph - 1, s_ok)) return;
+        // tag_split: a staging after a split projection (W1/V after the
+        // out-projection, QKV and the LM head after W2) waits for the tags of
+        // the partial sums it reads, not for the phase counter; the residual it
+        // adds them to is the CTA's own copy in shared memory.
+        const bool by_tags = TP && p.tag_split && (kind == kW13 || (kind == kQKV && l > 0) || kind == kLM);
+        if (ph > 0 && !by_tags && !wait_phase(p, ph - 1, s_ok)) return;
         if (t == 0) trace_at(p, ph, kTrConsStart);
         // Stage this phase's input vector.
         if (kind == kQKV) {
             if (l == 0)
                 stage_norm(p, p.emb + static_cast<size_t>(st->in.token_in) * p.H, nullptr, nullptr, 0, y->g1, xs, red,
-                           p.xa);
+                           p.xa, xr, false);
             else if (TP)
-                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, xtag(p, l - 1, 1), nb_w2, y->g1, xs, red, p.xa);
+                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, xtag(p, l - 1, 1), nb_w2, y->g1, xs, red, p.xa, xr,
+                              false);
             else
-                stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, y->g1, xs, red, p.xa);
+                stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, y->g1, xs, red, p.xa, xr, false);
         } else if (kind == kWo) {
             stage_copy(p.att, p.Hl, xs);
         } else if (kind == kW13) {
             if (TP)
-                stage_norm_tp(p, p.xa, y->bo, 0, xtag(p, l, 0), nb_wo, y->g2, xs, red, p.xb);
+                stage_norm_tp(p, p.xa, y->bo, 0, xtag(p, l, 0), nb_wo, y->g2, xs, red, p.xb, xr, false);
             else
-                stage_norm(p, p.xa, y->bo, p.cres, nb_wo, y->g2, xs, red, p.xb);
+                stage_norm(p, p.xa, y->bo, p.cres, nb_wo, y->g2, xs, red, p.xb, xr, false);
         } else if (kind == kW2) {
             stage_copy(p.ffh, p.Fl, xs);
-        } else {  // kLM
+        } else {  // kLM: the final residual also goes to xa (the LM head's input in global memory)
             if (TP)
-                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, xtag(p, l - 1, 1), nb_w2, p.gnorm, xs, red, p.xa);
+                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, xtag(p, l - 1, 1), nb_w2, p.gnorm, xs, red, p.xa, xr,
+                              true);
             else
-                stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, p.gnorm, xs, red, p.xa);
+                stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, p.gnorm, xs, red, p.xa, xr, true);
         }
         consumer_sync();
         if (t == 0) *quiet = 0;
@@ -957,8 +1068,13 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
             acc_b = warp_sum(acc_b);
             switch (kind) {
                 case kQKV:
-                    if (lane == 0 && va) p.qkv[Ra] = acc_a + ea;
-                    if (lane == 1 && vb) p.qkv[Rb] = acc_b + eb;
+                    if (p.tag_qkv) {
+                        if (lane == 0 && va) st_relaxed_u64(p.qkvw + Ra, xword(acc_a + ea, qtag(p, l)));
+                        if (lane == 1 && vb) st_relaxed_u64(p.qkvw + Rb, xword(acc_b + eb, qtag(p, l)));
+                    } else {
+                        if (lane == 0 && va) p.qkv[Ra] = acc_a + ea;
+                        if (lane == 1 && vb) p.qkv[Rb] = acc_b + eb;
+                    }
                     break;
                 case kWo:
                 case kW2: {  // partial row sums of this CTA's boxes of group g (c: this CTA's rank among its owners)
@@ -967,6 +1083,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                         float* q = p.cres + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows;
                         if (lane == 0) q[ra] = acc_a;
                         if (lane == 1) q[rb] = acc_b;
+                    } else if (lane < 2 && p.tag_split) {  // every rank's slot now
+                        store_all_tp(p, l, kind == kW2, g, c, lane == 0 ? ra : rb, lane == 0 ? acc_a : acc_b);
                     } else if (lane < 2) {  // this rank's own slot; forwarded to the peers after the signal
                         store_own_tp(p, l, kind == kW2, g, c, lane == 0 ? ra : rb, lane == 0 ? acc_a : acc_b);
                     }
@@ -991,8 +1109,9 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 }
             }
         }
-        if (kind != kLM) signal_phase(p, ph);
-        if (TP && split && lane < 2) forward_partials_tp(p, r.t0, r.t1, r.nb, r.T, kind == kW2, lane == 0 ? ra : rb);
+        if (kind != kLM && !(TP && p.tag_split && split) && !(kind == kQKV && p.tag_qkv)) signal_phase(p, ph);
+        if (TP && split && !p.tag_split && lane < 2)
+            forward_partials_tp(p, r.t0, r.t1, r.nb, r.T, kind == kW2, lane == 0 ? ra : rb);
         if (t == 0) trace_at(p, ph, kTrConsEnd);
     }
     // LM head: CTA argmax -> global max; the last CTA publishes the winner.
@@ -1033,6 +1152,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     unsigned long long* best_s = reinterpret_cast<unsigned long long*>(red + 16);  // 8
     int* s_ok = reinterpret_cast<int*>(best_s + kConsumerWarps);            // 1 (+pad)
     volatile int* quiet = s_ok + 8;                                           // producer pause flag
+    // resid_smem: this CTA's copy of the residual stream [H], after the fixed layout
+    float* xr = p.resid_smem ? reinterpret_cast<float*>(smem + kSmemBytes) : nullptr;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
@@ -1051,20 +1172,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
     // all-reduce.  A smaller sum means a peer did not join (the host aborted
     // the communicator after its step timeout): leave before any load or any
     // store to peer memory.  Every CTA reads the same word.
-    if (TP && *reinterpret_cast<const volatile int*>(&p.st->tp_sync) != p.tp) {
+    if (TP && p.tp > 1 && *reinterpret_cast<const volatile int*>(&p.st->tp_sync) != p.tp) {
         if (threadIdx.x == 0) atomicOr(&p.st->err, kErrPeer);
         return;
     }
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) producer(p, ring, full, empty, quiet);
     } else {
-        consumers<TP>(p, ring, xs, full, empty, red, best_s, s_ok, quiet);
+        consumers<TP>(p, ring, xs, full, empty, red, best_s, s_ok, quiet, xr);
     }
 }
 
 }  // namespace
 
-size_t persistent_smem_bytes() { return kSmemBytes; }
+size_t persistent_smem_bytes(int H, int resid_smem) {
+    return kSmemBytes + (resid_smem ? static_cast<size_t>(H) * sizeof(float) : 0);
+}
 
 cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cudaStream_t s) {
     if (p.H <= 0 || p.Hl <= 0 || p.Fl <= 0 || p.H > kMaxK || p.Hl > kMaxK || p.Fl > kMaxK ||
@@ -1076,19 +1199,22 @@ cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cud
     if (p.inflight < 1 || p.inflight > kSlots) return cudaErrorInvalidValue;
     if (p.tp < 1 || p.tp > kMaxTp || p.rank < 0 || p.rank >= p.tp || (p.tp > 1 && p.finish_greedy))
         return cudaErrorInvalidValue;
-    for (int r = 0; r < p.tp && p.tp > 1; ++r)
+    const bool exchange = p.tp > 1 || p.tag_split;  // the instantiation with tagged partial sums
+    for (int r = 0; r < p.tp && exchange; ++r)
         if (!p.xc[r]) return cudaErrorInvalidValue;
+    if (p.tag_split && !p.resid_smem) return cudaErrorInvalidValue;  // tag-ordered stagings read no global residual
     if (persist_max_contrib(p.H, p.Hl, num_sms) > kPersistMaxContrib ||
         persist_max_contrib(p.H, p.Fl, num_sms) > kPersistMaxContrib)
         return cudaErrorInvalidValue;
-    auto kern = p.tp > 1 ? decode_persistent_kernel<true> : decode_persistent_kernel<false>;
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    const size_t smem = persistent_smem_bytes(p.H, p.resid_smem);
+    if (smem > kMaxSmemPerBlock) return cudaErrorInvalidValue;
+    auto kern = exchange ? decode_persistent_kernel<true> : decode_persistent_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;

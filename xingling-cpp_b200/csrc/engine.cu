@@ -12,6 +12,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <random>
 #include <string>
@@ -322,6 +323,7 @@ int Engine::alloc_all() {
     add(&xa_, H * 4);
     add(&xb_, H * 4);
     add(&qkv_, 3 * Hl * 4);
+    add(&qkvw_, 3 * Hl * 8);
     add(&att_, Hl * 4);
     add(&ffh_, Fl * 4);
     add(&part_, H * 4);
@@ -364,8 +366,9 @@ int Engine::alloc_all() {
     XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&arena_), total));
     arena_bytes_ = total;
     XL_CUDA(cudaMemset(arena_, 0, total));
-    if (tp_ > 1 && tp_ <= kMaxTp) {
-        // Its own allocation, so that the peers can map it (an IPC handle covers a whole allocation).
+    if (tp_ <= kMaxTp) {
+        // Its own allocation, so that the peers can map it (an IPC handle covers a whole allocation);
+        // one GPU uses it too when the split projections' partial sums are ordered by tags (tag_split).
         const size_t xc = 2 * static_cast<size_t>(tp_) * (H / kPersistTileRows) * kPersistMaxContrib *
                           kPersistTileRows * 8;
         XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&xbuf_), xc));
@@ -725,6 +728,11 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     p.T = T_;
     p.finish_greedy = sampled || tpk ? 0 : 1;
     p.tma_evict_first = tma_evict_first_;
+    p.sig_cta = sig_cta_;
+    p.resid_smem = (resid_smem_ || tag_split_) && persistent_smem_bytes(H_, 1) <= 232448 ? 1 : 0;
+    p.tag_split = tag_split_ && p.resid_smem ? 1 : 0;
+    p.tag_qkv = tag_qkv_;
+    p.qkvw = qkvw_;
     p.tp = tp_;
     p.rank = rank_;
     if (tpk) {
@@ -738,6 +746,8 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
         // leaves before touching any peer's memory.
         XL_CUDA(cudaMemsetAsync(&st_->tp_sync, 0, sizeof(int), s));
         XL_NCCL(ncclAllReduce(&st_->tp_one, &st_->tp_sync, 1, ncclInt32, ncclSum, comm_, s));
+    } else {
+        p.xc[0] = reinterpret_cast<unsigned long long*>(xbuf_);  // tag_split on one GPU: this engine's own slots
     }
     XL_CUDA(cudaMemsetAsync(
         done_, 0, (5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_) * sizeof(int),
@@ -1078,16 +1088,25 @@ bool Engine::drain_stream(int timeout_ms) {
 // missing rank return; the persistent kernel of that step finds the liveness
 // sum short and leaves.  The engine refuses every later call.
 int Engine::abort_tp(const std::string& why) {
+    // XL_TRACE_ABORT=1: each step of the abort on stderr (diagnosis of a stuck abort).
+    static const bool trace = std::getenv("XL_TRACE_ABORT") != nullptr;
+    auto note = [&](const char* what) {
+        if (trace) std::fprintf(stderr, "[xl rank %d] abort: %s\n", rank_, what), std::fflush(stderr);
+    };
+    note(why.c_str());
     for (cudaGraphExec_t* e : {&decode_exec_, &decode_exec_s_, &gen_exec_, &gen_exec_s_}) {
         if (*e) cudaGraphExecDestroy(*e);
         *e = nullptr;
     }
+    note("graphs released");
     if (comm_) ncclCommAbort(comm_);
     comm_ = nullptr;
+    note("communicator aborted");
     failed_ = true;
     fail_msg_ = "tensor parallel: " + why + "; the communicator was aborted and this engine is unusable: create a new "
                 "one on every rank";
     const bool idle = drain_stream(10000);
+    note(idle ? "stream drained" : "stream still busy after 10 s");
     if (!idle) fail_msg_ += " (its stream did not drain within 10 s)";
     stream_idle_ = idle;
     has_seq_ = false;
@@ -1414,6 +1433,14 @@ int Engine::set_option(const char* key, int value) {
             return XL_ERR_ARG;
         }
         tma_evict_first_ = value;
+        return loaded_ ? capture_decode_graph() : XL_OK;
+    }
+    if (k == "sig_cta" || k == "resid_smem" || k == "tag_split" || k == "tag_qkv") {
+        if (value != 0 && value != 1) {
+            set_error(k + " must be 0 or 1");
+            return XL_ERR_ARG;
+        }
+        (k == "sig_cta" ? sig_cta_ : k == "resid_smem" ? resid_smem_ : k == "tag_split" ? tag_split_ : tag_qkv_) = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
     if (k == "kernel_events") {

@@ -179,6 +179,12 @@ struct PersistentParams {
     int H, Hl, heads, Fl, V, T;  // V: rows of this rank's vocab shard
     int finish_greedy;          // 1: the LM head's last CTA writes the argmax as the step's id
     int tma_evict_first;        // 1: weight boxes are loaded with an L2 evict-first policy
+    int sig_cta;                // 1: one release per CTA signals a phase (after a consumer barrier); 0: one per warp
+    int resid_smem;             // 1: every CTA keeps the whole residual stream in shared memory (H floats)
+    int tag_qkv;                // 1: QKV outputs are tagged words in qkvw; attention waits for its head's tags
+    unsigned long long* qkvw;   // [3*Hl] tagged QKV outputs (tag_qkv)
+    int tag_split;              // 1: out-proj / W2 partial sums go tagged to every rank's xc, the next staging
+                                //    waits for the tags (no phase counter); needs resid_smem (also at tp == 1)
     // Tensor parallel (tp > 1): every CTA writes its out-projection / W2 partial
     // row sums into every rank's exchange buffer xc[r] (peer memory over NVLink),
     // laid out [2 (out-proj, W2)][tp][H/16][kPersistMaxContrib][16] words of
@@ -189,7 +195,7 @@ struct PersistentParams {
     unsigned long long* xc[kMaxTp];
 };
 constexpr int kTraceFields = 5;
-size_t persistent_smem_bytes();
+size_t persistent_smem_bytes(int H, int resid_smem);
 // The TMA map (no swizzle) of a row-major [rows][cols] weight viewed as
 // [rows][cols/tw][tw] (tw = persist_tile_w(cols)), box [16 rows]
 // [persist_box_tiles(cols) k-tiles][tw floats]; cols must be a multiple of 64.
