@@ -48,6 +48,15 @@ for _p in (PKG, ORACLE):
 import xl_synth as S  # noqa: E402
 
 PROMPT, DECODE, PREFILL_N = 32, 128, 512
+ENGINE_OPTS: dict[str, int] = {}  # --opt KEY=VALUE, applied to every engine the bench creates
+
+
+def apply_opts(eng):
+    for k, v in ENGINE_OPTS.items():
+        eng.set_option(k, v)
+    return eng
+
+
 REF_DECODE_SAMPLE = 128  # the reference arm times the whole decode workload each step
 WEIGHT_DIR = os.environ.get("XL_BENCH_WEIGHTS", os.path.join(tempfile.gettempdir(), "xl_weights", "full"))
 METRIC = "decode tokens/s, XingLing-0.68B fp32, batch 1"
@@ -327,7 +336,7 @@ def xl_arm(args) -> None:
             sys.stdout.flush()
         dist.destroy_process_group()
         return
-    eng = llm_cpp_engine.InferenceEngine(f"cuda:{local}")
+    eng = apply_opts(llm_cpp_engine.InferenceEngine(f"cuda:{local}"))
     eng.load(WEIGHT_DIR)
     eng.load(WEIGHT_DIR)  # the second load reads the tree from the page cache
     load_s = eng.last_load_s()
@@ -561,7 +570,7 @@ def phase_summary(raw: bytes, sms: int, layers: int) -> dict:
 def tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, path, trace=False) -> dict:
     id_holder = [llm_cpp_engine.nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(id_holder, src=0)
-    eng = llm_cpp_engine.InferenceEngine(f"cuda:{local}", tp=world, rank=rank, nccl_id=id_holder[0])
+    eng = apply_opts(llm_cpp_engine.InferenceEngine(f"cuda:{local}", tp=world, rank=rank, nccl_id=id_holder[0]))
     eng.set_option("decode_path", path)
     eng.set_option("kernel_events", 1)  # the persistent kernel's own time, apart from the NCCL steps
     eng.load(WEIGHT_DIR)
@@ -679,7 +688,7 @@ def ncu_case(args) -> None:
     shape = S.WIDE2 if args.ncu_case == "decode-wide" else S.FULL
     wdir = WEIGHT_DIR if shape is S.FULL else WEIGHT_DIR + "_wide2"
     S.write_weight_tree(wdir, shape)
-    eng = llm_cpp_engine.InferenceEngine("cuda:0", **shape.engine_kwargs())
+    eng = apply_opts(llm_cpp_engine.InferenceEngine("cuda:0", **shape.engine_kwargs()))
     eng.load(wdir)
     eng.set_option("decode_path", args.decode_path)
     if args.ncu_case == "prefill-512":
@@ -712,12 +721,17 @@ def main() -> None:
                     default=None)
     ap.add_argument("--decode-path", type=int, default=0, choices=[0, 1])
     ap.add_argument("--tp-only", action="store_true", help="only the tensor-parallel decode latency (torchrun, N>1)")
+    ap.add_argument("--opt", action="append", default=[], metavar="KEY=VALUE",
+                    help="engine option (InferenceEngine.set_option) for every engine the bench creates")
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--budget", type=float, default=15.0, help=argparse.SUPPRESS)
     ap.add_argument("--weights", default=WEIGHT_DIR, help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    for kv in args.opt:
+        k, _, v = kv.partition("=")
+        ENGINE_OPTS[k] = int(v)
     if args.ncu_case:
         ncu_case(args)
     elif args.cpu_worker:

@@ -266,60 +266,6 @@ __device__ __forceinline__ unsigned xtag(const PersistentParams& p, int l, int w
 __device__ __forceinline__ unsigned long long xword(float v, unsigned tag) {
     return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
 }
-// tag_qkv: the QKV phase's outputs are tagged words (value, step and layer),
-// so an attention CTA waits for its own head's q / k / v, not for the grid.
-__device__ __forceinline__ unsigned qtag(const PersistentParams& p, int l) {
-    return static_cast<unsigned>(p.st->epoch) * static_cast<unsigned>(p.layers) + static_cast<unsigned>(l) + 1u;
-}
-__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* a) {
-    unsigned long long v;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_relaxed_u64(unsigned long long* a, unsigned long long v) {
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
-}
-__device__ __forceinline__ bool tag_is(unsigned long long w, unsigned tag) { return static_cast<unsigned>(w >> 32) == tag; }
-__device__ __forceinline__ float word_val(unsigned long long w) { return __uint_as_float(static_cast<unsigned>(w)); }
-// One warp of head h's attention: q (and, for the chunk holding position n,
-// k and v) of layer l, spinning (bounded) until every word carries this
-// step's tag.  On a timeout the error bit is set and zeros come back.
-struct QkvWords {
-    float qa, qb, ka, kb, vx, vy;
-};
-__device__ __noinline__ QkvWords load_qkv_tagged(const PersistentParams& p, int l, int h, bool has_n) {
-    const int lane = threadIdx.x & 31;
-    const unsigned tag = qtag(p, l);
-    const unsigned long long* q = p.qkvw + h * kHeadDim;
-    const unsigned long long* k = p.qkvw + p.Hl + h * kHeadDim;
-    const unsigned long long* v = p.qkvw + 2 * p.Hl + h * kHeadDim;
-    uint32_t it = 0;
-    unsigned long long t0 = 0;
-    for (;;) {
-        const unsigned long long a = ld_relaxed_u64(q + lane), b = ld_relaxed_u64(q + lane + kHalfHead);
-        unsigned long long c = 0, d = 0, e = 0, f = 0;
-        bool ok = tag_is(a, tag) && tag_is(b, tag);
-        if (has_n) {
-            c = ld_relaxed_u64(k + lane);
-            d = ld_relaxed_u64(k + lane + kHalfHead);
-            e = ld_relaxed_u64(v + 2 * lane);
-            f = ld_relaxed_u64(v + 2 * lane + 1);
-            ok = ok && tag_is(c, tag) && tag_is(d, tag) && tag_is(e, tag) && tag_is(f, tag);
-        }
-        if (__all_sync(0xffffffffu, ok))
-            return QkvWords{word_val(a), word_val(b), word_val(c), word_val(d), word_val(e), word_val(f)};
-        ++it;
-        if ((it & 15u) == 0) {
-            const unsigned long long now = globaltimer();
-            if (t0 == 0) t0 = now;
-            if (it >= kFlagSpinLimit || now - t0 > kWaitLimitNs || aborted(p.st)) {
-                if (lane == 0) atomicOr(&p.st->err, kErrFlag);
-                return QkvWords{0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-            }
-        }
-    }
-}
-
 // This rank's partial sum of row `row` of group g (slot c) of layer l's split
 // projection w2, tagged, into its own exchange buffer.
 __device__ __noinline__ void store_own_tp(const PersistentParams& p, int l, int w2, int g, int c, int row, float v) {
@@ -802,7 +748,7 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
     // A CTA without an attention item neither waits nor signals: the next
     // phase waits for the heads' outputs, which imply the QKV phase.
     if (!has) return true;
-    if (!p.tag_qkv && !wait_phase(p, ph - 1, s_ok)) return false;  // tag_qkv: each warp waits for its head's words
+    if (!wait_phase(p, ph - 1, s_ok)) return false;
     if (t == 0) trace_at(p, ph, kTrConsStart);
     float* qsh = xs + warp * kAttnWarpScratch;
     float* apart = xs + kConsumerWarps * kAttnWarpScratch;  // [8][68]
@@ -812,20 +758,13 @@ __device__ bool attention_phase(const PersistentParams& p, int layer, int ph, in
         const float* q = p.qkv + h * kHeadDim;
         const float* kn = p.qkv + p.Hl + h * kHeadDim;
         const float* vn = p.qkv + 2 * p.Hl + h * kHeadDim;
-        float qa, qb, ka = 0.0f, kb = 0.0f;
+        const float qa = __ldcg(q + lane), qb = __ldcg(q + lane + kHalfHead);
+        float ka = 0.0f, kb = 0.0f;
         float2 vnew = make_float2(0.0f, 0.0f);
-        if (p.tag_qkv) {
-            const QkvWords w = load_qkv_tagged(p, layer, h, has_n);
-            qa = w.qa, qb = w.qb, ka = w.ka, kb = w.kb;
-            vnew = make_float2(w.vx, w.vy);
-        } else {
-            qa = __ldcg(q + lane);
-            qb = __ldcg(q + lane + kHalfHead);
-            if (has_n) {
-                ka = __ldcg(kn + lane);
-                kb = __ldcg(kn + lane + kHalfHead);
-                vnew = __ldcg(reinterpret_cast<const float2*>(vn) + lane);
-            }
+        if (has_n) {
+            ka = __ldcg(kn + lane);
+            kb = __ldcg(kn + lane + kHalfHead);
+            vnew = __ldcg(reinterpret_cast<const float2*>(vn) + lane);
         }
         qsh[lane] = (qa * cs.x + qb * cs.y) * 0.125f;  // 1/sqrt(64) is exact
         qsh[lane + kHalfHead] = (-qa * cs.y + qb * cs.x) * 0.125f;
@@ -1068,13 +1007,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
             acc_b = warp_sum(acc_b);
             switch (kind) {
                 case kQKV:
-                    if (p.tag_qkv) {
-                        if (lane == 0 && va) st_relaxed_u64(p.qkvw + Ra, xword(acc_a + ea, qtag(p, l)));
-                        if (lane == 1 && vb) st_relaxed_u64(p.qkvw + Rb, xword(acc_b + eb, qtag(p, l)));
-                    } else {
-                        if (lane == 0 && va) p.qkv[Ra] = acc_a + ea;
-                        if (lane == 1 && vb) p.qkv[Rb] = acc_b + eb;
-                    }
+                    if (lane == 0 && va) p.qkv[Ra] = acc_a + ea;
+                    if (lane == 1 && vb) p.qkv[Rb] = acc_b + eb;
                     break;
                 case kWo:
                 case kW2: {  // partial row sums of this CTA's boxes of group g (c: this CTA's rank among its owners)
@@ -1109,7 +1043,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 }
             }
         }
-        if (kind != kLM && !(TP && p.tag_split && split) && !(kind == kQKV && p.tag_qkv)) signal_phase(p, ph);
+        if (kind != kLM && !(TP && p.tag_split && split)) signal_phase(p, ph);
         if (TP && split && !p.tag_split && lane < 2)
             forward_partials_tp(p, r.t0, r.t1, r.nb, r.T, kind == kW2, lane == 0 ? ra : rb);
         if (t == 0) trace_at(p, ph, kTrConsEnd);

@@ -16,6 +16,7 @@
 #include <cstring>
 #include <random>
 #include <string>
+#include <memory>
 #include <mutex>
 #include <thread>
 #include <utility>
@@ -323,7 +324,6 @@ int Engine::alloc_all() {
     add(&xa_, H * 4);
     add(&xb_, H * 4);
     add(&qkv_, 3 * Hl * 4);
-    add(&qkvw_, 3 * Hl * 8);
     add(&att_, Hl * 4);
     add(&ffh_, Fl * 4);
     add(&part_, H * 4);
@@ -336,7 +336,7 @@ int Engine::alloc_all() {
     add(&logits_, vl * 4);
     add(&attn_ws_, static_cast<size_t>(heads_l_) * maxs * (kHeadDim + 2) * 4);
     add(&attn_cnt_, heads_l_ * 4);
-    add(&done_, (5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_) * 4);
+    add(&done_, done_words() * 4);
     add(&rep_flags_, vl);
     add(&st_, sizeof(DevState));
     samp_grid_ = sample_grid(vl_, num_sms_, 1);
@@ -731,8 +731,6 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     p.sig_cta = sig_cta_;
     p.resid_smem = (resid_smem_ || tag_split_) && persistent_smem_bytes(H_, 1) <= 232448 ? 1 : 0;
     p.tag_split = tag_split_ && p.resid_smem ? 1 : 0;
-    p.tag_qkv = tag_qkv_;
-    p.qkvw = qkvw_;
     p.tp = tp_;
     p.rank = rank_;
     if (tpk) {
@@ -749,9 +747,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     } else {
         p.xc[0] = reinterpret_cast<unsigned long long*>(xbuf_);  // tag_split on one GPU: this engine's own slots
     }
-    XL_CUDA(cudaMemsetAsync(
-        done_, 0, (5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_) * sizeof(int),
-        s));
+    XL_CUDA(cudaMemsetAsync(done_, 0, done_words() * sizeof(int), s));
     // Optional event-record nodes around the kernel (kernel_events): its own
     // duration, read back by last_kernel_ms.
     if (kernel_events_) XL_CUDA(cudaEventRecordWithFlags(kev0_, s, cudaEventRecordExternal));
@@ -1094,14 +1090,40 @@ int Engine::abort_tp(const std::string& why) {
         if (trace) std::fprintf(stderr, "[xl rank %d] abort: %s\n", rank_, what), std::fflush(stderr);
     };
     note(why.c_str());
+    // ncclCommAbort raises the communicator's abort flag first (the collectives
+    // waiting for the missing rank return), then waits until no executable
+    // graph holds its collectives.  Releasing an executable graph that is still
+    // running blocks until it completes, and it completes only once the flag is
+    // up: so the abort runs on a helper thread while this one releases the
+    // graphs.  Both waits are bounded here; a helper still blocked after them
+    // is detached (the engine is unusable either way).
+    std::thread aborter;
+    auto done = std::make_shared<std::atomic<bool>>(false);
+    if (comm_) {
+        ncclComm_t c = comm_;
+        aborter = std::thread([c, done]() {
+            ncclCommAbort(c);
+            done->store(true);
+        });
+    }
+    comm_ = nullptr;
     for (cudaGraphExec_t* e : {&decode_exec_, &decode_exec_s_, &gen_exec_, &gen_exec_s_}) {
         if (*e) cudaGraphExecDestroy(*e);
         *e = nullptr;
     }
     note("graphs released");
-    if (comm_) ncclCommAbort(comm_);
-    comm_ = nullptr;
-    note("communicator aborted");
+    if (aborter.joinable()) {
+        const auto t0 = std::chrono::steady_clock::now();
+        while (!done->load() && std::chrono::steady_clock::now() - t0 < std::chrono::seconds(20))
+            std::this_thread::sleep_for(std::chrono::milliseconds(1));
+        if (done->load()) {
+            aborter.join();
+            note("communicator aborted");
+        } else {
+            aborter.detach();
+            note("communicator abort still running after 20 s (detached)");
+        }
+    }
     failed_ = true;
     fail_msg_ = "tensor parallel: " + why + "; the communicator was aborted and this engine is unusable: create a new "
                 "one on every rank";
@@ -1435,12 +1457,12 @@ int Engine::set_option(const char* key, int value) {
         tma_evict_first_ = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
-    if (k == "sig_cta" || k == "resid_smem" || k == "tag_split" || k == "tag_qkv") {
+    if (k == "sig_cta" || k == "resid_smem" || k == "tag_split") {
         if (value != 0 && value != 1) {
             set_error(k + " must be 0 or 1");
             return XL_ERR_ARG;
         }
-        (k == "sig_cta" ? sig_cta_ : k == "resid_smem" ? resid_smem_ : k == "tag_split" ? tag_split_ : tag_qkv_) = value;
+        (k == "sig_cta" ? sig_cta_ : k == "resid_smem" ? resid_smem_ : tag_split_) = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
     if (k == "kernel_events") {

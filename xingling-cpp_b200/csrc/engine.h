@@ -125,7 +125,6 @@ class Engine {
     float* xb_ = nullptr;      // decode residual stream (pong)
     float* cres_ = nullptr;    // persistent decode: partial row sums of the residual projections
     float* qkv_ = nullptr;     // [3*Hl]
-    unsigned long long* qkvw_ = nullptr;  // [3*Hl] tagged QKV outputs of the persistent kernel (tag_qkv)
     float* att_ = nullptr;     // [Hl]
     float* ffh_ = nullptr;     // [Fl]
     float* part_ = nullptr;    // [H] TP partial sums
@@ -182,10 +181,14 @@ class Engine {
     float last_load_s_ = 0.0f;  // wall time of the last load's file reads and copies
     int inflight_ = 3;  // persistent decode: weight boxes requested but not landed, per SM
     int tma_evict_first_ = 1;  // persistent decode: weight boxes loaded with an L2 evict-first policy
-    int sig_cta_ = 0;          // persistent decode: one phase signal per CTA (else per warp)
-    int resid_smem_ = 0;       // persistent decode: the residual stream kept in each CTA's shared memory
+    int sig_cta_ = 1;          // persistent decode: one phase signal per CTA (else per warp)
+    int resid_smem_ = 1;       // persistent decode: the residual stream kept in each CTA's shared memory
     int tag_split_ = 0;        // persistent decode: split-projection partial sums ordered by tags (implies resid_smem)
-    int tag_qkv_ = 0;          // persistent decode: QKV outputs ordered by tags (attention waits per head)
+    // Persistent kernel counters, zeroed before each launch: phase counters
+    // [5*layers + 1], then the attention merge tickets [layers][heads].
+    size_t done_words() const {
+        return 5 * static_cast<size_t>(cfg_.layers) + 1 + static_cast<size_t>(cfg_.layers) * heads_l_;
+    }
     bool loaded_ = false;
     bool failed_ = false;          // tensor parallel: aborted or a device error; every later step is refused
     std::string fail_msg_;

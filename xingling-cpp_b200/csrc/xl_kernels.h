@@ -181,8 +181,6 @@ struct PersistentParams {
     int tma_evict_first;        // 1: weight boxes are loaded with an L2 evict-first policy
     int sig_cta;                // 1: one release per CTA signals a phase (after a consumer barrier); 0: one per warp
     int resid_smem;             // 1: every CTA keeps the whole residual stream in shared memory (H floats)
-    int tag_qkv;                // 1: QKV outputs are tagged words in qkvw; attention waits for its head's tags
-    unsigned long long* qkvw;   // [3*Hl] tagged QKV outputs (tag_qkv)
     int tag_split;              // 1: out-proj / W2 partial sums go tagged to every rank's xc, the next staging
                                 //    waits for the tags (no phase counter); needs resid_smem (also at tp == 1)
     // Tensor parallel (tp > 1): every CTA writes its out-projection / W2 partial
