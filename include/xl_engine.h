@@ -71,7 +71,15 @@ XL_API void xl_config_default(xl_config* cfg);
  * ranks, and every rank must create its engine concurrently, one process per
  * GPU of one node: creation also maps every rank's exchange buffer over CUDA
  * IPC (the persistent decode kernel writes its partial sums there) and fails
- * with XL_ERR_CUDA if a mapping cannot be made. */
+ * with XL_ERR_CUDA if a mapping cannot be made, or with XL_ERR_ARG if the
+ * ranks' SM counts or shapes differ (the exchange slots are laid out by each
+ * rank's grid).  Tensor parallel, every later call: the host's wait for the
+ * call's GPU work is bounded by the option step_timeout_ms (default 30000)
+ * and by NCCL's asynchronous error; past either, the engine aborts its
+ * communicator and returns XL_ERR_NCCL, and every later call returns
+ * XL_ERR_STATE (the ranks must create new engines).  A device error on a
+ * tensor-parallel rank makes the engine unusable the same way; on one GPU it
+ * drops the cached sequence instead (the next prefill starts clean). */
 #define XL_NCCL_ID_BYTES 128
 XL_API int xl_engine_create(const xl_config* cfg, int device, int tp_size, int tp_rank, const void* nccl_id,
                             xl_engine** out);
