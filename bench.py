@@ -524,10 +524,11 @@ def tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks) -
     NVLink inside the kernel) and on the per-op path (NCCL all-reduces) for
     comparison."""
     out = tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, 0, trace=args.tp_only)
-    per_op = tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, 1)
-    out["per_op_ms_per_token"] = per_op["ms_per_token"]
-    out["per_op_first_tokens"] = per_op["first_tokens"]
-    out["per_op_gpu_launches"] = per_op["gpu_launches"]
+    if args.tp_per_op:
+        per_op = tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, 1)
+        out["per_op_ms_per_token"] = per_op["ms_per_token"]
+        out["per_op_first_tokens"] = per_op["first_tokens"]
+        out["per_op_gpu_launches"] = per_op["gpu_launches"]
     return out
 
 
@@ -721,6 +722,8 @@ def main() -> None:
                     default=None)
     ap.add_argument("--decode-path", type=int, default=0, choices=[0, 1])
     ap.add_argument("--tp-only", action="store_true", help="only the tensor-parallel decode latency (torchrun, N>1)")
+    ap.add_argument("--tp-per-op", type=int, default=1, choices=[0, 1],
+                    help="also time the per-op tensor-parallel path (NCCL all-reduces) beside the persistent one")
     ap.add_argument("--opt", action="append", default=[], metavar="KEY=VALUE",
                     help="engine option (InferenceEngine.set_option) for every engine the bench creates")
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)

@@ -303,6 +303,51 @@ __device__ __noinline__ void forward_partials_tp(const PersistentParams& p, int 
         tau += bi1 - bi0;
     }
 }
+// Tensor parallel, greedy steps: the merge area after the partial-sum slots of
+// rank r's exchange buffer holds one (key, tag) pair of 64-bit words per rank.
+__device__ __forceinline__ unsigned long long* xmerge(const PersistentParams& p, int r) {
+    const int groups = p.H / kPersistTileRows;
+    return p.xc[r] + static_cast<size_t>(2 * p.tp) * groups * kPersistMaxContrib * kPersistTileRows;
+}
+// This rank's packed argmax key (value key, ~global id) goes to slot [rank]
+// of every rank's merge area: the key word, one system-scope fence, then the
+// step's tag word (every slot then holds this step's key before its tag).
+// The step's winner is the largest key of all ranks, read back from this
+// rank's own area once every tag is there.  Slot reuse is safe: a rank
+// overwrites its slots only in the next step, which starts with an NCCL
+// barrier that every rank joins after this kernel.  Returns 0 (and sets the
+// error bit) if a peer's tag does not arrive within the wait limit.
+__device__ unsigned long long merge_argmax_tp(const PersistentParams& p, unsigned long long key) {
+    const unsigned long long tag = static_cast<unsigned long long>(static_cast<unsigned>(p.st->epoch)) + 1ull;
+    for (int r = 0; r < p.tp; ++r)
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(xmerge(p, r) + 2 * p.rank), "l"(key) : "memory");
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int r = 0; r < p.tp; ++r)
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(xmerge(p, r) + 2 * p.rank + 1), "l"(tag) : "memory");
+    const unsigned long long* mine = xmerge(p, p.rank);
+    unsigned long long best = 0;
+    for (int src = 0; src < p.tp; ++src) {
+        uint32_t it = 0;
+        unsigned long long t0 = 0, tg = 0;
+        for (;;) {
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(tg) : "l"(mine + 2 * src + 1) : "memory");
+            if (tg == tag) break;
+            if ((++it & 63u) == 0) {
+                const unsigned long long now = globaltimer();
+                if (t0 == 0) t0 = now;
+                if (it >= kFlagSpinLimit || now - t0 > kWaitLimitNs || aborted(p.st)) {
+                    atomicOr(&p.st->err, kErrFlag);
+                    return 0ull;
+                }
+            }
+        }
+        unsigned long long k;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(k) : "l"(mine + 2 * src) : "memory");
+        best = k > best ? k : best;
+    }
+    return best;
+}
+
 // ---------------------------------------------------------------------------
 // Producer: walks this CTA's boxes of every GEMV phase in order.
 struct Cursor {
@@ -1060,7 +1105,9 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
         const int ticket = atomicAdd(p.done + last, 1);
         if (ticket == static_cast<int>(gridDim.x) - 1) {
             __threadfence();
-            const unsigned long long fin = atomicExch(&st->argmax_key, 0ull);
+            unsigned long long fin = atomicExch(&st->argmax_key, 0ull);
+            // Tensor-parallel greedy step: the maximum over every rank's vocab shard.
+            if (TP && p.tp > 1 && p.finish_greedy) fin = merge_argmax_tp(p, fin);
             const int tok = unpack_argmax_index(fin);
             st->argmax_final = fin;
             st->greedy_token = tok;
@@ -1068,7 +1115,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
             if (p.finish_greedy) {
                 // Greedy step: the argmax is the step's id (no sampler launch follows).
                 st->token_out = tok;
-                if (tok >= 0 && tok < p.V) p.rep_flags[tok] = 1;
+                const int local = tok - p.v0;
+                if (local >= 0 && local < p.V) p.rep_flags[local] = 1;
                 if (st->in.decode_mode) st->pos += 1;
             }
         }
@@ -1131,8 +1179,7 @@ cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cud
     const int nct = persist_attn_ctas_per_head(p.T);
     if (p.heads * nct > num_sms || nct > 32) return cudaErrorInvalidValue;
     if (p.inflight < 1 || p.inflight > kSlots) return cudaErrorInvalidValue;
-    if (p.tp < 1 || p.tp > kMaxTp || p.rank < 0 || p.rank >= p.tp || (p.tp > 1 && p.finish_greedy))
-        return cudaErrorInvalidValue;
+    if (p.tp < 1 || p.tp > kMaxTp || p.rank < 0 || p.rank >= p.tp) return cudaErrorInvalidValue;
     const bool exchange = p.tp > 1 || p.tag_split;  // the instantiation with tagged partial sums
     for (int r = 0; r < p.tp && exchange; ++r)
         if (!p.xc[r]) return cudaErrorInvalidValue;

@@ -369,8 +369,10 @@ int Engine::alloc_all() {
     if (tp_ <= kMaxTp) {
         // Its own allocation, so that the peers can map it (an IPC handle covers a whole allocation);
         // one GPU uses it too when the split projections' partial sums are ordered by tags (tag_split).
+        // the partial-sum slots, then the greedy merge area: (key, tag) per rank
         const size_t xc = 2 * static_cast<size_t>(tp_) * (H / kPersistTileRows) * kPersistMaxContrib *
-                          kPersistTileRows * 8;
+                              kPersistTileRows * 8 +
+                          2 * kMaxTp * 8;
         XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&xbuf_), xc));
         XL_CUDA(cudaMemset(xbuf_, 0, xc));  // tag 0: no use has written a word yet
     }
@@ -726,7 +728,8 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     p.V = vl_;
     p.v0 = v0_;
     p.T = T_;
-    p.finish_greedy = sampled || tpk ? 0 : 1;
+    // Greedy steps end in the kernel; tensor parallel merges the ranks' argmax keys there too (tp_merge).
+    p.finish_greedy = sampled || (tpk && !tp_merge_) ? 0 : 1;
     p.tma_evict_first = tma_evict_first_;
     p.sig_cta = sig_cta_;
     p.resid_smem = (resid_smem_ || tag_split_) && persistent_smem_bytes(H_, 1) <= 232448 ? 1 : 0;
@@ -754,7 +757,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     XL_CUDA(launch_decode_persistent(p, num_sms_, s));
     if (kernel_events_) XL_CUDA(cudaEventRecordWithFlags(kev1_, s, cudaEventRecordExternal));
     lm_x_ = xa_;
-    if (tpk) return lm_tail(s, sampled);
+    if (tpk && !p.finish_greedy) return lm_tail(s, sampled);
     if (sampled) XL_CUDA(launch_sample_chain(sample_params(), 1, true, s));
     return XL_OK;
 }
@@ -1455,6 +1458,14 @@ int Engine::set_option(const char* key, int value) {
             return XL_ERR_ARG;
         }
         tma_evict_first_ = value;
+        return loaded_ ? capture_decode_graph() : XL_OK;
+    }
+    if (k == "tp_merge") {
+        if (value != 0 && value != 1) {
+            set_error("tp_merge must be 0 or 1");
+            return XL_ERR_ARG;
+        }
+        tp_merge_ = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
     if (k == "sig_cta" || k == "resid_smem" || k == "tag_split") {

@@ -184,6 +184,7 @@ class Engine {
     int sig_cta_ = 1;          // persistent decode: one phase signal per CTA (else per warp)
     int resid_smem_ = 1;       // persistent decode: the residual stream kept in each CTA's shared memory
     int tag_split_ = 0;        // persistent decode: split-projection partial sums ordered by tags (implies resid_smem)
+    int tp_merge_ = 0;         // tensor parallel, greedy: the ranks' argmax keys merged inside the persistent kernel
     // Persistent kernel counters, zeroed before each launch: phase counters
     // [5*layers + 1], then the attention merge tickets [layers][heads].
     size_t done_words() const {
