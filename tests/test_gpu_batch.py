@@ -44,11 +44,26 @@ def logits_of(bd, seq, vocab):
     return np.frombuffer(bd.last_logits(seq, vocab), np.float32)
 
 
+PATHS = pytest.mark.parametrize("path", [0, 1], ids=["persistent", "per_op"])
+
+
+def greedy_launches(path, sh):
+    # persistent: the step inputs + one batched persistent kernel (it writes the greedy ids);
+    # per-op: inputs, six kernels per layer, the LM head and the greedy finish
+    return 2 if path == 0 else 1 + 6 * sh.layers + 2
+
+
+def sampled_launches(path, sh):
+    return (2 if path == 0 else 1 + 6 * sh.layers + 1) + 4  # ... then the sampler chain
+
+
+@PATHS
 @pytest.mark.parametrize("shape_name,steps", [("TINY", 6), ("WIDE2", 3)])
-def test_batch_greedy_matches_oracle_per_sequence(eng_mod, shape_name, steps):
+def test_batch_greedy_matches_oracle_per_sequence(eng_mod, shape_name, steps, path):
     sh = getattr(S, shape_name)
     wdir = S.write_weight_tree(f"/tmp/xl_weights/{shape_name.lower()}", sh)
     eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
+    eng.set_option("decode_path", path)  # the batched decoder follows the engine's decode path
     eng.load(wdir)
     bd = eng_mod.BatchDecoder(eng)
     assert eng_mod.BatchDecoder.size == B
@@ -67,7 +82,7 @@ def test_batch_greedy_matches_oracle_per_sequence(eng_mod, shape_name, steps):
     for step in range(steps):
         n0 = eng_mod.kernel_launches()
         out = bd.step(teach, temperature=0.7, top_p=0.0, repetition_penalty=1.0)
-        assert eng_mod.kernel_launches() - n0 == 1 + 6 * sh.layers + 2  # inputs, layers, LM head, greedy finish
+        assert eng_mod.kernel_launches() - n0 == greedy_launches(path, sh)
         nxt = []
         for b in range(B):
             ref = ports[b].decode(teach[b])
@@ -79,10 +94,12 @@ def test_batch_greedy_matches_oracle_per_sequence(eng_mod, shape_name, steps):
         assert bd.ctx_len(b) == 5 + 9 * b + steps
 
 
-def test_batch_sampled_draws_match_sample_cpu(eng_mod):
+@PATHS
+def test_batch_sampled_draws_match_sample_cpu(eng_mod, path):
     sh = S.TINY
     wdir = S.write_weight_tree("/tmp/xl_weights/tiny", sh)
     eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
+    eng.set_option("decode_path", path)
     eng.load(wdir)
     bd = eng_mod.BatchDecoder(eng)
     T, P, RP = 0.7, 0.9, 1.1
@@ -103,7 +120,7 @@ def test_batch_sampled_draws_match_sample_cpu(eng_mod):
     for step in range(5):
         n0 = eng_mod.kernel_launches()
         out = bd.step(toks, temperature=T, top_p=P, repetition_penalty=RP)
-        assert eng_mod.kernel_launches() - n0 == 1 + 6 * sh.layers + 1 + 4  # ..., LM head, sampler chain
+        assert eng_mod.kernel_launches() - n0 == sampled_launches(path, sh)
         for b in range(B):
             got = logits_of(bd, b, sh.vocab)
             u = float(S.philox_uniforms(seeds[b], 1, step + 1)[0])
@@ -112,6 +129,42 @@ def test_batch_sampled_draws_match_sample_cpu(eng_mod):
             close(got, ref, f"seq {b} step {step}")
             hist[b].append(out[b])
         toks = list(out)
+
+
+@PATHS
+def test_batch_full_model_greedy(eng_mod, full_weights, path):
+    """XingLing-0.68B, eight prompts with lengths drawn like the replica workload
+    (uniform in [16, 512], seed 5), four greedy batched steps.  Each sequence is
+    then replayed on one oracle port: the prefill and every step's logits on the
+    same history (the ids the batch fed itself) within 1e-3 of their range, and
+    every id the oracle's argmax except at near-ties."""
+    sh = S.FULL
+    eng = eng_mod.InferenceEngine("cuda")
+    eng.set_option("decode_path", path)
+    eng.load(full_weights)
+    bd = eng_mod.BatchDecoder(eng)
+    lens = np.random.default_rng(5).integers(16, 513, B)
+    prompts = [S.prompt_ids(500 + b, int(lens[b]), sh.vocab) for b in range(B)]
+    first, pre_logits = [], []
+    for b in range(B):
+        first.append(bd.prefill(b, prompts[b], top_p=0.0, repetition_penalty=1.0))
+        pre_logits.append(np.frombuffer(eng.last_logits(), np.float32).copy())
+    steps, toks, logits = 4, [first], []
+    for _ in range(steps):
+        out = bd.step(toks[-1], top_p=0.0, repetition_penalty=1.0)
+        logits.append([logits_of(bd, b, sh.vocab).copy() for b in range(B)])
+        toks.append(list(out))
+    port = O.Port(sh)
+    port.load(full_weights)
+    for b in range(B):
+        ref = port.prefill(prompts[b])
+        close(pre_logits[b], ref, f"seq {b} prefill")
+        token_ok(toks[0][b], ref, f"seq {b} prefill")
+        for step in range(steps):
+            ref = port.decode(toks[step][b])
+            close(logits[step][b], ref, f"seq {b} step {step}")
+            token_ok(toks[step + 1][b], ref, f"seq {b} step {step}")
+        assert bd.ctx_len(b) == int(lens[b]) + steps
 
 
 def test_batch_requires_prefill_and_checks_ids(eng_mod):

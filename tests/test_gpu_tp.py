@@ -4,9 +4,10 @@ engine's own NCCL communicator (rank 0's id handed over through a queue),
 against the oracle port on the same weight tree.
 
 Both decode paths: the persistent kernel (the out-projection and W2 partial
-sums of every CTA go to every rank's exchange buffer over NVLink and each
-rank sums them in the same order; one kernel + the greedy finish per step)
-and the per-op path (NCCL all-reduces).  The shard widths covered: heads
+sums of every CTA go, tagged, to every rank's exchange buffer over NVLink and
+each rank sums them in the same order; the ranks' argmax keys merge there
+too, so a greedy step is this one kernel) and the per-op path (NCCL
+all-reduces).  The shard widths covered: heads
 12/6/3 per rank, attention widths 768/384/192 (k-tiles of 256/128/64 in the
 persistent kernel's weight boxes), FFN columns 2048/1024/512, contiguous
 vocab shards.
@@ -154,8 +155,9 @@ def _rank_logits(out, world):
 def _check_greedy(out, refs, shape, world, path):
     _check_ranks(out, shape, world)
     if path == 0:
-        # the persistent kernel (NVLink exchange of the split projections) + the greedy finish
-        assert all(out[r][5] == 2 for r in range(world)), [out[r][5] for r in range(world)]
+        # the persistent kernel alone: the split projections' partial sums and the greedy merge of the
+        # ranks' argmax keys cross NVLink inside it
+        assert all(out[r][5] == 1 for r in range(world)), [out[r][5] for r in range(world)]
     shards = _rank_logits(out, world)
     for step, ref in enumerate(refs):
         got = np.concatenate([shards[r][step] for r in range(world)])

@@ -490,6 +490,12 @@ int BatchDecoder::init() {
         add(&vc_[l], kv);
     }
     add(&x_, kBatch * H * 4);
+    // batched persistent kernel: the second residual stream, the split projections' partial sums,
+    // the attention partials and the phase counters / merge tickets
+    add(&xb_, kBatch * H * 4);
+    add(&cres_, kBatch * (H / kPersistTileRows) * kPersistMaxContrib * kPersistTileRows * 4);
+    add(&part_, kBatch * heads * static_cast<size_t>(persistent_max_splits(E.T_)) * (kHeadDim + 2) * 4);
+    add(&done_, done_words() * 4);
     add(&qkv_, kBatch * 3 * Hl * 4);
     add(&att_, kBatch * Hl * 4);
     add(&ffh_, kBatch * Fl * 4);
@@ -523,8 +529,90 @@ int BatchDecoder::init() {
     return capture();
 }
 
+// The batched persistent kernel serves when the engine uses the persistent
+// decode path and the shape fits it (one GPU, widths multiples of 64 up to
+// kBatchPersistMaxK, at most 32 CTAs per attention item, at most
+// kPersistMaxContrib CTAs per row group of the split projections).
+bool BatchDecoder::persistent_fits() const {
+    const Engine& E = *eng_;
+    return E.decode_path_ == 0 && E.tp_ == 1 && E.cfg_.layers <= kMaxLayers && E.H_ % kPersistKAlign == 0 &&
+           E.Hl_ % kPersistKAlign == 0 && E.Fl_ % kPersistKAlign == 0 && E.H_ <= kBatchPersistMaxK &&
+           E.Hl_ <= kBatchPersistMaxK && E.Fl_ <= kBatchPersistMaxK && persist_attn_ctas_per_head(E.T_) <= 32 &&
+           persist_max_contrib(E.H_, E.Hl_, E.num_sms_) <= kPersistMaxContrib &&
+           persist_max_contrib(E.H_, E.Fl_, E.num_sms_) <= kPersistMaxContrib;
+}
+
+// One step as a single cooperative launch (after the step inputs): every
+// weight box is streamed once and dotted with all kBatch sequences' inputs.
+int BatchDecoder::enqueue_persistent(cudaStream_t s, bool sampled) {
+    Engine& E = *eng_;
+    BatchPersistParams bp{};
+    PersistentParams& p = bp.base;
+    for (int l = 0; l < E.cfg_.layers; ++l) {
+        const LayerWeights& L = E.layers_[l];
+        p.layer[l] = LayerPtrs{L.wqkv, L.bqkv, L.wo, L.bo, L.w13, L.b13, L.w2, L.b2, L.g1, L.g2, L.kc, L.vc};
+        XB_CUDA(make_stream_map(&p.maps[4 * l + 0], L.wqkv, 3 * E.Hl_, E.H_));
+        XB_CUDA(make_stream_map(&p.maps[4 * l + 1], L.wo, E.H_, E.Hl_));
+        XB_CUDA(make_stream_map(&p.maps[4 * l + 2], L.w13, 2 * E.Fl_, E.H_));
+        XB_CUDA(make_stream_map(&p.maps[4 * l + 3], L.w2, E.H_, E.Fl_));
+        bp.kc[l] = kc_[l];
+        bp.vc[l] = vc_[l];
+    }
+    XB_CUDA(make_stream_map(&p.maps[kPersistMaps - 1], E.emb_, E.V_, E.H_));
+    p.layers = E.cfg_.layers;
+    p.emb = E.emb_;
+    p.gnorm = E.gnorm_;
+    p.rope = E.rope_;
+    p.st = st_;
+    p.done = done_;
+    p.inflight = std::min(E.inflight_, 3);
+    p.tma_evict_first = E.tma_evict_first_;
+    p.H = E.H_;
+    p.Hl = E.Hl_;
+    p.heads = E.heads_l_;
+    p.Fl = E.Fl_;
+    p.V = E.V_;
+    p.v0 = 0;
+    p.T = E.T_;
+    p.tp = 1;
+    p.rank = 0;
+    bp.xa = x_;
+    bp.xb = xb_;
+    bp.cres = cres_;
+    bp.qkv = qkv_;
+    bp.att = att_;
+    bp.ffh = ffh_;
+    bp.logits = logits_;
+    bp.rep = rep_;
+    bp.st = st_;
+    bp.part = part_;
+    bp.done = done_;
+    bp.head_done = done_ + 5 * E.cfg_.layers + 1;
+    bp.finish_greedy = sampled ? 0 : 1;
+    count_launch();
+    batch_in_kernel<<<1, 32, 0, s>>>(in_, st_, tokens_);
+    XB_CUDA(cudaGetLastError());
+    XB_CUDA(cudaMemsetAsync(done_, 0, done_words() * sizeof(int), s));
+    XB_CUDA(launch_decode_batch_persistent(bp, E.num_sms_, s));
+    if (!sampled) return XL_OK;  // the kernel wrote every sequence's greedy id
+    SampleParams sp{};
+    sp.logits = logits_;
+    sp.V = E.V_;
+    sp.v0 = 0;
+    sp.st = st_;
+    sp.rep_flags = rep_;
+    sp.full = 0;
+    sp.work = samp_work_;
+    sp.work_stride = samp_stride_;
+    sp.stride = E.V_;
+    sp.grid = samp_grid_;
+    XB_CUDA(launch_sample_chain(sp, kBatch, false, s));
+    return XL_OK;
+}
+
 int BatchDecoder::enqueue(cudaStream_t s, bool sampled) {
     Engine& E = *eng_;
+    if (persistent_fits()) return enqueue_persistent(s, sampled);
     const int H = E.H_, Hl = E.Hl_, Fl = E.Fl_, T = E.T_, V = E.V_, heads = E.heads_l_;
     count_launch();
     batch_in_kernel<<<1, 32, 0, s>>>(in_, st_, tokens_);

@@ -372,6 +372,7 @@ __device__ void cursor_first(const PersistentParams& p, int ph, Cursor& c) {
     c.valid = false;
 }
 
+template <int SLOTS>
 __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, uint64_t* empty,
                          const volatile int* quiet) {
     DevState* st = p.st;
@@ -403,7 +404,7 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
         // adds latency to every other memory access once HBM is saturated.
         if (issued >= inflight) {
             const int k = issued - inflight;
-            if (!wait_parity(&full[k % kSlots], static_cast<uint32_t>((k / kSlots) & 1), st)) {
+            if (!wait_parity(&full[k % SLOTS], static_cast<uint32_t>((k / SLOTS) & 1), st)) {
                 ok = false;
                 break;
             }
@@ -419,7 +420,7 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
         else
             tma_box(ring + static_cast<size_t>(slot) * kSlotBytes, c.map, bi * c.kd, g * kPersistTileRows, &full[slot]);
         ++issued;
-        if (++slot == kSlots) {
+        if (++slot == SLOTS) {
             slot = 0;
             par ^= 1u;
         }
@@ -430,11 +431,11 @@ __device__ void producer(const PersistentParams& p, char* ring, uint64_t* full, 
     }
     if (!ok) {
         // Drain: every copy already issued must land before this CTA exits.
-        const int pending = issued < kSlots ? issued : kSlots;
+        const int pending = issued < SLOTS ? issued : SLOTS;
         for (int i = 1; i <= pending; ++i) {
-            const int k = issued - i;  // box k went to slot k % kSlots with parity (k / kSlots) & 1
-            const int s = k % kSlots;
-            const uint32_t pp = static_cast<uint32_t>((k / kSlots) & 1);
+            const int k = issued - i;  // box k went to slot k % SLOTS with parity (k / SLOTS) & 1
+            const int s = k % SLOTS;
+            const uint32_t pp = static_cast<uint32_t>((k / SLOTS) & 1);
             uint32_t it = 0;
             unsigned long long t0 = 0;
             while (!mbar_try_wait(&full[s], pp) && ++it < kMbarSpinLimit) {
@@ -1159,9 +1160,534 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
         return;
     }
     if (threadIdx.x < 32) {
-        if (threadIdx.x == 0) producer(p, ring, full, empty, quiet);
+        if (threadIdx.x == 0) producer<kSlots>(p, ring, full, empty, quiet);
     } else {
         consumers<TP>(p, ring, xs, full, empty, red, best_s, s_ok, quiet, xr);
+    }
+}
+
+
+// ===========================================================================
+// Batched persistent decode: kBatch sequences over one pass of the weights.
+//
+// The same weight stream as decode_persistent_kernel (producer, ring of TMA
+// boxes, quiet window), with a 3-slot ring: shared memory holds every
+// sequence's staged input instead ([kBatch][4096] floats, 128 KB).  Each box
+// is dotted with all kBatch inputs: warp w owns rows 2w, 2w + 1 of the box and
+// keeps 2 x kBatch accumulators; one 16-value butterfly leaves lane l (and
+// l + 16) with the sum for (sequence l / 2, row l % 2).  The residual streams
+// ping-pong in global memory as in the first form of the single-sequence
+// kernel (no room for them in shared memory).  Attention runs per
+// (sequence, head) item, spread over the grid, several per CTA when there
+// are more items than SMs.  The LM head applies each sequence's penalty and
+// keeps each sequence's argmax; a greedy step ends in the kernel.
+constexpr int kSlotsB = 3;
+constexpr size_t kSmemBytesB = static_cast<size_t>(kSlotsB) * kSlotBytes +
+                               static_cast<size_t>(kBatch) * kBatchPersistMaxK * 4 + 2 * kSlotsB * 8 +
+                               kBatch * kConsumerWarps * 4 + kBatch * kConsumerWarps * 8 + 64;
+static_assert(kSmemBytesB <= kMaxSmemPerBlock, "batched persistent kernel fits in 227 KB of shared memory");
+static_assert(2 * kBatch == 16, "one (sequence, row) sum per half-warp lane");
+
+// Butterfly reduce-scatter of 16 values held by every lane: afterwards lanes
+// l and l + 16 hold the warp-wide sum of value l % 16.
+__device__ __forceinline__ float reduce_scatter16(float (&v)[16]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], 16);
+#pragma unroll
+    for (int half = 8; half > 0; half >>= 1) {
+        const bool upper = (lane & half) != 0;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = upper ? v[i] : v[i + half];
+            const float keep = upper ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+        }
+    }
+    return v[0];
+}
+
+// Wait until phase ph's counter reaches target (bounded like every wait).
+__device__ bool wait_count(const PersistentParams& p, int ph, int target, int* s_ok) {
+    if (threadIdx.x == 32) {
+        const int* c = p.done + ph;
+        uint32_t it = 0;
+        unsigned long long t0 = 0;
+        int ok = 1;
+        while (ld_acquire(c) < target) {
+            ++it;
+            if ((it & 255u) == 0) {
+                const unsigned long long now = globaltimer();
+                if (t0 == 0) t0 = now;
+                if (it >= kFlagSpinLimit || now - t0 > kWaitLimitNs || aborted(p.st)) {
+                    atomicOr(&p.st->err, kErrFlag);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        *s_ok = ok;
+    }
+    consumer_sync();
+    return *s_ok != 0;
+}
+
+// xs8[b] = rmsnorm(x_b) * gamma for every sequence b: x_b is the embedding row
+// of b's input id (gather) or x_old_b + its partial row sums + bias after a
+// split projection of nb boxes per group; this CTA stores its slice of x_b to
+// x_out_b.  The RMSNorm is that of the single-sequence staging
+// (src/rmsnorm.cu:99-101).  Sequences go two at a time, each pair's loads
+// issued before its stores.
+__device__ __noinline__ void stage_norm8(const BatchPersistParams& bp, const float* x_old, const float* bias,
+                                         const float* cres, int nb, const float* gamma, float* xs8, float* red8,
+                                         float* x_out, bool gather) {
+    const PersistentParams& p = bp.base;
+    const int t = threadIdx.x - 32;
+    const int K = p.H, K4 = K >> 2;
+    const int T = (K / kPersistTileRows) * nb;
+    const int s0 = static_cast<int>(blockIdx.x) * K / static_cast<int>(gridDim.x);
+    const int s1 = static_cast<int>(blockIdx.x + 1) * K / static_cast<int>(gridDim.x);
+    const size_t cstride = static_cast<size_t>(K / kPersistTileRows) * kPersistMaxContrib * kPersistTileRows;
+    float ss[kBatch];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) ss[b] = 0.0f;
+    for (int q = t; q < K4; q += kConsumerThreads) {
+#pragma unroll
+        for (int b0 = 0; b0 < kBatch; b0 += 2) {
+            float4 v[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int b = b0 + u;
+                const float* src = gather ? p.emb + static_cast<size_t>(bp.st[b].in.token_in) * K
+                                          : x_old + static_cast<size_t>(b) * K;
+                const float4 xo = __ldcg(reinterpret_cast<const float4*>(src) + q);
+                v[u] = gather ? xo : residual_quad(xo, bias, cres + b * cstride, q, nb, T);
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int b = b0 + u;
+                reinterpret_cast<float4*>(xs8 + static_cast<size_t>(b) * kBatchPersistMaxK)[q] = v[u];
+                const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (4 * q + c >= s0 && 4 * q + c < s1) x_out[static_cast<size_t>(b) * K + 4 * q + c] = e[c];
+                ss[b] = dot4(v[u], v[u], ss[b]);
+            }
+        }
+    }
+    const int warp = t >> 5, lane = t & 31;
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+        const float w = warp_sum(ss[b]);
+        if (lane == 0) red8[b * kConsumerWarps + warp] = w;
+    }
+    consumer_sync();
+    float inv[kBatch];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+        float tot = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) tot += red8[b * kConsumerWarps + w];
+        inv[b] = static_cast<float>(1.0 / sqrt(static_cast<double>(tot / static_cast<float>(K)) + 1e-6));
+    }
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+    for (int q = t; q < K4; q += kConsumerThreads) {
+        const float4 g = g4[q];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            float4* x4 = reinterpret_cast<float4*>(xs8 + static_cast<size_t>(b) * kBatchPersistMaxK) + q;
+            float4 v = *x4;
+            v.x = v.x * inv[b] * g.x;
+            v.y = v.y * inv[b] * g.y;
+            v.z = v.z * inv[b] * g.z;
+            v.w = v.w * inv[b] * g.w;
+            *x4 = v;
+        }
+    }
+}
+
+// xs8[b] = src_b[0, K) for every sequence b (src_b = src + b * K).
+__device__ void stage_copy8(const float* src, int K, float* xs8) {
+    const int t = threadIdx.x - 32;
+    const int K4 = K >> 2;
+    for (int q = t; q < K4; q += kConsumerThreads) {
+#pragma unroll
+        for (int b0 = 0; b0 < kBatch; b0 += 4) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(b0 + u) * K) + q);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                reinterpret_cast<float4*>(xs8 + static_cast<size_t>(b0 + u) * kBatchPersistMaxK)[q] = v[u];
+        }
+    }
+}
+
+// The attention phase of one layer for every sequence: items (sequence b,
+// head h, CTA j of the item's nct_b), nct_b = ceil(chunks_b / 8) with 16
+// positions per warp chunk, enumerated sequence by sequence and dealt to the
+// CTAs round robin; a CTA runs its items one after another.  Per item the
+// warps do what the single-sequence attention phase does (RoPE at position
+// n_b, KV append, scores, softmax, P.V, src/attn.cu:490-547) and merge in
+// shared memory; an item split over several CTAs merges through global memory
+// (last-CTA ticket).  Every item's final writer signals once: the phase's
+// target is kBatch x heads.  Returns false if the wait for the QKV phase failed.
+__device__ bool attention_batch(const BatchPersistParams& bp, int layer, int ph, float* xs, int* s_ok) {
+    const PersistentParams& p = bp.base;
+    const int t = threadIdx.x - 32;
+    const int warp = t >> 5, lane = t & 31;
+    const int G = gridDim.x;
+    int nct[kBatch], ustart[kBatch + 1];
+    ustart[0] = 0;
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+        const int nsplit = bp.st[b].pos / kPersistChunk + 1;
+        nct[b] = (nsplit + kConsumerWarps - 1) / kConsumerWarps;
+        ustart[b + 1] = ustart[b] + p.heads * nct[b];
+    }
+    const int U = ustart[kBatch];
+    if (static_cast<int>(blockIdx.x) >= U) return true;  // no item: neither waits nor signals
+    if (!wait_count(p, ph - 1, static_cast<int>(gridDim.x), s_ok)) return false;
+    if (t == 0) trace_at(p, ph, kTrConsStart);
+    float* qsh = xs + warp * kAttnWarpScratch;
+    float* apart = xs + kConsumerWarps * kAttnWarpScratch;  // [8][68]
+    float* knew = xs + kConsumerWarps * (kAttnWarpScratch + kAttnPartStride) + warp * kHeadDim;
+    const int maxs = persistent_max_splits(p.T);
+    for (int u = blockIdx.x; u < U; u += G) {
+        int b = 0;
+#pragma unroll
+        for (int i = 1; i < kBatch; ++i)
+            if (u >= ustart[i]) b = i;
+        const int h = (u - ustart[b]) / nct[b], j = (u - ustart[b]) % nct[b];
+        const int n = bp.st[b].pos;
+        const int nsplit = n / kPersistChunk + 1;
+        const int s = j * kConsumerWarps + warp;
+        const bool active = s < nsplit;
+        const int t0 = s * kPersistChunk;
+        const size_t head_off = (static_cast<size_t>(b) * p.heads + h) * p.T * kHeadDim;
+        float* kc = bp.kc[layer] + head_off;
+        float* vc = bp.vc[layer] + head_off;
+        const float* qkv = bp.qkv + static_cast<size_t>(b) * 3 * p.Hl;
+        if (active) {
+            const int kp = lane >> 1, kh = lane & 1;
+            const int posk = t0 + kp;
+            const int cached = min(kPersistChunk, n - t0);
+            const bool has_n = n >= t0 && n < t0 + kPersistChunk;
+            const float2 cs = p.rope[n * kHalfHead + lane];
+            const float* q = qkv + h * kHeadDim;
+            const float* kn = qkv + p.Hl + h * kHeadDim;
+            const float* vn = qkv + 2 * p.Hl + h * kHeadDim;
+            float4 kv[8];
+            const float4* kr =
+                reinterpret_cast<const float4*>(kc + static_cast<size_t>(kp < cached ? posk : 0) * kHeadDim) + 8 * kh;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) kv[i] = kp < cached ? __ldcg(kr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const float qa = __ldcg(q + lane), qb = __ldcg(q + lane + kHalfHead);
+            float ka = 0.0f, kb = 0.0f;
+            float2 vnew = make_float2(0.0f, 0.0f);
+            if (has_n) {
+                ka = __ldcg(kn + lane);
+                kb = __ldcg(kn + lane + kHalfHead);
+                vnew = __ldcg(reinterpret_cast<const float2*>(vn) + lane);
+            }
+            qsh[lane] = (qa * cs.x + qb * cs.y) * 0.125f;  // 1/sqrt(64) is exact
+            qsh[lane + kHalfHead] = (-qa * cs.y + qb * cs.x) * 0.125f;
+            if (has_n) {
+                const float k0 = ka * cs.x + kb * cs.y, k1 = -ka * cs.y + kb * cs.x;
+                knew[lane] = k0;
+                knew[lane + kHalfHead] = k1;
+                kc[n * kHeadDim + lane] = k0;
+                kc[n * kHeadDim + lane + kHalfHead] = k1;
+                reinterpret_cast<float2*>(vc + n * kHeadDim)[lane] = vnew;
+            }
+            __syncwarp();
+            const float4* q4 = reinterpret_cast<const float4*>(qsh) + 8 * kh;
+            if (posk == n) {
+                const float4* k4 = reinterpret_cast<const float4*>(knew) + 8 * kh;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) kv[i] = k4[i];
+            }
+            float d = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d = dot4(kv[i], q4[i], d);
+            d += __shfl_xor_sync(0xffffffffu, d, 1);
+            const bool mine = posk <= n;
+            const float sc = mine ? d : -INFINITY;
+            const float m = warp_max(sc);
+            const float e = mine ? expf(sc - m) : 0.0f;
+            const float l = warp_sum(kh == 0 ? e : 0.0f);
+            const float2* vr = reinterpret_cast<const float2*>(vc + static_cast<size_t>(t0) * kHeadDim) + lane;
+            float2 o = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int jp = 0; jp < kPersistChunk; ++jp) {
+                const float ej = __shfl_sync(0xffffffffu, e, 2 * jp);
+                const float2 v = t0 + jp == n ? vnew : (jp < cached ? __ldcg(vr + jp * (kHeadDim / 2))
+                                                                    : make_float2(0.0f, 0.0f));
+                o.x = fmaf(ej, v.x, o.x);
+                o.y = fmaf(ej, v.y, o.y);
+            }
+            float* ap = apart + warp * kAttnPartStride;
+            reinterpret_cast<float2*>(ap + 4)[lane] = o;
+            if (lane == 0) {
+                ap[0] = m;
+                ap[1] = l;
+            }
+        }
+        consumer_sync();
+        if (warp == 0) {
+            const int nw = min(kConsumerWarps, nsplit - j * kConsumerWarps);
+            const float mk = lane < nw ? apart[lane * kAttnPartStride] : -INFINITY;
+            const float lk = lane < nw ? apart[lane * kAttnPartStride + 1] : 0.0f;
+            const float M = warp_max(mk);
+            const float wk = lane < nw ? expf(mk - M) : 0.0f;
+            const float L = warp_sum(lk * wk);
+            float2 acc = make_float2(0.0f, 0.0f);
+            for (int k = 0; k < nw; ++k) {
+                const float wt = __shfl_sync(0xffffffffu, wk, k);
+                const float2 ok = reinterpret_cast<const float2*>(apart + k * kAttnPartStride + 4)[lane];
+                acc.x = fmaf(wt, ok.x, acc.x);
+                acc.y = fmaf(wt, ok.y, acc.y);
+            }
+            float2* out = reinterpret_cast<float2*>(bp.att + static_cast<size_t>(b) * p.Hl + h * kHeadDim);
+            if (nct[b] == 1) {
+                out[lane] = make_float2(acc.x / L, acc.y / L);
+                signal_warp(p, ph);
+            } else {
+                float* base = bp.part + (static_cast<size_t>(b) * p.heads + h) * maxs * (kHeadDim + 2);
+                float* pp = base + j * (kHeadDim + 2);
+                reinterpret_cast<float2*>(pp + 2)[lane] = acc;
+                if (lane == 0) {
+                    pp[0] = M;
+                    pp[1] = L;
+                }
+                __syncwarp();
+                int ticket = 0;
+                if (lane == 0) {
+                    __threadfence();
+                    ticket = atomicAdd(bp.head_done + (layer * kBatch + b) * p.heads + h, 1);
+                }
+                ticket = __shfl_sync(0xffffffffu, ticket, 0);
+                if (ticket == nct[b] - 1) {
+                    __threadfence();
+                    const int nc = nct[b];
+                    const float mc = lane < nc ? __ldcg(base + lane * (kHeadDim + 2)) : -INFINITY;
+                    const float lc = lane < nc ? __ldcg(base + lane * (kHeadDim + 2) + 1) : 0.0f;
+                    const float M2 = warp_max(mc);
+                    const float wc = lane < nc ? expf(mc - M2) : 0.0f;
+                    const float L2 = warp_sum(lc * wc);
+                    float2 acc2 = make_float2(0.0f, 0.0f);
+                    for (int k = 0; k < nc; ++k) {
+                        const float wt = __shfl_sync(0xffffffffu, wc, k);
+                        const float2 ok = __ldcg(reinterpret_cast<const float2*>(base + k * (kHeadDim + 2) + 2) + lane);
+                        acc2.x = fmaf(wt, ok.x, acc2.x);
+                        acc2.y = fmaf(wt, ok.y, acc2.y);
+                    }
+                    out[lane] = make_float2(acc2.x / L2, acc2.y / L2);
+                    signal_warp(p, ph);
+                }
+            }
+        }
+        consumer_sync();  // the scratch is reused by the next item
+    }
+    return true;
+}
+
+__device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float* xs8, uint64_t* full, uint64_t* empty,
+                                float* red8, unsigned long long* best8, int* s_ok, volatile int* quiet) {
+    const PersistentParams& p = bp.base;
+    DevState* st0 = bp.st;  // sequence 0's state holds the step's error word
+    const int t = threadIdx.x - 32;
+    const int warp = t >> 5, lane = t & 31;
+    const int nb_wo = persist_boxes_per_group(p.Hl), nb_w2 = persist_boxes_per_group(p.Fl);
+    const int G = gridDim.x;
+    const size_t cstride = static_cast<size_t>(p.H / kPersistTileRows) * kPersistMaxContrib * kPersistTileRows;
+    int slot = 0;
+    uint32_t par = 0;
+    bool ok = true;
+    // LM head: lane l < 16 keeps the running argmax of sequence l / 2 over the rows it finishes.
+    float best_v = -INFINITY;
+    int best_i = -1;
+    const int my_seq = (lane & 15) >> 1, my_row = lane & 1;
+    const float my_rp = bp.st[my_seq].in.rp;
+    const int last = 5 * p.layers;
+    for (int ph = 0; ph <= last; ++ph) {
+        const int kind = phase_kind(ph, p.layers);
+        const int l = ph / 5;
+        if (kind == kAttn) {
+            if (!attention_batch(bp, l, ph, xs8, s_ok)) return;
+            if (t == 0) *quiet = 0;
+            if (t == 0) trace_at(p, ph, kTrConsEnd);
+            continue;
+        }
+        const LayerPtrs* y = ph < last ? &p.layer[l] : nullptr;
+        const Gemv d = gemv_of(p, ph);
+        const Boxes r = boxes_of(d);
+        if (ph > 0) {
+            // the attention phase is signalled once per (sequence, head) item; the others once per CTA
+            const int target = phase_kind(ph - 1, p.layers) == kAttn ? kBatch * p.heads : G;
+            if (!wait_count(p, ph - 1, target, s_ok)) return;
+        }
+        if (t == 0) trace_at(p, ph, kTrConsStart);
+        if (kind == kQKV) {
+            if (l == 0)
+                stage_norm8(bp, nullptr, nullptr, nullptr, 0, y->g1, xs8, red8, bp.xa, true);
+            else
+                stage_norm8(bp, bp.xb, p.layer[l - 1].b2, bp.cres, nb_w2, y->g1, xs8, red8, bp.xa, false);
+        } else if (kind == kWo) {
+            stage_copy8(bp.att, p.Hl, xs8);
+        } else if (kind == kW13) {
+            stage_norm8(bp, bp.xa, y->bo, bp.cres, nb_wo, y->g2, xs8, red8, bp.xb, false);
+        } else if (kind == kW2) {
+            stage_copy8(bp.ffh, p.Fl, xs8);
+        } else {  // kLM
+            stage_norm8(bp, bp.xb, p.layer[l - 1].b2, bp.cres, nb_w2, p.gnorm, xs8, red8, bp.xa, false);
+        }
+        consumer_sync();
+        if (t == 0) *quiet = 0;
+        if (t == 0) trace_at(p, ph, kTrConsStaged);
+        const int rs4 = r.bw / 4;
+        const int ra = 2 * warp, rb = ra + 1;
+        for (int tau = r.t0; tau < r.t1;) {
+            const int g = tau / r.nb;
+            const int bi0 = tau % r.nb, bi1 = min(r.nb, bi0 + (r.t1 - tau));
+            const int rows = min(kPersistTileRows, d.M - g * kPersistTileRows);
+            // this lane's (sequence, row) after the butterfly
+            const int Rl = g * kPersistTileRows + (my_row ? rb : ra);
+            const bool vl = (my_row ? rb : ra) < rows;
+            float el = 0.0f;  // bias of the lane's row, or its sequence's repetition flag in the LM head
+            if (kind == kLM) {
+                if (vl) el = bp.rep[static_cast<size_t>(my_seq) * p.V + Rl] ? 1.0f : 0.0f;
+            } else if (kind == kQKV || kind == kW13) {
+                if (vl) el = d.bias[Rl];
+            }
+            float acc[2 * kBatch];
+#pragma unroll
+            for (int i = 0; i < 2 * kBatch; ++i) acc[i] = 0.0f;
+            for (int bi = bi0; bi < bi1; ++bi) {
+                if (ok && !wait_parity(&full[slot], par, st0)) ok = false;
+                if (t == 0 && kind != kLM && tau + (bi - bi0) == r.t1 - 1) *quiet = 1;
+                if (ok) {
+                    const int k0 = bi * r.bw;
+                    const int kc4 = min(r.bw, d.K - k0) >> 2;
+                    const float4* tile = reinterpret_cast<const float4*>(ring + static_cast<size_t>(slot) * kSlotBytes);
+                    const float4* wa = tile + ra * rs4;
+                    const float4* wb = tile + rb * rs4;
+#pragma unroll
+                    for (int j0 = 0; j0 < kBoxK / 4; j0 += 32) {
+                        const int j = j0 + lane;
+                        if (j < kc4) {
+                            const float4 a4 = wa[j], b4 = wb[j];
+#pragma unroll
+                            for (int b = 0; b < kBatch; ++b) {
+                                const float4 xv =
+                                    reinterpret_cast<const float4*>(xs8 + static_cast<size_t>(b) * kBatchPersistMaxK)[(k0 >> 2) + j];
+                                acc[2 * b] = dot4(a4, xv, acc[2 * b]);
+                                acc[2 * b + 1] = dot4(b4, xv, acc[2 * b + 1]);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[slot]);
+                }
+                if (++slot == kSlotsB) {
+                    slot = 0;
+                    par ^= 1u;
+                }
+            }
+            tau += bi1 - bi0;
+            const float sum = reduce_scatter16(acc);  // lanes l, l + 16: sequence (l % 16) / 2, row l % 2
+            switch (kind) {
+                case kQKV:
+                    if (lane < 16 && vl) bp.qkv[static_cast<size_t>(my_seq) * 3 * p.Hl + Rl] = sum + el;
+                    break;
+                case kWo:
+                case kW2: {
+                    const int c = persist_contrib_slot(blockIdx.x, g, bi0, r.nb, r.T, G);
+                    if (lane < 16)
+                        bp.cres[my_seq * cstride + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows +
+                                (my_row ? rb : ra)] = sum;
+                    break;
+                }
+                case kW13: {
+                    // rows (2i, 2i + 1) = (W1 row i, V row i) sit in lanes (2s, 2s + 1) of sequence s
+                    const float gate = __shfl_xor_sync(0xffffffffu, sum + el, 1);
+                    if (lane < 16 && my_row == 1 && vl)
+                        bp.ffh[static_cast<size_t>(my_seq) * p.Fl + (Rl >> 1)] = silu(gate) * (sum + el);
+                    break;
+                }
+                default: {  // kLM: logits with the sequence's repetition penalty, running argmax
+                    if (lane < 16 && vl) {
+                        float v = sum;
+                        if (el != 0.0f) v = rep_penalty(v, my_rp);
+                        bp.logits[static_cast<size_t>(my_seq) * p.V + Rl] = v;
+                        if (v > best_v) best_v = v, best_i = Rl;
+                    }
+                }
+            }
+        }
+        if (kind != kLM) {
+            consumer_sync();  // every warp's stores of the phase, then one release per CTA
+            if (t == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(p.done + ph) : "memory");
+        }
+        if (t == 0) trace_at(p, ph, kTrConsEnd);
+    }
+    // LM head: per sequence, lane pair -> warp -> CTA -> grid maximum; the last CTA finishes the step.
+    unsigned long long k = lane < 16 && best_i >= 0 ? pack_argmax(best_v, best_i) : 0ull;
+    const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, 1);
+    k = k2 > k ? k2 : k;
+    if (lane < 16 && my_row == 0) best8[warp * kBatch + my_seq] = k;
+    consumer_sync();
+    if (t < kBatch) {
+        unsigned long long m = 0;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) m = best8[w * kBatch + t] > m ? best8[w * kBatch + t] : m;
+        if (m) atomicMax(&bp.st[t].argmax_key, m);
+    }
+    consumer_sync();
+    if (t == 0) {
+        __threadfence();
+        const int ticket = atomicAdd(p.done + last, 1);
+        if (ticket == G - 1) {
+            __threadfence();
+            for (int b = 0; b < kBatch; ++b) {
+                DevState* sb = bp.st + b;
+                const unsigned long long fin = atomicExch(&sb->argmax_key, 0ull);
+                const int tok = unpack_argmax_index(fin);
+                sb->argmax_final = fin;
+                sb->greedy_token = tok;
+                if (bp.finish_greedy) {
+                    sb->token_out = tok;
+                    if (tok >= 0 && tok < p.V) bp.rep[static_cast<size_t>(b) * p.V + tok] = 1;
+                    if (sb->in.decode_mode) sb->pos += 1;
+                }
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) decode_batch_persistent_kernel(const __grid_constant__ BatchPersistParams bp) {
+    extern __shared__ __align__(128) char smem[];
+    char* ring = smem;
+    float* xs8 = reinterpret_cast<float*>(smem + static_cast<size_t>(kSlotsB) * kSlotBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(xs8 + static_cast<size_t>(kBatch) * kBatchPersistMaxK);
+    uint64_t* empty = full + kSlotsB;
+    float* red8 = reinterpret_cast<float*>(empty + kSlotsB);                            // [kBatch][8 warps]
+    unsigned long long* best8 = reinterpret_cast<unsigned long long*>(red8 + kBatch * kConsumerWarps);  // [8][kBatch]
+    int* s_ok = reinterpret_cast<int*>(best8 + kBatch * kConsumerWarps);
+    volatile int* quiet = s_ok + 8;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kSlotsB; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        *quiet = 0;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        if (threadIdx.x == 0) producer<kSlotsB>(bp.base, ring, full, empty, quiet);
+    } else {
+        consumers_batch(bp, ring, xs8, full, empty, red8, best8, s_ok, quiet);
     }
 }
 
@@ -1204,6 +1730,36 @@ cudaError_t launch_decode_persistent(const PersistentParams& p, int num_sms, cud
     cfg.numAttrs = 1;
     count_launch();
     return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+size_t batch_persistent_smem_bytes() { return kSmemBytesB; }
+
+cudaError_t launch_decode_batch_persistent(const BatchPersistParams& bp, int num_sms, cudaStream_t s) {
+    const PersistentParams& p = bp.base;
+    if (p.H <= 0 || p.Hl <= 0 || p.Fl <= 0 || p.H > kBatchPersistMaxK || p.Hl > kBatchPersistMaxK ||
+        p.Fl > kBatchPersistMaxK || p.H % kPersistKAlign || p.Hl % kPersistKAlign || p.Fl % kPersistKAlign)
+        return cudaErrorInvalidValue;
+    // one GPU; the error word and the producer's state are sequence 0's; at most 32 CTAs per attention item
+    if (p.tp != 1 || p.st != bp.st || persist_attn_ctas_per_head(p.T) > 32) return cudaErrorInvalidValue;
+    if (p.inflight < 1 || p.inflight > kSlotsB) return cudaErrorInvalidValue;
+    if (persist_max_contrib(p.H, p.Hl, num_sms) > kPersistMaxContrib ||
+        persist_max_contrib(p.H, p.Fl, num_sms) > kPersistMaxContrib)
+        return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(decode_batch_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemBytesB));
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytesB;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    count_launch();
+    return cudaLaunchKernelEx(&cfg, decode_batch_persistent_kernel, bp);
 }
 
 }  // namespace xl

@@ -732,8 +732,9 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     p.finish_greedy = sampled || (tpk && !tp_merge_) ? 0 : 1;
     p.tma_evict_first = tma_evict_first_;
     p.sig_cta = sig_cta_;
-    p.resid_smem = (resid_smem_ || tag_split_) && persistent_smem_bytes(H_, 1) <= 232448 ? 1 : 0;
-    p.tag_split = tag_split_ && p.resid_smem ? 1 : 0;
+    const bool tag_split = tag_split_ < 0 ? tpk : tag_split_ != 0;
+    p.resid_smem = (resid_smem_ || tag_split) && persistent_smem_bytes(H_, 1) <= 232448 ? 1 : 0;
+    p.tag_split = tag_split && p.resid_smem ? 1 : 0;
     p.tp = tp_;
     p.rank = rank_;
     if (tpk) {

@@ -183,8 +183,10 @@ class Engine {
     int tma_evict_first_ = 1;  // persistent decode: weight boxes loaded with an L2 evict-first policy
     int sig_cta_ = 1;          // persistent decode: one phase signal per CTA (else per warp)
     int resid_smem_ = 1;       // persistent decode: the residual stream kept in each CTA's shared memory
-    int tag_split_ = 0;        // persistent decode: split-projection partial sums ordered by tags (implies resid_smem)
-    int tp_merge_ = 0;         // tensor parallel, greedy: the ranks' argmax keys merged inside the persistent kernel
+    // persistent decode: split-projection partial sums ordered by tags (implies resid_smem); -1: on under
+    // tensor parallelism (TP2: 0.742 -> 0.679 ms/token), off on one GPU (where it is 13 % slower)
+    int tag_split_ = -1;
+    int tp_merge_ = 1;         // tensor parallel, greedy: the ranks' argmax keys merged inside the persistent kernel
     // Persistent kernel counters, zeroed before each launch: phase counters
     // [5*layers + 1], then the attention merge tickets [layers][heads].
     size_t done_words() const {
@@ -227,6 +229,8 @@ class BatchDecoder {
     BatchDecoder() = default;
     int init();
     int enqueue(cudaStream_t s, bool sampled);
+    int enqueue_persistent(cudaStream_t s, bool sampled);  // the batched persistent kernel
+    bool persistent_fits() const;
     int capture();
     float next_uniform(int seq);
     int cuda_fail(cudaError_t e, const char* what);
@@ -235,6 +239,14 @@ class BatchDecoder {
     char* arena_ = nullptr;
     std::vector<float*> kc_, vc_;  // per layer [kBatch][heads][T][64]
     float *x_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *ffh_ = nullptr, *logits_ = nullptr;
+    // batched persistent kernel: second residual stream [kBatch][H], partial row sums
+    // [kBatch][H/16][kPersistMaxContrib][16], attention partials, phase counters + merge tickets
+    float *xb_ = nullptr, *cres_ = nullptr, *part_ = nullptr;
+    int* done_ = nullptr;
+    size_t done_words() const {
+        return 5 * static_cast<size_t>(eng_->cfg_.layers) + 1 +
+               static_cast<size_t>(eng_->cfg_.layers) * kBatch * eng_->heads_l_;
+    }
     uint8_t* rep_ = nullptr;       // [kBatch][V]
     DevState* st_ = nullptr;       // [kBatch]
     StepIn* in_ = nullptr;         // [kBatch]

@@ -193,6 +193,32 @@ struct PersistentParams {
     unsigned long long* xc[kMaxTp];
 };
 constexpr int kTraceFields = 5;
+
+// Batched persistent decode step (decode_persistent.cu): kBatch sequences
+// advance one token over a single pass of the weights, in one cooperative
+// launch, with the same weight stream and phases as decode_persistent_kernel.
+struct BatchPersistParams {
+    PersistentParams base;   // weights, maps, geometry, stream options; base.st = st (sequence 0 holds the error word)
+    float* xa;               // [kBatch][H] residual streams entering a layer (and the LM head's inputs)
+    float* xb;               // [kBatch][H] after the out-projection
+    float* cres;             // [kBatch][H/16][kPersistMaxContrib][16] partial row sums of out-proj / W2
+    float* qkv;              // [kBatch][3*Hl]
+    float* att;              // [kBatch][Hl]
+    float* ffh;              // [kBatch][Fl]
+    float* logits;           // [kBatch][V]
+    uint8_t* rep;            // [kBatch][V]
+    DevState* st;            // [kBatch]
+    float* kc[kMaxLayers];   // per layer [kBatch][heads][T][64]
+    float* vc[kMaxLayers];
+    float* part;             // [kBatch][heads][persistent_max_splits(T)][66] attention partials across CTAs
+    int* head_done;          // [layers][kBatch][heads] CTA tickets of the cross-CTA attention merge
+    int* done;               // [5*layers + 1] phase counters; head_done follows; zeroed before each launch
+    int finish_greedy;       // 1: the LM head's last CTA writes every sequence's argmax as its id
+};
+size_t batch_persistent_smem_bytes();
+// The batched kernel streams K up to this many floats (every sequence's staged input in shared memory).
+constexpr int kBatchPersistMaxK = 4096;
+cudaError_t launch_decode_batch_persistent(const BatchPersistParams& p, int num_sms, cudaStream_t s);
 size_t persistent_smem_bytes(int H, int resid_smem);
 // The TMA map (no swizzle) of a row-major [rows][cols] weight viewed as
 // [rows][cols/tw][tw] (tw = persist_tile_w(cols)), box [16 rows]
