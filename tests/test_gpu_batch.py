@@ -44,7 +44,7 @@ def logits_of(bd, seq, vocab):
     return np.frombuffer(bd.last_logits(seq, vocab), np.float32)
 
 
-PATHS = pytest.mark.parametrize("path", [0, 1], ids=["persistent", "per_op"])
+PATHS = pytest.mark.parametrize("path", [0, 1], ids=["persistent", "per_op"])  # 0: batch_persistent 1
 
 
 def greedy_launches(path, sh):
@@ -64,6 +64,7 @@ def test_batch_greedy_matches_oracle_per_sequence(eng_mod, shape_name, steps, pa
     wdir = S.write_weight_tree(f"/tmp/xl_weights/{shape_name.lower()}", sh)
     eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
     eng.set_option("decode_path", path)  # the batched decoder follows the engine's decode path
+    eng.set_option("batch_persistent", 1 if path == 0 else 0)
     eng.load(wdir)
     bd = eng_mod.BatchDecoder(eng)
     assert eng_mod.BatchDecoder.size == B
@@ -100,6 +101,7 @@ def test_batch_sampled_draws_match_sample_cpu(eng_mod, path):
     wdir = S.write_weight_tree("/tmp/xl_weights/tiny", sh)
     eng = eng_mod.InferenceEngine("cuda", **sh.engine_kwargs())
     eng.set_option("decode_path", path)
+    eng.set_option("batch_persistent", 1 if path == 0 else 0)
     eng.load(wdir)
     bd = eng_mod.BatchDecoder(eng)
     T, P, RP = 0.7, 0.9, 1.1
@@ -141,6 +143,7 @@ def test_batch_full_model_greedy(eng_mod, full_weights, path):
     sh = S.FULL
     eng = eng_mod.InferenceEngine("cuda")
     eng.set_option("decode_path", path)
+    eng.set_option("batch_persistent", 1 if path == 0 else 0)
     eng.load(full_weights)
     bd = eng_mod.BatchDecoder(eng)
     lens = np.random.default_rng(5).integers(16, 513, B)

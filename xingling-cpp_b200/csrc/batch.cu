@@ -530,12 +530,12 @@ int BatchDecoder::init() {
 }
 
 // The batched persistent kernel serves when the engine uses the persistent
-// decode path and the shape fits it (one GPU, widths multiples of 64 up to
+// decode path, its option batch_persistent is 1, and the shape fits it (one GPU, widths multiples of 64 up to
 // kBatchPersistMaxK, at most 32 CTAs per attention item, at most
 // kPersistMaxContrib CTAs per row group of the split projections).
 bool BatchDecoder::persistent_fits() const {
     const Engine& E = *eng_;
-    return E.decode_path_ == 0 && E.tp_ == 1 && E.cfg_.layers <= kMaxLayers && E.H_ % kPersistKAlign == 0 &&
+    return E.decode_path_ == 0 && E.batch_persistent_ && E.tp_ == 1 && E.cfg_.layers <= kMaxLayers && E.H_ % kPersistKAlign == 0 &&
            E.Hl_ % kPersistKAlign == 0 && E.Fl_ % kPersistKAlign == 0 && E.H_ <= kBatchPersistMaxK &&
            E.Hl_ <= kBatchPersistMaxK && E.Fl_ <= kBatchPersistMaxK && persist_attn_ctas_per_head(E.T_) <= 32 &&
            persist_max_contrib(E.H_, E.Hl_, E.num_sms_) <= kPersistMaxContrib &&

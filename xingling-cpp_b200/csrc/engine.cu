@@ -1461,6 +1461,14 @@ int Engine::set_option(const char* key, int value) {
         tma_evict_first_ = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
+    if (k == "batch_persistent") {
+        if (value != 0 && value != 1) {
+            set_error("batch_persistent must be 0 or 1");
+            return XL_ERR_ARG;
+        }
+        batch_persistent_ = value;  // read when a BatchDecoder is created
+        return XL_OK;
+    }
     if (k == "tp_merge") {
         if (value != 0 && value != 1) {
             set_error("tp_merge must be 0 or 1");
