@@ -1187,6 +1187,7 @@ constexpr size_t kSmemBytesB = static_cast<size_t>(kSlotsB) * kSlotBytes +
                                kBatch * kConsumerWarps * 4 + kBatch * kConsumerWarps * 8 + 64;
 static_assert(kSmemBytesB <= kMaxSmemPerBlock, "batched persistent kernel fits in 227 KB of shared memory");
 static_assert(2 * kBatch == 16, "one (sequence, row) sum per half-warp lane");
+static_assert(kConsumerWarps == kBatch, "the RMSNorm staging gives each sequence one warp");
 
 // Butterfly reduce-scatter of 16 values held by every lane: afterwards lanes
 // l and l + 16 hold the warp-wide sum of value l % 16.
@@ -1236,91 +1237,86 @@ __device__ bool wait_count(const PersistentParams& p, int ph, int target, int* s
 // of b's input id (gather) or x_old_b + its partial row sums + bias after a
 // split projection of nb boxes per group; this CTA stores its slice of x_b to
 // x_out_b.  The RMSNorm is that of the single-sequence staging
-// (src/rmsnorm.cu:99-101).  Sequences go two at a time, each pair's loads
-// issued before its stores.
+// (src/rmsnorm.cu:99-101).  Warp w stages sequence w alone: its lanes load
+// four quads of the vector at a time (one L2 round trip per four), store x_b
+// to shared memory, reduce the sum of squares within the warp, then scale.
 __device__ __noinline__ void stage_norm8(const BatchPersistParams& bp, const float* x_old, const float* bias,
                                          const float* cres, int nb, const float* gamma, float* xs8, float* red8,
                                          float* x_out, bool gather) {
     const PersistentParams& p = bp.base;
     const int t = threadIdx.x - 32;
+    const int b = t >> 5, lane = t & 31;  // kConsumerWarps == kBatch
     const int K = p.H, K4 = K >> 2;
     const int T = (K / kPersistTileRows) * nb;
     const int s0 = static_cast<int>(blockIdx.x) * K / static_cast<int>(gridDim.x);
     const int s1 = static_cast<int>(blockIdx.x + 1) * K / static_cast<int>(gridDim.x);
     const size_t cstride = static_cast<size_t>(K / kPersistTileRows) * kPersistMaxContrib * kPersistTileRows;
-    float ss[kBatch];
+    const float* src = gather ? p.emb + static_cast<size_t>(bp.st[b].in.token_in) * K : x_old + static_cast<size_t>(b) * K;
+    const float* cb = gather ? nullptr : cres + b * cstride;
+    float4* x4 = reinterpret_cast<float4*>(xs8 + static_cast<size_t>(b) * kBatchPersistMaxK);
+    float ss = 0.0f;
+    constexpr int kU = 4;  // quads of a lane whose loads are issued together
+    for (int q0 = lane; q0 < K4; q0 += 32 * kU) {
+        float4 v[kU];
 #pragma unroll
-    for (int b = 0; b < kBatch; ++b) ss[b] = 0.0f;
-    for (int q = t; q < K4; q += kConsumerThreads) {
-#pragma unroll
-        for (int b0 = 0; b0 < kBatch; b0 += 2) {
-            float4 v[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int b = b0 + u;
-                const float* src = gather ? p.emb + static_cast<size_t>(bp.st[b].in.token_in) * K
-                                          : x_old + static_cast<size_t>(b) * K;
+        for (int u = 0; u < kU; ++u) {
+            const int q = q0 + 32 * u;
+            if (q < K4) {
                 const float4 xo = __ldcg(reinterpret_cast<const float4*>(src) + q);
-                v[u] = gather ? xo : residual_quad(xo, bias, cres + b * cstride, q, nb, T);
+                v[u] = gather ? xo : residual_quad(xo, bias, cb, q, nb, T);
             }
+        }
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int b = b0 + u;
-                reinterpret_cast<float4*>(xs8 + static_cast<size_t>(b) * kBatchPersistMaxK)[q] = v[u];
+        for (int u = 0; u < kU; ++u) {
+            const int q = q0 + 32 * u;
+            if (q < K4) {
+                x4[q] = v[u];
                 const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
                     if (4 * q + c >= s0 && 4 * q + c < s1) x_out[static_cast<size_t>(b) * K + 4 * q + c] = e[c];
-                ss[b] = dot4(v[u], v[u], ss[b]);
+                ss = dot4(v[u], v[u], ss);
             }
         }
     }
-    const int warp = t >> 5, lane = t & 31;
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-        const float w = warp_sum(ss[b]);
-        if (lane == 0) red8[b * kConsumerWarps + warp] = w;
-    }
-    consumer_sync();
-    float inv[kBatch];
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-        float tot = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) tot += red8[b * kConsumerWarps + w];
-        inv[b] = static_cast<float>(1.0 / sqrt(static_cast<double>(tot / static_cast<float>(K)) + 1e-6));
-    }
+    const float tot = warp_sum(ss);
+    const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(tot / static_cast<float>(K)) + 1e-6));
     const float4* g4 = reinterpret_cast<const float4*>(gamma);
-    for (int q = t; q < K4; q += kConsumerThreads) {
+    for (int q = lane; q < K4; q += 32) {
         const float4 g = g4[q];
-#pragma unroll
-        for (int b = 0; b < kBatch; ++b) {
-            float4* x4 = reinterpret_cast<float4*>(xs8 + static_cast<size_t>(b) * kBatchPersistMaxK) + q;
-            float4 v = *x4;
-            v.x = v.x * inv[b] * g.x;
-            v.y = v.y * inv[b] * g.y;
-            v.z = v.z * inv[b] * g.z;
-            v.w = v.w * inv[b] * g.w;
-            *x4 = v;
-        }
+        float4 v = x4[q];
+        v.x = v.x * inv * g.x;
+        v.y = v.y * inv * g.y;
+        v.z = v.z * inv * g.z;
+        v.w = v.w * inv * g.w;
+        x4[q] = v;
     }
+    (void)red8;
 }
 
-// xs8[b] = src_b[0, K) for every sequence b (src_b = src + b * K).
-__device__ void stage_copy8(const float* src, int K, float* xs8) {
+// xs8[b] = src_b[0, K) for every sequence b (src_b = src + b * K), by bulk
+// copies of the tensor memory accelerator: the first consumer thread issues
+// one cp.async.bulk per sequence onto an mbarrier that every consumer waits
+// for.  The rows were written by other CTAs in the previous phase (generic
+// proxy, ordered by that phase's counter): a proxy fence makes them visible
+// to the copies.  Bounded wait; false on a timeout.
+__device__ bool stage_copy8(const PersistentParams& p, const float* src, int K, float* xs8, uint64_t* bar,
+                            uint32_t& bar_par) {
     const int t = threadIdx.x - 32;
-    const int K4 = K >> 2;
-    for (int q = t; q < K4; q += kConsumerThreads) {
-#pragma unroll
-        for (int b0 = 0; b0 < kBatch; b0 += 4) {
-            float4 v[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(b0 + u) * K) + q);
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-                reinterpret_cast<float4*>(xs8 + static_cast<size_t>(b0 + u) * kBatchPersistMaxK)[q] = v[u];
-        }
+    const uint32_t bytes = static_cast<uint32_t>(K) * 4u;
+    if (t == 0) {
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        mbar_arrive_expect_tx(bar, bytes * kBatch);
+        for (int b = 0; b < kBatch; ++b)
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    smem_u32(xs8 + static_cast<size_t>(b) * kBatchPersistMaxK)),
+                "l"(src + static_cast<size_t>(b) * K), "r"(bytes), "r"(smem_u32(bar))
+                : "memory");
     }
+    const bool ok = wait_parity(bar, bar_par, p.st);
+    bar_par ^= 1u;
+    return ok;
 }
 
 // The attention phase of one layer for every sequence: items (sequence b,
@@ -1493,7 +1489,9 @@ __device__ bool attention_batch(const BatchPersistParams& bp, int layer, int ph,
 }
 
 __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float* xs8, uint64_t* full, uint64_t* empty,
-                                float* red8, unsigned long long* best8, int* s_ok, volatile int* quiet) {
+                                float* red8, unsigned long long* best8, int* s_ok, volatile int* quiet,
+                                uint64_t* copy_bar) {
+    uint32_t copy_par = 0;  // phase parity of the staging copies' mbarrier
     const PersistentParams& p = bp.base;
     DevState* st0 = bp.st;  // sequence 0's state holds the step's error word
     const int t = threadIdx.x - 32;
@@ -1534,11 +1532,11 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
             else
                 stage_norm8(bp, bp.xb, p.layer[l - 1].b2, bp.cres, nb_w2, y->g1, xs8, red8, bp.xa, false);
         } else if (kind == kWo) {
-            stage_copy8(bp.att, p.Hl, xs8);
+            if (!stage_copy8(p, bp.att, p.Hl, xs8, copy_bar, copy_par)) ok = false;
         } else if (kind == kW13) {
             stage_norm8(bp, bp.xa, y->bo, bp.cres, nb_wo, y->g2, xs8, red8, bp.xb, false);
         } else if (kind == kW2) {
-            stage_copy8(bp.ffh, p.Fl, xs8);
+            if (!stage_copy8(p, bp.ffh, p.Fl, xs8, copy_bar, copy_par)) ok = false;
         } else {  // kLM
             stage_norm8(bp, bp.xb, p.layer[l - 1].b2, bp.cres, nb_w2, p.gnorm, xs8, red8, bp.xa, false);
         }
@@ -1675,11 +1673,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_persistent_kernel(co
     unsigned long long* best8 = reinterpret_cast<unsigned long long*>(red8 + kBatch * kConsumerWarps);  // [8][kBatch]
     int* s_ok = reinterpret_cast<int*>(best8 + kBatch * kConsumerWarps);
     volatile int* quiet = s_ok + 8;
+    uint64_t* copy_bar = reinterpret_cast<uint64_t*>(s_ok + 12);  // 8-byte aligned: s_ok is
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlotsB; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
+        mbar_init(copy_bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         *quiet = 0;
     }
@@ -1687,7 +1687,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_persistent_kernel(co
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) producer<kSlotsB>(bp.base, ring, full, empty, quiet);
     } else {
-        consumers_batch(bp, ring, xs8, full, empty, red8, best8, s_ok, quiet);
+        consumers_batch(bp, ring, xs8, full, empty, red8, best8, s_ok, quiet, copy_bar);
     }
 }
 
