@@ -11,6 +11,8 @@ Bar (see the module docstring of xl_synth for the workload):
   any id that differs from the oracle's is explained by the measured logit
   difference moving r * total across a cumulative-probability boundary.
 """
+import time
+
 import numpy as np
 import pytest
 
@@ -362,3 +364,34 @@ def test_full_long_context_sampled(eng_mod, full_weights, path):
     assert eng.ctx_len() == 768
     with pytest.raises(RuntimeError):
         eng.next_token(tok, temperature=T, top_p=P, repetition_penalty=RP)
+
+
+def test_tagged_exchange_wait_runs_out_into_a_device_error(eng_mod, tiny_weights):
+    """The tagged exchange of the split projections (the tensor-parallel form,
+    here on one GPU with tag_split 1) waits for its words with a bounded spin.
+    With the test hook tag_skew the stagings wait for a tag nobody writes: the
+    step must end with RuntimeError (the kernel's device error) within a few
+    seconds instead of hanging.  One GPU then clears the error word and drops
+    the sequence: a decode without a new prompt is refused, and after a new
+    prefill the engine gives the same ids as before."""
+    sh = S.TINY
+    eng = make_engine(eng_mod, 0, **sh.engine_kwargs())
+    eng.set_option("tag_split", 1)
+    eng.load(tiny_weights)
+    ids = S.prompt_ids(11, 21, sh.vocab)
+    t = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
+    want = [eng.next_token(t, top_p=0.0, repetition_penalty=1.0)]
+    want.append(eng.next_token(want[-1], top_p=0.0, repetition_penalty=1.0))
+    eng.set_option("tag_skew", 1 << 20)
+    eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
+    t0 = time.monotonic()
+    with pytest.raises(RuntimeError, match="device error"):
+        eng.next_token(t, top_p=0.0, repetition_penalty=1.0)
+    assert time.monotonic() - t0 < 10.0
+    with pytest.raises(RuntimeError):
+        eng.next_token(t, top_p=0.0, repetition_penalty=1.0)  # the sequence was dropped
+    eng.set_option("tag_skew", 0)
+    assert eng.next_token(ids, top_p=0.0, repetition_penalty=1.0) == t
+    got = [eng.next_token(t, top_p=0.0, repetition_penalty=1.0)]
+    got.append(eng.next_token(got[-1], top_p=0.0, repetition_penalty=1.0))
+    assert got == want

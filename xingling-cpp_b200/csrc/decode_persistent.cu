@@ -263,6 +263,11 @@ __device__ __forceinline__ unsigned long long* xc_part(const PersistentParams& p
 __device__ __forceinline__ unsigned xtag(const PersistentParams& p, int l, int w2) {
     return static_cast<unsigned>(p.st->epoch) * (2u * static_cast<unsigned>(p.layers)) + 2u * l + w2 + 1u;
 }
+// The tag a staging waits for: xtag shifted by tag_skew (0 in service; a test
+// sets it to a tag nobody writes, so that the bounded wait runs out).
+__device__ __forceinline__ unsigned rtag(const PersistentParams& p, int l, int w2) {
+    return xtag(p, l, w2) + static_cast<unsigned>(p.tag_skew);
+}
 __device__ __forceinline__ unsigned long long xword(float v, unsigned tag) {
     return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
 }
@@ -969,7 +974,7 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                 stage_norm(p, p.emb + static_cast<size_t>(st->in.token_in) * p.H, nullptr, nullptr, 0, y->g1, xs, red,
                            p.xa, xr, false);
             else if (TP)
-                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, xtag(p, l - 1, 1), nb_w2, y->g1, xs, red, p.xa, xr,
+                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, rtag(p, l - 1, 1), nb_w2, y->g1, xs, red, p.xa, xr,
                               false);
             else
                 stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, y->g1, xs, red, p.xa, xr, false);
@@ -977,14 +982,14 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
             stage_copy(p.att, p.Hl, xs);
         } else if (kind == kW13) {
             if (TP)
-                stage_norm_tp(p, p.xa, y->bo, 0, xtag(p, l, 0), nb_wo, y->g2, xs, red, p.xb, xr, false);
+                stage_norm_tp(p, p.xa, y->bo, 0, rtag(p, l, 0), nb_wo, y->g2, xs, red, p.xb, xr, false);
             else
                 stage_norm(p, p.xa, y->bo, p.cres, nb_wo, y->g2, xs, red, p.xb, xr, false);
         } else if (kind == kW2) {
             stage_copy(p.ffh, p.Fl, xs);
         } else {  // kLM: the final residual also goes to xa (the LM head's input in global memory)
             if (TP)
-                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, xtag(p, l - 1, 1), nb_w2, p.gnorm, xs, red, p.xa, xr,
+                stage_norm_tp(p, p.xb, p.layer[l - 1].b2, 1, rtag(p, l - 1, 1), nb_w2, p.gnorm, xs, red, p.xa, xr,
                               true);
             else
                 stage_norm(p, p.xb, p.layer[l - 1].b2, p.cres, nb_w2, p.gnorm, xs, red, p.xa, xr, true);

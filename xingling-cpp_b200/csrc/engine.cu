@@ -735,6 +735,7 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     const bool tag_split = tag_split_ < 0 ? tpk : tag_split_ != 0;
     p.resid_smem = (resid_smem_ || tag_split) && persistent_smem_bytes(H_, 1) <= 232448 ? 1 : 0;
     p.tag_split = tag_split && p.resid_smem ? 1 : 0;
+    p.tag_skew = tag_skew_;
     p.tp = tp_;
     p.rank = rank_;
     if (tpk) {
@@ -1459,6 +1460,12 @@ int Engine::set_option(const char* key, int value) {
             return XL_ERR_ARG;
         }
         tma_evict_first_ = value;
+        return loaded_ ? capture_decode_graph() : XL_OK;
+    }
+    if (k == "tag_skew") {
+        // Test hook: the tagged exchange's stagings wait for a tag shifted by this amount; a tag nobody writes
+        // makes their bounded wait run out, and the step reports a device error.
+        tag_skew_ = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
     if (k == "batch_persistent") {
