@@ -251,6 +251,12 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const float* __restrict_
 // Causal softmax of one score row per warp: P[h][q][k] = exp(s - max) / sum for
 // k <= q (the online-softmax result of src/attn.cu:47-167 written out), zero
 // for q < k < kpad (the P.V GEMM reads keys up to kpad), plus the lo half.
+// One warp per (head, query) row of S: the row is read once into registers
+// (float4, up to kSmRowMax positions; longer rows take three passes over
+// memory), the maximum and the sum of exponentials over keys 0 .. q are warp
+// reductions, and P = e / sum and its TF32 lo half are written as float4 up to
+// kpad (zeros past q).
+constexpr int kSmRowMax = 2048;
 __global__ void __launch_bounds__(256) attn_softmax_kernel(float* __restrict__ S, float* __restrict__ P_lo, int n,
                                                            int heads, int max_ctx, int kpad) {
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
@@ -258,6 +264,48 @@ __global__ void __launch_bounds__(256) attn_softmax_kernel(float* __restrict__ S
     const int h = row / n, q = row % n;
     float* s = S + (static_cast<size_t>(h) * max_ctx + q) * max_ctx;
     float* pl = P_lo + (static_cast<size_t>(h) * max_ctx + q) * max_ctx;
+    if (kpad <= kSmRowMax) {
+        constexpr int kV = kSmRowMax / 128;  // float4 per lane
+        float4 v[kV];
+        float m = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kV; ++i) {
+            const int k = 4 * (lane + 32 * i);
+            if (k < kpad) {
+                v[i] = reinterpret_cast<const float4*>(s)[lane + 32 * i];
+                v[i].x = k <= q ? v[i].x : -INFINITY;
+                v[i].y = k + 1 <= q ? v[i].y : -INFINITY;
+                v[i].z = k + 2 <= q ? v[i].z : -INFINITY;
+                v[i].w = k + 3 <= q ? v[i].w : -INFINITY;
+                m = fmaxf(m, fmaxf(fmaxf(v[i].x, v[i].y), fmaxf(v[i].z, v[i].w)));
+            }
+        }
+        m = warp_max(m);
+        float l = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kV; ++i) {
+            const int k = 4 * (lane + 32 * i);
+            if (k < kpad) {  // masked keys hold -inf: expf gives 0
+                v[i].x = expf(v[i].x - m);
+                v[i].y = expf(v[i].y - m);
+                v[i].z = expf(v[i].z - m);
+                v[i].w = expf(v[i].w - m);
+                l += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+            }
+        }
+        l = warp_sum(l);
+        const float inv = 1.0f / l;
+#pragma unroll
+        for (int i = 0; i < kV; ++i) {
+            const int k = 4 * (lane + 32 * i);
+            if (k < kpad) {
+                const float4 p = make_float4(v[i].x * inv, v[i].y * inv, v[i].z * inv, v[i].w * inv);
+                reinterpret_cast<float4*>(s)[lane + 32 * i] = p;
+                reinterpret_cast<float4*>(pl)[lane + 32 * i] = make_float4(lo19(p.x), lo19(p.y), lo19(p.z), lo19(p.w));
+            }
+        }
+        return;
+    }
     float m = -INFINITY;
     for (int k = lane; k <= q; k += 32) m = fmaxf(m, s[k]);
     m = warp_max(m);
