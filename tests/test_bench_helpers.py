@@ -43,3 +43,30 @@ def test_peaks_fall_back_without_the_measured_file(tmp_path, monkeypatch):
     monkeypatch.setattr(b, "ROOT", str(tmp_path))
     pk, kind = b.peaks()
     assert kind == "fallback" and pk["hbm_gbs"] > 0 and pk["bf16_tflops"] > 0
+
+
+def test_library_record_names_the_timed_library(tmp_path, monkeypatch):
+    """The reference arm reports which library it timed: its path relative to
+    the repository, its size and hash, and whether the process maps it."""
+    b = _bench()
+    lib = tmp_path / "libfake.so"
+    lib.write_bytes(b"\x7fELF" + b"\0" * 60)
+    monkeypatch.setattr(b, "ROOT", str(tmp_path))
+    rec = b.library_record(str(lib))
+    assert rec["path"] == "libfake.so" and rec["bytes"] == 64 and len(rec["sha256_16"]) == 16
+    assert rec["mapped"] is False  # not loaded by this process
+    assert "restatement" in rec["what"]
+
+
+def test_engine_options_from_the_command_line(monkeypatch):
+    b = _bench()
+    seen = []
+
+    class Eng:
+        def set_option(self, k, v):
+            seen.append((k, v))
+
+    monkeypatch.setattr(b, "ENGINE_OPTS", {"tag_split": 1, "tp_merge": 0})
+    e = Eng()
+    assert b.apply_opts(e) is e
+    assert seen == [("tag_split", 1), ("tp_merge", 0)]
