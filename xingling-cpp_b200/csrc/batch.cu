@@ -565,6 +565,7 @@ int BatchDecoder::enqueue_persistent(cudaStream_t s, bool sampled) {
     p.rope = E.rope_;
     p.st = st_;
     p.done = done_;
+    p.trace = E.trace_;  // the engine's phase_trace option, when on before the decoder was created
     p.inflight = std::min(E.inflight_, 3);
     p.tma_evict_first = E.tma_evict_first_;
     p.H = E.H_;
