@@ -1037,7 +1037,11 @@ int Engine::device_error(int bits) {
                     "); this engine is unusable: create a new one on every rank";
         msg = fail_msg_;
     } else {
+        // The failed step's tagged words carry its step counter, which its last CTA never advanced: move the
+        // counter past it, so that the next step's waits never accept one of those words.
+        const int epoch = reinterpret_cast<const DevState*>(h_out_)->epoch + 1;
         XL_CUDA(cudaMemsetAsync(&st_->err, 0, sizeof(int), stream_));
+        XL_CUDA(cudaMemcpyAsync(&st_->epoch, &epoch, sizeof(int), cudaMemcpyHostToDevice, stream_));
         XL_CUDA(cudaStreamSynchronize(stream_));
         msg += "; the sequence was dropped: prefill a new prompt";
     }
