@@ -110,7 +110,7 @@ def _rank(rank, world, wdir, shape_kw, ids, teach, q_id, q_out, sampled=None, pa
         q_out.put((rank, "error", repr(e)[:400], None, None, None))
 
 
-def _spawn(world, target, args_of, timeout=900):
+def _spawn(world, target, args_of, timeout=300):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
