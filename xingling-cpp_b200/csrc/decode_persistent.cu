@@ -588,10 +588,7 @@ __device__ __noinline__ void stage_norm(const PersistentParams& p, const float* 
         for (int u = 0; u < kStageBatch; ++u) {
             const int q = t + (k0 + u) * kConsumerThreads;
             if (q < (K >> 2)) {
-                // norm_factor: the staged vector is x * gamma; the 1 / rms scale is applied in the epilogues
-                x4[q] = p.norm_factor ? make_float4(v[u].x * gk[k0 + u].x, v[u].y * gk[k0 + u].y,
-                                                    v[u].z * gk[k0 + u].z, v[u].w * gk[k0 + u].w)
-                                      : v[u];
+                x4[q] = v[u];
                 if (xr) reinterpret_cast<float4*>(xr)[q] = v[u];
                 if (!xr || out_too) {
                     const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
@@ -602,11 +599,6 @@ __device__ __noinline__ void stage_norm(const PersistentParams& p, const float* 
                 ss = dot4(v[u], v[u], ss);
             }
         }
-    }
-    if (p.norm_factor) {  // each warp's share of the sum of squares; read after the caller's barrier
-        const float w = warp_sum(ss);
-        if ((t & 31) == 0) red[t >> 5] = w;
-        return;
     }
     const float tot = consumer_sum(ss, red);
     // RMSNorm of src/rmsnorm.cu:99-101: 1 / sqrt(mean + 1e-6), in double.
@@ -713,7 +705,7 @@ __device__ __noinline__ void stage_norm_tp(const PersistentParams& p, const floa
             const float4 xo = xr ? reinterpret_cast<const float4*>(xr)[q]
                                  : __ldcg(reinterpret_cast<const float4*>(x_old) + q);
             const float4 v = residual_quad_tp(p, xo, bias, w2, q, nb, T, tag);
-            x4[q] = p.norm_factor ? make_float4(v.x * gk[k].x, v.y * gk[k].y, v.z * gk[k].z, v.w * gk[k].w) : v;
+            x4[q] = v;
             if (xr) reinterpret_cast<float4*>(xr)[q] = v;
             if (!xr || out_too) {
                 const float e[4] = {v.x, v.y, v.z, v.w};
@@ -723,11 +715,6 @@ __device__ __noinline__ void stage_norm_tp(const PersistentParams& p, const floa
             }
             ss = dot4(v, v, ss);
         }
-    }
-    if (p.norm_factor) {
-        const float w = warp_sum(ss);
-        if ((t & 31) == 0) red[t >> 5] = w;
-        return;
     }
     const float tot = consumer_sum(ss, red);
     const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(tot / static_cast<float>(K)) + 1e-6));
@@ -1010,14 +997,6 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
         consumer_sync();
         if (t == 0) *quiet = 0;
         if (t == 0) trace_at(p, ph, kTrConsStaged);
-        // norm_factor: 1 / rms of the staged residual, from the warps' shares of the sum of squares
-        float rscale = 1.0f;
-        if (p.norm_factor && kind != kWo && kind != kW2) {
-            float tot = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) tot += red[w];
-            rscale = static_cast<float>(1.0 / sqrt(static_cast<double>(tot / static_cast<float>(p.H)) + 1e-6));
-        }
         const int rs4 = r.bw / 4;  // float4 per row of a box
         const float4* x4 = reinterpret_cast<const float4*>(xs);
         const bool split = kind == kWo || kind == kW2;
@@ -1079,8 +1058,8 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
             acc_b = warp_sum(acc_b);
             switch (kind) {
                 case kQKV:
-                    if (lane == 0 && va) p.qkv[Ra] = acc_a * rscale + ea;
-                    if (lane == 1 && vb) p.qkv[Rb] = acc_b * rscale + eb;
+                    if (lane == 0 && va) p.qkv[Ra] = acc_a + ea;
+                    if (lane == 1 && vb) p.qkv[Rb] = acc_b + eb;
                     break;
                 case kWo:
                 case kW2: {  // partial row sums of this CTA's boxes of group g (c: this CTA's rank among its owners)
@@ -1097,17 +1076,17 @@ __device__ void consumers(const PersistentParams& p, char* ring, float* xs, uint
                     break;
                 }
                 case kW13:
-                    if (lane == 0 && vb) p.ffh[Ra >> 1] = silu(acc_a * rscale + ea) * (acc_b * rscale + eb);
+                    if (lane == 0 && vb) p.ffh[Ra >> 1] = silu(acc_a + ea) * (acc_b + eb);
                     break;
                 default: {  // kLM: logits with the repetition penalty, running argmax
                     if (va) {
-                        float v = acc_a * rscale;
+                        float v = acc_a;
                         if (ea != 0.0f) v = rep_penalty(v, rp);
                         if (lane == 0) p.logits[Ra] = v;
                         if (v > best_v) best_v = v, best_i = Ra;
                     }
                     if (vb) {
-                        float v = acc_b * rscale;
+                        float v = acc_b;
                         if (eb != 0.0f) v = rep_penalty(v, rp);
                         if (lane == 1) p.logits[Rb] = v;
                         if (v > best_v) best_v = v, best_i = Rb;

@@ -736,7 +736,6 @@ int Engine::enqueue_decode_persistent(cudaStream_t s, bool sampled) {
     p.resid_smem = (resid_smem_ || tag_split) && persistent_smem_bytes(H_, 1) <= 232448 ? 1 : 0;
     p.tag_split = tag_split && p.resid_smem ? 1 : 0;
     p.tag_skew = tag_skew_;
-    p.norm_factor = norm_factor_;
     p.tp = tp_;
     p.rank = rank_;
     if (tpk) {
@@ -1489,13 +1488,12 @@ int Engine::set_option(const char* key, int value) {
         tp_merge_ = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
-    if (k == "sig_cta" || k == "resid_smem" || k == "tag_split" || k == "norm_factor") {
+    if (k == "sig_cta" || k == "resid_smem" || k == "tag_split") {
         if (value != 0 && value != 1) {
             set_error(k + " must be 0 or 1");
             return XL_ERR_ARG;
         }
-        (k == "sig_cta" ? sig_cta_ : k == "resid_smem" ? resid_smem_ : k == "tag_split" ? tag_split_ : norm_factor_) =
-            value;
+        (k == "sig_cta" ? sig_cta_ : k == "resid_smem" ? resid_smem_ : tag_split_) = value;
         return loaded_ ? capture_decode_graph() : XL_OK;
     }
     if (k == "kernel_events") {

@@ -188,7 +188,6 @@ class Engine {
     int tag_split_ = -1;
     int tp_merge_ = 1;         // tensor parallel, greedy: the ranks' argmax keys merged inside the persistent kernel
     int tag_skew_ = 0;         // test hook: shift of the tag the tagged exchange's stagings wait for
-    int norm_factor_ = 0;      // persistent decode: the RMSNorm scale applied in the GEMV epilogues
     // BatchDecoder: 1 = the batched persistent kernel (one launch per step), 0 = per-op kernels (faster today:
     // 1.35 against ~2 ms per 8-token step on the replica workload; the batched kernel's stagings serialise)
     int batch_persistent_ = 0;

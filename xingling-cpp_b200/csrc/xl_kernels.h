@@ -181,7 +181,6 @@ struct PersistentParams {
     int tma_evict_first;        // 1: weight boxes are loaded with an L2 evict-first policy
     int sig_cta;                // 1: one release per CTA signals a phase (after a consumer barrier); 0: one per warp
     int resid_smem;             // 1: every CTA keeps the whole residual stream in shared memory (H floats)
-    int norm_factor;            // 1: RMSNorm stagings store x * gamma; the 1 / rms scale multiplies each row sum
     int tag_skew;               // added to the tag a staging waits for: 0 in service (tests: a tag nobody writes)
     int tag_split;              // 1: out-proj / W2 partial sums go tagged to every rank's xc, the next staging
                                 //    waits for the tags (no phase counter); needs resid_smem (also at tp == 1)
