@@ -444,6 +444,10 @@ def xl_arm(args) -> None:
             tp_info = tp_latency(args, llm_cpp_engine, dist, rank, world, local, max_over_ranks)
         except Exception as e:  # noqa: BLE001
             tp_info = {"tp": world, "error": repr(e)[:300]}
+    del eng  # this rank's engine (its own graphs and streams) before the process group goes
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
 
     if rank != 0:
         return
