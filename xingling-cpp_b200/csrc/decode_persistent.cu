@@ -1178,30 +1178,29 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
 // The same weight stream as decode_persistent_kernel (producer, ring of TMA
 // boxes, quiet window), with a 3-slot ring: shared memory holds every
 // sequence's staged input instead ([kBatch][4096] floats, 128 KB).  Each box
-// is dotted with all kBatch inputs: warp w owns rows 2w, 2w + 1 of the box and
-// keeps 2 x kBatch accumulators; one 16-value butterfly leaves lane l (and
-// l + 16) with the sum for (sequence l / 2, row l % 2).  The residual streams
-// ping-pong in global memory as in the first form of the single-sequence
-// kernel (no room for them in shared memory).  Attention runs per
-// (sequence, head) item, spread over the grid, several per CTA when there
-// are more items than SMs.  The LM head applies each sequence's penalty and
-// keeps each sequence's argmax; a greedy step ends in the kernel.
+// is dotted with all kBatch inputs: warp w owns rows 4 (w % 4) .. + 3 of the box
+// over half of its K and keeps 4 x kBatch accumulators; one 32-value
+// butterfly leaves lane l with (row l / 8, sequence l % 8), and the two halves
+// meet in shared memory.  The residual streams ping-pong in global memory as
+// in the first form of the single-sequence kernel (no room for them in shared
+// memory).  Attention runs per (sequence, head, 128-position part) item,
+// spread over the grid, four at once per CTA.  The LM head applies each
+// sequence's penalty and keeps each sequence's argmax; a greedy step ends in
+// the kernel.
 constexpr int kSlotsB = 3;
 constexpr size_t kSmemBytesB = static_cast<size_t>(kSlotsB) * kSlotBytes +
                                static_cast<size_t>(kBatch) * kBatchPersistMaxK * 4 + 2 * kSlotsB * 8 +
-                               kBatch * kConsumerWarps * 4 + kBatch * kConsumerWarps * 8 + 64;
+                               128 * 4 + kBatch * kConsumerWarps * 8 + 64;
 static_assert(kSmemBytesB <= kMaxSmemPerBlock, "batched persistent kernel fits in 227 KB of shared memory");
-static_assert(2 * kBatch == 16, "one (sequence, row) sum per half-warp lane");
+static_assert(4 * kBatch == 32, "one (row, sequence) sum per lane of a row quad");
 static_assert(kConsumerWarps == kBatch, "the RMSNorm staging gives each sequence one warp");
 
-// Butterfly reduce-scatter of 16 values held by every lane: afterwards lanes
-// l and l + 16 hold the warp-wide sum of value l % 16.
-__device__ __forceinline__ float reduce_scatter16(float (&v)[16]) {
+// Butterfly reduce-scatter of 32 values held by every lane: afterwards lane l
+// holds the warp-wide sum of value l.
+__device__ __forceinline__ float reduce_scatter32(float (&v)[32]) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], 16);
-#pragma unroll
-    for (int half = 8; half > 0; half >>= 1) {
+    for (int half = 16; half > 0; half >>= 1) {
         const bool upper = (lane & half) != 0;
 #pragma unroll
         for (int i = 0; i < half; ++i) {
@@ -1324,19 +1323,31 @@ __device__ bool stage_copy8(const PersistentParams& p, const float* src, int K, 
     return ok;
 }
 
-// The attention phase of one layer for every sequence: items (sequence b,
-// head h, CTA j of the item's nct_b), nct_b = ceil(chunks_b / 8) with 16
-// positions per warp chunk, enumerated sequence by sequence and dealt to the
-// CTAs round robin; a CTA runs its items one after another.  Per item the
-// warps do what the single-sequence attention phase does (RoPE at position
-// n_b, KV append, scores, softmax, P.V, src/attn.cu:490-547) and merge in
-// shared memory; an item split over several CTAs merges through global memory
-// (last-CTA ticket).  Every item's final writer signals once: the phase's
-// target is kBatch x heads.  Returns false if the wait for the QKV phase failed.
+// The attention phase of one layer for every sequence.  Items (sequence b,
+// head h, part j of nct_b): an item covers 128 positions, eight 16-position
+// chunks.  Items are enumerated sequence by sequence and dealt to the CTAs
+// round robin; a CTA runs four items at once, one per warp pair (slot), so
+// that their load latencies overlap.  Each warp of a pair takes four chunks of
+// the item in turn (RoPE at position n_b, the KV append by the chunk holding
+// n_b, scores, softmax, P.V, src/attn.cu:490-547), keeping a running (max,
+// sum, output); the pair merges in shared memory behind a named barrier of
+// its own, and an item split over several CTAs merges through global memory
+// (last-CTA ticket).  Every (sequence, head)'s final writer signals once: the
+// phase's target is kBatch x heads.  Returns false if the wait for the QKV
+// phase failed.
+constexpr int kBAttnSlots = kConsumerWarps / 2;  // items in flight per CTA
+constexpr int kBAttnChunks = 4;                  // chunks per warp of an item
+static_assert(2 * kBAttnChunks == kConsumerWarps, "an item covers as many chunks as the single-sequence CTA");
+
+__device__ __forceinline__ void pair_sync(int slot) {
+    asm volatile("bar.sync %0, 64;" ::"r"(2 + slot) : "memory");
+}
+
 __device__ bool attention_batch(const BatchPersistParams& bp, int layer, int ph, float* xs, int* s_ok) {
     const PersistentParams& p = bp.base;
     const int t = threadIdx.x - 32;
     const int warp = t >> 5, lane = t & 31;
+    const int slot = warp >> 1, half = warp & 1;
     const int G = gridDim.x;
     int nct[kBatch], ustart[kBatch + 1];
     ustart[0] = 0;
@@ -1354,59 +1365,63 @@ __device__ bool attention_batch(const BatchPersistParams& bp, int layer, int ph,
     float* apart = xs + kConsumerWarps * kAttnWarpScratch;  // [8][68]
     float* knew = xs + kConsumerWarps * (kAttnWarpScratch + kAttnPartStride) + warp * kHeadDim;
     const int maxs = persistent_max_splits(p.T);
-    for (int u = blockIdx.x; u < U; u += G) {
+    const int kp = lane >> 1, kh = lane & 1;
+    for (int k = slot;; k += kBAttnSlots) {
+        const int u = static_cast<int>(blockIdx.x) + k * G;
+        if (u >= U) break;
         int b = 0;
 #pragma unroll
         for (int i = 1; i < kBatch; ++i)
             if (u >= ustart[i]) b = i;
-        const int h = (u - ustart[b]) / nct[b], j = (u - ustart[b]) % nct[b];
+        const int nb = nct[b];
+        const int h = (u - ustart[b]) / nb, j = (u - ustart[b]) % nb;
         const int n = bp.st[b].pos;
         const int nsplit = n / kPersistChunk + 1;
-        const int s = j * kConsumerWarps + warp;
-        const bool active = s < nsplit;
-        const int t0 = s * kPersistChunk;
         const size_t head_off = (static_cast<size_t>(b) * p.heads + h) * p.T * kHeadDim;
         float* kc = bp.kc[layer] + head_off;
         float* vc = bp.vc[layer] + head_off;
         const float* qkv = bp.qkv + static_cast<size_t>(b) * 3 * p.Hl;
-        if (active) {
-            const int kp = lane >> 1, kh = lane & 1;
+        const float2 cs = p.rope[n * kHalfHead + lane];
+        {
+            const float* q = qkv + h * kHeadDim;
+            const float qa = __ldcg(q + lane), qb = __ldcg(q + lane + kHalfHead);
+            qsh[lane] = (qa * cs.x + qb * cs.y) * 0.125f;  // 1/sqrt(64) is exact
+            qsh[lane + kHalfHead] = (-qa * cs.y + qb * cs.x) * 0.125f;
+        }
+        __syncwarp();
+        const float4* q4 = reinterpret_cast<const float4*>(qsh) + 8 * kh;
+        float m_run = -INFINITY, l_run = 0.0f;
+        float2 o_run = make_float2(0.0f, 0.0f);
+        for (int c = 0; c < kBAttnChunks; ++c) {
+            const int s = j * kConsumerWarps + half * kBAttnChunks + c;
+            if (s >= nsplit) break;
+            const int t0 = s * kPersistChunk;
             const int posk = t0 + kp;
             const int cached = min(kPersistChunk, n - t0);
             const bool has_n = n >= t0 && n < t0 + kPersistChunk;
-            const float2 cs = p.rope[n * kHalfHead + lane];
-            const float* q = qkv + h * kHeadDim;
-            const float* kn = qkv + p.Hl + h * kHeadDim;
-            const float* vn = qkv + 2 * p.Hl + h * kHeadDim;
             float4 kv[8];
             const float4* kr =
                 reinterpret_cast<const float4*>(kc + static_cast<size_t>(kp < cached ? posk : 0) * kHeadDim) + 8 * kh;
 #pragma unroll
             for (int i = 0; i < 8; ++i) kv[i] = kp < cached ? __ldcg(kr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            const float qa = __ldcg(q + lane), qb = __ldcg(q + lane + kHalfHead);
-            float ka = 0.0f, kb = 0.0f;
             float2 vnew = make_float2(0.0f, 0.0f);
             if (has_n) {
-                ka = __ldcg(kn + lane);
-                kb = __ldcg(kn + lane + kHalfHead);
+                const float* kn = qkv + p.Hl + h * kHeadDim;
+                const float* vn = qkv + 2 * p.Hl + h * kHeadDim;
+                const float ka = __ldcg(kn + lane), kb = __ldcg(kn + lane + kHalfHead);
                 vnew = __ldcg(reinterpret_cast<const float2*>(vn) + lane);
-            }
-            qsh[lane] = (qa * cs.x + qb * cs.y) * 0.125f;  // 1/sqrt(64) is exact
-            qsh[lane + kHalfHead] = (-qa * cs.y + qb * cs.x) * 0.125f;
-            if (has_n) {
                 const float k0 = ka * cs.x + kb * cs.y, k1 = -ka * cs.y + kb * cs.x;
                 knew[lane] = k0;
                 knew[lane + kHalfHead] = k1;
                 kc[n * kHeadDim + lane] = k0;
                 kc[n * kHeadDim + lane + kHalfHead] = k1;
                 reinterpret_cast<float2*>(vc + n * kHeadDim)[lane] = vnew;
-            }
-            __syncwarp();
-            const float4* q4 = reinterpret_cast<const float4*>(qsh) + 8 * kh;
-            if (posk == n) {
-                const float4* k4 = reinterpret_cast<const float4*>(knew) + 8 * kh;
+                __syncwarp();
+                if (posk == n) {
+                    const float4* k4 = reinterpret_cast<const float4*>(knew) + 8 * kh;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) kv[i] = k4[i];
+                    for (int i = 0; i < 8; ++i) kv[i] = k4[i];
+                }
             }
             float d = 0.0f;
 #pragma unroll
@@ -1427,30 +1442,32 @@ __device__ bool attention_batch(const BatchPersistParams& bp, int layer, int ph,
                 o.x = fmaf(ej, v.x, o.x);
                 o.y = fmaf(ej, v.y, o.y);
             }
-            float* ap = apart + warp * kAttnPartStride;
-            reinterpret_cast<float2*>(ap + 4)[lane] = o;
-            if (lane == 0) {
-                ap[0] = m;
-                ap[1] = l;
-            }
+            // running merge over this warp's chunks
+            const float mn = fmaxf(m_run, m);
+            const float sa = expf(m_run - mn), sb = expf(m - mn);
+            l_run = l_run * sa + l * sb;
+            o_run = make_float2(o_run.x * sa + o.x * sb, o_run.y * sa + o.y * sb);
+            m_run = mn;
         }
-        consumer_sync();
-        if (warp == 0) {
-            const int nw = min(kConsumerWarps, nsplit - j * kConsumerWarps);
-            const float mk = lane < nw ? apart[lane * kAttnPartStride] : -INFINITY;
-            const float lk = lane < nw ? apart[lane * kAttnPartStride + 1] : 0.0f;
-            const float M = warp_max(mk);
-            const float wk = lane < nw ? expf(mk - M) : 0.0f;
-            const float L = warp_sum(lk * wk);
-            float2 acc = make_float2(0.0f, 0.0f);
-            for (int k = 0; k < nw; ++k) {
-                const float wt = __shfl_sync(0xffffffffu, wk, k);
-                const float2 ok = reinterpret_cast<const float2*>(apart + k * kAttnPartStride + 4)[lane];
-                acc.x = fmaf(wt, ok.x, acc.x);
-                acc.y = fmaf(wt, ok.y, acc.y);
-            }
+        float* ap = apart + warp * kAttnPartStride;
+        reinterpret_cast<float2*>(ap + 4)[lane] = o_run;
+        if (lane == 0) {
+            ap[0] = m_run;
+            ap[1] = l_run;
+        }
+        pair_sync(slot);
+        if (half == 0) {
+            const float* a0 = apart + warp * kAttnPartStride;
+            const float* a1 = a0 + kAttnPartStride;
+            const float m0 = a0[0], m1 = a1[0];
+            const float M = fmaxf(m0, m1);
+            const float w0 = expf(m0 - M), w1 = expf(m1 - M);  // a warp without a chunk holds (-inf, 0, 0)
+            const float L = a0[1] * w0 + a1[1] * w1;
+            const float2 o0 = reinterpret_cast<const float2*>(a0 + 4)[lane];
+            const float2 o1 = reinterpret_cast<const float2*>(a1 + 4)[lane];
+            const float2 acc = make_float2(o0.x * w0 + o1.x * w1, o0.y * w0 + o1.y * w1);
             float2* out = reinterpret_cast<float2*>(bp.att + static_cast<size_t>(b) * p.Hl + h * kHeadDim);
-            if (nct[b] == 1) {
+            if (nb == 1) {
                 out[lane] = make_float2(acc.x / L, acc.y / L);
                 signal_warp(p, ph);
             } else {
@@ -1468,18 +1485,17 @@ __device__ bool attention_batch(const BatchPersistParams& bp, int layer, int ph,
                     ticket = atomicAdd(bp.head_done + (layer * kBatch + b) * p.heads + h, 1);
                 }
                 ticket = __shfl_sync(0xffffffffu, ticket, 0);
-                if (ticket == nct[b] - 1) {
+                if (ticket == nb - 1) {
                     __threadfence();
-                    const int nc = nct[b];
-                    const float mc = lane < nc ? __ldcg(base + lane * (kHeadDim + 2)) : -INFINITY;
-                    const float lc = lane < nc ? __ldcg(base + lane * (kHeadDim + 2) + 1) : 0.0f;
+                    const float mc = lane < nb ? __ldcg(base + lane * (kHeadDim + 2)) : -INFINITY;
+                    const float lc = lane < nb ? __ldcg(base + lane * (kHeadDim + 2) + 1) : 0.0f;
                     const float M2 = warp_max(mc);
-                    const float wc = lane < nc ? expf(mc - M2) : 0.0f;
+                    const float wc = lane < nb ? expf(mc - M2) : 0.0f;
                     const float L2 = warp_sum(lc * wc);
                     float2 acc2 = make_float2(0.0f, 0.0f);
-                    for (int k = 0; k < nc; ++k) {
-                        const float wt = __shfl_sync(0xffffffffu, wc, k);
-                        const float2 ok = __ldcg(reinterpret_cast<const float2*>(base + k * (kHeadDim + 2) + 2) + lane);
+                    for (int q = 0; q < nb; ++q) {
+                        const float wt = __shfl_sync(0xffffffffu, wc, q);
+                        const float2 ok = __ldcg(reinterpret_cast<const float2*>(base + q * (kHeadDim + 2) + 2) + lane);
                         acc2.x = fmaf(wt, ok.x, acc2.x);
                         acc2.y = fmaf(wt, ok.y, acc2.y);
                     }
@@ -1488,7 +1504,7 @@ __device__ bool attention_batch(const BatchPersistParams& bp, int layer, int ph,
                 }
             }
         }
-        consumer_sync();  // the scratch is reused by the next item
+        pair_sync(slot);  // the pair's scratch is reused by its next item
     }
     return true;
 }
@@ -1507,11 +1523,9 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
     int slot = 0;
     uint32_t par = 0;
     bool ok = true;
-    // LM head: lane l < 16 keeps the running argmax of sequence l / 2 over the rows it finishes.
+    // LM head: lane l of a lower-half warp keeps the running argmax of sequence l % 8 over the rows it finishes.
     float best_v = -INFINITY;
     int best_i = -1;
-    const int my_seq = (lane & 15) >> 1, my_row = lane & 1;
-    const float my_rp = bp.st[my_seq].in.rp;
     const int last = 5 * p.layers;
     for (int ph = 0; ph <= last; ++ph) {
         const int kind = phase_kind(ph, p.layers);
@@ -1549,43 +1563,52 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
         if (t == 0) *quiet = 0;
         if (t == 0) trace_at(p, ph, kTrConsStaged);
         const int rs4 = r.bw / 4;
-        const int ra = 2 * warp, rb = ra + 1;
+        // Warp w owns rows 4 (w % 4) .. 4 (w % 4) + 3 of each box over half of its K (w / 4); after a group's
+        // boxes, a 32-value butterfly leaves lane l with (row l / 8, sequence l % 8) of that half, the upper
+        // half's warp hands its sums over in shared memory, and the lower half's warp finishes the group.
+        const int quad = warp & 3, khalf = warp >> 2;
+        const int r0 = 4 * quad;
+        const int my_r = r0 + (lane >> 3), my_b = lane & 7;
+        const float my_rp = bp.st[my_b].in.rp;
+        float* xch = red8 + quad * 32;  // [4 quads][32 lanes]
         for (int tau = r.t0; tau < r.t1;) {
             const int g = tau / r.nb;
             const int bi0 = tau % r.nb, bi1 = min(r.nb, bi0 + (r.t1 - tau));
             const int rows = min(kPersistTileRows, d.M - g * kPersistTileRows);
-            // this lane's (sequence, row) after the butterfly
-            const int Rl = g * kPersistTileRows + (my_row ? rb : ra);
-            const bool vl = (my_row ? rb : ra) < rows;
+            const int Rl = g * kPersistTileRows + my_r;
+            const bool vl = my_r < rows;
             float el = 0.0f;  // bias of the lane's row, or its sequence's repetition flag in the LM head
-            if (kind == kLM) {
-                if (vl) el = bp.rep[static_cast<size_t>(my_seq) * p.V + Rl] ? 1.0f : 0.0f;
-            } else if (kind == kQKV || kind == kW13) {
-                if (vl) el = d.bias[Rl];
+            if (khalf == 0) {
+                if (kind == kLM) {
+                    if (vl) el = bp.rep[static_cast<size_t>(my_b) * p.V + Rl] ? 1.0f : 0.0f;
+                } else if (kind == kQKV || kind == kW13) {
+                    if (vl) el = d.bias[Rl];
+                }
             }
-            float acc[2 * kBatch];
+            float acc[32];
 #pragma unroll
-            for (int i = 0; i < 2 * kBatch; ++i) acc[i] = 0.0f;
+            for (int i2 = 0; i2 < 32; ++i2) acc[i2] = 0.0f;
             for (int bi = bi0; bi < bi1; ++bi) {
                 if (ok && !wait_parity(&full[slot], par, st0)) ok = false;
                 if (t == 0 && kind != kLM && tau + (bi - bi0) == r.t1 - 1) *quiet = 1;
                 if (ok) {
                     const int k0 = bi * r.bw;
                     const int kc4 = min(r.bw, d.K - k0) >> 2;
+                    const int hq = rs4 >> 1;  // float4 per half row
                     const float4* tile = reinterpret_cast<const float4*>(ring + static_cast<size_t>(slot) * kSlotBytes);
-                    const float4* wa = tile + ra * rs4;
-                    const float4* wb = tile + rb * rs4;
 #pragma unroll
-                    for (int j0 = 0; j0 < kBoxK / 4; j0 += 32) {
-                        const int j = j0 + lane;
-                        if (j < kc4) {
-                            const float4 a4 = wa[j], b4 = wb[j];
+                    for (int j0 = 0; j0 < kBoxK / 8; j0 += 32) {
+                        const int j = khalf * hq + j0 + lane;
+                        if (j0 + lane < hq && j < kc4) {
+                            float4 w4[4];
+#pragma unroll
+                            for (int rr = 0; rr < 4; ++rr) w4[rr] = tile[(r0 + rr) * rs4 + j];
 #pragma unroll
                             for (int b = 0; b < kBatch; ++b) {
-                                const float4 xv =
-                                    reinterpret_cast<const float4*>(xs8 + static_cast<size_t>(b) * kBatchPersistMaxK)[(k0 >> 2) + j];
-                                acc[2 * b] = dot4(a4, xv, acc[2 * b]);
-                                acc[2 * b + 1] = dot4(b4, xv, acc[2 * b + 1]);
+                                const float4 xv = reinterpret_cast<const float4*>(
+                                    xs8 + static_cast<size_t>(b) * kBatchPersistMaxK)[(k0 >> 2) + j];
+#pragma unroll
+                                for (int rr = 0; rr < 4; ++rr) acc[rr * 8 + b] = dot4(w4[rr], xv, acc[rr * 8 + b]);
                             }
                         }
                     }
@@ -1598,35 +1621,40 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
                 }
             }
             tau += bi1 - bi0;
-            const float sum = reduce_scatter16(acc);  // lanes l, l + 16: sequence (l % 16) / 2, row l % 2
-            switch (kind) {
-                case kQKV:
-                    if (lane < 16 && vl) bp.qkv[static_cast<size_t>(my_seq) * 3 * p.Hl + Rl] = sum + el;
-                    break;
-                case kWo:
-                case kW2: {
-                    const int c = persist_contrib_slot(blockIdx.x, g, bi0, r.nb, r.T, G);
-                    if (lane < 16)
-                        bp.cres[my_seq * cstride + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows +
-                                (my_row ? rb : ra)] = sum;
-                    break;
-                }
-                case kW13: {
-                    // rows (2i, 2i + 1) = (W1 row i, V row i) sit in lanes (2s, 2s + 1) of sequence s
-                    const float gate = __shfl_xor_sync(0xffffffffu, sum + el, 1);
-                    if (lane < 16 && my_row == 1 && vl)
-                        bp.ffh[static_cast<size_t>(my_seq) * p.Fl + (Rl >> 1)] = silu(gate) * (sum + el);
-                    break;
-                }
-                default: {  // kLM: logits with the sequence's repetition penalty, running argmax
-                    if (lane < 16 && vl) {
-                        float v = sum;
-                        if (el != 0.0f) v = rep_penalty(v, my_rp);
-                        bp.logits[static_cast<size_t>(my_seq) * p.V + Rl] = v;
-                        if (v > best_v) best_v = v, best_i = Rl;
+            float sum = reduce_scatter32(acc);  // lane l: row r0 + l / 8, sequence l % 8, this half of K
+            if (khalf == 1) xch[lane] = sum;
+            pair_sync(4 + quad);  // warps quad and quad + 4
+            if (khalf == 0) {
+                sum += xch[lane];
+                switch (kind) {
+                    case kQKV:
+                        if (vl) bp.qkv[static_cast<size_t>(my_b) * 3 * p.Hl + Rl] = sum + el;
+                        break;
+                    case kWo:
+                    case kW2: {
+                        const int c = persist_contrib_slot(blockIdx.x, g, bi0, r.nb, r.T, G);
+                        bp.cres[my_b * cstride + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows +
+                                my_r] = sum;
+                        break;
+                    }
+                    case kW13: {
+                        // rows (2i, 2i + 1) = (W1 row i, V row i) sit in lanes l and l + 8 (same sequence)
+                        const float gate = __shfl_xor_sync(0xffffffffu, sum + el, 8);
+                        if ((my_r & 1) == 1 && vl)
+                            bp.ffh[static_cast<size_t>(my_b) * p.Fl + (Rl >> 1)] = silu(gate) * (sum + el);
+                        break;
+                    }
+                    default: {  // kLM: logits with the sequence's repetition penalty, running argmax
+                        if (vl) {
+                            float v = sum;
+                            if (el != 0.0f) v = rep_penalty(v, my_rp);
+                            bp.logits[static_cast<size_t>(my_b) * p.V + Rl] = v;
+                            if (v > best_v) best_v = v, best_i = Rl;
+                        }
                     }
                 }
             }
+            pair_sync(4 + quad);  // xch is reused by the next group
         }
         if (kind != kLM) {
             consumer_sync();  // every warp's stores of the phase, then one release per CTA
@@ -1634,11 +1662,15 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
         }
         if (t == 0) trace_at(p, ph, kTrConsEnd);
     }
-    // LM head: per sequence, lane pair -> warp -> CTA -> grid maximum; the last CTA finishes the step.
-    unsigned long long k = lane < 16 && best_i >= 0 ? pack_argmax(best_v, best_i) : 0ull;
-    const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, 1);
-    k = k2 > k ? k2 : k;
-    if (lane < 16 && my_row == 0) best8[warp * kBatch + my_seq] = k;
+    // LM head: per sequence, the lanes of a warp -> the warp -> the CTA -> the grid maximum; the last CTA
+    // finishes the step.  Lane l of a lower-half warp holds sequence l % 8.
+    unsigned long long k = best_i >= 0 ? pack_argmax(best_v, best_i) : 0ull;
+#pragma unroll
+    for (int off = 8; off < 32; off <<= 1) {
+        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, off);
+        k = k2 > k ? k2 : k;
+    }
+    if (lane < kBatch) best8[warp * kBatch + lane] = k;
     consumer_sync();
     if (t < kBatch) {
         unsigned long long m = 0;
@@ -1674,8 +1706,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_persistent_kernel(co
     float* xs8 = reinterpret_cast<float*>(smem + static_cast<size_t>(kSlotsB) * kSlotBytes);
     uint64_t* full = reinterpret_cast<uint64_t*>(xs8 + static_cast<size_t>(kBatch) * kBatchPersistMaxK);
     uint64_t* empty = full + kSlotsB;
-    float* red8 = reinterpret_cast<float*>(empty + kSlotsB);                            // [kBatch][8 warps]
-    unsigned long long* best8 = reinterpret_cast<unsigned long long*>(red8 + kBatch * kConsumerWarps);  // [8][kBatch]
+    float* red8 = reinterpret_cast<float*>(empty + kSlotsB);  // [4 row quads][32]: K-half hand-over
+    unsigned long long* best8 = reinterpret_cast<unsigned long long*>(red8 + 128);  // [8 warps][kBatch]
     int* s_ok = reinterpret_cast<int*>(best8 + kBatch * kConsumerWarps);
     volatile int* quiet = s_ok + 8;
     uint64_t* copy_bar = reinterpret_cast<uint64_t*>(s_ok + 12);  // 8-byte aligned: s_ok is
