@@ -496,6 +496,8 @@ int BatchDecoder::init() {
     add(&cres_, kBatch * (H / kPersistTileRows) * kPersistMaxContrib * kPersistTileRows * 4);
     add(&part_, kBatch * heads * static_cast<size_t>(persistent_max_splits(E.T_)) * (kHeadDim + 2) * 4);
     add(&done_, done_words() * 4);
+    add(&tick_, tick_words() * 4);
+    add(&ssq_, kBatch * (H / 4) * 4);
     add(&qkv_, kBatch * 3 * Hl * 4);
     add(&att_, kBatch * Hl * 4);
     add(&ffh_, kBatch * Fl * 4);
@@ -580,6 +582,8 @@ int BatchDecoder::enqueue_persistent(cudaStream_t s, bool sampled) {
     bp.xa = x_;
     bp.xb = xb_;
     bp.cres = cres_;
+    bp.tickets = tick_;
+    bp.ssq = ssq_;
     bp.qkv = qkv_;
     bp.att = att_;
     bp.ffh = ffh_;
@@ -594,6 +598,7 @@ int BatchDecoder::enqueue_persistent(cudaStream_t s, bool sampled) {
     batch_in_kernel<<<1, 32, 0, s>>>(in_, st_, tokens_);
     XB_CUDA(cudaGetLastError());
     XB_CUDA(cudaMemsetAsync(done_, 0, done_words() * sizeof(int), s));
+    XB_CUDA(cudaMemsetAsync(tick_, 0, tick_words() * sizeof(int), s));
     XB_CUDA(launch_decode_batch_persistent(bp, E.num_sms_, s));
     if (!sampled) return XL_OK;  // the kernel wrote every sequence's greedy id
     SampleParams sp{};

@@ -1237,49 +1237,45 @@ __device__ bool wait_count(const PersistentParams& p, int ph, int target, int* s
     return *s_ok != 0;
 }
 
-// xs8[b] = rmsnorm(x_b) * gamma for every sequence b: x_b is the embedding row
-// of b's input id (gather) or x_old_b + its partial row sums + bias after a
-// split projection of nb boxes per group; this CTA stores its slice of x_b to
-// x_out_b.  The RMSNorm is that of the single-sequence staging
-// (src/rmsnorm.cu:99-101).  Warp w stages sequence w alone: its lanes load
-// four quads of the vector at a time (one L2 round trip per four), store x_b
-// to shared memory, reduce the sum of squares within the warp, then scale.
-__device__ __noinline__ void stage_norm8(const BatchPersistParams& bp, const float* x_old, const float* bias,
-                                         const float* cres, int nb, const float* gamma, float* xs8, float* red8,
-                                         float* x_out, bool gather) {
+// xs8[b] = rmsnorm(x_b) * gamma for every sequence b (src/rmsnorm.cu:99-101).
+// Either x_b is the embedding row of b's input id (gather: this CTA also
+// stores its slice of x_b to x_out), or it is the residual the previous split
+// projection finished (x_fin, with ssq its sums of squares per 4-row quad).
+// Warp w stages sequence w alone: its lanes load four quads of the vector at a
+// time (one L2 round trip per four) and reduce the sum of squares in the warp.
+__device__ __noinline__ void stage_norm8(const BatchPersistParams& bp, const float* x_fin, const float* ssq,
+                                         const float* gamma, float* xs8, float* x_out, bool gather) {
     const PersistentParams& p = bp.base;
     const int t = threadIdx.x - 32;
     const int b = t >> 5, lane = t & 31;  // kConsumerWarps == kBatch
     const int K = p.H, K4 = K >> 2;
-    const int T = (K / kPersistTileRows) * nb;
     const int s0 = static_cast<int>(blockIdx.x) * K / static_cast<int>(gridDim.x);
     const int s1 = static_cast<int>(blockIdx.x + 1) * K / static_cast<int>(gridDim.x);
-    const size_t cstride = static_cast<size_t>(K / kPersistTileRows) * kPersistMaxContrib * kPersistTileRows;
-    const float* src = gather ? p.emb + static_cast<size_t>(bp.st[b].in.token_in) * K : x_old + static_cast<size_t>(b) * K;
-    const float* cb = gather ? nullptr : cres + b * cstride;
+    const float* src = gather ? p.emb + static_cast<size_t>(bp.st[b].in.token_in) * K : x_fin + static_cast<size_t>(b) * K;
     float4* x4 = reinterpret_cast<float4*>(xs8 + static_cast<size_t>(b) * kBatchPersistMaxK);
     float ss = 0.0f;
+    if (!gather)
+        for (int i = lane; i < K4; i += 32) ss += __ldcg(ssq + static_cast<size_t>(b) * K4 + i);
     constexpr int kU = 4;  // quads of a lane whose loads are issued together
     for (int q0 = lane; q0 < K4; q0 += 32 * kU) {
         float4 v[kU];
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
             const int q = q0 + 32 * u;
-            if (q < K4) {
-                const float4 xo = __ldcg(reinterpret_cast<const float4*>(src) + q);
-                v[u] = gather ? xo : residual_quad(xo, bias, cb, q, nb, T);
-            }
+            if (q < K4) v[u] = __ldcg(reinterpret_cast<const float4*>(src) + q);
         }
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
             const int q = q0 + 32 * u;
             if (q < K4) {
                 x4[q] = v[u];
-                const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                if (gather) {
+                    const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    if (4 * q + c >= s0 && 4 * q + c < s1) x_out[static_cast<size_t>(b) * K + 4 * q + c] = e[c];
-                ss = dot4(v[u], v[u], ss);
+                    for (int c = 0; c < 4; ++c)
+                        if (4 * q + c >= s0 && 4 * q + c < s1) x_out[static_cast<size_t>(b) * K + 4 * q + c] = e[c];
+                    ss = dot4(v[u], v[u], ss);
+                }
             }
         }
     }
@@ -1295,7 +1291,37 @@ __device__ __noinline__ void stage_norm8(const BatchPersistParams& bp, const flo
         v.w = v.w * inv * g.w;
         x4[q] = v;
     }
-    (void)red8;
+}
+
+// A split projection's group g (16 rows, nc contributing CTAs): each
+// contributor's lower-half warp for row quad `quad` stores its partial sums,
+// then takes a ticket; the last one finishes the quad's rows for every
+// sequence: x_new = x_old + (partials in CTA order + bias), as the
+// single-sequence staging forms it, stored to x_out, with the quad's sum of
+// squares per sequence stored to ssq.  Lane l holds row r0 + l / 8 of
+// sequence l % 8.  The tickets are zeroed before each launch.
+__device__ void finish_quad(const BatchPersistParams& bp, int* ticket, int nc, int g, int quad, int my_r, int my_b,
+                            const float* x_old, const float* bias, float* x_out, float* ssq) {
+    const PersistentParams& p = bp.base;
+    const int lane = threadIdx.x & 31;
+    const size_t cstride = static_cast<size_t>(p.H / kPersistTileRows) * kPersistMaxContrib * kPersistTileRows;
+    __threadfence();
+    __syncwarp();
+    int tk = 0;
+    if (lane == 0) tk = atomicAdd(ticket, 1);
+    tk = __shfl_sync(0xffffffffu, tk, 0);
+    if (tk != nc - 1) return;
+    __threadfence();
+    const float* part = bp.cres + my_b * cstride + static_cast<size_t>(g) * kPersistMaxContrib * kPersistTileRows + my_r;
+    float sp = __ldcg(part);
+    for (int c = 1; c < nc; ++c) sp += __ldcg(part + c * kPersistTileRows);
+    const int R = g * kPersistTileRows + my_r;
+    const float x = __ldcg(x_old + static_cast<size_t>(my_b) * p.H + R) + (sp + bias[R]);
+    x_out[static_cast<size_t>(my_b) * p.H + R] = x;
+    float q2 = x * x;  // the quad's four rows of this sequence: lanes l, l + 8, l + 16, l + 24
+    q2 += __shfl_xor_sync(0xffffffffu, q2, 8);
+    q2 += __shfl_xor_sync(0xffffffffu, q2, 16);
+    if (lane < kBatch) ssq[static_cast<size_t>(my_b) * (p.H >> 2) + g * 4 + quad] = q2;
 }
 
 // xs8[b] = src_b[0, K) for every sequence b (src_b = src + b * K), by bulk
@@ -1517,7 +1543,6 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
     DevState* st0 = bp.st;  // sequence 0's state holds the step's error word
     const int t = threadIdx.x - 32;
     const int warp = t >> 5, lane = t & 31;
-    const int nb_wo = persist_boxes_per_group(p.Hl), nb_w2 = persist_boxes_per_group(p.Fl);
     const int G = gridDim.x;
     const size_t cstride = static_cast<size_t>(p.H / kPersistTileRows) * kPersistMaxContrib * kPersistTileRows;
     int slot = 0;
@@ -1545,19 +1570,20 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
             if (!wait_count(p, ph - 1, target, s_ok)) return;
         }
         if (t == 0) trace_at(p, ph, kTrConsStart);
+        // The residual streams: the W2 phase finishes xa (from xb), the out-projection finishes xb (from xa).
         if (kind == kQKV) {
             if (l == 0)
-                stage_norm8(bp, nullptr, nullptr, nullptr, 0, y->g1, xs8, red8, bp.xa, true);
+                stage_norm8(bp, nullptr, nullptr, y->g1, xs8, bp.xa, true);
             else
-                stage_norm8(bp, bp.xb, p.layer[l - 1].b2, bp.cres, nb_w2, y->g1, xs8, red8, bp.xa, false);
+                stage_norm8(bp, bp.xa, bp.ssq, y->g1, xs8, nullptr, false);
         } else if (kind == kWo) {
             if (!stage_copy8(p, bp.att, p.Hl, xs8, copy_bar, copy_par)) ok = false;
         } else if (kind == kW13) {
-            stage_norm8(bp, bp.xa, y->bo, bp.cres, nb_wo, y->g2, xs8, red8, bp.xb, false);
+            stage_norm8(bp, bp.xb, bp.ssq, y->g2, xs8, nullptr, false);
         } else if (kind == kW2) {
             if (!stage_copy8(p, bp.ffh, p.Fl, xs8, copy_bar, copy_par)) ok = false;
         } else {  // kLM
-            stage_norm8(bp, bp.xb, p.layer[l - 1].b2, bp.cres, nb_w2, p.gnorm, xs8, red8, bp.xa, false);
+            stage_norm8(bp, bp.xa, bp.ssq, p.gnorm, xs8, nullptr, false);
         }
         consumer_sync();
         if (t == 0) *quiet = 0;
@@ -1635,6 +1661,11 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
                         const int c = persist_contrib_slot(blockIdx.x, g, bi0, r.nb, r.T, G);
                         bp.cres[my_b * cstride + (static_cast<size_t>(g) * kPersistMaxContrib + c) * kPersistTileRows +
                                 my_r] = sum;
+                        const bool w2 = kind == kW2;
+                        int* tk = bp.tickets + ((static_cast<size_t>(w2) * p.layers + l) * (p.H / kPersistTileRows) + g) * 4 +
+                                  quad;
+                        finish_quad(bp, tk, persist_group_contrib(g, r.nb, r.T, G), g, quad, my_r, my_b,
+                                    w2 ? bp.xb : bp.xa, w2 ? y->b2 : y->bo, w2 ? bp.xa : bp.xb, bp.ssq);
                         break;
                     }
                     case kW13: {

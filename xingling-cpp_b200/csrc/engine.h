@@ -245,8 +245,10 @@ class BatchDecoder {
     float *x_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *ffh_ = nullptr, *logits_ = nullptr;
     // batched persistent kernel: second residual stream [kBatch][H], partial row sums
     // [kBatch][H/16][kPersistMaxContrib][16], attention partials, phase counters + merge tickets
-    float *xb_ = nullptr, *cres_ = nullptr, *part_ = nullptr;
-    int* done_ = nullptr;
+    float *xb_ = nullptr, *cres_ = nullptr, *part_ = nullptr, *ssq_ = nullptr;
+    int *done_ = nullptr, *tick_ = nullptr;
+    // residual-finishing tickets [2][layers][H/16][4] of the split projections
+    size_t tick_words() const { return 2 * static_cast<size_t>(eng_->cfg_.layers) * (eng_->H_ / kPersistTileRows) * 4; }
     size_t done_words() const {
         return 5 * static_cast<size_t>(eng_->cfg_.layers) + 1 +
                static_cast<size_t>(eng_->cfg_.layers) * kBatch * eng_->heads_l_;
