@@ -1369,7 +1369,7 @@ __device__ __forceinline__ void pair_sync(int slot) {
     asm volatile("bar.sync %0, 64;" ::"r"(2 + slot) : "memory");
 }
 
-__device__ bool attention_batch(const BatchPersistParams& bp, int layer, int ph, float* xs, int* s_ok) {
+__device__ __noinline__ bool attention_batch(const BatchPersistParams& bp, int layer, int ph, float* xs, int* s_ok) {
     const PersistentParams& p = bp.base;
     const int t = threadIdx.x - 32;
     const int warp = t >> 5, lane = t & 31;
@@ -1425,11 +1425,17 @@ __device__ bool attention_batch(const BatchPersistParams& bp, int layer, int ph,
             const int posk = t0 + kp;
             const int cached = min(kPersistChunk, n - t0);
             const bool has_n = n >= t0 && n < t0 + kPersistChunk;
+            // the chunk's cached K and V rows, all loads issued together (one memory round trip)
             float4 kv[8];
+            float2 vrow[kPersistChunk];
             const float4* kr =
                 reinterpret_cast<const float4*>(kc + static_cast<size_t>(kp < cached ? posk : 0) * kHeadDim) + 8 * kh;
 #pragma unroll
             for (int i = 0; i < 8; ++i) kv[i] = kp < cached ? __ldcg(kr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const float2* vr = reinterpret_cast<const float2*>(vc + static_cast<size_t>(t0) * kHeadDim) + lane;
+#pragma unroll
+            for (int jp = 0; jp < kPersistChunk; ++jp)
+                vrow[jp] = jp < cached ? __ldcg(vr + jp * (kHeadDim / 2)) : make_float2(0.0f, 0.0f);
             float2 vnew = make_float2(0.0f, 0.0f);
             if (has_n) {
                 const float* kn = qkv + p.Hl + h * kHeadDim;
@@ -1458,13 +1464,11 @@ __device__ bool attention_batch(const BatchPersistParams& bp, int layer, int ph,
             const float m = warp_max(sc);
             const float e = mine ? expf(sc - m) : 0.0f;
             const float l = warp_sum(kh == 0 ? e : 0.0f);
-            const float2* vr = reinterpret_cast<const float2*>(vc + static_cast<size_t>(t0) * kHeadDim) + lane;
             float2 o = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int jp = 0; jp < kPersistChunk; ++jp) {
                 const float ej = __shfl_sync(0xffffffffu, e, 2 * jp);
-                const float2 v = t0 + jp == n ? vnew : (jp < cached ? __ldcg(vr + jp * (kHeadDim / 2))
-                                                                    : make_float2(0.0f, 0.0f));
+                const float2 v = t0 + jp == n ? vnew : vrow[jp];
                 o.x = fmaf(ej, v.x, o.x);
                 o.y = fmaf(ej, v.y, o.y);
             }
