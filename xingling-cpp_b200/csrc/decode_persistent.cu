@@ -1190,7 +1190,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
 constexpr int kSlotsB = 3;
 constexpr size_t kSmemBytesB = static_cast<size_t>(kSlotsB) * kSlotBytes +
                                static_cast<size_t>(kBatch) * kBatchPersistMaxK * 4 + 2 * kSlotsB * 8 +
-                               128 * 4 + kBatch * kConsumerWarps * 8 + 64;
+                               256 * 4 + kBatch * kConsumerWarps * 8 + 64;
 static_assert(kSmemBytesB <= kMaxSmemPerBlock, "batched persistent kernel fits in 227 KB of shared memory");
 static_assert(4 * kBatch == 32, "one (row, sequence) sum per lane of a row quad");
 static_assert(kConsumerWarps == kBatch, "the RMSNorm staging gives each sequence one warp");
@@ -1256,7 +1256,7 @@ __device__ __noinline__ void stage_norm8(const BatchPersistParams& bp, const flo
     float ss = 0.0f;
     if (!gather)
         for (int i = lane; i < K4; i += 32) ss += __ldcg(ssq + static_cast<size_t>(b) * K4 + i);
-    constexpr int kU = 4;  // quads of a lane whose loads are issued together
+    constexpr int kU = 6;  // quads of a lane whose loads are issued together (two batches at H = 1536)
     for (int q0 = lane; q0 < K4; q0 += 32 * kU) {
         float4 v[kU];
 #pragma unroll
@@ -1600,7 +1600,7 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
         const int r0 = 4 * quad;
         const int my_r = r0 + (lane >> 3), my_b = lane & 7;
         const float my_rp = bp.st[my_b].in.rp;
-        float* xch = red8 + quad * 32;  // [4 quads][32 lanes]
+        int xbuf = 0;  // hand-over buffer of the current group: [2][4 quads][32 lanes], alternating
         for (int tau = r.t0; tau < r.t1;) {
             const int g = tau / r.nb;
             const int bi0 = tau % r.nb, bi1 = min(r.nb, bi0 + (r.t1 - tau));
@@ -1652,6 +1652,10 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
             }
             tau += bi1 - bi0;
             float sum = reduce_scatter32(acc);  // lane l: row r0 + l / 8, sequence l % 8, this half of K
+            // Two buffers: the upper warp writes group i + 2's sums only after the barrier of group i + 1, which
+            // the lower warp reaches after reading group i's.
+            float* xch = red8 + (xbuf * 4 + quad) * 32;
+            xbuf ^= 1;
             if (khalf == 1) xch[lane] = sum;
             pair_sync(4 + quad);  // warps quad and quad + 4
             if (khalf == 0) {
@@ -1689,7 +1693,6 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
                     }
                 }
             }
-            pair_sync(4 + quad);  // xch is reused by the next group
         }
         if (kind != kLM) {
             consumer_sync();  // every warp's stores of the phase, then one release per CTA
@@ -1741,8 +1744,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_batch_persistent_kernel(co
     float* xs8 = reinterpret_cast<float*>(smem + static_cast<size_t>(kSlotsB) * kSlotBytes);
     uint64_t* full = reinterpret_cast<uint64_t*>(xs8 + static_cast<size_t>(kBatch) * kBatchPersistMaxK);
     uint64_t* empty = full + kSlotsB;
-    float* red8 = reinterpret_cast<float*>(empty + kSlotsB);  // [4 row quads][32]: K-half hand-over
-    unsigned long long* best8 = reinterpret_cast<unsigned long long*>(red8 + 128);  // [8 warps][kBatch]
+    float* red8 = reinterpret_cast<float*>(empty + kSlotsB);  // [2][4 row quads][32]: K-half hand-over
+    unsigned long long* best8 = reinterpret_cast<unsigned long long*>(red8 + 256);  // [8 warps][kBatch]
     int* s_ok = reinterpret_cast<int*>(best8 + kBatch * kConsumerWarps);
     volatile int* quiet = s_ok + 8;
     uint64_t* copy_bar = reinterpret_cast<uint64_t*>(s_ok + 12);  // 8-byte aligned: s_ok is
