@@ -187,6 +187,9 @@ XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, fl
  *                    own duration;
  *   "prefill_gemm" 0  prefill projections on tcgen05 with the 3xTF32 split
  *                     (default); 1  fp32 FMA tiles.
+ *   "batch_persistent" 1  a batch decoder created afterwards runs each step
+ *                    as one batched persistent kernel (default, where the
+ *                    shape fits it); 0  per-op batched kernels;
  *   "prefill_attn" 0  prefill attention on tcgen05 with the 3xTF32 split:
  *                     S = q k^T per head, causal row softmax, P v (default);
  *                  1  fp32 FMA flash-style tiles with online softmax.

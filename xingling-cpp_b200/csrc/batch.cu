@@ -497,7 +497,6 @@ int BatchDecoder::init() {
     add(&part_, kBatch * heads * static_cast<size_t>(persistent_max_splits(E.T_)) * (kHeadDim + 2) * 4);
     add(&done_, done_words() * 4);
     add(&tick_, tick_words() * 4);
-    add(&ssq_, kBatch * (H / 4) * 4);
     add(&qkv_, kBatch * 3 * Hl * 4);
     add(&att_, kBatch * Hl * 4);
     add(&ffh_, kBatch * Fl * 4);
@@ -583,7 +582,6 @@ int BatchDecoder::enqueue_persistent(cudaStream_t s, bool sampled) {
     bp.xb = xb_;
     bp.cres = cres_;
     bp.tickets = tick_;
-    bp.ssq = ssq_;
     bp.qkv = qkv_;
     bp.att = att_;
     bp.ffh = ffh_;

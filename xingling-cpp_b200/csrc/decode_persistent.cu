@@ -1238,26 +1238,27 @@ __device__ bool wait_count(const PersistentParams& p, int ph, int target, int* s
 }
 
 // xs8[b] = rmsnorm(x_b) * gamma for every sequence b (src/rmsnorm.cu:99-101).
-// Either x_b is the embedding row of b's input id (gather: this CTA also
-// stores its slice of x_b to x_out), or it is the residual the previous split
-// projection finished (x_fin, with ssq its sums of squares per 4-row quad).
-// Warp w stages sequence w alone: its lanes load four quads of the vector at a
-// time (one L2 round trip per four) and reduce the sum of squares in the warp.
-__device__ __noinline__ void stage_norm8(const BatchPersistParams& bp, const float* x_fin, const float* ssq,
-                                         const float* gamma, float* xs8, float* x_out, bool gather) {
+// Either x_b is the embedding row of b's input id (gather: loaded here, six
+// quads of a lane per L2 round trip; this CTA also stores its slice of x_b to
+// x_out), or it is the residual the previous split projection finished,
+// already copied into xs8 by stage_copy8.  Warp w normalises sequence w alone
+// (sum of squares reduced in the warp); the gains were prefetched into L1
+// before the phase's wait.
+__device__ __noinline__ void stage_norm8(const BatchPersistParams& bp, const float* gamma, float* xs8, float* x_out,
+                                         bool gather) {
     const PersistentParams& p = bp.base;
     const int t = threadIdx.x - 32;
     const int b = t >> 5, lane = t & 31;  // kConsumerWarps == kBatch
     const int K = p.H, K4 = K >> 2;
     const int s0 = static_cast<int>(blockIdx.x) * K / static_cast<int>(gridDim.x);
     const int s1 = static_cast<int>(blockIdx.x + 1) * K / static_cast<int>(gridDim.x);
-    const float* src = gather ? p.emb + static_cast<size_t>(bp.st[b].in.token_in) * K : x_fin + static_cast<size_t>(b) * K;
     float4* x4 = reinterpret_cast<float4*>(xs8 + static_cast<size_t>(b) * kBatchPersistMaxK);
     float ss = 0.0f;
     if (!gather)
-        for (int i = lane; i < K4; i += 32) ss += __ldcg(ssq + static_cast<size_t>(b) * K4 + i);
+        for (int q = lane; q < K4; q += 32) ss = dot4(x4[q], x4[q], ss);
+    const float* src = gather ? p.emb + static_cast<size_t>(bp.st[b].in.token_in) * K : nullptr;
     constexpr int kU = 6;  // quads of a lane whose loads are issued together (two batches at H = 1536)
-    for (int q0 = lane; q0 < K4; q0 += 32 * kU) {
+    for (int q0 = lane; gather && q0 < K4; q0 += 32 * kU) {
         float4 v[kU];
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
@@ -1283,7 +1284,7 @@ __device__ __noinline__ void stage_norm8(const BatchPersistParams& bp, const flo
     const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(tot / static_cast<float>(K)) + 1e-6));
     const float4* g4 = reinterpret_cast<const float4*>(gamma);
     for (int q = lane; q < K4; q += 32) {
-        const float4 g = g4[q];
+        const float4 g = __ldg(g4 + q);
         float4 v = x4[q];
         v.x = v.x * inv * g.x;
         v.y = v.y * inv * g.y;
@@ -1297,11 +1298,10 @@ __device__ __noinline__ void stage_norm8(const BatchPersistParams& bp, const flo
 // contributor's lower-half warp for row quad `quad` stores its partial sums,
 // then takes a ticket; the last one finishes the quad's rows for every
 // sequence: x_new = x_old + (partials in CTA order + bias), as the
-// single-sequence staging forms it, stored to x_out, with the quad's sum of
-// squares per sequence stored to ssq.  Lane l holds row r0 + l / 8 of
-// sequence l % 8.  The tickets are zeroed before each launch.
-__device__ void finish_quad(const BatchPersistParams& bp, int* ticket, int nc, int g, int quad, int my_r, int my_b,
-                            const float* x_old, const float* bias, float* x_out, float* ssq) {
+// single-sequence staging forms it, stored to x_out.  Lane l holds row
+// r0 + l / 8 of sequence l % 8.  The tickets are zeroed before each launch.
+__device__ void finish_quad(const BatchPersistParams& bp, int* ticket, int nc, int g, int my_r, int my_b,
+                            const float* x_old, const float* bias, float* x_out) {
     const PersistentParams& p = bp.base;
     const int lane = threadIdx.x & 31;
     const size_t cstride = static_cast<size_t>(p.H / kPersistTileRows) * kPersistMaxContrib * kPersistTileRows;
@@ -1318,10 +1318,6 @@ __device__ void finish_quad(const BatchPersistParams& bp, int* ticket, int nc, i
     const int R = g * kPersistTileRows + my_r;
     const float x = __ldcg(x_old + static_cast<size_t>(my_b) * p.H + R) + (sp + bias[R]);
     x_out[static_cast<size_t>(my_b) * p.H + R] = x;
-    float q2 = x * x;  // the quad's four rows of this sequence: lanes l, l + 8, l + 16, l + 24
-    q2 += __shfl_xor_sync(0xffffffffu, q2, 8);
-    q2 += __shfl_xor_sync(0xffffffffu, q2, 16);
-    if (lane < kBatch) ssq[static_cast<size_t>(my_b) * (p.H >> 2) + g * 4 + quad] = q2;
 }
 
 // xs8[b] = src_b[0, K) for every sequence b (src_b = src + b * K), by bulk
@@ -1569,25 +1565,27 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
         const Gemv d = gemv_of(p, ph);
         const Boxes r = boxes_of(d);
         if (ph > 0) {
+            if (kind == kQKV || kind == kW13 || kind == kLM) {  // the staging's gains into L1 during the wait
+                const float* gm = kind == kQKV ? y->g1 : kind == kW13 ? y->g2 : p.gnorm;
+                for (int i = t; i < (p.H >> 5); i += kConsumerWarps * 32)
+                    asm volatile("prefetch.global.L1 [%0];" ::"l"(gm + 32 * i));
+            }
             // the attention phase is signalled once per (sequence, head) item; the others once per CTA
             const int target = phase_kind(ph - 1, p.layers) == kAttn ? kBatch * p.heads : G;
             if (!wait_count(p, ph - 1, target, s_ok)) return;
         }
         if (t == 0) trace_at(p, ph, kTrConsStart);
         // The residual streams: the W2 phase finishes xa (from xb), the out-projection finishes xb (from xa).
-        if (kind == kQKV) {
-            if (l == 0)
-                stage_norm8(bp, nullptr, nullptr, y->g1, xs8, bp.xa, true);
-            else
-                stage_norm8(bp, bp.xa, bp.ssq, y->g1, xs8, nullptr, false);
+        if (kind == kQKV && l == 0) {
+            stage_norm8(bp, y->g1, xs8, bp.xa, true);
         } else if (kind == kWo) {
             if (!stage_copy8(p, bp.att, p.Hl, xs8, copy_bar, copy_par)) ok = false;
-        } else if (kind == kW13) {
-            stage_norm8(bp, bp.xb, bp.ssq, y->g2, xs8, nullptr, false);
         } else if (kind == kW2) {
             if (!stage_copy8(p, bp.ffh, p.Fl, xs8, copy_bar, copy_par)) ok = false;
-        } else {  // kLM
-            stage_norm8(bp, bp.xa, bp.ssq, p.gnorm, xs8, nullptr, false);
+        } else {  // QKV (layers past the first), W1/V, LM head: the finished residual copied in, then normalised
+            const bool xa = kind != kW13;
+            if (!stage_copy8(p, xa ? bp.xa : bp.xb, p.H, xs8, copy_bar, copy_par)) ok = false;
+            else stage_norm8(bp, kind == kQKV ? y->g1 : kind == kW13 ? y->g2 : p.gnorm, xs8, nullptr, false);
         }
         consumer_sync();
         if (t == 0) *quiet = 0;
@@ -1672,8 +1670,8 @@ __device__ void consumers_batch(const BatchPersistParams& bp, char* ring, float*
                         const bool w2 = kind == kW2;
                         int* tk = bp.tickets + ((static_cast<size_t>(w2) * p.layers + l) * (p.H / kPersistTileRows) + g) * 4 +
                                   quad;
-                        finish_quad(bp, tk, persist_group_contrib(g, r.nb, r.T, G), g, quad, my_r, my_b,
-                                    w2 ? bp.xb : bp.xa, w2 ? y->b2 : y->bo, w2 ? bp.xa : bp.xb, bp.ssq);
+                        finish_quad(bp, tk, persist_group_contrib(g, r.nb, r.T, G), g, my_r, my_b,
+                                    w2 ? bp.xb : bp.xa, w2 ? y->b2 : y->bo, w2 ? bp.xa : bp.xb);
                         break;
                     }
                     case kW13: {

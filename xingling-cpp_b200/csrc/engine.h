@@ -188,9 +188,9 @@ class Engine {
     int tag_split_ = -1;
     int tp_merge_ = 1;         // tensor parallel, greedy: the ranks' argmax keys merged inside the persistent kernel
     int tag_skew_ = 0;         // test hook: shift of the tag the tagged exchange's stagings wait for
-    // BatchDecoder: 1 = the batched persistent kernel (one launch per step), 0 = per-op kernels (faster today:
-    // 1.35 against ~2 ms per 8-token step on the replica workload; the batched kernel's stagings serialise)
-    int batch_persistent_ = 0;
+    // BatchDecoder: 1 = the batched persistent kernel (one launch per step; 1.37 against 1.43 ms per greedy
+    // 8-token step of the replica workload's prompts), 0 = per-op kernels
+    int batch_persistent_ = 1;
     // Persistent kernel counters, zeroed before each launch: phase counters
     // [5*layers + 1], then the attention merge tickets [layers][heads].
     size_t done_words() const {
@@ -245,7 +245,7 @@ class BatchDecoder {
     float *x_ = nullptr, *qkv_ = nullptr, *att_ = nullptr, *ffh_ = nullptr, *logits_ = nullptr;
     // batched persistent kernel: second residual stream [kBatch][H], partial row sums
     // [kBatch][H/16][kPersistMaxContrib][16], attention partials, phase counters + merge tickets
-    float *xb_ = nullptr, *cres_ = nullptr, *part_ = nullptr, *ssq_ = nullptr;
+    float *xb_ = nullptr, *cres_ = nullptr, *part_ = nullptr;
     int *done_ = nullptr, *tick_ = nullptr;
     // residual-finishing tickets [2][layers][H/16][4] of the split projections
     size_t tick_words() const { return 2 * static_cast<size_t>(eng_->cfg_.layers) * (eng_->H_ / kPersistTileRows) * 4; }

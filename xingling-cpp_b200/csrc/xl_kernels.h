@@ -204,7 +204,6 @@ struct BatchPersistParams {
     float* xb;               // [kBatch][H] after the out-projection
     float* cres;             // [kBatch][H/16][kPersistMaxContrib][16] partial row sums of out-proj / W2
     int* tickets;            // [2][layers][H/16][4] per (projection, layer, group, row quad); zeroed before each launch
-    float* ssq;              // [kBatch][H/4] sums of squares of the finished residual per 4-row quad
     float* qkv;              // [kBatch][3*Hl]
     float* att;              // [kBatch][Hl]
     float* ffh;              // [kBatch][Fl]
