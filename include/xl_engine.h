@@ -190,9 +190,12 @@ XL_API int xl_engine_kv_copy(xl_engine* e, int layer, int npos, float* k_out, fl
  *   "batch_persistent" 1  a batch decoder created afterwards runs each step
  *                    as one batched persistent kernel (default, where the
  *                    shape fits it); 0  per-op batched kernels;
- *   "prefill_attn" 0  prefill attention on tcgen05 with the 3xTF32 split:
- *                     S = q k^T per head, causal row softmax, P v (default);
- *                  1  fp32 FMA flash-style tiles with online softmax.
+ *   "prefill_attn" 0  prefill attention in one tcgen05 kernel per layer
+ *                     (3xTF32, flash-style: scores in TMEM, online softmax,
+ *                     P in shared memory; the default);
+ *                  1  fp32 FMA flash-style tiles with online softmax;
+ *                  2  tcgen05 in three kernels: S = q k^T per head, causal
+ *                     row softmax, P v.
  * Changing an option re-captures the decode graph. */
 XL_API int xl_engine_set_option(xl_engine* e, const char* key, int value);
 /* The last decode step's phase timeline: n = SMs x (5 x layers + 1) x 5

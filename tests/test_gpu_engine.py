@@ -319,7 +319,7 @@ def test_full_generate_prompt32_matches_oracle(eng_mod, full_weights):
 
 def test_full_prefill_512(eng_mod, full_weights):
     """Prefill-only workload: XingLing-0.68B, 512 uniform ids (seed 1), the
-    default tensor-core path (3xTF32 tcgen05 projections and attention).
+    default tensor-core path (3xTF32 tcgen05 projections, the fused attention).
     The last row's logits within 1e-3 of their range of the oracle's, the
     greedy id equal except at a near-tie, and the KV cache of the first and
     last layers within 1e-4 of the largest cached value (src/transformer.cu:163-178,
@@ -342,6 +342,54 @@ def test_full_prefill_512(eng_mod, full_weights):
         kr, vr = port.kv(layer, 512)
         # relative to the largest cached value: the 3xTF32 products' rounding
         # grows through the layers (1.8e-4 absolute at layer 15)
+        ek = float(np.abs(k - kr).max() / np.abs(kr).max())
+        ev = float(np.abs(v - vr).max() / np.abs(vr).max())
+        assert ek < 1e-4 and ev < 1e-4, f"layer {layer}: KV max err {ek:.2e} / {ev:.2e} of the largest value"
+
+
+ATTN_CASES = [("TINY", n) for n in (1, 63, 64, 65, 127, 128, 129, 255, 300, 767, 768)] + \
+             [("WIDE2", n) for n in (129, 512, 768)]
+
+
+@pytest.fixture(scope="module")
+def attn_rigs(eng_mod):
+    """One engine and one oracle port per shape, and the oracle's prefill of each case."""
+    rigs = {}
+    for name in ("TINY", "WIDE2"):
+        sh = getattr(S, name)
+        wdir = S.write_weight_tree(f"/tmp/xl_weights/{name.lower()}", sh)
+        eng = make_engine(eng_mod, 0, **sh.engine_kwargs())
+        eng.load(wdir)
+        port = O.Port(sh)
+        port.load(wdir)
+        rigs[name] = (sh, eng, port, {})
+    return rigs
+
+
+@pytest.mark.parametrize("attn", [0, 2], ids=["fused", "three_kernels"])
+@pytest.mark.parametrize("shape_name,n", ATTN_CASES, ids=[f"{a.lower()}-{n}" for a, n in ATTN_CASES])
+def test_prefill_attention_tc_lengths(attn_rigs, shape_name, n, attn):
+    """The tcgen05 prefill attention paths (option prefill_attn 0: one fused
+    flash-style kernel; 2: S GEMM, softmax, P.V GEMM) at prompt lengths on
+    both sides of the 64-key and 128-query tile edges up to the 768-position
+    limit, on 4 heads (tiny) and 24 full-width heads: the last row's logits
+    within 1e-3 of the oracle's range and every layer's KV cache within 1e-4
+    of its largest value (src/attn.cu:47-167, src/transformer.cu:163-178)."""
+    sh, eng, port, refs = attn_rigs[shape_name]
+    ids = S.prompt_ids(20 + n, n, sh.vocab)
+    if n not in refs:
+        ref = port.prefill(ids)
+        refs[n] = (ref, [port.kv(layer, n) for layer in range(sh.layers)])
+    ref, kvs = refs[n]
+    eng.set_option("prefill_attn", attn)
+    tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
+    assert_logits_close(logits_of(eng), ref)
+    check_token(tok, int(np.argmax(ref)), ref)
+    for layer in range(sh.layers):
+        kb, vb = eng.kv(layer, n, sh.heads)
+        k = np.frombuffer(kb, np.float32).reshape(-1, sh.heads, 64)
+        v = np.frombuffer(vb, np.float32).reshape(-1, sh.heads, 64)
+        kr, vr = kvs[layer]
         ek = float(np.abs(k - kr).max() / np.abs(kr).max())
         ev = float(np.abs(v - vr).max() / np.abs(vr).max())
         assert ek < 1e-4 and ev < 1e-4, f"layer {layer}: KV max err {ek:.2e} / {ev:.2e} of the largest value"

@@ -359,8 +359,9 @@ int Engine::alloc_all() {
     add(&ak_lo_, T * Hl * 4);
     add(&avt_, T * Hl * 4);
     add(&avt_lo_, T * Hl * 4);
-    add(&ap_, static_cast<size_t>(heads_l_) * T * T * 4);
+    add(&ap_, static_cast<size_t>(heads_l_) * T * T * 4);  // S / P, or the fused kernel's split rows
     add(&ap_lo_, static_cast<size_t>(heads_l_) * T * T * 4);
+    add(&fa_tickets_, static_cast<size_t>(heads_l_) * ((T + 127) / 128) * 4 * 4);
     size_t total = 0;
     for (auto& pr : plan) total += align_up(pr.second, 256);
     XL_CUDA(cudaMalloc(reinterpret_cast<void**>(&arena_), total));
@@ -663,6 +664,12 @@ int Engine::prepare_prefill_operands() {
         XL_CUDA(make_tile_map(&tc_attn_pv_.x_lo, ap_lo_, heads_l_ * T_, T_));
         XL_CUDA(make_tile_map(&tc_attn_pv_.w, avt_, heads_l_ * kHeadDim, T_));
         XL_CUDA(make_tile_map(&tc_attn_pv_.w_lo, avt_lo_, heads_l_ * kHeadDim, T_));
+        XL_CUDA(make_tile_map(&flash_.q, aq_, T_, Hl_));
+        XL_CUDA(make_tile_map(&flash_.q_lo, aq_lo_, T_, Hl_));
+        XL_CUDA(make_tile_map(&flash_.k, ak_, heads_l_ * T_, kHeadDim, 64));
+        XL_CUDA(make_tile_map(&flash_.k_lo, ak_lo_, heads_l_ * T_, kHeadDim, 64));
+        XL_CUDA(make_tile_map(&flash_.v, avt_, heads_l_ * kHeadDim, T_, 64));
+        XL_CUDA(make_tile_map(&flash_.v_lo, avt_lo_, heads_l_ * kHeadDim, T_, 64));
     }
     XL_CUDA(cudaStreamSynchronize(stream_));
     return XL_OK;
@@ -1199,6 +1206,8 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
     XL_CUDA(cudaMemcpyAsync(st_, hs, offsetof(DevState, pos) + sizeof(int), cudaMemcpyHostToDevice, s));
     // A new prompt clears the repetition set (src/inference.cu:116-136); an appended one keeps it.
     if (!append) XL_CUDA(cudaMemsetAsync(rep_flags_, 0, vl_, s));
+    // the fused attention's merge tickets (left zero by every complete launch; reset after a failed one)
+    XL_CUDA(cudaMemsetAsync(fa_tickets_, 0, static_cast<size_t>(heads_l_) * ((T_ + 127) / 128) * 4 * 4, s));
     XL_CUDA(cudaEventRecord(ev0_, s));
 
     const size_t H = H_;
@@ -1209,12 +1218,17 @@ int Engine::prefill(const int* ids, int n, float temperature, float top_p, float
         XL_CUDA(launch_rmsnorm_rows(px_, L.g1, pxn_, pxn_lo_, n, H_, s));
         rc = prefill_linear(kGemvPlain, L.tc_qkv, pxn_, L.wqkv, L.bqkv, pqkv_, nullptr, n, 3 * Hl_, H_, s);
         if (rc != XL_OK) break;
-        if (prefill_attn_ == 0 && T_ % 32 == 0 && p0 == 0) {
+        if (prefill_attn_ != 1 && T_ % 32 == 0 && p0 == 0) {
             XL_CUDA(launch_attn_prep(pqkv_, rope_, L.kc, L.vc, aq_, aq_lo_, ak_, ak_lo_, avt_, avt_lo_, n, heads_l_, T_,
                                      s));
-            XL_CUDA(launch_attn_scores_tc(tc_attn_s_, ap_, n, heads_l_, T_, &st_->err, s));
-            XL_CUDA(launch_attn_softmax(ap_, ap_lo_, n, heads_l_, T_, s));
-            XL_CUDA(launch_attn_pv_tc(tc_attn_pv_, patt_, patt_lo_, n, heads_l_, T_, &st_->err, s));
+            if (prefill_attn_ == 0) {
+                XL_CUDA(launch_attn_flash_tc(flash_, patt_, patt_lo_, n, heads_l_, T_, ap_,
+                                             static_cast<size_t>(heads_l_) * T_ * T_, fa_tickets_, &st_->err, s));
+            } else {
+                XL_CUDA(launch_attn_scores_tc(tc_attn_s_, ap_, n, heads_l_, T_, &st_->err, s));
+                XL_CUDA(launch_attn_softmax(ap_, ap_lo_, n, heads_l_, T_, s));
+                XL_CUDA(launch_attn_pv_tc(tc_attn_pv_, patt_, patt_lo_, n, heads_l_, T_, &st_->err, s));
+            }
         } else {
             XL_CUDA(launch_rope_kv_prefill(pqkv_, rope_, L.kc, L.vc, n, heads_l_, T_, s, p0));
             XL_CUDA(launch_attn_prefill(pqkv_, L.kc, L.vc, patt_, patt_lo_, n, heads_l_, T_, s, p0));
@@ -1427,8 +1441,8 @@ int Engine::set_option(const char* key, int value) {
         return XL_OK;
     }
     if (k == "prefill_attn") {
-        if (value != 0 && value != 1) {
-            set_error("prefill_attn must be 0 (tcgen05 3xTF32) or 1 (fp32 FMA tiles)");
+        if (value < 0 || value > 2) {
+            set_error("prefill_attn must be 0 (fused tcgen05), 1 (fp32 FMA tiles) or 2 (tcgen05 S, softmax, P.V)");
             return XL_ERR_ARG;
         }
         prefill_attn_ = value;

@@ -171,11 +171,14 @@ class Engine {
 
     int decode_path_ = 0;      // 0: persistent kernel (where it fits), 1: per-op kernels
     int prefill_gemm_ = 0;     // 0: tcgen05 3xTF32, 1: fp32 SIMT tiles
-    int prefill_attn_ = 0;     // 0: tcgen05 3xTF32 (S GEMM, softmax, PV GEMM), 1: fp32 FMA flash tiles
+    int prefill_attn_ = 0;     // 0: one fused tcgen05 kernel (flash-style), 1: fp32 FMA flash tiles,
+                               // 2: tcgen05 S GEMM, softmax, P.V GEMM (all 3xTF32)
     // tensor-core prefill attention: q/8 [T][Hl], k [heads][T][64], v^T [heads*64][T], S/P [heads][T][T]
     float *aq_ = nullptr, *aq_lo_ = nullptr, *ak_ = nullptr, *ak_lo_ = nullptr, *avt_ = nullptr, *avt_lo_ = nullptr;
     float *ap_ = nullptr, *ap_lo_ = nullptr;
+    int* fa_tickets_ = nullptr;  // the fused prefill attention's merge tickets [heads][T / 128][4]
     TcOperands tc_attn_s_{}, tc_attn_pv_{};
+    FlashOperands flash_{};  // TMA maps of the fused prefill attention's operands
     long long decode_graph_kernels_ = 0;  // kernels recorded in the decode graph
     int load_threads_ = 4;      // weight loader worker threads
     float last_load_s_ = 0.0f;  // wall time of the last load's file reads and copies

@@ -369,13 +369,14 @@ EncodeTiledFn encode_fn() {
 size_t gemm_tc_smem_bytes() { return kGemmSmem; }
 
 // Row-major [rows][cols] fp32 matrix as a 2D TMA map with {32, 128} boxes, 128B swizzle.
-cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int cols) {
+cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int cols, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
-    if (reinterpret_cast<uintptr_t>(base) % 16 || (cols * 4) % 16) return cudaErrorInvalidValue;
+    if (reinterpret_cast<uintptr_t>(base) % 16 || (cols * 4) % 16 || box_rows <= 0 || box_rows > 256)
+        return cudaErrorInvalidValue;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
-    const cuuint32_t box[2] = {kBK, kBM};
+    const cuuint32_t box[2] = {kBK, static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t elem[2] = {1, 1};
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, elem,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -400,6 +401,384 @@ cudaError_t make_stream_map(CUtensorMap* map, const float* base, int rows, int c
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// ---- Causal prefill attention in one kernel (flash-style, tcgen05, 3xTF32) ----
+//
+// The causal MultiHeadAttention::prefill of src/attn.cu:47-167 for one head
+// and 128 queries per CTA, with the scores and probabilities kept on chip:
+// for each tile of 64 keys, S = (q/8) k^T goes to TMEM, the four softmax
+// warps (one thread per query row) read their row of S, update the row's
+// running maximum and sum (online softmax), write P = exp(s - max) and its
+// TF32 lo half into shared memory as the A operand of the next MMA, and fold
+// the previous tile's P.V from TMEM into the row's output held in registers,
+// rescaled by exp(old max - new max).  The output row is divided by the sum
+// at the end and stored with its lo half (the out-projection's operands).
+//   warp 0: TMA producer (lane 0: q, then the k tiles through one stage,
+//           loaded while the previous tile's scores are consumed; lane 1:
+//           the v^T tiles through two stages);
+//   warp 1: one thread issues the MMAs, S one tile ahead of P.V; S and P.V
+//           each have two TMEM slots of 64 columns;
+// A 128-query tile with more than kFaSplit key tiles is cut into balanced runs
+// of at most kFaSplit, one CTA each (so that the longest CTA is short and the
+// grid covers the SMs); each run stores its rows' (output, max, sum) to a
+// workspace and the warp that takes the last ticket of its 32 rows merges
+// them (src/attn.cu's online softmax across runs).
+//   warps 2..5: softmax and output, TMEM lane quarter warp % 4; each thread
+//           writes its row of P and signals before it folds the previous
+//           tile's P.V, so that the next P.V MMA starts meanwhile.
+// Products use the 3xTF32 split of the projections (hi.hi + hi.lo + lo.hi).
+// Keys past a row's query get probability 0; key tiles past the CTA's last
+// query are not visited.  Operands come from attn_prep_kernel: q/8 [T][heads
+// * 64], k [heads * T][64], v^T [heads * 64][T], each with its lo half.
+constexpr int kFaKeys = 64;                        // keys per tile: the scores' MMA N
+constexpr int kFaQTile = kBM * kBK * 4;            // 16 KB: 128 rows x 32 floats
+constexpr int kFaKTile = kFaKeys * kBK * 4;        // 8 KB: 64 rows x 32 floats
+constexpr int kFaQBytes = 4 * kFaQTile;            // q and q_lo, two 32-float K-blocks each
+constexpr int kFaKStage = 4 * kFaKTile;            // k and k_lo of one tile
+constexpr int kFaVBytes = 4 * kFaKTile;            // v^T and its lo half of one tile
+constexpr int kFaPBytes = 4 * kFaQTile;            // P and P_lo of one tile
+constexpr int kFaOffK = kFaQBytes;
+constexpr int kFaOffV = kFaOffK + kFaKStage;
+constexpr int kFaVStages = 2;
+constexpr int kFaOffP = kFaOffV + kFaVStages * kFaVBytes;
+constexpr int kFaOffBar = kFaOffP + kFaPBytes;
+constexpr size_t kFaSmem = static_cast<size_t>(kFaOffBar) + 256 + 1024;
+constexpr int kFaThreads = 6 * 32;                 // producer, MMA issuer, four softmax warps
+constexpr int kFaSplit = 4;                        // key tiles per CTA at most (longer rows split over CTAs)
+constexpr int kFaPart = kHeadDim + 4;              // a run's partial row in the workspace: output, max, sum
+constexpr uint32_t kFaTmemCols = 256;              // S slots at 0 and 64, P.V slots at 128 and 192
+// kind::tf32, fp32 accumulate, K-major A and B, M = 128, N = 64
+constexpr uint32_t kIdescN64 = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(kFaKeys >> 3) << 17) |
+                               (static_cast<uint32_t>(kBM >> 4) << 24);
+static_assert(kFaSmem <= 232448, "fused attention shared memory");
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ void mma_tf32_n64(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(kIdescN64), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// 32 consecutive TMEM columns of the warp's lane quarter (one row per thread).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
+        "[%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 3 x 4 K-steps x 2 K-blocks of 32 floats: D (=|+=) A . B^T over 64 columns of K.
+__device__ __forceinline__ void mma_3xtf32_k64(uint32_t d, uint32_t a, uint32_t a_lo, uint32_t b, uint32_t b_lo,
+                                               int a_tile, int b_tile) {
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb) {
+        const uint64_t da = umma_desc(a + kb * a_tile), dal = umma_desc(a_lo + kb * a_tile);
+        const uint64_t db = umma_desc(b + kb * b_tile), dbl = umma_desc(b_lo + kb * b_tile);
+#pragma unroll
+        for (int ks = 0; ks < kBK / 8; ++ks) {
+            const uint64_t adv = static_cast<uint64_t>(ks * 32) >> 4;  // 8 tf32 = 32 B per K-step
+            mma_tf32_n64(d, da + adv, db + adv, (kb | ks) != 0);
+            mma_tf32_n64(d, da + adv, dbl + adv, 1u);
+            mma_tf32_n64(d, dal + adv, db + adv, 1u);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kFaThreads, 1)
+    attn_flash_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_qlo,
+                         const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_klo,
+                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_vlo,
+                         float* __restrict__ out, float* __restrict__ out_lo, int n, int max_ctx, int ldo,
+                         float* __restrict__ ws, int* __restrict__ tickets, int ws_splits, int* err) {
+    extern __shared__ __align__(1024) char smem_raw[];
+    char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kFaOffBar);
+    uint64_t* q_full = bars;        // q landed
+    uint64_t* k_full = bars + 1;    // k tile landed
+    uint64_t* k_empty = bars + 2;   // its scores MMA done
+    uint64_t* v_full = bars + 3;    // [kFaVStages] v^T tile landed
+    uint64_t* v_empty = bars + 5;   // [kFaVStages] its P.V MMA done
+    uint64_t* s_full = bars + 7;    // [2] scores in TMEM
+    uint64_t* p_full = bars + 9;    // P written (128 arrivals)
+    uint64_t* pv_full = bars + 10;  // [2] P.V in TMEM (and the P buffer free again)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Work unit blockIdx.x: the query tiles from the last (longest) down, each tile's key tiles cut into
+    // `splits` balanced runs of at most kFaSplit; this unit takes run sp, key tiles [kt0, kt0 + nkt).
+    const int nqt = (n + kBM - 1) / kBM;
+    int qt = nqt - 1, splits = 1, sp = static_cast<int>(blockIdx.x), kt_all = 1;
+    for (; qt > 0; --qt) {
+        kt_all = (min(n, (qt + 1) * kBM) + kFaKeys - 1) / kFaKeys;
+        splits = (kt_all + kFaSplit - 1) / kFaSplit;
+        if (sp < splits) break;
+        sp -= splits;
+    }
+    if (qt == 0) {
+        kt_all = (min(n, kBM) + kFaKeys - 1) / kFaKeys;
+        splits = (kt_all + kFaSplit - 1) / kFaSplit;
+    }
+    const int q0 = qt * kBM;
+    const int h = blockIdx.y;
+    const int per = (kt_all + splits - 1) / splits;
+    const int kt0 = sp * per;
+    const int nkt = min(kt_all, kt0 + per) - kt0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        mbar_init(k_full, 1);
+        mbar_init(k_empty, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&pv_full[i], 1);
+        }
+        mbar_init(p_full, 4 * 32);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kFaTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            mbar_expect_tx(q_full, kFaQBytes);
+            for (int kb = 0; kb < 2; ++kb) {
+                tma_load_2d(smem + kb * kFaQTile, &tm_q, h * kHeadDim + kb * kBK, q0, q_full);
+                tma_load_2d(smem + 2 * kFaQTile + kb * kFaQTile, &tm_qlo, h * kHeadDim + kb * kBK, q0, q_full);
+            }
+            for (int j = 0; j < nkt; ++j) {
+                if (!wait_bar(k_empty, (j & 1) ^ 1u, err)) break;
+                char* kst = smem + kFaOffK;
+                mbar_expect_tx(k_full, kFaKStage);
+                for (int kb = 0; kb < 2; ++kb) {
+                    const int y = h * max_ctx + (kt0 + j) * kFaKeys;
+                    tma_load_2d(kst + kb * kFaKTile, &tm_k, kb * kBK, y, k_full);
+                    tma_load_2d(kst + 2 * kFaKTile + kb * kFaKTile, &tm_klo, kb * kBK, y, k_full);
+                }
+            }
+        } else if (lane == 1) {
+            for (int j = 0; j < nkt; ++j) {
+                const int st = j % kFaVStages;
+                if (!wait_bar(&v_empty[st], ((j / kFaVStages) & 1) ^ 1u, err)) break;
+                char* vs = smem + kFaOffV + st * kFaVBytes;
+                mbar_expect_tx(&v_full[st], kFaVBytes);
+                for (int kb = 0; kb < 2; ++kb) {
+                    const int x = (kt0 + j) * kFaKeys + kb * kBK;
+                    tma_load_2d(vs + kb * kFaKTile, &tm_v, x, h * kHeadDim, &v_full[st]);
+                    tma_load_2d(vs + 2 * kFaKTile + kb * kFaKTile, &tm_vlo, x, h * kHeadDim, &v_full[st]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t qa = smem_u32(smem), pa = smem_u32(smem + kFaOffP);
+            bool ok = wait_bar(q_full, 0, err);
+            // scores of key tile j into S slot j % 2 (its previous use, tile j - 2, was read before P_{j-2} was
+            // written, which the P.V MMA of tile j - 2 waited for)
+            auto scores = [&](int j) -> bool {
+                const int st = j & 1;
+                if (!wait_bar(k_full, j & 1, err)) return false;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t ka = smem_u32(smem + kFaOffK);
+                mma_3xtf32_k64(tmem + st * kFaKeys, qa, qa + 2 * kFaQTile, ka, ka + 2 * kFaKTile, kFaQTile, kFaKTile);
+                mma_commit(k_empty);
+                mma_commit(&s_full[st]);
+                return true;
+            };
+            if (ok) ok = scores(0);
+            for (int j = 0; ok && j < nkt; ++j) {
+                if (j + 1 < nkt && !scores(j + 1)) break;
+                const int vs = j % kFaVStages;
+                if (!wait_bar(p_full, j & 1, err) || !wait_bar(&v_full[vs], (j / kFaVStages) & 1, err)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t va = smem_u32(smem + kFaOffV + vs * kFaVBytes);
+                mma_3xtf32_k64(tmem + 2 * kFaKeys + (j & 1) * kFaKeys, pa, pa + 2 * kFaQTile, va, va + 2 * kFaKTile,
+                               kFaQTile, kFaKTile);
+                mma_commit(&v_empty[vs]);
+                mma_commit(&pv_full[j & 1]);
+            }
+        }
+    } else {
+        const int qq = warp & 3;  // TMEM lane quarter of this warp: rows 32 qq .. 32 qq + 31
+        const int r = 32 * qq + lane;
+        const int q = q0 + r;
+        const uint32_t trow = tmem + (static_cast<uint32_t>(32 * qq) << 16);
+        char* pb = smem + kFaOffP;
+        float o[kHeadDim];
+#pragma unroll
+        for (int d = 0; d < kHeadDim; ++d) o[d] = 0.0f;
+        float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < nkt; ++j) {
+            const int st = j & 1;
+            // waits are warp-uniform: tcgen05.ld needs the whole warp
+            if (!__all_sync(0xffffffffu, wait_bar(&s_full[st], (j >> 1) & 1, err))) {
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            float sv[kFaKeys];
+            tmem_ld32(trow + st * kFaKeys, sv);
+            tmem_ld32(trow + st * kFaKeys + 32, sv + 32);
+            tmem_wait_ld();
+            const int k0 = (kt0 + j) * kFaKeys;
+            if (k0 + kFaKeys - 1 > q0) {  // a tile on the diagonal: keys past the row's query masked
+#pragma unroll
+                for (int c = 0; c < kFaKeys; ++c)
+                    if (k0 + c > q) sv[c] = -INFINITY;
+            }
+            // the row maximum and sum as eight independent chains
+            float mx[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mx[i] = sv[i];
+#pragma unroll
+            for (int c = 8; c < kFaKeys; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+            const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                   fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            const float mn = fmaxf(m, mt);
+            // exp(x) = 2^(x log2 e): one FMA and one exp2f per key; a masked key (-inf) gives 0
+            const float mb = mn * kLog2e;
+            const float alpha = exp2f(fmaf(m, kLog2e, -mb));  // 0 at the first tile (m = -inf; key 0 is in every row)
+            float ls[8];
+#pragma unroll
+            for (int c = 0; c < kFaKeys; ++c) {
+                const float pc = exp2f(fmaf(sv[c], kLog2e, -mb));
+                sv[c] = pc;
+                if (c < 8) ls[c] = pc;
+                else ls[c & 7] += pc;
+            }
+            l = fmaf(l, alpha, ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7])));
+            m = mn;
+            const int pj = j - 1;
+            if (j > 0) {  // the previous tile's P.V done: the P buffer is free, its result in TMEM
+                if (!__all_sync(0xffffffffu, wait_bar(&pv_full[pj & 1], (pj >> 1) & 1, err))) {
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            }
+            // P and its lo half as K-major, 128B-swizzled A tiles: row r, 16-byte chunk c of K-block kb at
+            // kb * 16 KB + (r / 8) * 1024 + (r % 8) * 128 + (c ^ (r % 8)) * 16
+#pragma unroll
+            for (int kb = 0; kb < 2; ++kb) {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float* e = sv + kb * kBK + 4 * c;
+                    const int off = kb * kFaQTile + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4);
+                    *reinterpret_cast<float4*>(pb + off) = make_float4(e[0], e[1], e[2], e[3]);
+                    *reinterpret_cast<float4*>(pb + 2 * kFaQTile + off) =
+                        make_float4(tf32_lo(e[0]), tf32_lo(e[1]), tf32_lo(e[2]), tf32_lo(e[3]));
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            mbar_arrive(p_full);
+            if (j > 0) {  // fold the previous tile's P.V while this tile's runs (another TMEM slot)
+                float pv[kHeadDim];
+                tmem_ld32(trow + 2 * kFaKeys + (pj & 1) * kFaKeys, pv);
+                tmem_ld32(trow + 2 * kFaKeys + (pj & 1) * kFaKeys + 32, pv + 32);
+                tmem_wait_ld();
+#pragma unroll
+                for (int d = 0; d < kHeadDim; ++d) o[d] = fmaf(o[d], alpha_prev, pv[d]);
+            }
+            alpha_prev = alpha;
+        }
+        if (ok && nkt > 0) {
+            const int pj = nkt - 1;
+            if (__all_sync(0xffffffffu, wait_bar(&pv_full[pj & 1], (pj >> 1) & 1, err))) {
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                float pv[kHeadDim];
+                tmem_ld32(trow + 2 * kFaKeys + (pj & 1) * kFaKeys, pv);
+                tmem_ld32(trow + 2 * kFaKeys + (pj & 1) * kFaKeys + 32, pv + 32);
+                tmem_wait_ld();
+#pragma unroll
+                for (int d = 0; d < kHeadDim; ++d) o[d] = fmaf(o[d], alpha_prev, pv[d]);
+                bool write = true;
+                if (splits > 1) {
+                    // this run's (output, max, sum) of the row to the workspace; the warp that takes the last
+                    // ticket of its 32 rows merges every run's (the tickets return to 0 for the next launch)
+                    const size_t unit = (static_cast<size_t>(h) * nqt + qt) * ws_splits;
+                    float4* mine = reinterpret_cast<float4*>(ws + ((unit + sp) * kBM + r) * kFaPart);
+#pragma unroll
+                    for (int d = 0; d < kHeadDim; d += 4) mine[d >> 2] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+                    mine[kHeadDim / 4] = make_float4(m, l, 0.0f, 0.0f);
+                    __threadfence();
+                    __syncwarp();
+                    int* tk = tickets + (static_cast<size_t>(h) * nqt + qt) * 4 + qq;
+                    int last = 0;
+                    if (lane == 0) last = atomicAdd(tk, 1) == splits - 1;
+                    write = __shfl_sync(0xffffffffu, last, 0) != 0;
+                    if (write) {
+                        __threadfence();
+                        if (lane == 0) *tk = 0;
+                        float mm = m;
+                        for (int s2 = 0; s2 < splits; ++s2)
+                            if (s2 != sp) mm = fmaxf(mm, __ldcg(ws + ((unit + s2) * kBM + r) * kFaPart + kHeadDim));
+                        const float wm = exp2f((m - mm) * kLog2e);
+                        l *= wm;
+#pragma unroll
+                        for (int d = 0; d < kHeadDim; ++d) o[d] *= wm;
+                        for (int s2 = 0; s2 < splits; ++s2) {
+                            if (s2 == sp) continue;
+                            const float4* th = reinterpret_cast<const float4*>(ws + ((unit + s2) * kBM + r) * kFaPart);
+                            const float4 ml = __ldcg(th + kHeadDim / 4);
+                            const float w = exp2f((ml.x - mm) * kLog2e);
+                            l = fmaf(ml.y, w, l);
+#pragma unroll
+                            for (int d = 0; d < kHeadDim; d += 4) {
+                                const float4 v = __ldcg(th + (d >> 2));
+                                o[d] = fmaf(v.x, w, o[d]);
+                                o[d + 1] = fmaf(v.y, w, o[d + 1]);
+                                o[d + 2] = fmaf(v.z, w, o[d + 2]);
+                                o[d + 3] = fmaf(v.w, w, o[d + 3]);
+                            }
+                        }
+                    }
+                }
+                if (write && q < n) {
+                    const float inv = 1.0f / l;
+                    float4* dst = reinterpret_cast<float4*>(out + static_cast<size_t>(q) * ldo + h * kHeadDim);
+                    float4* dlo = reinterpret_cast<float4*>(out_lo + static_cast<size_t>(q) * ldo + h * kHeadDim);
+#pragma unroll
+                    for (int d = 0; d < kHeadDim; d += 4) {
+                        const float4 v = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+                        dst[d >> 2] = v;
+                        dlo[d >> 2] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+                    }
+                }
+            }
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    }
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kFaTmemCols) : "memory");
+    }
 }
 
 template <int MODE>
@@ -486,6 +865,37 @@ cudaError_t launch_attn_pv_tc(const TcOperands& o, float* out, float* out_lo, in
     const int k = ((n + kBK - 1) / kBK) * kBK;
     const unsigned t = static_cast<unsigned>((n + kBN - 1) / kBN);
     return launch_tc<kGemmPV>(dim3(1, t, heads), o, nullptr, out, out_lo, kHeadDim, n, k, err, s, bt);
+}
+
+int attn_flash_ws_splits(int max_ctx) {
+    return ((max_ctx + kFaKeys - 1) / kFaKeys + kFaSplit - 1) / kFaSplit;
+}
+
+size_t attn_flash_ws_floats(int heads, int max_ctx) {
+    const int splits = attn_flash_ws_splits(max_ctx);
+    if (splits <= 1) return 0;
+    return static_cast<size_t>(heads) * ((max_ctx + kBM - 1) / kBM) * splits * kBM * kFaPart;
+}
+
+cudaError_t launch_attn_flash_tc(const FlashOperands& o, float* out, float* out_lo, int n, int heads, int max_ctx,
+                                 float* ws, size_t ws_floats, int* tickets, int* err, cudaStream_t s) {
+    if (n <= 0 || n > max_ctx || heads <= 0 || max_ctx % kBK || ws_floats < attn_flash_ws_floats(heads, max_ctx))
+        return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(attn_flash_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kFaSmem));
+    if (e != cudaSuccess) return e;
+    // one CTA per run of at most kFaSplit key tiles of each 128-query tile
+    int units = 0;
+    for (int qt = 0; qt * kBM < n; ++qt) {
+        const int kt = (std::min(n, (qt + 1) * kBM) + kFaKeys - 1) / kFaKeys;
+        units += (kt + kFaSplit - 1) / kFaSplit;
+    }
+    count_launch();
+    const dim3 grid(static_cast<unsigned>(units), static_cast<unsigned>(heads));
+    attn_flash_tc_kernel<<<grid, kFaThreads, kFaSmem, s>>>(o.q, o.q_lo, o.k, o.k_lo, o.v, o.v_lo, out, out_lo, n,
+                                                             max_ctx, heads * kHeadDim, ws, tickets,
+                                                             attn_flash_ws_splits(max_ctx), err);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_split_lo(const float* x, float* lo, size_t n, cudaStream_t s) {

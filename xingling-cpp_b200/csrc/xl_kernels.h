@@ -320,7 +320,7 @@ cudaError_t launch_sample_merge(const SampleMergeParams& p, bool pdl, cudaStream
 struct TcOperands {
     CUtensorMap w, w_lo, x, x_lo;
 };
-cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int cols);
+cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int cols, int box_rows = 128);
 // C[N][M] (+)= X[N][K] . W[M][K]^T + b with the 3xTF32 split; SwiGLU writes C and C_lo as [N][M/2].
 // With a workspace (ws, ws_floats) and fewer output tiles than SMs, K is split
 // into slices whose partial sums are added in slice order by a second kernel.
@@ -347,6 +347,21 @@ cudaError_t launch_attn_scores_tc(const TcOperands& o, float* S, int n, int head
 // o.x / o.x_lo: P [heads*T][T]; o.w / o.w_lo: v transposed [heads*64][T].
 cudaError_t launch_attn_pv_tc(const TcOperands& o, float* out, float* out_lo, int n, int heads, int max_ctx, int* err,
                               cudaStream_t s);
+// Causal attention of a prompt starting at position 0 in one kernel per layer
+// (flash-style: scores and probabilities stay in TMEM and shared memory):
+// out[q][h*64 + d] and its lo half for q < n.  Operand maps ({32, rows}
+// boxes, 128B swizzle): q/8 and q_lo [T][heads*64] with 128-row boxes; k and
+// k_lo [heads*T][64] and v^T and its lo half [heads*64][T] with 64-row boxes.
+struct FlashOperands {
+    CUtensorMap q, q_lo, k, k_lo, v, v_lo;
+};
+// Rows longer than 4 key tiles of 64 are split over CTAs, whose partial rows
+// meet in a workspace of attn_flash_ws_floats(heads, max_ctx) floats, merged
+// by the last of them (tickets: heads * ceil(max_ctx / 128) * 4 ints, zero
+// before the first launch and left zero by every complete launch).
+size_t attn_flash_ws_floats(int heads, int max_ctx);
+cudaError_t launch_attn_flash_tc(const FlashOperands& o, float* out, float* out_lo, int n, int heads, int max_ctx,
+                                 float* ws, size_t ws_floats, int* tickets, int* err, cudaStream_t s);
 cudaError_t launch_gemm_tc(int mode, const TcOperands& o, const float* bias, float* C, float* C_lo, int n, int m,
                            int k, int* err, cudaStream_t s, float* ws = nullptr, size_t ws_floats = 0,
                            int num_sms = 148);
