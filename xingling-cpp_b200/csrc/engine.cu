@@ -641,6 +641,9 @@ int Engine::prepare_prefill_operands() {
         XL_CUDA(make_tile_map(&L.tc_qkv.w_lo, L.wqkv_lo, 3 * Hl_, H_));
         XL_CUDA(make_tile_map(&L.tc_qkv.x, pxn_, T_, H_));
         XL_CUDA(make_tile_map(&L.tc_qkv.x_lo, pxn_lo_, T_, H_));
+        XL_CUDA(make_tile_map(&L.tc_qkv.x_wide, pxn_, T_, H_, 256));
+        XL_CUDA(make_tile_map(&L.tc_qkv.x_lo_wide, pxn_lo_, T_, H_, 256));
+        L.tc_qkv.wide = true;
         XL_CUDA(make_tile_map(&L.tc_wo.w, L.wo, H_, Hl_));
         XL_CUDA(make_tile_map(&L.tc_wo.w_lo, L.wo_lo, H_, Hl_));
         XL_CUDA(make_tile_map(&L.tc_wo.x, patt_, T_, Hl_));
@@ -649,6 +652,9 @@ int Engine::prepare_prefill_operands() {
         XL_CUDA(make_tile_map(&L.tc_w13.w_lo, L.w13_lo, 2 * Fl_, H_));
         XL_CUDA(make_tile_map(&L.tc_w13.x, pxn_, T_, H_));
         XL_CUDA(make_tile_map(&L.tc_w13.x_lo, pxn_lo_, T_, H_));
+        XL_CUDA(make_tile_map(&L.tc_w13.x_wide, pxn_, T_, H_, 256));
+        XL_CUDA(make_tile_map(&L.tc_w13.x_lo_wide, pxn_lo_, T_, H_, 256));
+        L.tc_w13.wide = true;
         XL_CUDA(make_tile_map(&L.tc_w2.w, L.w2, H_, Fl_));
         XL_CUDA(make_tile_map(&L.tc_w2.w_lo, L.w2_lo, H_, Fl_));
         XL_CUDA(make_tile_map(&L.tc_w2.x, pffh_, T_, Fl_));

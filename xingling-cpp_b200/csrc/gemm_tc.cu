@@ -124,9 +124,33 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
+__device__ __forceinline__ void mma_tf32_i(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// A projection tile of 128 features x BN tokens: the token operand's tile
+// (X, X_lo) grows with BN; 128 tokens keep three stages of 64 KB, 256 tokens
+// two of 96 KB (the same shared memory, twice the MMA work per byte of W).
+template <int BN>
+struct TileCfg {
+    static_assert(BN == 128 || BN == 256, "tile width");
+    static constexpr int kXTile = BN * kBK * 4;
+    static constexpr int kStage = 2 * kTileBytes + 2 * kXTile;
+    static constexpr int kStages = BN == 128 ? 3 : 2;
+    static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStage + 1024 + 256;
+    // kind::tf32, fp32 accumulate, K-major A and B, M = 128, N = BN
+    static constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                       (static_cast<uint32_t>(kBM >> 4) << 24);
+};
+
 __device__ __forceinline__ float tf32_lo(float v) { return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
 
-template <int MODE>
+template <int MODE, int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wlo,
                    const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_xlo,
@@ -134,16 +158,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                    int K, int* err, const GemmBatch bt) {
     extern __shared__ __align__(1024) char smem_raw[];
     constexpr bool kBatched = MODE == kGemmScores || MODE == kGemmPV;
+    using Cfg = TileCfg<BN>;
+    static_assert(BN == 128 || !kBatched, "the attention modes use 128-token tiles");
     // Scores: a tile whose first key follows its last query is fully masked (causal).
-    if (MODE == kGemmScores && static_cast<int>(blockIdx.x) * kBM >= static_cast<int>(blockIdx.y + 1) * kBN) return;
+    if (MODE == kGemmScores && static_cast<int>(blockIdx.x) * kBM >= static_cast<int>(blockIdx.y + 1) * BN) return;
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-    uint64_t* empty = full + kStages;
-    uint64_t* accum = empty + kStages;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kStages * Cfg::kStage);
+    uint64_t* empty = full + Cfg::kStages;
+    uint64_t* accum = empty + Cfg::kStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
+    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
     // split-K: this CTA's K-blocks [kb0, kb1) of blockIdx.z of gridDim.z slices;
     // batched (attention) modes: blockIdx.z is the head and K is whole, or for
     // P.V cut at the tile's last query (P is zero past it).
@@ -153,14 +179,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         kb0 = static_cast<int>(static_cast<long long>(blockIdx.z) * nkb_all / gridDim.z);
         kb1 = static_cast<int>(static_cast<long long>(blockIdx.z + 1) * nkb_all / gridDim.z);
     } else if (MODE == kGemmPV) {
-        kb1 = min(nkb_all, (min(N, n0 + kBN) + kBK - 1) / kBK);
+        kb1 = min(nkb_all, (min(N, n0 + BN) + kBK - 1) / kBK);
     }
     const int nkb = kb1 - kb0;
     const int bz = kBatched ? static_cast<int>(blockIdx.z) : 0;
     const int wx0 = bz * bt.w_x, wy0 = bz * bt.w_y, xx0 = bz * bt.x_x, xy0 = bz * bt.x_y;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < Cfg::kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -169,7 +195,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(kBN)
+                     "r"(BN)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -181,34 +207,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % kStages;
-                const uint32_t ph = static_cast<uint32_t>(kb / kStages) & 1u;
+                const int s = kb % Cfg::kStages;
+                const uint32_t ph = static_cast<uint32_t>(kb / Cfg::kStages) & 1u;
                 if (!wait_bar(&empty[s], ph ^ 1u, err)) break;
-                char* st = smem + s * kStageBytes;
+                char* st = smem + s * Cfg::kStage;
                 const int kx = (kb0 + kb) * kBK;
-                mbar_expect_tx(&full[s], kStageBytes);
+                mbar_expect_tx(&full[s], Cfg::kStage);
                 tma_load_2d(st, &tm_w, kx + wx0, m0 + wy0, &full[s]);
                 tma_load_2d(st + kTileBytes, &tm_wlo, kx + wx0, m0 + wy0, &full[s]);
                 tma_load_2d(st + 2 * kTileBytes, &tm_x, kx + xx0, n0 + xy0, &full[s]);
-                tma_load_2d(st + 3 * kTileBytes, &tm_xlo, kx + xx0, n0 + xy0, &full[s]);
+                tma_load_2d(st + 2 * kTileBytes + Cfg::kXTile, &tm_xlo, kx + xx0, n0 + xy0, &full[s]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % kStages;
-                const uint32_t ph = static_cast<uint32_t>(kb / kStages) & 1u;
+                const int s = kb % Cfg::kStages;
+                const uint32_t ph = static_cast<uint32_t>(kb / Cfg::kStages) & 1u;
                 if (!wait_bar(&full[s], ph, err)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t base = smem_u32(smem + s * kStageBytes);
+                const uint32_t base = smem_u32(smem + s * Cfg::kStage);
                 const uint64_t dw = umma_desc(base), dwl = umma_desc(base + kTileBytes);
-                const uint64_t dx = umma_desc(base + 2 * kTileBytes), dxl = umma_desc(base + 3 * kTileBytes);
+                const uint64_t dx = umma_desc(base + 2 * kTileBytes);
+                const uint64_t dxl = umma_desc(base + 2 * kTileBytes + Cfg::kXTile);
 #pragma unroll
                 for (int ks = 0; ks < kBK / 8; ++ks) {
                     const uint64_t adv = static_cast<uint64_t>(ks * 32) >> 4;  // 8 tf32 = 32 B per K-step
-                    mma_tf32(tmem, dw + adv, dx + adv, (kb | ks) != 0);
-                    mma_tf32(tmem, dw + adv, dxl + adv, 1u);
-                    mma_tf32(tmem, dwl + adv, dx + adv, 1u);
+                    mma_tf32_i(tmem, dw + adv, dx + adv, Cfg::kIdesc, (kb | ks) != 0);
+                    mma_tf32_i(tmem, dw + adv, dxl + adv, Cfg::kIdesc, 1u);
+                    mma_tf32_i(tmem, dwl + adv, dx + adv, Cfg::kIdesc, 1u);
                 }
                 mma_commit(&empty[s]);
             }
@@ -223,7 +250,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (wait_bar(accum, 0, err)) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll 1
-            for (int c0 = 0; c0 < kBN; c0 += 32) {
+            for (int c0 = 0; c0 < BN; c0 += 32) {
                 uint32_t r[32];
                 const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(c0);
                 asm volatile(
@@ -274,7 +301,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
     }
 }
 
@@ -781,15 +808,17 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     }
 }
 
-template <int MODE>
+template <int MODE, int BN = kBN>
 cudaError_t launch_tc(dim3 grid, const TcOperands& o, const float* bias, float* C, float* C_lo, int m, int n, int k,
                       int* err, cudaStream_t s, const GemmBatch& bt = GemmBatch{}) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kGemmSmem));
+    constexpr size_t smem = TileCfg<BN>::kSmem;
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<MODE, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     count_launch();
-    gemm_tc_kernel<MODE><<<grid, kGemmThreads, kGemmSmem, s>>>(o.w, o.w_lo, o.x, o.x_lo, bias, C, C_lo, m, n, k, err,
-                                                                bt);
+    const CUtensorMap& x = BN == kBN ? o.x : o.x_wide;
+    const CUtensorMap& x_lo = BN == kBN ? o.x_lo : o.x_lo_wide;
+    gemm_tc_kernel<MODE, BN><<<grid, kGemmThreads, smem, s>>>(o.w, o.w_lo, x, x_lo, bias, C, C_lo, m, n, k, err, bt);
     return cudaGetLastError();
 }
 
@@ -829,6 +858,24 @@ cudaError_t launch_gemm_tc(int mode, const TcOperands& o, const float* bias, flo
                 return cudaErrorInvalidValue;
         }
         return cudaGetLastError();
+    }
+    // 256-token tiles where the operands have them and they take at most half the waves of 128-token ones
+    // (a 512-id W1/V: 128 tiles in one wave against 256 in two)
+    const int mt = (m + kBM - 1) / kBM;
+    const int w128 = (tiles + num_sms - 1) / num_sms;
+    const int w256 = (mt * ((n + 255) / 256) + num_sms - 1) / num_sms;
+    if (o.wide && n > kBN && 2 * w256 <= w128) {
+        const dim3 g2(mt, (n + 255) / 256, 1);
+        switch (mode) {
+            case kGemvPlain:
+                return launch_tc<kGemvPlain, 256>(g2, o, bias, C, C_lo, m, n, k, err, s);
+            case kGemvSwiGLU:
+                return launch_tc<kGemvSwiGLU, 256>(g2, o, bias, C, C_lo, m, n, k, err, s);
+            case kGemvResidual:
+                return launch_tc<kGemvResidual, 256>(g2, o, bias, C, C_lo, m, n, k, err, s);
+            default:
+                return cudaErrorInvalidValue;
+        }
     }
     switch (mode) {
         case kGemvPlain:

@@ -316,9 +316,12 @@ cudaError_t launch_sample_merge(const SampleMergeParams& p, bool pdl, cudaStream
 
 // ---- prefill on tcgen05 (gemm_tc.cu) ----
 // Operand maps of one projection: W and W_lo ([M][K]), X and X_lo ([rows][K]),
-// each a 2D TMA map with {32, 128} boxes and 128B swizzle (make_tile_map).
+// each a 2D TMA map with {32, 128} boxes and 128B swizzle (make_tile_map);
+// with `wide`, X and X_lo also with {32, 256} boxes for 256-token tiles.
 struct TcOperands {
     CUtensorMap w, w_lo, x, x_lo;
+    CUtensorMap x_wide, x_lo_wide;
+    bool wide = false;
 };
 cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int cols, int box_rows = 128);
 // C[N][M] (+)= X[N][K] . W[M][K]^T + b with the 3xTF32 split; SwiGLU writes C and C_lo as [N][M/2].
