@@ -432,28 +432,29 @@ cudaError_t make_stream_map(CUtensorMap* map, const float* base, int rows, int c
 
 // ---- Causal prefill attention in one kernel (flash-style, tcgen05, 3xTF32) ----
 //
-// The causal MultiHeadAttention::prefill of src/attn.cu:47-167 for one head
-// and 128 queries per CTA, with the scores and probabilities kept on chip:
-// for each tile of 64 keys, S = (q/8) k^T goes to TMEM, the four softmax
-// warps (one thread per query row) read their row of S, update the row's
-// running maximum and sum (online softmax), write P = exp(s - max) and its
-// TF32 lo half into shared memory as the A operand of the next MMA, and fold
-// the previous tile's P.V from TMEM into the row's output held in registers,
-// rescaled by exp(old max - new max).  The output row is divided by the sum
-// at the end and stored with its lo half (the out-projection's operands).
+// The causal MultiHeadAttention::prefill of src/attn.cu:47-167 for one head,
+// 128 queries and a run of key tiles per CTA, with the scores and
+// probabilities kept on chip: for each tile of 64 keys, S = (q/8) k^T goes to
+// TMEM, the four softmax warps (one thread per query row) read their row of
+// S, update the row's running maximum and sum (online softmax; exp as exp2f of
+// one FMA), write P = exp(s - max) and its TF32 lo half into shared memory as
+// the A operand of the next MMA, and fold the previous tile's P.V from TMEM
+// into the row's output held in registers, rescaled by exp(old max - new
+// max).  The output row is divided by the sum at the end and stored with its
+// lo half (the out-projection's operands).
 //   warp 0: TMA producer (lane 0: q, then the k tiles through one stage,
 //           loaded while the previous tile's scores are consumed; lane 1:
 //           the v^T tiles through two stages);
 //   warp 1: one thread issues the MMAs, S one tile ahead of P.V; S and P.V
 //           each have two TMEM slots of 64 columns;
+//   warps 2..5: softmax and output, TMEM lane quarter warp % 4; each thread
+//           writes its row of P and signals before it folds the previous
+//           tile's P.V, so that the next P.V MMA starts meanwhile.
 // A 128-query tile with more than kFaSplit key tiles is cut into balanced runs
 // of at most kFaSplit, one CTA each (so that the longest CTA is short and the
 // grid covers the SMs); each run stores its rows' (output, max, sum) to a
 // workspace and the warp that takes the last ticket of its 32 rows merges
-// them (src/attn.cu's online softmax across runs).
-//   warps 2..5: softmax and output, TMEM lane quarter warp % 4; each thread
-//           writes its row of P and signals before it folds the previous
-//           tile's P.V, so that the next P.V MMA starts meanwhile.
+// them (the same online-softmax rule across runs).
 // Products use the 3xTF32 split of the projections (hi.hi + hi.lo + lo.hi).
 // Keys past a row's query get probability 0; key tiles past the CTA's last
 // query are not visited.  Operands come from attn_prep_kernel: q/8 [T][heads
