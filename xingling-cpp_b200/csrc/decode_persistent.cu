@@ -1381,6 +1381,30 @@ __device__ __noinline__ bool attention_batch(const BatchPersistParams& bp, int l
     }
     const int U = ustart[kBatch];
     if (static_cast<int>(blockIdx.x) >= U) return true;  // no item: neither waits nor signals
+    // The cached K and V rows of this warp's chunks (positions before n_b, which the QKV phase does not
+    // touch) into L2 while that phase still runs: a lane pair takes the two 128-byte lines of one row.
+    for (int k = slot;; k += kBAttnSlots) {
+        const int u = static_cast<int>(blockIdx.x) + k * G;
+        if (u >= U) break;
+        int b = 0;
+#pragma unroll
+        for (int i = 1; i < kBatch; ++i)
+            if (u >= ustart[i]) b = i;
+        const int h = (u - ustart[b]) / nct[b], j = (u - ustart[b]) % nct[b];
+        const int n = bp.st[b].pos;
+        const size_t head_off = (static_cast<size_t>(b) * p.heads + h) * p.T * kHeadDim;
+        const float* kc = bp.kc[layer] + head_off;
+        const float* vc = bp.vc[layer] + head_off;
+        for (int c = 0; c < kBAttnChunks; ++c) {
+            const int row = (j * kConsumerWarps + half * kBAttnChunks + c) * kPersistChunk + (lane >> 1);
+            if (row - (lane >> 1) > n) break;  // chunk past the new position
+            if (row < n) {
+                const size_t off = static_cast<size_t>(row) * kHeadDim + (lane & 1) * 32;
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(kc + off));
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(vc + off));
+            }
+        }
+    }
     if (!wait_count(p, ph - 1, static_cast<int>(gridDim.x), s_ok)) return false;
     if (t == 0) trace_at(p, ph, kTrConsStart);
     float* qsh = xs + warp * kAttnWarpScratch;
