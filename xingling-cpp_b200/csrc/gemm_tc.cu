@@ -97,6 +97,11 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
+// A 2D tile of a tensor map into L2 only (no shared memory, no multicast).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
+                 : "memory");
+}
 // Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B apart.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
     uint64_t d = 0;
@@ -142,6 +147,9 @@ struct TileCfg {
     static constexpr int kXTile = BN * kBK * 4;
     static constexpr int kStage = 2 * kTileBytes + 2 * kXTile;
     static constexpr int kStages = BN == 128 ? 3 : 2;
+    // W and W_lo of K-block kb + kPrefetch go to L2 when K-block kb's loads are issued: the weight tiles come
+    // from DRAM, and the stages alone hold too few bytes in flight to cover that latency
+    static constexpr int kPrefetch = BN == 128 ? 4 : 2;
     static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStage + 1024 + 256;
     // kind::tf32, fp32 accumulate, K-major A and B, M = 128, N = BN
     static constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
@@ -217,6 +225,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 tma_load_2d(st + kTileBytes, &tm_wlo, kx + wx0, m0 + wy0, &full[s]);
                 tma_load_2d(st + 2 * kTileBytes, &tm_x, kx + xx0, n0 + xy0, &full[s]);
                 tma_load_2d(st + 2 * kTileBytes + Cfg::kXTile, &tm_xlo, kx + xx0, n0 + xy0, &full[s]);
+                if (!kBatched && kb + Cfg::kPrefetch < nkb) {
+                    const int px = (kb0 + kb + Cfg::kPrefetch) * kBK;
+                    tma_prefetch_2d(&tm_w, px + wx0, m0 + wy0);
+                    tma_prefetch_2d(&tm_wlo, px + wx0, m0 + wy0);
+                }
             }
         }
     } else if (warp == 1) {
