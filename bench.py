@@ -600,6 +600,16 @@ def tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, pa
     launches = llm_cpp_engine.kernel_launches() - n0
     dev = max_over_ranks(dev)
     kern = max_over_ranks(kern)
+    gen = None
+    if path == 0:
+        # the same workload through the device-side loop: one generate call per rank, no host round trip
+        # between steps (CUDA events around the call's steps, max over ranks)
+        tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
+        dist.barrier()
+        gen_ids = eng.generate(tok, n_dec, top_p=0.0, repetition_penalty=1.0)
+        gms = max_over_ranks(eng.last_device_ms())
+        gen = {"api": "llm_cpp_engine.InferenceEngine.generate", "ms_per_token": gms / n_dec,
+               "tokens_per_s": n_dec / (gms / 1e3), "same_ids_as_next_token": list(gen_ids) == toks[1:]}
     phases = None
     if trace and path == 0:
         # Phase timeline of one more step (the kernel stamps %globaltimer itself), rank 0's.
@@ -617,6 +627,8 @@ def tp_latency_path(llm_cpp_engine, dist, rank, world, local, max_over_ranks, pa
     out = {"tp": world, "prompt": 64, "decode_tokens": n_dec, "ms_per_token": dev / n_dec,
            "tokens_per_s": n_dec / (dev / 1e3), "first_tokens": toks[:8], "decode_path": path,
            "persistent_kernel_ms_per_token": kern / n_dec if path == 0 else None, "gpu_launches": launches}
+    if gen is not None:
+        out["generate"] = gen
     if phases is not None:
         out["phase_timeline_rank0"] = phases
     return out

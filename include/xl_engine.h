@@ -123,9 +123,11 @@ XL_API int xl_engine_decode(xl_engine* e, int token, float temperature, float to
  * after producing stop_id (when >= 0; it is returned) or when the cache is
  * full.  tokens_out receives the ids (capacity n), *n_out their count.  The
  * ids, the uniforms consumed (one per step taken) and the engine state equal
- * those of *n_out successive xl_engine_decode calls.  On a single GPU with the
- * persistent decode kernel the loop runs on the device; otherwise it is that
- * host loop. */
+ * those of *n_out successive xl_engine_decode calls.  With the persistent
+ * decode kernel the loop runs on the device: on one GPU for greedy and sampled
+ * steps, under tensor parallelism for greedy steps (option tp_merge 1, the
+ * default; every rank must make the same call, as for decode).  Otherwise it
+ * is that host loop. */
 XL_API int xl_engine_generate(xl_engine* e, int token, int n, float temperature, float top_p,
                               float repetition_penalty, int stop_id, int* tokens_out, int* n_out);
 

@@ -23,6 +23,8 @@ vocab shards.
   logits (the all-gather merge of per-shard top-1024 lists), and those logits
   match the oracle's, penalised with the engine's own history, within 1e-3 of
   their range.
+* Greedy generate on the device (every rank the same call): the same ids as
+  the next_token loop, one generation-graph launch per step.
 * A rank that stops calling between steps: the survivor's next step ends
   with RuntimeError within its step timeout (the communicator is aborted, no
   GPU work is left waiting), and the engine refuses later steps.
@@ -291,6 +293,57 @@ def _rank_stops(rank, world, wdir, shape_kw, ids, q_id, q_out, q_ctl, path, time
         q_out.put((rank, "ok", first, second, time.monotonic() - t2, None))
     except Exception as e:  # noqa: BLE001
         q_out.put((rank, "error", repr(e)[:400], None, None, None))
+
+
+def _rank_generate(rank, world, wdir, shape_kw, ids, steps, q_id, q_out):
+    """One rank: greedy generate(steps) after a prefill, then the same steps as
+    a next_token loop after the same prefill again; both id lists, the
+    positions and the launches the generate call made."""
+    try:
+        m, eng = _engine(rank, world, shape_kw, q_id, 0)
+        eng.load(wdir)
+        tok = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
+        n0 = m.kernel_launches()
+        gen = eng.generate(tok, steps, top_p=0.0, repetition_penalty=1.0)
+        launches = m.kernel_launches() - n0
+        ctx_gen = eng.ctx_len()
+        tok2 = eng.next_token(ids, top_p=0.0, repetition_penalty=1.0)
+        loop, t = [], tok2
+        for _ in range(steps):
+            t = eng.next_token(t, top_p=0.0, repetition_penalty=1.0)
+            loop.append(t)
+        q_out.put((rank, "ok", gen, loop, (tok, tok2, ctx_gen, eng.ctx_len()), launches))
+    except Exception as e:  # noqa: BLE001
+        q_out.put((rank, "error", repr(e)[:400], None, None, None))
+
+
+GEN_WORLDS = [2, 4, 8]
+
+
+@pytest.mark.parametrize("world", GEN_WORLDS, ids=[f"wide2-tp{w}" for w in GEN_WORLDS])
+def test_tp_generate_on_device_matches_next_token_loop(built, world):
+    """Greedy generate on tensor-parallel engines runs on the device: one
+    launch of the generation graph per step on every rank (gen_feed, the
+    persistent kernel after the step-start all-reduce, gen_collect), no host
+    round trip between steps, and the same ids, on every rank, as the
+    next_token loop after the same prefill."""
+    _need(world)
+    shape = S.WIDE2
+    wdir = S.write_weight_tree(os.path.join("/tmp/xl_weights", "wide2"), shape)
+    ids = S.prompt_ids(7, 31, shape.vocab)
+    steps = 40
+    out = _spawn(world, _rank_generate,
+                 lambda r, q_id, q_out: (r, world, wdir, shape.engine_kwargs(), ids, steps, q_id, q_out))
+    assert sorted(out) == list(range(world)), f"ranks missing: {out}"
+    for r in range(world):
+        assert out[r][1] == "ok", out[r][2]
+    for r in range(world):
+        tok, tok2, ctx_gen, ctx_loop = out[r][4]
+        assert tok == tok2
+        assert out[r][2] == out[r][3], f"rank {r}: generate {out[r][2]} != loop {out[r][3]}"
+        assert out[r][2] == out[0][2], "ranks disagree"
+        assert ctx_gen == ctx_loop == len(ids) + steps
+        assert out[r][5] == 3 * steps, f"rank {r}: {out[r][5]} launches for {steps} steps"
 
 
 @pytest.mark.parametrize("path", [0, 1], ids=["persistent", "per_op"])

@@ -974,8 +974,11 @@ int Engine::capture_decode_graph() {
 }
 
 // Device-side generation graphs: gen_feed, the persistent decode step and
-// gen_collect (single GPU, persistent path only: its kernels skip a step
-// once the run has stopped).
+// gen_collect (persistent path only: its kernels skip a step once the run has
+// stopped).  Tensor parallel: greedy steps whose argmax merges inside the
+// kernel (tp_merge), the step-start all-reduce included, so that every rank
+// runs the same collectives whether a step is skipped or not; sampled
+// tensor-parallel steps keep the host loop.
 int Engine::capture_gen_graphs() {
     for (int sampled = 0; sampled < 2; ++sampled) {
         cudaGraphExec_t& exec = sampled ? gen_exec_s_ : gen_exec_;
@@ -984,13 +987,14 @@ int Engine::capture_gen_graphs() {
             exec = nullptr;
         }
     }
-    if (!persistent_graph_ || tp_ > 1) return XL_OK;
+    if (!persistent_graph_) return XL_OK;
     GenParams gp{};
     gp.ctl = gen_ctl_;
     gp.uniforms = gen_u_;
     gp.out = gen_out_;
     gp.st = st_;
     for (int sampled = 0; sampled < 2; ++sampled) {
+        if (tp_ > 1 && (sampled || !tp_merge_)) continue;
         cudaGraphExec_t& exec = sampled ? gen_exec_s_ : gen_exec_;
         long long& kernels = sampled ? gen_graph_kernels_s_ : gen_graph_kernels_;
         cudaGraph_t g = nullptr;
@@ -1342,8 +1346,10 @@ int Engine::generate(int token, int n, float temperature, float top_p, float rp,
         set_error("KV cache full: position " + std::to_string(n_) + " of max_seq_len " + std::to_string(T_));
         return XL_ERR_CTX;
     }
-    if (!gen_exec_) {
-        // Per-op or tensor-parallel engines: the same loop on the host.
+    const bool sampled = top_p > 0.0f;
+    cudaGraphExec_t exec = sampled ? gen_exec_s_ : gen_exec_;
+    if (!exec) {
+        // Per-op engines and sampled tensor-parallel steps: the same loop on the host.
         int tok = token;
         for (int i = 0; i < n && n_ < T_; ++i) {
             const int rc = decode(tok, temperature, top_p, rp, &tok);
@@ -1373,8 +1379,6 @@ int Engine::generate(int token, int n, float temperature, float top_p, float rp,
     XL_CUDA(cudaMemcpyAsync(gen_ctl_, c, sizeof(GenCtl), cudaMemcpyHostToDevice, stream_));
     XL_CUDA(cudaMemcpyAsync(gen_u_, hu, static_cast<size_t>(steps) * 4, cudaMemcpyHostToDevice, stream_));
     XL_CUDA(cudaEventRecord(ev0_, stream_));
-    const bool sampled = top_p > 0.0f;
-    cudaGraphExec_t exec = sampled ? gen_exec_s_ : gen_exec_;
     for (int i = 0; i < steps; ++i) {
         XL_CUDA(cudaGraphLaunch(exec, stream_));
         count_graph_kernels(sampled ? gen_graph_kernels_s_ : gen_graph_kernels_);
@@ -1383,7 +1387,8 @@ int Engine::generate(int token, int n, float temperature, float top_p, float rp,
     XL_CUDA(cudaMemcpyAsync(c, gen_ctl_, sizeof(GenCtl), cudaMemcpyDeviceToHost, stream_));
     XL_CUDA(cudaMemcpyAsync(ho, gen_out_, static_cast<size_t>(steps) * 4, cudaMemcpyDeviceToHost, stream_));
     XL_CUDA(cudaMemcpyAsync(h_out_, st_, sizeof(DevState), cudaMemcpyDeviceToHost, stream_));
-    XL_CUDA(cudaStreamSynchronize(stream_));
+    // tensor parallel: bounded by the step timeout and NCCL's asynchronous error (a peer that stops)
+    if (const int rc = wait_stream("generate")) return rc;
     XL_CUDA(cudaEventElapsedTime(&last_ms_, ev0_, ev1_));
     const DevState* hs = reinterpret_cast<const DevState*>(h_out_);
     if (hs->err != 0) return device_error(hs->err);
