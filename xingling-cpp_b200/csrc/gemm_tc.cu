@@ -12,14 +12,15 @@
 // (about 1.5e-3 of the logit range after 16 layers), three do not.  W_lo is
 // prepared once at load time, X_lo by the kernel that produces X.
 //
-// Tile: 128 output features (MMA M) x 128 tokens (MMA N), K-blocks of 32
-// floats (128 B, the SWIZZLE_128B span).  Warp 0 issues TMA loads of the four
-// operand tiles of a K-block into a 3-stage ring; warp 1 (one thread) issues
-// 4 K-steps x 3 tcgen05.mma per K-block into a 128 x 128 fp32 accumulator in
-// TMEM and frees each stage with tcgen05.commit; warps 2..5 read the
-// accumulator with tcgen05.ld and apply the epilogue (bias; residual add;
-// SwiGLU over interleaved (W1 j, V j) feature pairs, which also writes the
-// lo half for the next GEMM).
+// Tile: 128 output features (MMA M) x 128 or 256 tokens (MMA N), K-blocks of
+// 32 floats (128 B, the SWIZZLE_128B span).  Warp 0 issues TMA loads of the
+// four operand tiles of a K-block into a ring (3 stages of 64 KB, or 2 of 96 KB
+// for 256 tokens) and prefetches the weight tiles of a later K-block into L2;
+// warp 1 (one thread) issues 4 K-steps x 3 tcgen05.mma per K-block into an fp32
+// accumulator in TMEM and frees each stage with tcgen05.commit; warps 2..5
+// read the accumulator with tcgen05.ld and apply the epilogue (bias; residual
+// add; SwiGLU over interleaved (W1 j, V j) feature pairs, which also writes
+// the lo half for the next GEMM).
 #include <cuda.h>
 #include <math.h>
 
@@ -33,13 +34,10 @@ namespace xl {
 namespace {
 
 constexpr int kBM = 128;               // output features per tile (MMA M)
-constexpr int kBN = 128;               // tokens per tile (MMA N)
+constexpr int kBN = 128;               // tokens per tile (MMA N; 256-token tiles: TileCfg<256>)
 constexpr int kBK = 32;                // floats per K-block (128 B rows)
-constexpr int kStages = 3;
-constexpr int kTileBytes = kBM * kBK * 4;  // 16 KB (kBN == kBM)
-constexpr int kStageBytes = 4 * kTileBytes;  // W, W_lo, X, X_lo
+constexpr int kTileBytes = kBM * kBK * 4;  // 16 KB: one 128-row operand tile of a K-block
 constexpr int kGemmThreads = 192;
-constexpr size_t kGemmSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 256;
 constexpr uint32_t kSpinLimit = 1u << 26;
 constexpr unsigned long long kWaitLimitNs = 200ull * 1000 * 1000;  // a tile's operands land in microseconds
 constexpr int kGemmPartial = 4;  // epilogue: raw slice accumulator into the split-K workspace
@@ -111,18 +109,6 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
     d |= static_cast<uint64_t>(1) << 46;                  // descriptor version (sm_100)
     d |= static_cast<uint64_t>(2) << 61;                  // SWIZZLE_128B
     return d;
-}
-// Instruction descriptor: kind::tf32, fp32 accumulate, K-major A and B, M = 128, N = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
-                            (static_cast<uint32_t>(kBM >> 4) << 24);
-
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate)
-        : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -405,8 +391,6 @@ EncodeTiledFn encode_fn() {
 }
 
 }  // namespace
-
-size_t gemm_tc_smem_bytes() { return kGemmSmem; }
 
 // Row-major [rows][cols] fp32 matrix as a 2D TMA map with {32, 128} boxes, 128B swizzle.
 cudaError_t make_tile_map(CUtensorMap* map, const float* base, int rows, int cols, int box_rows) {

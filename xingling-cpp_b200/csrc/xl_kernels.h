@@ -370,7 +370,6 @@ cudaError_t launch_gemm_tc(int mode, const TcOperands& o, const float* bias, flo
                            int num_sms = 148);
 // lo[i] = x[i] - (x[i] with its 13 low mantissa bits cleared): the TF32 residual.
 cudaError_t launch_split_lo(const float* x, float* lo, size_t n, cudaStream_t s);
-size_t gemm_tc_smem_bytes();
 
 // ---- prefill ----
 cudaError_t launch_embed_gather(const float* table, const int* ids, float* out, int n, int k, cudaStream_t s);
