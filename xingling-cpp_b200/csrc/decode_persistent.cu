@@ -1181,12 +1181,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_persistent_kernel(const __
 // is dotted with all kBatch inputs: warp w owns rows 4 (w % 4) .. + 3 of the box
 // over half of its K and keeps 4 x kBatch accumulators; one 32-value
 // butterfly leaves lane l with (row l / 8, sequence l % 8), and the two halves
-// meet in shared memory.  The residual streams ping-pong in global memory as
-// in the first form of the single-sequence kernel (no room for them in shared
-// memory).  Attention runs per (sequence, head, 128-position part) item,
-// spread over the grid, four at once per CTA.  The LM head applies each
-// sequence's penalty and keeps each sequence's argmax; a greedy step ends in
-// the kernel.
+// meet in shared memory (a double-buffered hand-over).  The residual streams
+// ping-pong in global memory (no room for them in shared memory): the last
+// contributor of each row quad of a split projection finishes it (a ticket),
+// and the next RMSNorm staging bulk-copies the eight finished vectors into
+// shared memory.  Attention runs per (sequence, head, 128-position part) item,
+// spread over the grid, four at once per CTA, with the cached K and V rows
+// prefetched into L2 before the wait.  The LM head applies each sequence's
+// penalty and keeps each sequence's argmax; a greedy step ends in the kernel.
 constexpr int kSlotsB = 3;
 constexpr size_t kSmemBytesB = static_cast<size_t>(kSlotsB) * kSlotBytes +
                                static_cast<size_t>(kBatch) * kBatchPersistMaxK * 4 + 2 * kSlotsB * 8 +
