@@ -434,16 +434,15 @@ cudaError_t make_stream_map(CUtensorMap* map, const float* base, int rows, int c
 // probabilities kept on chip: for each tile of 64 keys, S = (q/8) k^T goes to
 // TMEM, the four softmax warps (one thread per query row) read their row of
 // S, update the row's running maximum and sum (online softmax; exp as exp2f of
-// one FMA), write P = exp(s - max) and its TF32 lo half into shared memory as
-// the A operand of the next MMA, and fold the previous tile's P.V from TMEM
-// into the row's output held in registers, rescaled by exp(old max - new
-// max).  The output row is divided by the sum at the end and stored with its
+// one FMA), write P = exp(s - max) and its TF32 lo half into TMEM (tcgen05.st)
+// as the A operand of the next MMA (tcgen05.mma with A in tensor memory), and
+// fold the previous tile's P.V from TMEM into the row's output held in
+// registers, rescaled by exp(old max - new max).  The output row is divided by the sum at the end and stored with its
 // lo half (the out-projection's operands).
-//   warp 0: TMA producer (lane 0: q, then the k tiles through one stage,
-//           loaded while the previous tile's scores are consumed; lane 1:
-//           the v^T tiles through two stages);
+//   warp 0: TMA producer (lane 0: q, then the k tiles through two stages;
+//           lane 1: the v^T tiles through two stages);
 //   warp 1: one thread issues the MMAs, S one tile ahead of P.V; S and P.V
-//           each have two TMEM slots of 64 columns;
+//           each have two TMEM slots of 64 columns, P and P_lo 64 each;
 //   warps 2..5: softmax and output, TMEM lane quarter warp % 4; each thread
 //           writes its row of P and signals before it folds the previous
 //           tile's P.V, so that the next P.V MMA starts meanwhile.
@@ -462,17 +461,18 @@ constexpr int kFaKTile = kFaKeys * kBK * 4;        // 8 KB: 64 rows x 32 floats
 constexpr int kFaQBytes = 4 * kFaQTile;            // q and q_lo, two 32-float K-blocks each
 constexpr int kFaKStage = 4 * kFaKTile;            // k and k_lo of one tile
 constexpr int kFaVBytes = 4 * kFaKTile;            // v^T and its lo half of one tile
-constexpr int kFaPBytes = 4 * kFaQTile;            // P and P_lo of one tile
-constexpr int kFaOffK = kFaQBytes;
-constexpr int kFaOffV = kFaOffK + kFaKStage;
+constexpr int kFaKStages = 2;
 constexpr int kFaVStages = 2;
-constexpr int kFaOffP = kFaOffV + kFaVStages * kFaVBytes;
-constexpr int kFaOffBar = kFaOffP + kFaPBytes;
+constexpr int kFaOffK = kFaQBytes;
+constexpr int kFaOffV = kFaOffK + kFaKStages * kFaKStage;
+constexpr int kFaOffBar = kFaOffV + kFaVStages * kFaVBytes;
 constexpr size_t kFaSmem = static_cast<size_t>(kFaOffBar) + 256 + 1024;
 constexpr int kFaThreads = 6 * 32;                 // producer, MMA issuer, four softmax warps
 constexpr int kFaSplit = 4;                        // key tiles per CTA at most (longer rows split over CTAs)
 constexpr int kFaPart = kHeadDim + 4;              // a run's partial row in the workspace: output, max, sum
-constexpr uint32_t kFaTmemCols = 256;              // S slots at 0 and 64, P.V slots at 128 and 192
+constexpr uint32_t kFaTmemCols = 512;  // S slots at 0 and 64, P.V slots at 128 and 192, P at 256, P_lo at 320
+constexpr uint32_t kFaTmemP = 256;
+constexpr uint32_t kFaTmemPlo = 320;
 // kind::tf32, fp32 accumulate, K-major A and B, M = 128, N = 64
 constexpr uint32_t kIdescN64 = (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(kFaKeys >> 3) << 17) |
                                (static_cast<uint32_t>(kBM >> 4) << 24);
@@ -506,6 +506,33 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 32 consecutive TMEM columns of the warp's lane quarter (one row per thread), from registers.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])),
+        "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])),
+        "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
+        "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
+        "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// D (=|+=) A . B^T with A in TMEM (M = 128 lanes, one tf32 per column) and B in shared memory.
+__device__ __forceinline__ void mma_tf32_ts_n64(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(kIdescN64), "r"(accumulate)
+        : "memory");
+}
 
 // 3 x 4 K-steps x 2 K-blocks of 32 floats: D (=|+=) A . B^T over 64 columns of K.
 __device__ __forceinline__ void mma_3xtf32_k64(uint32_t d, uint32_t a, uint32_t a_lo, uint32_t b, uint32_t b_lo,
@@ -524,6 +551,24 @@ __device__ __forceinline__ void mma_3xtf32_k64(uint32_t d, uint32_t a, uint32_t 
     }
 }
 
+// P.V over one 64-key tile with P (and P_lo) in TMEM columns a, a_lo (key c at column c) and v^T in shared
+// memory: 3 x 4 K-steps x 2 K-blocks of 32 keys.
+__device__ __forceinline__ void mma_3xtf32_pv_tmem(uint32_t d, uint32_t a, uint32_t a_lo, uint32_t b, uint32_t b_lo,
+                                                   int b_tile) {
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb) {
+        const uint64_t db = umma_desc(b + kb * b_tile), dbl = umma_desc(b_lo + kb * b_tile);
+#pragma unroll
+        for (int ks = 0; ks < kBK / 8; ++ks) {
+            const uint32_t ac = static_cast<uint32_t>(kb * kBK + ks * 8);  // 8 tf32 keys = 8 columns per K-step
+            const uint64_t adv = static_cast<uint64_t>(ks * 32) >> 4;      // 8 tf32 = 32 B per K-step
+            mma_tf32_ts_n64(d, a + ac, db + adv, (kb | ks) != 0);
+            mma_tf32_ts_n64(d, a + ac, dbl + adv, 1u);
+            mma_tf32_ts_n64(d, a_lo + ac, db + adv, 1u);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kFaThreads, 1)
     attn_flash_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_qlo,
                          const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_klo,
@@ -534,14 +579,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kFaOffBar);
     uint64_t* q_full = bars;        // q landed
-    uint64_t* k_full = bars + 1;    // k tile landed
-    uint64_t* k_empty = bars + 2;   // its scores MMA done
-    uint64_t* v_full = bars + 3;    // [kFaVStages] v^T tile landed
-    uint64_t* v_empty = bars + 5;   // [kFaVStages] its P.V MMA done
-    uint64_t* s_full = bars + 7;    // [2] scores in TMEM
-    uint64_t* p_full = bars + 9;    // P written (128 arrivals)
-    uint64_t* pv_full = bars + 10;  // [2] P.V in TMEM (and the P buffer free again)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    uint64_t* k_full = bars + 1;    // [kFaKStages] k tile landed
+    uint64_t* k_empty = bars + 3;   // [kFaKStages] its scores MMA done
+    uint64_t* v_full = bars + 5;    // [kFaVStages] v^T tile landed
+    uint64_t* v_empty = bars + 7;   // [kFaVStages] its P.V MMA done
+    uint64_t* s_full = bars + 9;    // [2] scores in TMEM
+    uint64_t* p_full = bars + 11;   // P written to TMEM (128 arrivals)
+    uint64_t* pv_full = bars + 12;  // [2] P.V in TMEM (and the P columns free again)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Work unit blockIdx.x: the query tiles from the last (longest) down, each tile's key tiles cut into
@@ -566,9 +611,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        mbar_init(k_full, 1);
-        mbar_init(k_empty, 1);
         for (int i = 0; i < 2; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
@@ -596,13 +641,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 tma_load_2d(smem + 2 * kFaQTile + kb * kFaQTile, &tm_qlo, h * kHeadDim + kb * kBK, q0, q_full);
             }
             for (int j = 0; j < nkt; ++j) {
-                if (!wait_bar(k_empty, (j & 1) ^ 1u, err)) break;
-                char* kst = smem + kFaOffK;
-                mbar_expect_tx(k_full, kFaKStage);
+                const int st = j % kFaKStages;
+                if (!wait_bar(&k_empty[st], ((j / kFaKStages) & 1) ^ 1u, err)) break;
+                char* kst = smem + kFaOffK + st * kFaKStage;
+                mbar_expect_tx(&k_full[st], kFaKStage);
                 for (int kb = 0; kb < 2; ++kb) {
                     const int y = h * max_ctx + (kt0 + j) * kFaKeys;
-                    tma_load_2d(kst + kb * kFaKTile, &tm_k, kb * kBK, y, k_full);
-                    tma_load_2d(kst + 2 * kFaKTile + kb * kFaKTile, &tm_klo, kb * kBK, y, k_full);
+                    tma_load_2d(kst + kb * kFaKTile, &tm_k, kb * kBK, y, &k_full[st]);
+                    tma_load_2d(kst + 2 * kFaKTile + kb * kFaKTile, &tm_klo, kb * kBK, y, &k_full[st]);
                 }
             }
         } else if (lane == 1) {
@@ -620,17 +666,18 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t qa = smem_u32(smem), pa = smem_u32(smem + kFaOffP);
+            const uint32_t qa = smem_u32(smem);
             bool ok = wait_bar(q_full, 0, err);
             // scores of key tile j into S slot j % 2 (its previous use, tile j - 2, was read before P_{j-2} was
             // written, which the P.V MMA of tile j - 2 waited for)
             auto scores = [&](int j) -> bool {
                 const int st = j & 1;
-                if (!wait_bar(k_full, j & 1, err)) return false;
+                const int ks = j % kFaKStages;
+                if (!wait_bar(&k_full[ks], (j / kFaKStages) & 1, err)) return false;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t ka = smem_u32(smem + kFaOffK);
+                const uint32_t ka = smem_u32(smem + kFaOffK + ks * kFaKStage);
                 mma_3xtf32_k64(tmem + st * kFaKeys, qa, qa + 2 * kFaQTile, ka, ka + 2 * kFaKTile, kFaQTile, kFaKTile);
-                mma_commit(k_empty);
+                mma_commit(&k_empty[ks]);
                 mma_commit(&s_full[st]);
                 return true;
             };
@@ -641,8 +688,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 if (!wait_bar(p_full, j & 1, err) || !wait_bar(&v_full[vs], (j / kFaVStages) & 1, err)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t va = smem_u32(smem + kFaOffV + vs * kFaVBytes);
-                mma_3xtf32_k64(tmem + 2 * kFaKeys + (j & 1) * kFaKeys, pa, pa + 2 * kFaQTile, va, va + 2 * kFaKTile,
-                               kFaQTile, kFaKTile);
+                mma_3xtf32_pv_tmem(tmem + 2 * kFaKeys + (j & 1) * kFaKeys, tmem + kFaTmemP, tmem + kFaTmemPlo, va,
+                                   va + 2 * kFaKTile, kFaKTile);
                 mma_commit(&v_empty[vs]);
                 mma_commit(&pv_full[j & 1]);
             }
@@ -652,7 +699,6 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         const int r = 32 * qq + lane;
         const int q = q0 + r;
         const uint32_t trow = tmem + (static_cast<uint32_t>(32 * qq) << 16);
-        char* pb = smem + kFaOffP;
         float o[kHeadDim];
 #pragma unroll
         for (int d = 0; d < kHeadDim; ++d) o[d] = 0.0f;
@@ -699,27 +745,21 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             l = fmaf(l, alpha, ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7])));
             m = mn;
             const int pj = j - 1;
-            if (j > 0) {  // the previous tile's P.V done: the P buffer is free, its result in TMEM
+            if (j > 0) {  // the previous tile's P.V done: the P columns are free, its result in TMEM
                 if (!__all_sync(0xffffffffu, wait_bar(&pv_full[pj & 1], (pj >> 1) & 1, err))) {
                     ok = false;
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             }
-            // P and its lo half as K-major, 128B-swizzled A tiles: row r, 16-byte chunk c of K-block kb at
-            // kb * 16 KB + (r / 8) * 1024 + (r % 8) * 128 + (c ^ (r % 8)) * 16
+            // P and its lo half into TMEM, the A operand of the P.V MMA: this thread's row, key c at column c
+            tmem_st32(trow + kFaTmemP, sv);
+            tmem_st32(trow + kFaTmemP + 32, sv + 32);
 #pragma unroll
-            for (int kb = 0; kb < 2; ++kb) {
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const float* e = sv + kb * kBK + 4 * c;
-                    const int off = kb * kFaQTile + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4);
-                    *reinterpret_cast<float4*>(pb + off) = make_float4(e[0], e[1], e[2], e[3]);
-                    *reinterpret_cast<float4*>(pb + 2 * kFaQTile + off) =
-                        make_float4(tf32_lo(e[0]), tf32_lo(e[1]), tf32_lo(e[2]), tf32_lo(e[3]));
-                }
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            for (int c = 0; c < kFaKeys; ++c) sv[c] = tf32_lo(sv[c]);
+            tmem_st32(trow + kFaTmemPlo, sv);
+            tmem_st32(trow + kFaTmemPlo + 32, sv + 32);
+            tmem_wait_st();
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(p_full);
             if (j > 0) {  // fold the previous tile's P.V while this tile's runs (another TMEM slot)
